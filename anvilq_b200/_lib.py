@@ -1,0 +1,62 @@
+"""ctypes binding of libanvilq.so (include/anvilq.h).
+
+The library is the only compute path: if it is missing or fails to load this
+module raises, it never substitutes a CPU or PyTorch computation.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = Path(os.environ.get("ANVILQ_LIB", PKG / "libanvilq.so"))
+
+P = ctypes.c_void_p
+I = ctypes.c_int
+F = ctypes.c_float
+SZ = ctypes.c_size_t
+
+# name -> (restype, argtypes); kept in the order of include/anvilq.h
+SIGNATURES = {
+    "anvilq_abi_version": (I, []),
+    "anvilq_strerror": (ctypes.c_char_p, [I]),
+    "anvilq_w4a16_gemm_workspace_size": (SZ, [I, I, I, I]),
+    "anvilq_w4a16_gemm": (I, [P, P, P, P, P, P, I, I, I, I, P, SZ, P, P]),
+    "anvilq_w4a16_gemm_exact": (I, [P, P, P, P, P, P, I, I, I, I, P, P]),
+    "anvilq_awq_dequant": (I, [P, P, P, P, P, I, I, I, P, P]),
+    "anvilq_awq_pack": (I, [P, P, I, I, P]),
+    "anvilq_awq_unpack": (I, [P, P, I, I, P]),
+}
+
+_lib = None
+
+
+class AnvilqError(RuntimeError):
+    """A libanvilq call returned a negative status or a kernel raised a device error."""
+
+
+def load(path: Path | None = None):
+    """Load (once) and return the bound library."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path is not None else LIB_PATH
+    if not p.exists():
+        raise AnvilqError(f"{p} is missing: build it with `python -m anvilq_b200.build`")
+    lib = ctypes.CDLL(str(p))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if lib.anvilq_abi_version() != 1:
+        raise AnvilqError("libanvilq ABI version mismatch")
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def check(status: int, what: str = "anvilq call"):
+    if status != 0:
+        msg = load().anvilq_strerror(status).decode()
+        raise AnvilqError(f"{what} failed with status {status}: {msg}")

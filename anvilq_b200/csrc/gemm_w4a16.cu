@@ -1,0 +1,621 @@
+// gemm_w4a16.cu -- W4A16 AWQ GEMV / small-M GEMM on CUDA cores, the AWQ
+// dequantiser and the AWQ pack/unpack kernels, with their C-ABI entry points.
+//
+// Reference semantics: FP32Model.linear (anvil-q1/tests/official_weights.py:418-437),
+// dequant (anvil-q1/tests/verify.py:241-250), pack / pack_lanes / unpack_lanes
+// (verify.py:252-253, anvil-q1-fp/tests/awq_prepare.py:84-99).
+//
+// Fast path ("stream-K" over column bands):
+//   * A band is 32 consecutive qweight words of a row = 128 bytes = 256 output
+//     columns.  A slot is 16 consecutive rows of one band (2 KB of int4 data).
+//     The bands x slots items are linearised band-major and split into equal
+//     contiguous ranges, one per CTA of a persistent grid of (#SM x occupancy)
+//     CTAs, so every SM streams the same number of bytes (+-1 slot).
+//   * Inside a CTA, lane-groups (8 lanes x 4 words for M=1, a warp x 1 word for
+//     M>1) take the slots of the current band round-robin.  Each thread keeps
+//     16 row loads in flight, unpacks nibbles in registers (awq_common.cuh),
+//     accumulates x * (q - z) for the 16 rows in half2, then folds the partial
+//     into fp32 accumulators with the group's scale (a slot never straddles a
+//     group: G % 16 == 0).  The scale multiplies once per 16 products.
+//   * At the end of a band segment the lane-groups are reduced through shared
+//     memory in a fixed order.  A band covered by one CTA is written directly;
+//     a band split between CTAs leaves one fp32 partial per CTA in the
+//     workspace, and the CTA that arrives last (atomic ticket) sums them in
+//     CTA order -- deterministic, no spin-wait -- adds bias, rounds to fp16 and
+//     re-arms the ticket.
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <mutex>
+
+#include "../../include/anvilq.h"
+#include "awq_common.cuh"
+
+namespace anvilq {
+
+constexpr int kSlotRows = 16;
+constexpr int kBandWords = 32;
+constexpr int kBandCols = kBandWords * 8;   // 256
+constexpr int kThreads = 128;
+
+struct GemmParams {
+  const __half* x;        // [M][K]
+  const int32_t* qweight; // [K][W8]
+  const int32_t* qzeros;  // [K/G][W8]
+  const __half* scales;   // [K/G][N]
+  const __half* bias;     // [N] or null
+  __half* y;              // [M][N]
+  float* partials;        // [P][2][M][256]
+  int* tickets;           // [bands]
+  int* dev_err;
+  int K, N, W8, G;
+  int bands, slots;       // slots per band = K / 16
+  long long items;        // bands * slots
+};
+
+__device__ __forceinline__ long long range_begin(long long c, long long items, long long P) {
+  return c * items / P;
+}
+// CTA owning item i: the largest c with floor(c * items / P) <= i.
+__device__ __forceinline__ int owner_of(long long i, long long items, long long P) {
+  return (int)(((i + 1) * P + items - 1) / items - 1);
+}
+
+// Broadcast binary16 #j (0..7) of a uint4 into both halves of a half2.
+__device__ __forceinline__ half2 bcast_half(const uint4& v, int j) {
+  const uint32_t w = (j >> 1) == 0 ? v.x : (j >> 1) == 1 ? v.y : (j >> 1) == 2 ? v.z : v.w;
+  return u32_as_half2(__byte_perm(w, w, (j & 1) ? 0x3232 : 0x1010));
+}
+
+// Writes the CTA's reduced segment result for band `band` (M x 256 floats in
+// `seg`, one per thread-strided column) to y directly or through the workspace.
+template <int M>
+__device__ void finish_segment(const GemmParams& p, const float* seg, int band, bool whole,
+                               long long it, int* s_flag) {
+  const int col0 = band * kBandCols;
+  if (whole) {
+    for (int e = threadIdx.x; e < M * kBandCols; e += blockDim.x) {
+      const int m = e / kBandCols, c = e % kBandCols, col = col0 + c;
+      if (col < p.N) {
+        float v = seg[e];
+        if (p.bias) v += __half2float(p.bias[col]);
+        p.y[(size_t)m * p.N + col] = __float2half_rn(v);
+      }
+    }
+    return;
+  }
+  const long long P = gridDim.x;
+  const int me = blockIdx.x;
+  const int slot_j = (it == range_begin(me, p.items, P)) ? 0 : 1;
+  float* mine = p.partials + ((size_t)me * 2 + slot_j) * (M * kBandCols);
+  for (int e = threadIdx.x; e < M * kBandCols; e += blockDim.x) __stcg(mine + e, seg[e]);
+  __threadfence();
+  __syncthreads();
+  const long long band_first = (long long)band * p.slots;
+  const int c_lo = owner_of(band_first, p.items, P);
+  const int c_hi = owner_of(band_first + p.slots - 1, p.items, P);
+  if (threadIdx.x == 0) {
+    const int ticket = atomicAdd(p.tickets + band, 1);
+    const bool last = ticket == c_hi - c_lo;
+    if (last) p.tickets[band] = 0;   // re-arm for the next launch
+    *s_flag = last;
+  }
+  __syncthreads();
+  if (!*s_flag) return;
+  __threadfence();
+  for (int e = threadIdx.x; e < M * kBandCols; e += blockDim.x) {
+    const int m = e / kBandCols, c = e % kBandCols, col = col0 + c;
+    float v = 0.0f;
+    for (int q = c_lo; q <= c_hi; ++q) {
+      // Contributor q stored its partial for its first band in slot 0, else slot 1.
+      const int j = band == (int)(range_begin(q, p.items, P) / p.slots) ? 0 : 1;
+      v += __ldcg(p.partials + ((size_t)q * 2 + j) * (M * kBandCols) + e);
+    }
+    if (col < p.N) {
+      if (p.bias) v += __half2float(p.bias[col]);
+      p.y[(size_t)m * p.N + col] = __float2half_rn(v);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// M = 1: 8 lanes x 4 words (16-byte loads) per band row, 16 lane-groups.
+__global__ void __launch_bounds__(kThreads, 3) gemv_m1_kernel(const GemmParams p) {
+  constexpr int WPT = 4, LPR = 8, LG = kThreads / LPR;
+  __shared__ float red[LG][kBandCols + 4];
+  __shared__ float seg[kBandCols];
+  __shared__ int s_flag;
+  const int lane_in_row = threadIdx.x % LPR;
+  const int lg = threadIdx.x / LPR;
+  const long long P = gridDim.x;
+  const long long it0 = range_begin(blockIdx.x, p.items, P);
+  const long long it1 = range_begin(blockIdx.x + 1, p.items, P);
+  uint32_t bad = 0;
+
+  for (long long it = it0; it < it1;) {
+    const int band = (int)(it / p.slots);
+    const int s0 = (int)(it % p.slots);
+    const long long seg_end = min(it1, (long long)(band + 1) * p.slots);
+    const int s1 = (int)(seg_end - (long long)band * p.slots);
+    const int w0 = band * kBandWords + lane_in_row * WPT;
+    const bool active = w0 < p.W8;
+    float acc[WPT * 8];
+#pragma unroll
+    for (int j = 0; j < WPT * 8; ++j) acc[j] = 0.0f;
+
+    if (active) {
+      for (int s = s0 + lg; s < s1; s += LG) {
+        const int k0 = s * kSlotRows;
+        const int g = k0 / p.G;
+        Words<4> q[kSlotRows];
+#pragma unroll
+        for (int r = 0; r < kSlotRows; ++r)
+          q[r].load_stream(p.qweight + (size_t)(k0 + r) * p.W8 + w0);
+        Words<4> z;
+        z.load_ro(p.qzeros + (size_t)g * p.W8 + w0);
+        const uint4 xa = ld_ro_v4(p.x + k0);
+        const uint4 xb = ld_ro_v4(p.x + k0 + 8);
+        uint4 sc[WPT];
+#pragma unroll
+        for (int i = 0; i < WPT; ++i) sc[i] = ld_ro_v4(p.scales + (size_t)g * p.N + 8 * (w0 + i));
+
+        ZeroPoint zp[WPT];
+#pragma unroll
+        for (int i = 0; i < WPT; ++i) zp[i] = make_zero_point(z.w[i]);
+        half2 part[WPT * 4];
+#pragma unroll
+        for (int j = 0; j < WPT * 4; ++j) part[j] = __float2half2_rn(0.0f);
+#pragma unroll
+        for (int r = 0; r < kSlotRows; ++r) {
+          const half2 xx = bcast_half(r < 8 ? xa : xb, r & 7);
+#pragma unroll
+          for (int i = 0; i < WPT; ++i) {
+            half2 d[4];
+            unpack_deltas(q[r].w[i], zp[i], d);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) part[i * 4 + e] = __hfma2(xx, d[e], part[i * 4 + e]);
+          }
+        }
+        if (k0 % p.G == 0) {   // each (group, column) scale is checked exactly once
+#pragma unroll
+          for (int i = 0; i < WPT; ++i)
+            bad |= invalid_scale_pair(sc[i].x) | invalid_scale_pair(sc[i].y) |
+                   invalid_scale_pair(sc[i].z) | invalid_scale_pair(sc[i].w);
+        }
+#pragma unroll
+        for (int i = 0; i < WPT; ++i) {
+          const uint32_t sw[4] = {sc[i].x, sc[i].y, sc[i].z, sc[i].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(part[i * 4 + e]);
+            const float2 s2 = __half22float2(u32_as_half2(sw[e]));
+            acc[i * 8 + 2 * e] = fmaf(f.x, s2.x, acc[i * 8 + 2 * e]);
+            acc[i * 8 + 2 * e + 1] = fmaf(f.y, s2.y, acc[i * 8 + 2 * e + 1]);
+          }
+        }
+      }
+    }
+    // Reduce the lane-groups in a fixed order.
+#pragma unroll
+    for (int j = 0; j < WPT * 8; j += 4)
+      *reinterpret_cast<float4*>(&red[lg][lane_in_row * WPT * 8 + j]) =
+          make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+    __syncthreads();
+    for (int c = threadIdx.x; c < kBandCols; c += blockDim.x) {
+      float v = 0.0f;
+#pragma unroll
+      for (int l = 0; l < LG; ++l) v += red[l][c];
+      seg[c] = v;
+    }
+    __syncthreads();
+    finish_segment<1>(p, seg, band, s0 == 0 && s1 == p.slots, it, &s_flag);
+    __syncthreads();
+    it = seg_end;
+  }
+  if (bad && p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_SCALE);
+}
+
+// ---------------------------------------------------------------------------
+// 2 <= M <= 8: one warp per band row (1 word per lane), 4 warps; activations of
+// the slot are staged transposed in shared memory, xs[warp][row][m].
+template <int M>
+__global__ void __launch_bounds__(kThreads) gemm_smallm_kernel(const GemmParams p) {
+  constexpr int LG = kThreads / 32;
+  __shared__ float red[LG][M][kBandCols + 4];
+  __shared__ float seg[M * kBandCols];
+  __shared__ __align__(16) __half xs[LG][kSlotRows][8];
+  __shared__ int s_flag;
+  const int lane = threadIdx.x % 32;
+  const int lg = threadIdx.x / 32;
+  const long long P = gridDim.x;
+  const long long it0 = range_begin(blockIdx.x, p.items, P);
+  const long long it1 = range_begin(blockIdx.x + 1, p.items, P);
+  uint32_t bad = 0;
+
+  for (long long it = it0; it < it1;) {
+    const int band = (int)(it / p.slots);
+    const int s0 = (int)(it % p.slots);
+    const long long seg_end = min(it1, (long long)(band + 1) * p.slots);
+    const int s1 = (int)(seg_end - (long long)band * p.slots);
+    const int w0 = band * kBandWords + lane;
+    const bool active = w0 < p.W8;
+    float acc[M][8];
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[m][j] = 0.0f;
+
+    for (int s = s0 + lg; s < s1; s += LG) {   // warp-uniform loop
+      const int k0 = s * kSlotRows;
+      const int g = k0 / p.G;
+      uint32_t q[kSlotRows];
+      if (active) {
+#pragma unroll
+        for (int r = 0; r < kSlotRows; ++r)
+          q[r] = ld_stream_u32(p.qweight + (size_t)(k0 + r) * p.W8 + w0);
+      }
+      __syncwarp();
+      if (lane < 2 * M) {   // stage x[m][k0..k0+16) transposed
+        const int m = lane >> 1, h = lane & 1;
+        const uint4 v = ld_ro_v4(p.x + (size_t)m * p.K + k0 + 8 * h);
+        const __half* hv = reinterpret_cast<const __half*>(&v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) xs[lg][8 * h + j][m] = hv[j];
+      }
+      __syncwarp();
+      if (active) {
+        const uint32_t zw = __ldg(reinterpret_cast<const unsigned int*>(p.qzeros + (size_t)g * p.W8 + w0));
+        const uint4 sc = ld_ro_v4(p.scales + (size_t)g * p.N + 8 * w0);
+        const ZeroPoint zp = make_zero_point(zw);
+        half2 part[M][4];
+#pragma unroll
+        for (int m = 0; m < M; ++m)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) part[m][e] = __float2half2_rn(0.0f);
+#pragma unroll
+        for (int r = 0; r < kSlotRows; ++r) {
+          half2 d[4];
+          unpack_deltas(q[r], zp, d);
+          const uint4 xr = *reinterpret_cast<const uint4*>(&xs[lg][r][0]);
+#pragma unroll
+          for (int m = 0; m < M; ++m) {
+            const half2 xx = bcast_half(xr, m);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) part[m][e] = __hfma2(xx, d[e], part[m][e]);
+          }
+        }
+        if (k0 % p.G == 0)
+          bad |= invalid_scale_pair(sc.x) | invalid_scale_pair(sc.y) |
+                 invalid_scale_pair(sc.z) | invalid_scale_pair(sc.w);
+        const uint32_t sw[4] = {sc.x, sc.y, sc.z, sc.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 s2 = __half22float2(u32_as_half2(sw[e]));
+#pragma unroll
+          for (int m = 0; m < M; ++m) {
+            const float2 f = __half22float2(part[m][e]);
+            acc[m][2 * e] = fmaf(f.x, s2.x, acc[m][2 * e]);
+            acc[m][2 * e + 1] = fmaf(f.y, s2.y, acc[m][2 * e + 1]);
+          }
+        }
+      }
+      __syncwarp();
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      *reinterpret_cast<float4*>(&red[lg][m][lane * 8]) =
+          make_float4(acc[m][0], acc[m][1], acc[m][2], acc[m][3]);
+      *reinterpret_cast<float4*>(&red[lg][m][lane * 8 + 4]) =
+          make_float4(acc[m][4], acc[m][5], acc[m][6], acc[m][7]);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < M * kBandCols; e += blockDim.x) {
+      const int m = e / kBandCols, c = e % kBandCols;
+      float v = 0.0f;
+#pragma unroll
+      for (int l = 0; l < LG; ++l) v += red[l][m][c];
+      seg[e] = v;
+    }
+    __syncthreads();
+    finish_segment<M>(p, seg, band, s0 == 0 && s1 == p.slots, it, &s_flag);
+    __syncthreads();
+    it = seg_end;
+  }
+  if (bad && p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_SCALE);
+}
+
+// ---------------------------------------------------------------------------
+// Reference-order kernel: one thread per (row m, output column c), sequential
+// k, every binary32 operation rounded separately (no FMA contraction), as in
+// FP32Model.linear.  Bit-identical to the reference before the output store;
+// OutT = float keeps it, OutT = __half rounds it once (the fallback for shapes
+// the fast kernels do not take).
+__device__ __forceinline__ void store_out(float* y, long long i, float v) { y[i] = v; }
+__device__ __forceinline__ void store_out(__half* y, long long i, float v) { y[i] = __float2half_rn(v); }
+
+template <typename OutT>
+__global__ void gemm_exact_kernel(const __half* __restrict__ x, const int32_t* __restrict__ qweight,
+                                  const int32_t* __restrict__ qzeros, const __half* __restrict__ scales,
+                                  const __half* __restrict__ bias, OutT* __restrict__ y,
+                                  int M, int K, int N, int G, int* dev_err) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)M * N) return;
+  const int m = (int)(idx / N), c = (int)(idx % N);
+  const int W8 = N / 8, word = c / 8, lane = c % 8;
+  const int shift = (0x73625140 >> (4 * lane)) & 0xF;   // nibble index of lane: 0,4,1,5,2,6,3,7
+  float total = 0.0f;
+  bool bad = false;
+  for (int k = 0; k < K; ++k) {
+    const int g = k / G;
+    const __half hs = scales[(size_t)g * N + c];
+    const uint16_t hb = __half_as_ushort(hs);
+    if (((hb >> 10) & 31) == 31 || ((hb & 0x8000) && (hb & 0x7FFF))) { bad = true; break; }
+    const uint32_t qw = (uint32_t)qweight[(size_t)k * W8 + word];
+    const uint32_t qz = (uint32_t)qzeros[(size_t)g * W8 + word];
+    const int delta = (int)((qw >> (4 * shift)) & 15u) - (int)((qz >> (4 * shift)) & 15u);
+    const float weight = __fmul_rn((float)delta, __half2float(hs));
+    const float product = __fmul_rn(__half2float(x[(size_t)m * K + k]), weight);
+    total = __fadd_rn(total, product);
+  }
+  if (!bad && bias) total = __fadd_rn(total, __half2float(bias[c]));
+  store_out(y, idx, bad ? 0.0f : total);
+  if (bad && dev_err) atomicOr(dev_err, ANVILQ_DEV_ERR_SCALE);
+}
+
+// ---------------------------------------------------------------------------
+// Dequantiser: one thread per (row k, packed word), through unpack_deltas.
+__global__ void dequant_kernel(const int32_t* __restrict__ qweight, const int32_t* __restrict__ qzeros,
+                               const __half* __restrict__ scales, int8_t* __restrict__ delta_out,
+                               float* __restrict__ w_out, int K, int N, int G, int* dev_err) {
+  const int W8 = N / 8;
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)K * W8) return;
+  const int k = (int)(idx / W8), w = (int)(idx % W8), g = k / G;
+  const ZeroPoint zp = make_zero_point((uint32_t)qzeros[(size_t)g * W8 + w]);
+  half2 d[4];
+  unpack_deltas((uint32_t)qweight[idx], zp, d);
+  uint32_t bad = 0;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int c = 8 * w + 2 * e;
+    const uint32_t s = *reinterpret_cast<const uint32_t*>(scales + (size_t)g * N + c);
+    const uint32_t b = invalid_scale_pair(s);
+    bad |= b;
+    const float2 df = __half22float2(d[e]);
+    const float2 sf = __half22float2(u32_as_half2(s));
+    if (delta_out) {
+      delta_out[(size_t)k * N + c] = (int8_t)df.x;
+      delta_out[(size_t)k * N + c + 1] = (int8_t)df.y;
+    }
+    if (w_out) {
+      w_out[(size_t)k * N + c] = (b & 0x8000u) ? 0.0f : __fmul_rn(df.x, sf.x);
+      w_out[(size_t)k * N + c + 1] = (b & 0x80000000u) ? 0.0f : __fmul_rn(df.y, sf.y);
+    }
+  }
+  if (bad && dev_err) atomicOr(dev_err, ANVILQ_DEV_ERR_SCALE);
+}
+
+__global__ void pack_kernel(const uint8_t* __restrict__ codes, int32_t* __restrict__ packed, long long words) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= words) return;
+  const uint8_t* c = codes + idx * 8;
+  uint32_t w = 0;
+#pragma unroll
+  for (int lane = 0; lane < 8; ++lane) {
+    const int nib = (0x73625140 >> (4 * lane)) & 0xF;
+    w |= (uint32_t)(c[lane] & 15u) << (4 * nib);
+  }
+  packed[idx] = (int32_t)w;
+}
+
+__global__ void unpack_kernel(const int32_t* __restrict__ packed, uint8_t* __restrict__ codes, long long words) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= words) return;
+  const uint32_t w = (uint32_t)packed[idx];
+#pragma unroll
+  for (int lane = 0; lane < 8; ++lane) {
+    const int nib = (0x73625140 >> (4 * lane)) & 0xF;
+    codes[idx * 8 + lane] = (uint8_t)((w >> (4 * nib)) & 15u);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side.
+struct DeviceInfo {
+  int sms = 0;
+  int occ_m1 = 0;
+  int occ_small[9] = {0};
+};
+
+constexpr int kMaxDevices = 64;
+static DeviceInfo g_info[kMaxDevices];
+static std::once_flag g_once[kMaxDevices];
+
+static const DeviceInfo* device_info() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::call_once(g_once[dev], [dev] {
+    DeviceInfo& d = g_info[dev];
+    cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.occ_m1, gemv_m1_kernel, kThreads, 0);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.occ_small[2], gemm_smallm_kernel<2>, kThreads, 0);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.occ_small[3], gemm_smallm_kernel<3>, kThreads, 0);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.occ_small[4], gemm_smallm_kernel<4>, kThreads, 0);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.occ_small[5], gemm_smallm_kernel<5>, kThreads, 0);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.occ_small[6], gemm_smallm_kernel<6>, kThreads, 0);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.occ_small[7], gemm_smallm_kernel<7>, kThreads, 0);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.occ_small[8], gemm_smallm_kernel<8>, kThreads, 0);
+    cudaGetLastError();
+  });
+  return &g_info[dev];
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static bool fast_path_ok(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
+                         const uint16_t* scales, int M, int K, int N, int G) {
+  (void)M;
+  return G % kSlotRows == 0 && K % G == 0 && N % 32 == 0 && K % 8 == 0 && aligned16(x) &&
+         aligned16(qweight) && aligned16(qzeros) && aligned16(scales);
+}
+
+struct Plan {
+  int chunk_m;      // rows per launch (1 or 2..8)
+  int grid;         // persistent CTAs
+  int bands, slots;
+  long long items;
+  size_t partial_floats, ticket_offset_bytes, bytes;
+};
+
+static Plan plan_for(const DeviceInfo& d, int M, int K, int N) {
+  Plan pl{};
+  pl.chunk_m = M <= 1 ? 1 : std::min(M, 8);
+  pl.bands = (N / 8 + kBandWords - 1) / kBandWords;
+  pl.slots = K / kSlotRows;
+  pl.items = (long long)pl.bands * pl.slots;
+  const int occ = pl.chunk_m == 1 ? d.occ_m1 : d.occ_small[pl.chunk_m];
+  long long grid = (long long)d.sms * std::max(occ, 1);
+  grid = std::max<long long>(1, std::min<long long>(grid, pl.items));
+  pl.grid = (int)grid;
+  pl.partial_floats = (size_t)pl.grid * 2 * pl.chunk_m * kBandCols;
+  pl.ticket_offset_bytes = (pl.partial_floats * sizeof(float) + 255) & ~size_t(255);
+  pl.bytes = pl.ticket_offset_bytes + (((size_t)pl.bands * sizeof(int) + 255) & ~size_t(255));
+  return pl;
+}
+
+static int launch_fast(const Plan& pl, const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
+                       const uint16_t* scales, const uint16_t* bias, uint16_t* y, int M, int K, int N,
+                       int G, void* workspace, int* dev_err, cudaStream_t stream) {
+  GemmParams p;
+  p.qweight = qweight;
+  p.qzeros = qzeros;
+  p.scales = reinterpret_cast<const __half*>(scales);
+  p.bias = reinterpret_cast<const __half*>(bias);
+  p.partials = reinterpret_cast<float*>(workspace);
+  p.tickets = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + pl.ticket_offset_bytes);
+  p.dev_err = dev_err;
+  p.K = K; p.N = N; p.W8 = N / 8; p.G = G;
+  p.bands = pl.bands; p.slots = pl.slots; p.items = pl.items;
+  for (int m0 = 0; m0 < M; m0 += pl.chunk_m) {
+    const int mc = std::min(pl.chunk_m, M - m0);
+    p.x = reinterpret_cast<const __half*>(x) + (size_t)m0 * K;
+    p.y = reinterpret_cast<__half*>(y) + (size_t)m0 * N;
+    switch (mc) {
+      case 1: gemv_m1_kernel<<<pl.grid, kThreads, 0, stream>>>(p); break;
+      case 2: gemm_smallm_kernel<2><<<pl.grid, kThreads, 0, stream>>>(p); break;
+      case 3: gemm_smallm_kernel<3><<<pl.grid, kThreads, 0, stream>>>(p); break;
+      case 4: gemm_smallm_kernel<4><<<pl.grid, kThreads, 0, stream>>>(p); break;
+      case 5: gemm_smallm_kernel<5><<<pl.grid, kThreads, 0, stream>>>(p); break;
+      case 6: gemm_smallm_kernel<6><<<pl.grid, kThreads, 0, stream>>>(p); break;
+      case 7: gemm_smallm_kernel<7><<<pl.grid, kThreads, 0, stream>>>(p); break;
+      default: gemm_smallm_kernel<8><<<pl.grid, kThreads, 0, stream>>>(p); break;
+    }
+    if (cudaGetLastError() != cudaSuccess) return ANVILQ_ECUDA;
+  }
+  return ANVILQ_OK;
+}
+
+static bool shape_ok(int M, int K, int N, int G) {
+  return M >= 1 && K >= 1 && N >= 8 && N % 8 == 0 && G >= 1 && K % G == 0;
+}
+
+template <typename OutT>
+static int launch_exact(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
+                        const uint16_t* scales, const uint16_t* bias, OutT* y, int M, int K, int N,
+                        int G, int* dev_err, cudaStream_t stream) {
+  const long long n = (long long)M * N;
+  const int threads = 128;
+  gemm_exact_kernel<OutT><<<(unsigned)((n + threads - 1) / threads), threads, 0, stream>>>(
+      reinterpret_cast<const __half*>(x), qweight, qzeros, reinterpret_cast<const __half*>(scales),
+      reinterpret_cast<const __half*>(bias), y, M, K, N, G, dev_err);
+  return cudaGetLastError() == cudaSuccess ? ANVILQ_OK : ANVILQ_ECUDA;
+}
+
+}  // namespace anvilq
+
+using namespace anvilq;
+
+extern "C" {
+
+int anvilq_abi_version(void) { return ANVILQ_ABI_VERSION; }
+
+const char* anvilq_strerror(int status) {
+  switch (status) {
+    case ANVILQ_OK: return "ok";
+    case ANVILQ_EINVAL: return "invalid argument (null pointer or inconsistent size)";
+    case ANVILQ_EALIGN: return "pointer alignment required by the kernel is missing";
+    case ANVILQ_ECUDA: return "CUDA kernel launch failed";
+    case ANVILQ_EWORKSPACE: return "workspace missing or too small";
+    case ANVILQ_ESHAPE: return "shape outside the supported range";
+    default: return "unknown anvilq status";
+  }
+}
+
+size_t anvilq_w4a16_gemm_workspace_size(int M, int K, int N, int G) {
+  if (!shape_ok(M, K, N, G)) return 0;
+  const DeviceInfo* d = device_info();
+  if (!d) return 0;
+  return plan_for(*d, M, K, N).bytes;
+}
+
+int anvilq_w4a16_gemm(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
+                      const uint16_t* scales, const uint16_t* bias, uint16_t* y,
+                      int M, int K, int N, int G, void* workspace, size_t workspace_bytes,
+                      int* dev_err, anvilq_stream_t stream) {
+  if (!x || !qweight || !qzeros || !scales || !y) return ANVILQ_EINVAL;
+  if (!shape_ok(M, K, N, G)) return ANVILQ_EINVAL;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (!fast_path_ok(x, qweight, qzeros, scales, M, K, N, G))
+    return launch_exact(x, qweight, qzeros, scales, bias, reinterpret_cast<__half*>(y), M, K, N, G,
+                        dev_err, s);
+  const DeviceInfo* d = device_info();
+  if (!d) return ANVILQ_ECUDA;
+  const Plan pl = plan_for(*d, M, K, N);
+  if (!workspace || workspace_bytes < pl.bytes) return ANVILQ_EWORKSPACE;
+  if (!aligned16(workspace)) return ANVILQ_EALIGN;
+  return launch_fast(pl, x, qweight, qzeros, scales, bias, y, M, K, N, G, workspace, dev_err, s);
+}
+
+int anvilq_w4a16_gemm_exact(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
+                            const uint16_t* scales, const uint16_t* bias, float* y32,
+                            int M, int K, int N, int G, int* dev_err, anvilq_stream_t stream) {
+  if (!x || !qweight || !qzeros || !scales || !y32) return ANVILQ_EINVAL;
+  if (!shape_ok(M, K, N, G)) return ANVILQ_EINVAL;
+  return launch_exact(x, qweight, qzeros, scales, bias, y32, M, K, N, G, dev_err,
+                      reinterpret_cast<cudaStream_t>(stream));
+}
+
+int anvilq_awq_dequant(const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
+                       int8_t* delta_out, float* w_out, int K, int N, int G, int* dev_err,
+                       anvilq_stream_t stream) {
+  if (!qweight || !qzeros || !scales) return ANVILQ_EINVAL;
+  if (K < 1 || N < 8 || N % 8 || G < 1 || K % G) return ANVILQ_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(scales) & 3u) != 0) return ANVILQ_EALIGN;
+  const long long n = (long long)K * (N / 8);
+  const int threads = 256;
+  dequant_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0,
+                   reinterpret_cast<cudaStream_t>(stream)>>>(
+      qweight, qzeros, reinterpret_cast<const __half*>(scales), delta_out, w_out, K, N, G, dev_err);
+  return cudaGetLastError() == cudaSuccess ? ANVILQ_OK : ANVILQ_ECUDA;
+}
+
+int anvilq_awq_pack(const uint8_t* codes, int32_t* packed, int rows, int N, anvilq_stream_t stream) {
+  if (!codes || !packed || rows < 1 || N < 8 || N % 8) return ANVILQ_EINVAL;
+  const long long words = (long long)rows * (N / 8);
+  pack_kernel<<<(unsigned)((words + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      codes, packed, words);
+  return cudaGetLastError() == cudaSuccess ? ANVILQ_OK : ANVILQ_ECUDA;
+}
+
+int anvilq_awq_unpack(const int32_t* packed, uint8_t* codes, int rows, int N, anvilq_stream_t stream) {
+  if (!codes || !packed || rows < 1 || N < 8 || N % 8) return ANVILQ_EINVAL;
+  const long long words = (long long)rows * (N / 8);
+  unpack_kernel<<<(unsigned)((words + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      packed, codes, words);
+  return cudaGetLastError() == cudaSuccess ? ANVILQ_OK : ANVILQ_ECUDA;
+}
+
+}  // extern "C"

@@ -1,0 +1,176 @@
+"""Torch-tensor front end of the C ABI: shape/dtype checks, workspaces, device errors.
+
+PyTorch only provides device memory and streams here; every computation runs in
+libanvilq.so.  All functions take CUDA tensors and enqueue on the current torch
+stream.
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from . import _lib
+
+_state = threading.local()
+_dev_err = {}          # device index -> int32[1] device error word
+_workspaces = {}       # (device index, stream ptr) -> uint8 workspace
+_lock = threading.Lock()
+
+
+def _stream_ptr(device):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def device_error_word(device) -> torch.Tensor:
+    """Per-device int32 word that kernels OR their ANVILQ_DEV_ERR_* bits into."""
+    idx = torch.device(device).index
+    with _lock:
+        w = _dev_err.get(idx)
+        if w is None:
+            w = torch.zeros(1, dtype=torch.int32, device=device)
+            _dev_err[idx] = w
+    return w
+
+
+def raise_device_errors(device=None):
+    """Synchronise the device error word, clear it, and raise if a kernel flagged an error.
+
+    Mirrors the reference, where an invalid AWQ scale fails the operation
+    (anvil-q1/tests/official_weights.py:430, anvil-q1/design/SPEC.md:175-177).
+    """
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    w = device_error_word(device)
+    value = int(w.item())
+    if value:
+        w.zero_()
+        raise _lib.AnvilqError(f"device error bits 0x{value:x}: invalid AWQ scale "
+                               "(negative nonzero or nonfinite)")
+
+
+def workspace(device, nbytes: int) -> torch.Tensor:
+    """Zero-filled scratch reused by calls on the current stream (kernels leave it zeroed)."""
+    idx = torch.device(device).index
+    key = (idx, _stream_ptr(device))
+    with _lock:
+        ws = _workspaces.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            _workspaces[key] = ws
+    return ws
+
+
+def _check_awq(qweight, qzeros, scales, group):
+    if qweight.dtype != torch.int32 or qzeros.dtype != torch.int32:
+        raise TypeError("qweight and qzeros must be int32 (AWQ packed)")
+    if scales.dtype != torch.float16:
+        raise TypeError("scales must be float16")
+    if qweight.dim() != 2 or qzeros.dim() != 2 or scales.dim() != 2:
+        raise ValueError("qweight, qzeros and scales must be 2-D")
+    K, W8 = qweight.shape
+    N = W8 * 8
+    if group < 1 or K % group:
+        raise ValueError(f"K={K} is not a multiple of the group size {group}")
+    if tuple(qzeros.shape) != (K // group, W8) or tuple(scales.shape) != (K // group, N):
+        raise ValueError("qzeros/scales shapes do not match qweight and the group size")
+    for t in (qweight, qzeros, scales):
+        if not t.is_cuda or not t.is_contiguous():
+            raise ValueError("AWQ tensors must be contiguous CUDA tensors")
+    return K, N
+
+
+def gemm(x, qweight, qzeros, scales, bias=None, group: int = 128, out=None, dev_err=None):
+    """y[M, N] = x[M, K] @ dequant(qweight, qzeros, scales) (+ bias), fp16 out.
+
+    GPU counterpart of FP32Model.linear (anvil-q1/tests/official_weights.py:418-437)
+    for M rows at once.  Device-side scale errors are OR-ed into `dev_err`
+    (default: the per-device word read by ``raise_device_errors``).
+    """
+    K, N = _check_awq(qweight, qzeros, scales, group)
+    squeeze = x.dim() == 1
+    x2 = x.unsqueeze(0) if squeeze else x
+    if x2.dtype != torch.float16 or x2.dim() != 2 or x2.shape[1] != K:
+        raise ValueError(f"x must be float16 [M, {K}]")
+    if not x2.is_contiguous() or x2.device != qweight.device:
+        raise ValueError("x must be contiguous and on the weights' device")
+    M = x2.shape[0]
+    if bias is not None and (bias.dtype != torch.float16 or bias.numel() != N or not bias.is_contiguous()):
+        raise ValueError("bias must be contiguous float16 [N]")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float16, device=x2.device)
+    elif out.dtype != torch.float16 or tuple(out.shape) not in ((M, N), (N,) if squeeze else (M, N)) \
+            or not out.is_contiguous():
+        raise ValueError("out must be contiguous float16 [M, N]")
+    lib = _lib.load()
+    need = lib.anvilq_w4a16_gemm_workspace_size(M, K, N, group)
+    ws = workspace(x2.device, need)
+    err = device_error_word(x2.device) if dev_err is None else dev_err
+    _lib.check(lib.anvilq_w4a16_gemm(_ptr(x2), _ptr(qweight), _ptr(qzeros), _ptr(scales), _ptr(bias),
+                                     _ptr(out), M, K, N, group, _ptr(ws), ws.numel(), _ptr(err),
+                                     _stream_ptr(x2.device)), "anvilq_w4a16_gemm")
+    return out.view(N) if squeeze else out
+
+
+def gemm_exact(x, qweight, qzeros, scales, bias=None, group: int = 128, dev_err=None):
+    """Reference-order GEMM: fp32 output bit-identical to FP32Model.linear."""
+    K, N = _check_awq(qweight, qzeros, scales, group)
+    x2 = x.unsqueeze(0) if x.dim() == 1 else x
+    if x2.dtype != torch.float16 or x2.shape[1] != K or not x2.is_contiguous():
+        raise ValueError(f"x must be contiguous float16 [M, {K}]")
+    M = x2.shape[0]
+    out = torch.empty((M, N), dtype=torch.float32, device=x2.device)
+    err = device_error_word(x2.device) if dev_err is None else dev_err
+    _lib.check(_lib.load().anvilq_w4a16_gemm_exact(_ptr(x2), _ptr(qweight), _ptr(qzeros), _ptr(scales),
+                                                   _ptr(bias), _ptr(out), M, K, N, group, _ptr(err),
+                                                   _stream_ptr(x2.device)), "anvilq_w4a16_gemm_exact")
+    return out.view(N) if x.dim() == 1 else out
+
+
+def dequant(qweight, qzeros, scales, group: int = 128, dev_err=None):
+    """(delta int8 [K, N], w float32 [K, N]) through the kernels' in-register unpack."""
+    K, N = _check_awq(qweight, qzeros, scales, group)
+    delta = torch.empty((K, N), dtype=torch.int8, device=qweight.device)
+    w = torch.empty((K, N), dtype=torch.float32, device=qweight.device)
+    err = device_error_word(qweight.device) if dev_err is None else dev_err
+    _lib.check(_lib.load().anvilq_awq_dequant(_ptr(qweight), _ptr(qzeros), _ptr(scales), _ptr(delta), _ptr(w),
+                                              K, N, group, _ptr(err), _stream_ptr(qweight.device)),
+               "anvilq_awq_dequant")
+    return delta, w
+
+
+def pack(codes):
+    """Row-major codes uint8 [rows, N] -> AWQ int32 [rows, N/8]."""
+    if codes.dtype != torch.uint8 or codes.dim() != 2 or codes.shape[1] % 8 or not codes.is_contiguous():
+        raise ValueError("codes must be contiguous uint8 [rows, N], N % 8 == 0")
+    out = torch.empty((codes.shape[0], codes.shape[1] // 8), dtype=torch.int32, device=codes.device)
+    _lib.check(_lib.load().anvilq_awq_pack(_ptr(codes), _ptr(out), codes.shape[0], codes.shape[1],
+                                           _stream_ptr(codes.device)), "anvilq_awq_pack")
+    return out
+
+
+def unpack(packed, n: int | None = None):
+    """AWQ int32 [rows, N/8] -> codes uint8 [rows, N]."""
+    if packed.dtype != torch.int32 or packed.dim() != 2 or not packed.is_contiguous():
+        raise ValueError("packed must be contiguous int32 [rows, N/8]")
+    n = packed.shape[1] * 8 if n is None else n
+    if n != packed.shape[1] * 8:
+        raise ValueError("invalid packed output shape")
+    out = torch.empty((packed.shape[0], n), dtype=torch.uint8, device=packed.device)
+    _lib.check(_lib.load().anvilq_awq_unpack(_ptr(packed), _ptr(out), packed.shape[0], n,
+                                             _stream_ptr(packed.device)), "anvilq_awq_unpack")
+    return out
+
+
+def pack_lanes(codes):
+    """awq_prepare.pack_lanes signature (anvil-q1-fp/tests/awq_prepare.py:84-91):
+    output-major codes [N, K] -> int32 [K, N/8]."""
+    return pack(codes.t().contiguous())
+
+
+def unpack_lanes(words, outputs: int):
+    """awq_prepare.unpack_lanes signature (awq_prepare.py:94-99): int32 [K, N/8] -> uint8 [N, K]."""
+    return unpack(words, outputs).t().contiguous()

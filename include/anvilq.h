@@ -1,0 +1,116 @@
+/*
+ * anvilq.h -- C ABI of libanvilq.so, the B200 (sm_100a) W4A16 AWQ decode datapath.
+ *
+ * Conventions
+ *  - Every pointer argument is a DEVICE pointer owned by the caller, except
+ *    where stated.  Nothing here allocates device memory: scratch space is a
+ *    caller-provided workspace whose size is given by the *_workspace_size
+ *    query.
+ *  - binary16 tensors are passed as `uint16_t*` bit patterns; AWQ packed
+ *    tensors as `int32_t*` in the reference's layout:
+ *        qweight [K][N/8]   qzeros [K/G][N/8]   scales [K/G][N]   bias [N]
+ *    where logical output lane i of a packed word sits at bit shift
+ *    (0,16,4,20,8,24,12,28)[i] (anvil-q1/tests/verify.py:38).
+ *  - All work is asynchronous on `stream` (NULL = legacy default stream).
+ *  - Return value: ANVILQ_OK, or a negative ANVILQ_E* code for an argument
+ *    rejected on the host before anything was launched.  A condition found
+ *    on the device (an invalid AWQ scale) is OR-ed into *dev_err (optional,
+ *    device int, never cleared by the library); the whole operation is then
+ *    failed and its output must not be used, mirroring the reference, where
+ *    an invalid scale fails the GEMV instead of being consumed
+ *    (anvil-q1/design/SPEC.md:175-177).
+ *  - Calls are stateless and thread-safe; two calls that share a workspace
+ *    must be ordered on the GPU (same stream or events).
+ */
+#ifndef ANVILQ_H
+#define ANVILQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* anvilq_stream_t; /* same type as cudaStream_t */
+
+#define ANVILQ_ABI_VERSION 1
+
+#define ANVILQ_OK 0
+#define ANVILQ_EINVAL (-1)     /* null pointer, negative or inconsistent size */
+#define ANVILQ_EALIGN (-2)     /* pointer alignment the kernel needs is missing */
+#define ANVILQ_ECUDA (-3)      /* kernel launch failed (cudaGetLastError) */
+#define ANVILQ_EWORKSPACE (-4) /* workspace missing or smaller than required */
+#define ANVILQ_ESHAPE (-5)     /* shape outside the supported range */
+
+/* Bits OR-ed into *dev_err by a kernel. */
+#define ANVILQ_DEV_ERR_SCALE 1 /* an AWQ scale was negative-nonzero or nonfinite */
+
+int anvilq_abi_version(void);
+const char* anvilq_strerror(int status);
+
+/* ---------------------------------------------------------------------------
+ * W4A16 AWQ GEMV / small-M GEMM:  y[M][N] = x[M][K] @ dequant(W)[K][N] (+ bias)
+ *
+ * Replaces FP32Model.linear(x, layer, projection)
+ * (anvil-q1/tests/official_weights.py:418-437): for each output column c,
+ * sum over k of x[k] * ((u4 q[k][c] - u4 z[k/G][c]) * scale[k/G][c]), plus
+ * bias[c] for Q/K/V projections; M independent rows (the speculative-verify
+ * batch of anvil-q4/rtl/anvil_q4_speculative.sv:57-92 computed in one pass).
+ *
+ * x fp16 [M][K], y fp16 [M][N], bias fp16 [N] or NULL.  Products are
+ * accumulated in fp32 (partial sums of at most 16 products in fp16 for
+ * M<=8), then rounded once to fp16: results differ from the reference's
+ * strictly sequential binary32 sum only by accumulation order and the final
+ * fp16 rounding.
+ * Requirements: M >= 1, K >= 1, N >= 8, N % 8 == 0, G >= 1, K % G == 0.
+ * The fast kernels additionally use G % 16 == 0, N % 32 == 0 and 16-byte
+ * aligned pointers; other shapes fall back to the sequential kernel.
+ * workspace: device memory of anvilq_w4a16_gemm_workspace_size(M, K, N, G)
+ * bytes, zero-filled by the caller before its FIRST use; every call leaves
+ * it zero-filled again, so it may be reused by later calls on the same stream.
+ */
+size_t anvilq_w4a16_gemm_workspace_size(int M, int K, int N, int G);
+int anvilq_w4a16_gemm(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
+                      const uint16_t* scales, const uint16_t* bias, uint16_t* y,
+                      int M, int K, int N, int G,
+                      void* workspace, size_t workspace_bytes,
+                      int* dev_err, anvilq_stream_t stream);
+
+/* Reference-order W4A16 GEMM: one thread per output column sums its K products
+ * in increasing k from +0.0 with every binary32 multiply and add rounded
+ * separately (no FMA), exactly as FP32Model.linear does
+ * (official_weights.py:393-397, 418-437).  y32 (fp32 [M][N]) is therefore
+ * bit-identical to the reference; slow, meant for verification.
+ * Same layout and requirements as anvilq_w4a16_gemm (any G, no workspace). */
+int anvilq_w4a16_gemm_exact(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
+                            const uint16_t* scales, const uint16_t* bias, float* y32,
+                            int M, int K, int N, int G, int* dev_err, anvilq_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * AWQ dequantisation of a whole [K][N] matrix, using the same in-register
+ * unpack as the GEMM kernels.
+ * Replaces dequant(qw, qz, h, lane) (anvil-q1/tests/verify.py:241-250) and
+ * the weight f32(delta*scale) of official_weights.py:428-431:
+ *   delta_out int8 [K][N] = u4 q - u4 z          (may be NULL)
+ *   w_out   float  [K][N] = delta * scale, exact  (may be NULL; 0 where invalid)
+ * Invalid scales set ANVILQ_DEV_ERR_SCALE in *dev_err.  Any G >= 1. */
+int anvilq_awq_dequant(const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
+                       int8_t* delta_out, float* w_out, int K, int N, int G,
+                       int* dev_err, anvilq_stream_t stream);
+
+/* AWQ packing of row-major 4-bit codes: codes uint8 [rows][N] (values 0..15,
+ * higher bits ignored) <-> packed int32 [rows][N/8].
+ * Replaces pack(values) (anvil-q1/tests/verify.py:252-253) and
+ * pack_lanes / unpack_lanes (anvil-q1-fp/tests/awq_prepare.py:84-99), which
+ * use the output-major transpose of the same layout. */
+int anvilq_awq_pack(const uint8_t* codes, int32_t* packed, int rows, int N,
+                    anvilq_stream_t stream);
+int anvilq_awq_unpack(const int32_t* packed, uint8_t* codes, int rows, int N,
+                      anvilq_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ANVILQ_H */

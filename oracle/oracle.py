@@ -1,0 +1,274 @@
+"""CPU oracle for the W4A16 AWQ decode path -- TEST INFRASTRUCTURE ONLY.
+
+This module is the checker.  Only the tests, ``__graft_entry__.smoke()`` and the
+CPU-baseline / reference arm of ``bench.py`` import it; the product package
+(``anvilq_b200``) never does.  It restates the reference's golden models:
+
+* ``pack_lanes`` / ``unpack_lanes``: anvil-q1-fp/tests/awq_prepare.py:84-99
+  (nibble order (0, 4, 1, 5, 2, 6, 3, 7), i.e. bit shifts
+  (0, 16, 4, 20, 8, 24, 12, 28) of anvil-q1/tests/verify.py:38).
+* ``dequant``: anvil-q1/tests/verify.py:241-250 (Q16.16 integer) and
+  anvil-q1/tests/official_weights.py:428-431 (binary32 ``f32(delta*scale)``).
+* ``gemv_fp32``: FP32Model.linear, anvil-q1/tests/official_weights.py:418-437,
+  in C (oracle/awq_oracle.c) and, vectorised over columns, in numpy
+  (``gemv_fp32_numpy``); both sum in increasing k with every binary32 operation
+  rounded separately, so both are bit-exact against the reference.
+* ``gemv_q16``: FixedModel.linear, official_weights.py:592-612.
+* ``attention_f64``: anvil-q1-fp/tests/fp64_reference.py:164-170.
+* ``attention_fp32``: the FP32 loop of official_weights.py:471-486.
+
+Parity of these restatements is pinned by tests/test_oracle_golden.py against
+fixtures that tests/golden/make_golden.py produced by importing the reference.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "liboracle.so"
+
+NIBBLE_ORDER = (0, 4, 1, 5, 2, 6, 3, 7)   # awq_prepare.py:18
+SHIFTS = (0, 16, 4, 20, 8, 24, 12, 28)     # verify.py:38
+
+_lib = None
+
+
+def build(force: bool = False) -> Path:
+    """Compile oracle/awq_oracle.c into oracle/liboracle.so with make."""
+    src = HERE / "awq_oracle.c"
+    if force or not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < src.stat().st_mtime:
+        subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        L = ctypes.CDLL(str(LIB_PATH))
+        P = ctypes.c_void_p
+        I = ctypes.c_int
+        L.anvilq_oracle_pack.argtypes = [P, P, I, I]
+        L.anvilq_oracle_unpack.argtypes = [P, P, I, I]
+        L.anvilq_oracle_dequant.argtypes = [P, P, P, I, I, I, P, P, P, P]
+        L.anvilq_oracle_dequant.restype = ctypes.c_int64
+        L.anvilq_oracle_gemv_fp32.argtypes = [P, P, P, P, P, P, I, I, I, I, I, I, I]
+        L.anvilq_oracle_gemv_q16.argtypes = [P, P, P, P, P, P, I, I, I, I, I]
+        L.anvilq_oracle_attention_fp32.argtypes = [P, P, P, P, I, I, I, I, P, I]
+        L.anvilq_oracle_max_threads.restype = I
+        _lib = L
+    return _lib
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _c(a, dtype):
+    return None if a is None else np.ascontiguousarray(a, dtype=dtype)
+
+
+def max_threads() -> int:
+    return int(lib().anvilq_oracle_max_threads())
+
+
+class OracleError(ValueError):
+    """Raised where the reference raises CheckpointError (official_weights.py:37)."""
+
+
+_STATUS = {-1: "invalid argument", -2: "invalid AWQ scale (negative nonzero or nonfinite)",
+           -3: "FP32 nonfinite result"}
+
+
+def _check(status):
+    if status != 0:
+        raise OracleError(_STATUS.get(status, f"oracle status {status}"))
+
+
+# ---------------------------------------------------------------- packing
+def pack_lanes(codes):
+    """awq_prepare.py:84-91: codes uint8 [N, K] (output-major) -> uint32 [K, N/8]."""
+    codes = np.asarray(codes)
+    if codes.ndim != 2 or codes.shape[0] % 8 or codes.min(initial=0) < 0 or codes.max(initial=0) > 15:
+        raise OracleError("invalid nibble array")
+    out = np.zeros((codes.shape[1], codes.shape[0] // 8), dtype="<u4")
+    for lane, nib in enumerate(NIBBLE_ORDER):
+        out |= codes[lane::8].T.astype("<u4") << (4 * nib)
+    return out
+
+
+def unpack_lanes(words, outputs):
+    """awq_prepare.py:94-99: uint32 [K, N/8] -> uint8 [N, K]."""
+    words = np.asarray(words, dtype="<u4")
+    if words.ndim != 2 or words.shape[1] * 8 != outputs:
+        raise OracleError("invalid packed output shape")
+    out = np.empty((outputs, words.shape[0]), dtype=np.uint8)
+    for lane, nib in enumerate(NIBBLE_ORDER):
+        out[lane::8] = ((words >> (4 * nib)) & 15).T
+    return out
+
+
+def pack_rows(codes):
+    """Row-major codes uint8 [K, N] -> qweight uint32 [K, N/8] (C restatement)."""
+    codes = _c(codes, np.uint8)
+    K, N = codes.shape
+    out = np.empty((K, N // 8), dtype=np.uint32)
+    _check(lib().anvilq_oracle_pack(_ptr(codes), _ptr(out), K, N))
+    return out
+
+
+def unpack_rows(packed, n):
+    packed = _c(packed, np.uint32)
+    out = np.empty((packed.shape[0], n), dtype=np.uint8)
+    _check(lib().anvilq_oracle_unpack(_ptr(packed), _ptr(out), packed.shape[0], n))
+    return out
+
+
+def pack8(values):
+    """verify.py:252-253."""
+    return sum((int(v) & 15) << s for v, s in zip(values, SHIFTS))
+
+
+# ---------------------------------------------------------------- dequant
+def dequant(qweight, qzeros, scales_bits, G):
+    """Element-wise dequantisation of a [K, N] AWQ matrix.
+
+    Returns (delta int8 [K,N], w_f32 float32 [K,N], w_q16 int64 [K,N], invalid uint8 [K,N]).
+    """
+    qweight = _c(qweight, np.uint32)
+    qzeros = _c(qzeros, np.uint32)
+    scales_bits = _c(scales_bits, np.uint16)
+    K, N = qweight.shape[0], qweight.shape[1] * 8
+    delta = np.empty((K, N), np.int8)
+    w = np.empty((K, N), np.float32)
+    q16 = np.empty((K, N), np.int64)
+    bad = np.empty((K, N), np.uint8)
+    r = lib().anvilq_oracle_dequant(_ptr(qweight), _ptr(qzeros), _ptr(scales_bits), K, N, G,
+                                    _ptr(delta), _ptr(w), _ptr(q16), _ptr(bad))
+    if r < 0:
+        _check(int(r))
+    return delta, w, q16, bad
+
+
+def dequant_scalar(qw, qz, h, lane):
+    """verify.py:241-250 signature: (w_q16, invalid) for one lane of one word."""
+    qweight = np.array([[qw & 0xFFFFFFFF]], np.uint32)
+    qzeros = np.array([[qz & 0xFFFFFFFF]], np.uint32)
+    scales = np.zeros((1, 8), np.uint16)
+    scales[0, lane] = h
+    _, _, q16, bad = dequant(qweight, qzeros, scales, 1)
+    return int(q16[0, lane]), int(bad[0, lane])
+
+
+# ---------------------------------------------------------------- GEMV
+def gemv_fp32(x, qweight, qzeros, scales_bits, bias_bits=None, G=128, threads=1,
+              n_range=None):
+    """FP32Model.linear over M rows (C restatement, bit-exact).
+
+    x: float32-representable [M, K] (fp16 inputs are exact); returns float32 [M, N].
+    """
+    x = _c(np.atleast_2d(x), np.float32)
+    qweight = _c(qweight, np.uint32)
+    qzeros = _c(qzeros, np.uint32)
+    scales_bits = _c(scales_bits, np.uint16)
+    bias_bits = _c(bias_bits, np.uint16)
+    M, K = x.shape
+    N = qweight.shape[1] * 8
+    if qweight.shape[0] != K:
+        raise OracleError("activation width differs from qweight rows")
+    y = np.zeros((M, N), np.float32)
+    a, b = (0, N) if n_range is None else n_range
+    _check(lib().anvilq_oracle_gemv_fp32(_ptr(x), _ptr(qweight), _ptr(qzeros), _ptr(scales_bits),
+                                         _ptr(bias_bits), _ptr(y), M, K, N, G, a, b, threads))
+    return y
+
+
+def gemv_fp32_numpy(x, qweight, qzeros, scales_bits, bias_bits=None, G=128):
+    """Same arithmetic as ``gemv_fp32`` vectorised over columns with numpy float32.
+
+    numpy float32 multiply and add each round to binary32 (no fusion), and the
+    k loop runs in increasing order from +0.0, so this matches FP32Model.linear.
+    """
+    x = np.atleast_2d(np.asarray(x, np.float32))
+    _, w, _, bad = dequant(qweight, qzeros, scales_bits, G)
+    if bad.any():
+        raise OracleError(_STATUS[-2])
+    M, K = x.shape
+    y = np.zeros((M, w.shape[1]), np.float32)
+    for k in range(K):
+        y = y + (x[:, k:k + 1] * w[k][None, :])
+    if bias_bits is not None:
+        y = y + np.asarray(bias_bits, np.uint16).view(np.float16).astype(np.float32)[None, :]
+    if not np.isfinite(y).all():
+        raise OracleError(_STATUS[-3])
+    return y
+
+
+def gemv_q16(x_q16, qweight, qzeros, scales_bits, bias_bits=None, G=128, threads=1):
+    """FixedModel.linear (Q16.16 in, Q16.16 out, round-away, sat32)."""
+    x_q16 = _c(np.atleast_2d(x_q16), np.int32)
+    qweight = _c(qweight, np.uint32)
+    qzeros = _c(qzeros, np.uint32)
+    scales_bits = _c(scales_bits, np.uint16)
+    bias_bits = _c(bias_bits, np.uint16)
+    M, K = x_q16.shape
+    N = qweight.shape[1] * 8
+    y = np.zeros((M, N), np.int32)
+    _check(lib().anvilq_oracle_gemv_q16(_ptr(x_q16), _ptr(qweight), _ptr(qzeros), _ptr(scales_bits),
+                                        _ptr(bias_bits), _ptr(y), M, K, N, G, threads))
+    return y
+
+
+# ---------------------------------------------------------------- attention
+def attention_f64(q, keys, values):
+    """fp64_reference.py:164-170: q [Hq, D], keys/values [T, Hkv, D]."""
+    q = np.asarray(q, np.float64)
+    keys = np.asarray(keys, np.float64)
+    values = np.asarray(values, np.float64)
+    grouping = q.shape[0] // keys.shape[1]
+    kk = np.repeat(keys, grouping, axis=1)
+    vv = np.repeat(values, grouping, axis=1)
+    scores = np.einsum("hd,thd->ht", q, kk) / np.sqrt(q.shape[1])
+    e = np.exp(scores - scores.max(axis=1, keepdims=True))
+    p = e / e.sum(axis=1, keepdims=True)
+    return np.einsum("ht,thd->hd", p, vv)
+
+
+def attention_fp32(q_bits, k_bits, v_bits):
+    """official_weights.py:471-486 FP32 loop for one sequence; inputs are binary16 bits."""
+    q_bits = _c(q_bits, np.uint16)
+    k_bits = _c(k_bits, np.uint16)
+    v_bits = _c(v_bits, np.uint16)
+    Hq, D = q_bits.shape
+    T, Hkv, _ = k_bits.shape
+    out = np.empty((Hq, D), np.float32)
+    scratch = np.empty(T, np.float32)
+    _check(lib().anvilq_oracle_attention_fp32(_ptr(q_bits), _ptr(k_bits), _ptr(v_bits), _ptr(out),
+                                              Hq, Hkv, D, T, _ptr(scratch), 1))
+    return out
+
+
+def decode_attention_f64(q, k_cache, v_cache, seqlens):
+    """Batched GQA decode: q [B,Hq,D], caches [B,Tmax,Hkv,D]; sequence b uses positions < seqlens[b]."""
+    out = np.empty(q.shape, np.float64)
+    for b in range(q.shape[0]):
+        T = int(seqlens[b])
+        out[b] = attention_f64(q[b], k_cache[b, :T], v_cache[b, :T])
+    return out
+
+
+# ---------------------------------------------------------------- metrics
+def normalized_error(actual, reference):
+    """anvil-q1-fp/design/SPEC.md:311-317: max|a-r| / max(1, max|r|) and cosine."""
+    a = np.asarray(actual, np.float64).ravel()
+    r = np.asarray(reference, np.float64).ravel()
+    err = float(np.max(np.abs(a - r))) if a.size else 0.0
+    norm = max(1.0, float(np.max(np.abs(r)))) if r.size else 1.0
+    na, nr = float(np.linalg.norm(a)), float(np.linalg.norm(r))
+    cos = float(a @ r / (na * nr)) if na and nr else None
+    return err / norm, cos

@@ -1,0 +1,21 @@
+"""Shared pytest configuration: the `gpu` marker and import paths."""
+import os
+import sys
+from pathlib import Path
+
+import pytest
+
+REPO = Path(__file__).resolve().parents[1]
+GOLDEN = REPO / "tests" / "golden"
+for p in (str(REPO), str(REPO / "oracle")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA B200 (sm_100a) device")
+
+
+@pytest.fixture(scope="session")
+def golden_dir():
+    return GOLDEN
