@@ -23,10 +23,13 @@ SIGNATURES = {
     "anvilq_strerror": (ctypes.c_char_p, [I]),
     "anvilq_w4a16_gemm_workspace_size": (SZ, [I, I, I, I]),
     "anvilq_w4a16_gemm": (I, [P, P, P, P, P, P, I, I, I, I, P, SZ, P, P]),
+    "anvilq_w4a16_gemm_ex": (I, [P, P, P, P, P, P, I, I, I, I, P, SZ, P, ctypes.c_uint, P]),
     "anvilq_w4a16_gemm_exact": (I, [P, P, P, P, P, P, I, I, I, I, P, P]),
     "anvilq_awq_dequant": (I, [P, P, P, P, P, I, I, I, P, P]),
     "anvilq_awq_pack": (I, [P, P, I, I, P]),
     "anvilq_awq_unpack": (I, [P, P, I, I, P]),
+    "anvilq_gqa_decode_workspace_size": (SZ, [I, I, I, I, I]),
+    "anvilq_gqa_decode": (I, [P, P, P, P, P, I, I, I, I, I, F, P, SZ, P, P]),
 }
 
 _lib = None

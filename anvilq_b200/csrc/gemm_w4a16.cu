@@ -33,6 +33,7 @@
 
 #include "../../include/anvilq.h"
 #include "awq_common.cuh"
+#include "internal.h"
 
 namespace anvilq {
 
@@ -106,14 +107,29 @@ __device__ void finish_segment(const GemmParams& p, const float* seg, int band, 
   __syncthreads();
   if (!*s_flag) return;
   __threadfence();
+  // Contributor q stored its partial for its first band in slot 0, for its last
+  // band in slot 1.  Every contributor after c_lo starts inside this band (slot
+  // 0); c_lo used slot 1 unless its range starts exactly at the band start.
+  const int j_lo = range_begin(c_lo, p.items, P) < band_first ? 1 : 0;
+  const float* first = p.partials + ((size_t)c_lo * 2 + j_lo) * (M * kBandCols);
+  const float* rest = p.partials + ((size_t)(c_lo + 1) * 2) * (M * kBandCols);
+  const size_t stride = (size_t)2 * M * kBandCols;
+  const int n_rest = c_hi - c_lo;
   for (int e = threadIdx.x; e < M * kBandCols; e += blockDim.x) {
     const int m = e / kBandCols, c = e % kBandCols, col = col0 + c;
-    float v = 0.0f;
-    for (int q = c_lo; q <= c_hi; ++q) {
-      // Contributor q stored its partial for its first band in slot 0, else slot 1.
-      const int j = band == (int)(range_begin(q, p.items, P) / p.slots) ? 0 : 1;
-      v += __ldcg(p.partials + ((size_t)q * 2 + j) * (M * kBandCols) + e);
+    float v = __ldcg(first + e);
+    int q = 0;
+    for (; q + 4 <= n_rest; q += 4) {   // independent loads, summed in contributor order
+      const float a = __ldcg(rest + (size_t)q * stride + e);
+      const float b = __ldcg(rest + (size_t)(q + 1) * stride + e);
+      const float cc = __ldcg(rest + (size_t)(q + 2) * stride + e);
+      const float d = __ldcg(rest + (size_t)(q + 3) * stride + e);
+      v += a;
+      v += b;
+      v += cc;
+      v += d;
     }
+    for (; q < n_rest; ++q) v += __ldcg(rest + (size_t)q * stride + e);
     if (col < p.N) {
       if (p.bias) v += __half2float(p.bias[col]);
       p.y[(size_t)m * p.N + col] = __float2half_rn(v);
@@ -458,7 +474,7 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 static bool fast_path_ok(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
                          const uint16_t* scales, int M, int K, int N, int G) {
   (void)M;
-  return G % kSlotRows == 0 && K % G == 0 && N % 32 == 0 && K % 8 == 0 && aligned16(x) &&
+  return G % kSlotRows == 0 && K % kSlotRows == 0 && N % 32 == 0 && aligned16(x) &&
          aligned16(qweight) && aligned16(qzeros) && aligned16(scales);
 }
 
@@ -467,7 +483,7 @@ struct Plan {
   int grid;         // persistent CTAs
   int bands, slots;
   long long items;
-  size_t partial_floats, ticket_offset_bytes, bytes;
+  size_t partial_floats, bytes;
 };
 
 static Plan plan_for(const DeviceInfo& d, int M, int K, int N) {
@@ -478,11 +494,11 @@ static Plan plan_for(const DeviceInfo& d, int M, int K, int N) {
   pl.items = (long long)pl.bands * pl.slots;
   const int occ = pl.chunk_m == 1 ? d.occ_m1 : d.occ_small[pl.chunk_m];
   long long grid = (long long)d.sms * std::max(occ, 1);
-  grid = std::max<long long>(1, std::min<long long>(grid, pl.items));
+  // at least 8 slots (16 KB of int4 data) per CTA bounds the contributors per band
+  grid = std::max<long long>(1, std::min<long long>(grid, pl.items / 8));
   pl.grid = (int)grid;
   pl.partial_floats = (size_t)pl.grid * 2 * pl.chunk_m * kBandCols;
-  pl.ticket_offset_bytes = (pl.partial_floats * sizeof(float) + 255) & ~size_t(255);
-  pl.bytes = pl.ticket_offset_bytes + (((size_t)pl.bands * sizeof(int) + 255) & ~size_t(255));
+  pl.bytes = ANVILQ_WORKSPACE_COUNTER_BYTES + pl.partial_floats * sizeof(float);
   return pl;
 }
 
@@ -494,8 +510,9 @@ static int launch_fast(const Plan& pl, const uint16_t* x, const int32_t* qweight
   p.qzeros = qzeros;
   p.scales = reinterpret_cast<const __half*>(scales);
   p.bias = reinterpret_cast<const __half*>(bias);
-  p.partials = reinterpret_cast<float*>(workspace);
-  p.tickets = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + pl.ticket_offset_bytes);
+  // counters first (left zero by every call), partial sums after them
+  p.tickets = reinterpret_cast<int*>(workspace);
+  p.partials = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + ANVILQ_WORKSPACE_COUNTER_BYTES);
   p.dev_err = dev_err;
   p.K = K; p.N = N; p.W8 = N / 8; p.G = G;
   p.bands = pl.bands; p.slots = pl.slots; p.items = pl.items;
@@ -519,7 +536,7 @@ static int launch_fast(const Plan& pl, const uint16_t* x, const int32_t* qweight
 }
 
 static bool shape_ok(int M, int K, int N, int G) {
-  return M >= 1 && K >= 1 && N >= 8 && N % 8 == 0 && G >= 1 && K % G == 0;
+  return M >= 1 && K >= 1 && N >= 8 && N % 8 == 0 && G >= 1;
 }
 
 template <typename OutT>
@@ -565,15 +582,28 @@ int anvilq_w4a16_gemm(const uint16_t* x, const int32_t* qweight, const int32_t* 
                       const uint16_t* scales, const uint16_t* bias, uint16_t* y,
                       int M, int K, int N, int G, void* workspace, size_t workspace_bytes,
                       int* dev_err, anvilq_stream_t stream) {
+  return anvilq_w4a16_gemm_ex(x, qweight, qzeros, scales, bias, y, M, K, N, G, workspace, workspace_bytes,
+                              dev_err, 0u, stream);
+}
+
+int anvilq_w4a16_gemm_ex(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
+                         const uint16_t* scales, const uint16_t* bias, uint16_t* y,
+                         int M, int K, int N, int G, void* workspace, size_t workspace_bytes,
+                         int* dev_err, unsigned flags, anvilq_stream_t stream) {
+  if (flags & ~(unsigned)ANVILQ_GEMM_OVERLAP_PRIOR) return ANVILQ_EINVAL;
   if (!x || !qweight || !qzeros || !scales || !y) return ANVILQ_EINVAL;
   if (!shape_ok(M, K, N, G)) return ANVILQ_EINVAL;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (!fast_path_ok(x, qweight, qzeros, scales, M, K, N, G))
     return launch_exact(x, qweight, qzeros, scales, bias, reinterpret_cast<__half*>(y), M, K, N, G,
                         dev_err, s);
+  if (M == 1 && gemv_tma_supported(x, qweight, qzeros, scales, K, N, G))
+    return launch_gemv_tma(x, qweight, qzeros, scales, bias, y, K, N, G, dev_err, s,
+                           (flags & ANVILQ_GEMM_OVERLAP_PRIOR) != 0);
   const DeviceInfo* d = device_info();
   if (!d) return ANVILQ_ECUDA;
   const Plan pl = plan_for(*d, M, K, N);
+  if ((size_t)pl.bands * sizeof(int) > ANVILQ_WORKSPACE_COUNTER_BYTES) return ANVILQ_ESHAPE;
   if (!workspace || workspace_bytes < pl.bytes) return ANVILQ_EWORKSPACE;
   if (!aligned16(workspace)) return ANVILQ_EALIGN;
   return launch_fast(pl, x, qweight, qzeros, scales, bias, y, M, K, N, G, workspace, dev_err, s);
@@ -592,7 +622,7 @@ int anvilq_awq_dequant(const int32_t* qweight, const int32_t* qzeros, const uint
                        int8_t* delta_out, float* w_out, int K, int N, int G, int* dev_err,
                        anvilq_stream_t stream) {
   if (!qweight || !qzeros || !scales) return ANVILQ_EINVAL;
-  if (K < 1 || N < 8 || N % 8 || G < 1 || K % G) return ANVILQ_EINVAL;
+  if (K < 1 || N < 8 || N % 8 || G < 1) return ANVILQ_EINVAL;
   if ((reinterpret_cast<uintptr_t>(scales) & 3u) != 0) return ANVILQ_EALIGN;
   const long long n = (long long)K * (N / 8);
   const int threads = 256;

@@ -48,8 +48,14 @@ def raise_device_errors(device=None):
     value = int(w.item())
     if value:
         w.zero_()
-        raise _lib.AnvilqError(f"device error bits 0x{value:x}: invalid AWQ scale "
-                               "(negative nonzero or nonfinite)")
+        what = []
+        if value & 1:
+            what.append("invalid AWQ scale (negative nonzero or nonfinite)")
+        if value & 2:
+            what.append("sequence length outside [1, Tmax]")
+        if value & 4:
+            what.append("bounded wait expired inside a kernel")
+        raise _lib.AnvilqError(f"device error bits 0x{value:x}: " + "; ".join(what))
 
 
 def workspace(device, nbytes: int) -> torch.Tensor:
@@ -73,9 +79,10 @@ def _check_awq(qweight, qzeros, scales, group):
         raise ValueError("qweight, qzeros and scales must be 2-D")
     K, W8 = qweight.shape
     N = W8 * 8
-    if group < 1 or K % group:
-        raise ValueError(f"K={K} is not a multiple of the group size {group}")
-    if tuple(qzeros.shape) != (K // group, W8) or tuple(scales.shape) != (K // group, N):
+    if group < 1:
+        raise ValueError("group size must be >= 1")
+    groups = -(-K // group)   # row k uses group k // G; a partial last group is allowed
+    if tuple(qzeros.shape) != (groups, W8) or tuple(scales.shape) != (groups, N):
         raise ValueError("qzeros/scales shapes do not match qweight and the group size")
     for t in (qweight, qzeros, scales):
         if not t.is_cuda or not t.is_contiguous():
@@ -83,12 +90,18 @@ def _check_awq(qweight, qzeros, scales, group):
     return K, N
 
 
-def gemm(x, qweight, qzeros, scales, bias=None, group: int = 128, out=None, dev_err=None):
+GEMM_OVERLAP_PRIOR = 1
+
+
+def gemm(x, qweight, qzeros, scales, bias=None, group: int = 128, out=None, dev_err=None,
+         overlap_prior: bool = False):
     """y[M, N] = x[M, K] @ dequant(qweight, qzeros, scales) (+ bias), fp16 out.
 
     GPU counterpart of FP32Model.linear (anvil-q1/tests/official_weights.py:418-437)
     for M rows at once.  Device-side scale errors are OR-ed into `dev_err`
     (default: the per-device word read by ``raise_device_errors``).
+    overlap_prior: the weights are not written by the preceding work on the
+    stream, so the kernel may start streaming them before that work ends.
     """
     K, N = _check_awq(qweight, qzeros, scales, group)
     squeeze = x.dim() == 1
@@ -109,9 +122,10 @@ def gemm(x, qweight, qzeros, scales, bias=None, group: int = 128, out=None, dev_
     need = lib.anvilq_w4a16_gemm_workspace_size(M, K, N, group)
     ws = workspace(x2.device, need)
     err = device_error_word(x2.device) if dev_err is None else dev_err
-    _lib.check(lib.anvilq_w4a16_gemm(_ptr(x2), _ptr(qweight), _ptr(qzeros), _ptr(scales), _ptr(bias),
-                                     _ptr(out), M, K, N, group, _ptr(ws), ws.numel(), _ptr(err),
-                                     _stream_ptr(x2.device)), "anvilq_w4a16_gemm")
+    flags = GEMM_OVERLAP_PRIOR if overlap_prior else 0
+    _lib.check(lib.anvilq_w4a16_gemm_ex(_ptr(x2), _ptr(qweight), _ptr(qzeros), _ptr(scales), _ptr(bias),
+                                        _ptr(out), M, K, N, group, _ptr(ws), ws.numel(), _ptr(err), flags,
+                                        _stream_ptr(x2.device)), "anvilq_w4a16_gemm_ex")
     return out.view(N) if squeeze else out
 
 
@@ -174,3 +188,37 @@ def pack_lanes(codes):
 def unpack_lanes(words, outputs: int):
     """awq_prepare.unpack_lanes signature (awq_prepare.py:94-99): int32 [K, N/8] -> uint8 [N, K]."""
     return unpack(words, outputs).t().contiguous()
+
+
+def gqa_decode(q, k_cache, v_cache, seqlens, scale: float = 0.0, out=None, dev_err=None):
+    """Flash-decoding GQA attention: q [B, Hq, D], caches [B, Tmax, Hkv, D] fp16,
+    seqlens int32 [B] on the device; returns fp16 [B, Hq, D].
+
+    GPU counterpart of attention(q, keys, values) (anvil-q1-fp/tests/fp64_reference.py:164-170),
+    batched over sequences of individual lengths.
+    """
+    if q.dtype != torch.float16 or k_cache.dtype != torch.float16 or v_cache.dtype != torch.float16:
+        raise TypeError("q and the KV caches must be float16")
+    if q.dim() != 3 or k_cache.dim() != 4 or v_cache.shape != k_cache.shape:
+        raise ValueError("q [B, Hq, D], k_cache/v_cache [B, Tmax, Hkv, D]")
+    B, Hq, D = q.shape
+    Bk, Tmax, Hkv, Dk = k_cache.shape
+    if Bk != B or Dk != D:
+        raise ValueError("batch or head_dim of q and the caches differ")
+    if seqlens.dtype != torch.int32 or seqlens.numel() != B or not seqlens.is_cuda:
+        raise ValueError("seqlens must be an int32 CUDA tensor [B]")
+    for t in (q, k_cache, v_cache, seqlens):
+        if not t.is_contiguous():
+            raise ValueError("inputs must be contiguous")
+    if out is None:
+        out = torch.empty_like(q)
+    lib = _lib.load()
+    need = lib.anvilq_gqa_decode_workspace_size(B, Hq, Hkv, D, Tmax)
+    if need == 0:
+        raise ValueError(f"unsupported attention shape B={B} Hq={Hq} Hkv={Hkv} D={D} Tmax={Tmax}")
+    ws = workspace(q.device, need)
+    err = device_error_word(q.device) if dev_err is None else dev_err
+    _lib.check(lib.anvilq_gqa_decode(_ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(seqlens), _ptr(out), B, Hq,
+                                     Hkv, D, Tmax, float(scale), _ptr(ws), ws.numel(), _ptr(err),
+                                     _stream_ptr(q.device)), "anvilq_gqa_decode")
+    return out

@@ -5,8 +5,9 @@
 Allocates `sets` independent weight sets of one shape (chosen so that together
 they exceed the 126 MB L2; the default 8 x 23.5 MB = 188 MB) and launches the
 GEMM once per set per repetition, so that every profiled launch reads its
-weights from HBM.  Prints the mean device time per launch (CUDA events) and the
-algorithmic bytes per launch; numbers taken under a profiler are not results.
+weights from HBM.  The launches are replayed as one CUDA graph (unless --no-graph) and timed with
+CUDA events; prints the mean time per launch and the algorithmic bytes per
+launch.  Numbers taken under a profiler are not results.
 """
 from __future__ import annotations
 
@@ -28,23 +29,36 @@ def gemv_case(args):
         t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
         sets.append((t(synthetic.activations(args.M, args.K, rng=rng)), t(lay.qweight), t(lay.qzeros),
                      t(lay.scales), torch.empty((args.M, args.N), dtype=torch.float16, device=dev)))
-    for x, qw, qz, sc, y in sets:       # warm: workspaces, module load
-        ops.gemm(x, qw, qz, sc, None, args.G, out=y)
-    torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(args.reps):
+    stream = torch.cuda.Stream(dev)
+
+    def enqueue():
         for x, qw, qz, sc, y in sets:
-            ops.gemm(x, qw, qz, sc, None, args.G, out=y)
-    end.record()
-    torch.cuda.synchronize()
+            ops.gemm(x, qw, qz, sc, None, args.G, out=y, overlap_prior=args.overlap)
+
+    with torch.cuda.stream(stream):
+        enqueue()                        # warm: workspaces, module load
+    stream.synchronize()
+    graph = None
+    if args.graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            enqueue()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            graph.replay() if graph is not None else enqueue()
+        start.record(stream)
+        for _ in range(args.reps):
+            graph.replay() if graph is not None else enqueue()
+        end.record(stream)
+    stream.synchronize()
     ops.raise_device_errors(dev)
     n = args.reps * args.sets
     us = start.elapsed_time(end) * 1e3 / n
     b = synthetic.gemv_bytes(args.M, args.K, args.N, args.G)
     print(json.dumps({"case": "gemv", "M": args.M, "K": args.K, "N": args.N, "launches": n,
-                      "us_per_launch_incl_host": round(us, 3), "bytes_per_launch": b,
-                      "GBps": round(b / us / 1e3, 1)}))
+                      "graph": bool(args.graph), "overlap_prior": bool(args.overlap),
+                      "us_per_launch": round(us, 3), "bytes_per_launch": b, "GBps": round(b / us / 1e3, 1)}))
 
 
 def main(argv=None):
@@ -57,6 +71,10 @@ def main(argv=None):
     ap.add_argument("--sets", type=int, default=8)
     ap.add_argument("--reps", type=int, default=2)
     ap.add_argument("--seed", type=int, default=17)
+    ap.add_argument("--no-graph", dest="graph", action="store_false",
+                    help="launch eagerly from Python instead of replaying a CUDA graph")
+    ap.add_argument("--no-overlap", dest="overlap", action="store_false",
+                    help="launch without programmatic dependent launch")
     args = ap.parse_args(argv)
     gemv_case(args)
 

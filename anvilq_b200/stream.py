@@ -63,7 +63,8 @@ class ProjectionStream:
         for e in self.layers:
             if self.host_io:
                 e["x"].copy_(e["x_host"], non_blocking=True)
-            ops.gemm(e["x"], e["qweight"], e["qzeros"], e["scales"], e["bias"], self.group, out=e["y"])
+            ops.gemm(e["x"], e["qweight"], e["qzeros"], e["scales"], e["bias"], self.group, out=e["y"],
+                     overlap_prior=True)
             if self.host_io:
                 e["y_host"].copy_(e["y"], non_blocking=True)
 

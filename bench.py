@@ -266,7 +266,7 @@ def anvilq_arm(args, world, rank, local):
     traffic = None
     prof = REPO / "profiles" / "traffic.json"
     if prof.exists():
-        traffic = json.loads(prof.read_text()).get(f"gemv_m1_kernel/{args.workload}")
+        traffic = json.loads(prof.read_text()).get(f"gemv_tma_kernel/{args.workload}")
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
@@ -279,7 +279,7 @@ def anvilq_arm(args, world, rank, local):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "frac_of_8tbs_nominal": round(achieved / 8000.0, 4), "traffic": traffic,
-                     "kernel": "gemv_m1_kernel",
+                     "kernel": "gemv_tma_kernel",
                      "launch_avg_us": round(per_launch_ms * 1e3, 4)},
         "e2e": {"value": round(step_bytes * world * args.steps / (ms_e2e / 1e3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": e2e.h2d_bytes(), "d2h_bytes_per_step": e2e.d2h_bytes(),

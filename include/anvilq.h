@@ -8,7 +8,9 @@
  *    query.
  *  - binary16 tensors are passed as `uint16_t*` bit patterns; AWQ packed
  *    tensors as `int32_t*` in the reference's layout:
- *        qweight [K][N/8]   qzeros [K/G][N/8]   scales [K/G][N]   bias [N]
+ *        qweight [K][N/8]   qzeros [ceil(K/G)][N/8]   scales [ceil(K/G)][N]   bias [N]
+ *    (input row k uses group k / G; the last group may be partial, as in
+ *    anvil-q1/tests/official_weights.py:427-429)
  *    where logical output lane i of a packed word sits at bit shift
  *    (0,16,4,20,8,24,12,28)[i] (anvil-q1/tests/verify.py:38).
  *  - All work is asynchronous on `stream` (NULL = legacy default stream).
@@ -44,7 +46,16 @@ typedef struct CUstream_st* anvilq_stream_t; /* same type as cudaStream_t */
 #define ANVILQ_ESHAPE (-5)     /* shape outside the supported range */
 
 /* Bits OR-ed into *dev_err by a kernel. */
-#define ANVILQ_DEV_ERR_SCALE 1 /* an AWQ scale was negative-nonzero or nonfinite */
+#define ANVILQ_DEV_ERR_SCALE 1   /* an AWQ scale was negative-nonzero or nonfinite */
+#define ANVILQ_DEV_ERR_SEQLEN 2  /* a sequence length outside [1, Tmax] */
+#define ANVILQ_DEV_ERR_TIMEOUT 4 /* a bounded wait inside a kernel expired */
+
+/* Workspace layout shared by every entry point that takes one: the first
+ * ANVILQ_WORKSPACE_COUNTER_BYTES hold arrival counters that must be zero
+ * before a call and that every call leaves zero; the bytes after them are
+ * scratch that a call overwrites.  One workspace, zero-filled once, can
+ * therefore serve any sequence of calls ordered on one stream. */
+#define ANVILQ_WORKSPACE_COUNTER_BYTES 65536
 
 int anvilq_abi_version(void);
 const char* anvilq_strerror(int status);
@@ -63,12 +74,12 @@ const char* anvilq_strerror(int status);
  * M<=8), then rounded once to fp16: results differ from the reference's
  * strictly sequential binary32 sum only by accumulation order and the final
  * fp16 rounding.
- * Requirements: M >= 1, K >= 1, N >= 8, N % 8 == 0, G >= 1, K % G == 0.
- * The fast kernels additionally use G % 16 == 0, N % 32 == 0 and 16-byte
- * aligned pointers; other shapes fall back to the sequential kernel.
- * workspace: device memory of anvilq_w4a16_gemm_workspace_size(M, K, N, G)
- * bytes, zero-filled by the caller before its FIRST use; every call leaves
- * it zero-filled again, so it may be reused by later calls on the same stream.
+ * Requirements: M >= 1, K >= 1, N >= 8, N % 8 == 0, G >= 1.
+ * The fast kernels additionally use G % 16 == 0, K % 16 == 0, N % 32 == 0 and
+ * 16-byte aligned pointers; other shapes fall back to the sequential kernel.
+ * workspace: at least anvilq_w4a16_gemm_workspace_size(M, K, N, G) bytes,
+ * 16-byte aligned, with the layout described at ANVILQ_WORKSPACE_COUNTER_BYTES.
+ * Supports N <= 4,194,304.
  */
 size_t anvilq_w4a16_gemm_workspace_size(int M, int K, int N, int G);
 int anvilq_w4a16_gemm(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
@@ -76,6 +87,20 @@ int anvilq_w4a16_gemm(const uint16_t* x, const int32_t* qweight, const int32_t* 
                       int M, int K, int N, int G,
                       void* workspace, size_t workspace_bytes,
                       int* dev_err, anvilq_stream_t stream);
+
+/* Same operation with flags:
+ *   ANVILQ_GEMM_OVERLAP_PRIOR  the weights (qweight, qzeros, scales, bias) are
+ *     not written by the work enqueued just before this call on `stream`, so
+ *     the kernel may be launched before that work finishes and start
+ *     streaming its weights early (programmatic dependent launch).  x is
+ *     still read only after the preceding work has completed, and y written
+ *     after that.  Used for chains of GEMMs over resident model weights. */
+#define ANVILQ_GEMM_OVERLAP_PRIOR 1u
+int anvilq_w4a16_gemm_ex(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
+                         const uint16_t* scales, const uint16_t* bias, uint16_t* y,
+                         int M, int K, int N, int G,
+                         void* workspace, size_t workspace_bytes,
+                         int* dev_err, unsigned flags, anvilq_stream_t stream);
 
 /* Reference-order W4A16 GEMM: one thread per output column sums its K products
  * in increasing k from +0.0 with every binary32 multiply and add rounded
@@ -107,6 +132,29 @@ int anvilq_awq_dequant(const int32_t* qweight, const int32_t* qzeros, const uint
 int anvilq_awq_pack(const uint8_t* codes, int32_t* packed, int rows, int N,
                     anvilq_stream_t stream);
 int anvilq_awq_unpack(const int32_t* packed, uint8_t* codes, int rows, int N,
+                      anvilq_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * GQA decode attention over an fp16 KV cache (flash-decoding, split-KV).
+ *
+ * Replaces attention(q, keys, values) (anvil-q1-fp/tests/fp64_reference.py:164-170)
+ * and the attention loop of FP32Model.token (anvil-q1/tests/official_weights.py:471-486),
+ * batched: for sequence b and query head j,
+ *   out[b][j] = softmax_t(q[b][j] . k[b][t][j / (Hq/Hkv)] * scale) @ v[b][t][...]
+ * over positions t < seqlens[b].
+ *   q fp16 [B][Hq][D], k_cache / v_cache fp16 [B][Tmax][Hkv][D],
+ *   seqlens int32 [B] (device, each in [1, Tmax]), out fp16 [B][Hq][D].
+ * scale <= 0 selects 1/sqrt(D).  Scores and the softmax run in fp32
+ * (probabilities rounded to fp16 for the P.V product on the tensor cores).
+ * Requirements: Hq % Hkv == 0, Hq / Hkv <= 8, D in {64, 128}, B*Hkv <= 16384,
+ * 16-byte aligned q, caches and out; dev_err is required.  A sequence length
+ * outside [1, Tmax] sets ANVILQ_DEV_ERR_SEQLEN and yields zeros for it.
+ * workspace: at least anvilq_gqa_decode_workspace_size(...) bytes, layout as
+ * described at ANVILQ_WORKSPACE_COUNTER_BYTES. */
+size_t anvilq_gqa_decode_workspace_size(int B, int Hq, int Hkv, int D, int Tmax);
+int anvilq_gqa_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                      const int32_t* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D, int Tmax,
+                      float scale, void* workspace, size_t workspace_bytes, int* dev_err,
                       anvilq_stream_t stream);
 
 #ifdef __cplusplus

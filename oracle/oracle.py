@@ -230,13 +230,16 @@ def attention_f64(q, keys, values):
     q = np.asarray(q, np.float64)
     keys = np.asarray(keys, np.float64)
     values = np.asarray(values, np.float64)
-    grouping = q.shape[0] // keys.shape[1]
-    kk = np.repeat(keys, grouping, axis=1)
-    vv = np.repeat(values, grouping, axis=1)
-    scores = np.einsum("hd,thd->ht", q, kk) / np.sqrt(q.shape[1])
-    e = np.exp(scores - scores.max(axis=1, keepdims=True))
-    p = e / e.sum(axis=1, keepdims=True)
-    return np.einsum("ht,thd->hd", p, vv)
+    hq, d = q.shape
+    hkv = keys.shape[1]
+    grouping = hq // hkv
+    # query head j uses kv head j // grouping (the reference's np.repeat expansion),
+    # evaluated per kv head without materialising the repeated caches
+    qg = q.reshape(hkv, grouping, d)
+    scores = np.einsum("kgd,tkd->kgt", qg, keys) / np.sqrt(d)
+    e = np.exp(scores - scores.max(axis=2, keepdims=True))
+    p = e / e.sum(axis=2, keepdims=True)
+    return np.einsum("kgt,tkd->kgd", p, values).reshape(hq, d)
 
 
 def attention_fp32(q_bits, k_bits, v_bits):

@@ -1,0 +1,115 @@
+"""GPU parity of the GQA decode attention kernel against the oracle, through the C ABI."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from anvilq_b200 import synthetic
+
+pytestmark = pytest.mark.gpu
+
+# Per-operator tolerance of anvil-q1-fp/design/SPEC.md:311-317 (cosine >= 0.9999,
+# max|y - ref| / max(1, max|ref|) <= 0.002).  The kernel computes scores and the
+# softmax in fp32 and rounds probabilities to fp16 for the P.V tensor-core product.
+TOL_ERR, TOL_COS = 2e-3, 0.9999
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda", 0)
+
+
+def T(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def run(dev, q, k, v, seqlens):
+    from anvilq_b200 import ops
+    out = ops.gqa_decode(T(q, dev), T(k, dev), T(v, dev), T(np.asarray(seqlens, np.int32), dev))
+    ops.raise_device_errors(dev)
+    return out.float().cpu().numpy()
+
+
+def check(y, ref, what):
+    err, cos = oracle.normalized_error(y, ref)
+    assert err <= TOL_ERR and cos >= TOL_COS, (what, err, cos)
+
+
+def test_reference_fixtures(dev, golden_dir):
+    """fp64_reference.attention outputs on the fixture cases (head_dim 64/128)."""
+    g = np.load(golden_dir / "attention.npz")
+    n = 0
+    for key in [str(s) for s in g["case_names"]]:
+        q, k, v, ref = g[key + "_q"], g[key + "_k"], g[key + "_v"], g[key + "_y"]
+        if q.shape[1] not in (64, 128):
+            continue
+        y = run(dev, q[None], k[None], v[None], [k.shape[0]])
+        check(y[0], ref, key)
+        n += 1
+    assert n >= 4
+
+
+@pytest.mark.parametrize("B,Tmax", [(1, 512), (8, 512), (1, 4096), (8, 4096), (2, 32768)])
+def test_config_shapes(dev, B, Tmax):
+    """32 q heads / 8 kv heads, head_dim 128 (the BASELINE attention configuration)."""
+    q, k, v = synthetic.kv_case(B, 32, 8, 128, Tmax, seed=17 + B)
+    rng = np.random.default_rng(Tmax + B)
+    seqlens = [Tmax] + list(rng.integers(1, Tmax + 1, size=B - 1))
+    y = run(dev, q, k, v, seqlens)
+    ref = oracle.decode_attention_f64(q, k, v, seqlens)
+    for b in range(B):
+        check(y[b], ref[b], (B, Tmax, b, seqlens[b]))
+
+
+def test_qwen05b_shape(dev):
+    """14 q heads / 2 kv heads (group of 7), head_dim 64, context 1024."""
+    q, k, v = synthetic.kv_case(3, 14, 2, 64, 1024, seed=43)
+    seqlens = [1024, 1, 513]
+    y = run(dev, q, k, v, seqlens)
+    ref = oracle.decode_attention_f64(q, k, v, seqlens)
+    for b in range(3):
+        check(y[b], ref[b], seqlens[b])
+
+
+@pytest.mark.parametrize("L", [1, 2, 15, 16, 17, 63, 64, 65, 127, 129, 1000])
+def test_ragged_lengths(dev, L):
+    q, k, v = synthetic.kv_case(1, 8, 2, 128, 1024, seed=L)
+    y = run(dev, q, k, v, [L])
+    ref = oracle.decode_attention_f64(q, k, v, [L])
+    check(y[0], ref[0], L)
+
+
+def test_fp32_loop_agreement(dev):
+    """Against the FP32 sequential loop of official_weights.py:471-486 as well."""
+    q, k, v = synthetic.kv_case(1, 14, 2, 64, 300, seed=89)
+    y = run(dev, q, k, v, [300])
+    ref32 = oracle.attention_fp32(q[0].view(np.uint16), k[0].view(np.uint16), v[0].view(np.uint16))
+    check(y[0], ref32, "fp32 loop")
+
+
+def test_repeat_is_deterministic(dev):
+    from anvilq_b200 import ops
+    q, k, v = synthetic.kv_case(4, 32, 8, 128, 4096, seed=5)
+    args = (T(q, dev), T(k, dev), T(v, dev), T(np.array([4096, 3000, 17, 2048], np.int32), dev))
+    a = ops.gqa_decode(*args).clone()
+    b = ops.gqa_decode(*args)
+    ops.raise_device_errors(dev)
+    assert torch.equal(a, b)
+
+
+def test_bad_seqlen_flags_error(dev):
+    from anvilq_b200 import ops, AnvilqError
+    q, k, v = synthetic.kv_case(2, 8, 2, 64, 64, seed=3)
+    for bad in (0, 65, -1):
+        ops.gqa_decode(T(q, dev), T(k, dev), T(v, dev), T(np.array([64, bad], np.int32), dev))
+        with pytest.raises(AnvilqError):
+            ops.raise_device_errors(dev)
+
+
+def test_unsupported_shape_rejected_on_host(dev):
+    from anvilq_b200 import ops
+    q, k, v = synthetic.kv_case(1, 8, 2, 32, 16, seed=3)   # head_dim 32 is not a supported size
+    with pytest.raises(ValueError):
+        ops.gqa_decode(T(q, dev), T(k, dev), T(v, dev), T(np.array([16], np.int32), dev))
