@@ -30,6 +30,7 @@ SIGNATURES = {
     "anvilq_awq_unpack": (I, [P, P, I, I, P]),
     "anvilq_gqa_decode_workspace_size": (SZ, [I, I, I, I, I]),
     "anvilq_gqa_decode": (I, [P, P, P, P, P, I, I, I, I, I, F, P, SZ, P, P]),
+    "anvilq_gqa_decode_noalloc": (I, [P, P, P, P, P, I, I, I, I, I, F, P, P]),
 }
 
 _lib = None

@@ -567,6 +567,7 @@ const char* anvilq_strerror(int status) {
     case ANVILQ_ECUDA: return "CUDA kernel launch failed";
     case ANVILQ_EWORKSPACE: return "workspace missing or too small";
     case ANVILQ_ESHAPE: return "shape outside the supported range";
+    case ANVILQ_ENOSCRATCH: return "request needs more scratch than the fixed no-allocation buffer holds";
     default: return "unknown anvilq status";
   }
 }

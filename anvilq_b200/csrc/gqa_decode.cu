@@ -451,3 +451,88 @@ int anvilq_gqa_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Attention with no allocation and no caller workspace.
+//
+// Some callers cannot hand this library any device memory of their own:
+// a host whose allocator owns all of HBM and offers nothing per call, a
+// binding that only passes the tensors it was given, or a loop that must not
+// trigger cudaMalloc's implicit device synchronisation.  For them the split-KV
+// scratch (arrival counters, then per-split partial results) lives in a fixed
+// array in this library's device image instead.  Every GPU that loads the
+// library holds these bytes until the process exits.
+namespace anvilq {
+namespace attn {
+
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;   // 4 MiB, counters included
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+static void* g_noalloc_ptr[kMaxDevices];
+static int g_noalloc_rc[kMaxDevices];
+static std::once_flag g_noalloc_once[kMaxDevices];
+
+// Device address of g_noalloc_scratch on the current device.  In host code the
+// array's name is only a host-side stand-in, so the address is asked from the
+// runtime once per device, with that device current.
+static int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return ANVILQ_ECUDA;
+  }
+  std::call_once(g_noalloc_once[dev], [dev] {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    g_noalloc_rc[dev] = e == cudaSuccess && p != nullptr ? ANVILQ_OK : ANVILQ_ECUDA;
+    g_noalloc_ptr[dev] = e == cudaSuccess ? p : nullptr;
+    if (e != cudaSuccess) cudaGetLastError();
+  });
+  *out = g_noalloc_ptr[dev];
+  return g_noalloc_rc[dev];
+}
+
+}  // namespace attn
+}  // namespace anvilq
+
+extern "C" int anvilq_gqa_decode_noalloc(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                                         const int32_t* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D,
+                                         int Tmax, float scale, int* dev_err, anvilq_stream_t stream) {
+  using namespace anvilq::attn;
+  if (!q || !k_cache || !v_cache || !seqlens || !out || !dev_err) return ANVILQ_EINVAL;
+  if (!args_ok(B, Hq, Hkv, D, Tmax)) return ANVILQ_ESHAPE;
+  if (!a16(q) || !a16(k_cache) || !a16(v_cache) || !a16(out)) return ANVILQ_EALIGN;
+  const int sms = sm_count();
+  if (sms <= 0) return ANVILQ_ECUDA;
+  const Plan pl = plan_for(B, Hq, Hkv, D, Tmax, sms);
+  if (pl.bytes > kNoAllocScratchBytes) return ANVILQ_ENOSCRATCH;
+  void* ws = nullptr;
+  const int rc = noalloc_scratch(&ws);
+  if (rc != ANVILQ_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // The array keeps whatever the previous call left.  Counters must start at
+  // zero; a call cut short by a bounded wait may not have re-armed them.
+  if (cudaMemsetAsync(ws, 0, (size_t)B * Hkv * sizeof(int), st) != cudaSuccess) {
+    cudaGetLastError();
+    return ANVILQ_ECUDA;
+  }
+  Params p;
+  p.q = reinterpret_cast<const __half*>(q);
+  p.k = reinterpret_cast<const __half*>(k_cache);
+  p.v = reinterpret_cast<const __half*>(v_cache);
+  p.seqlens = seqlens;
+  p.out = reinterpret_cast<__half*>(out);
+  p.tickets = reinterpret_cast<int*>(ws);
+  p.partials = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + ANVILQ_WORKSPACE_COUNTER_BYTES);
+  p.dev_err = dev_err;
+  p.Hq = Hq; p.Hkv = Hkv; p.Tmax = Tmax; p.group = Hq / Hkv;
+  p.splits = pl.splits; p.tiles_per_split = pl.tiles_per_split;
+  const float s = scale > 0.0f ? scale : 1.0f / std::sqrt((float)D);
+  p.scale_log2 = s * 1.4426950408889634f;
+  const dim3 grid(pl.splits, Hkv, B);
+  if (D == 64)
+    gqa_decode_kernel<64><<<grid, kThreads, Layout<64>::kTotal, st>>>(p);
+  else
+    gqa_decode_kernel<128><<<grid, kThreads, Layout<128>::kTotal, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? ANVILQ_OK : ANVILQ_ECUDA;
+}

@@ -44,6 +44,7 @@ typedef struct CUstream_st* anvilq_stream_t; /* same type as cudaStream_t */
 #define ANVILQ_ECUDA (-3)      /* kernel launch failed (cudaGetLastError) */
 #define ANVILQ_EWORKSPACE (-4) /* workspace missing or smaller than required */
 #define ANVILQ_ESHAPE (-5)     /* shape outside the supported range */
+#define ANVILQ_ENOSCRATCH (-6) /* needs more than the fixed scratch of a no-allocation entry point */
 
 /* Bits OR-ed into *dev_err by a kernel. */
 #define ANVILQ_DEV_ERR_SCALE 1   /* an AWQ scale was negative-nonzero or nonfinite */
@@ -156,6 +157,30 @@ int anvilq_gqa_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t
                       const int32_t* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D, int Tmax,
                       float scale, void* workspace, size_t workspace_bytes, int* dev_err,
                       anvilq_stream_t stream);
+
+/* GQA decode attention that allocates nothing and takes no workspace.
+ *
+ * No counterpart in the reference: an addition for callers that cannot give
+ * this library device memory -- a host whose allocator already owns all of
+ * HBM and offers nothing per call, a binding that can only pass the tensors it
+ * was handed, or a decode loop that must not trigger cudaMalloc's implicit
+ * device synchronisation.
+ *
+ * Same operation, arguments and requirements as anvilq_gqa_decode, minus the
+ * workspace.  The split-KV scratch is a fixed 4 MiB array inside the library's
+ * device image, held by every GPU that loads the library until the process
+ * exits; a request whose scratch would exceed it is rejected with
+ * ANVILQ_ENOSCRATCH before anything is launched.  Nothing is allocated: no
+ * cudaMalloc, no cudaFree, no allocating library call.
+ * The first call on a device looks up the array's device address (once per
+ * device, with that device current); make that first call before any stream
+ * capture.  Every call on the device shares the one array, so calls that may
+ * overlap on the GPU (different streams without ordering) race and must not
+ * be issued; calls ordered on one stream are fine.  Each call zeroes the
+ * array's counters on `stream` before its kernel. */
+int anvilq_gqa_decode_noalloc(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                              const int32_t* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D,
+                              int Tmax, float scale, int* dev_err, anvilq_stream_t stream);
 
 #ifdef __cplusplus
 }
