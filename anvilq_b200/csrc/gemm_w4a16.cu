@@ -576,7 +576,8 @@ size_t anvilq_w4a16_gemm_workspace_size(int M, int K, int N, int G) {
   if (!shape_ok(M, K, N, G)) return 0;
   const DeviceInfo* d = device_info();
   if (!d) return 0;
-  return plan_for(*d, M, K, N).bytes;
+  const size_t b = plan_for(*d, M, K, N).bytes;
+  return M == 1 ? std::max(b, gemv_tma_workspace_bytes(K, N)) : b;
 }
 
 int anvilq_w4a16_gemm(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
@@ -599,7 +600,7 @@ int anvilq_w4a16_gemm_ex(const uint16_t* x, const int32_t* qweight, const int32_
     return launch_exact(x, qweight, qzeros, scales, bias, reinterpret_cast<__half*>(y), M, K, N, G,
                         dev_err, s);
   if (M == 1 && gemv_tma_supported(x, qweight, qzeros, scales, K, N, G))
-    return launch_gemv_tma(x, qweight, qzeros, scales, bias, y, K, N, G, dev_err, s,
+    return launch_gemv_tma(x, qweight, qzeros, scales, bias, y, K, N, G, workspace, workspace_bytes, dev_err, s,
                            (flags & ANVILQ_GEMM_OVERLAP_PRIOR) != 0);
   const DeviceInfo* d = device_info();
   if (!d) return ANVILQ_ECUDA;

@@ -1,37 +1,41 @@
 // gemv_tma.cu -- batch-1 W4A16 AWQ GEMV for B200: TMA-staged int4 stream,
-// thread-block-cluster split-K, DSMEM reduction.
+// two-level split-K (thread-block cluster + workspace), DSMEM reduction.
 //
 // Reference semantics: FP32Model.linear (anvil-q1/tests/official_weights.py:418-437),
 //   y[c] = sum_k x[k] * (u4 q[k][c] - u4 z[k/G][c]) * scale[k/G][c]  (+ bias[c]).
 //
 // Data movement.  The int4 matrix is the only large operand.  A band is 64
 // consecutive qweight words of every row (256 B per row, 512 output columns);
-// a tile is 32 rows of a band (8 KB), fetched by ONE cp.async.bulk.tensor.2d
-// from a tensor map over qweight [K][N/8].  Every warp streams its own range
-// of tiles through a private 3-stage shared-memory ring (one mbarrier per
-// stage), so the bytes in flight (up to 2 CTAs x 4 warps x 3 tiles = 192 KB
-// per SM) cost no registers.  Tiles past the last row or column are
-// zero-filled by the TMA unit and contribute nothing.
+// a tile is 16 rows of a band (4 KB), fetched by ONE cp.async.bulk.tensor.2d
+// from a tensor map over qweight [K][N/8], together with the tile's 16
+// activations (a 32-byte bulk copy) on the same mbarrier.  Every warp streams
+// its own range of tiles through a private 3-stage ring, so bytes in flight
+// cost no registers, and four 4-warp CTAs fit on an SM (16 warps, up to 192 KB
+// in flight).  Tiles past the last row or column are zero-filled by the TMA
+// unit and contribute nothing.
 //
-// Split-K.  The c CTAs of a thread-block cluster share one band and split its
-// tiles between their 4c warps; warps are reduced in shared memory, CTAs
-// through distributed shared memory in cluster-rank order (deterministic, no
-// global scratch, no atomics).  c in {1,2,4,8,16} is chosen on the host so that
-// all CTAs are resident at once and every warp has work.
+// Split-K, two levels.  The c CTAs of a thread-block cluster and kc clusters
+// share one band; the band's tiles are split evenly over all their warps.
+// Warps are reduced in shared memory and the CTAs of a cluster through
+// distributed shared memory, in rank order.  With kc > 1 every cluster leaves
+// one partial per column slice in the workspace and the CTA that arrives last
+// at the slice's ticket adds the kc partials in cluster order.  Every sum has a
+// fixed order, so results are bit-reproducible; there are no atomics on data
+// and no waits on other CTAs.
 //
-// Arithmetic (per thread: 4 words = 32 columns x 16 consecutive rows):
+// Arithmetic (per thread: 2 words = 16 columns x the 16 rows of a tile):
 //   * q is used as a binary16 SUBNORMAL: (w & 0x000F000F) reinterpreted as
 //     half2 is exactly (q0, q1) * 2^-24, (w & 0x00F000F0) is 16 (q2, q3) 2^-24,
 //     and the same on w >> 8 for lanes 4..7.  One AND per column pair.
-//   * x is pre-scaled per 16-row slot by an exact power of two 2^S (S from the
-//     slot's largest |x|, so |x 2^S| < 2^15): products x q land in the normal
-//     binary16 range and the 16-row partial sum acc = sum x 2^S q 2^-24 is
-//     accumulated with one HFMA2 per column pair per row.
-//   * The slot's partial is folded into fp32 as A += acc * 2^(24-S) (/16 for
-//     the shifted pairs), exact scaling.
-//   * The zero point is applied once per group through the slot sums of x:
-//     sum x (q - z) = sum x q - z sum x, and the group's scale once:
-//     y += s (A - z X).  Only the 16-product partials are binary16.
+//   * x is pre-scaled per tile by an exact power of two 2^S (S from the tile's
+//     largest |x|, so |x 2^S| < 2^15): products x q land in the normal binary16
+//     range and the 16-row partial acc = sum x 2^S q 2^-24 takes one HFMA2 per
+//     column pair per row.
+//   * The partial is folded into fp32 as A += acc * 2^(24-S) (/16 for the
+//     shifted pairs), an exact scaling.
+//   * The zero point is applied once per group through the tile sums of x,
+//     sum x (q - z) = sum x q - z sum x, and the scale once: y += s (A - z X).
+//     Only the 16-product partials are binary16.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -39,6 +43,8 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "../../include/anvilq.h"
@@ -50,21 +56,23 @@ namespace tma_gemv {
 
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
-constexpr int kBandWords = 64;                        // 256 B per row, 512 columns
+constexpr int kBandWords = 64;                          // 256 B per row, 512 columns
 constexpr int kBandCols = kBandWords * 8;
-constexpr int kTileRows = 32;
+constexpr int kTileRows = 16;
 constexpr int kStages = 3;
-constexpr int kTileBytes = kTileRows * kBandWords * 4;   // 8 KB
+constexpr int kTileBytes = kTileRows * kBandWords * 4;  // 4 KB
+constexpr int kMaxCluster = 16;
 constexpr unsigned long long kWaitLimitNs = 1000000000ull;
 
 // dynamic shared memory layout
 constexpr int kRingOff = 0;
-constexpr int kRingBytes = kWarps * kStages * kTileBytes;
-constexpr int kXsOff = kRingOff + kRingBytes;                    // [warp][32 rows] half2
-constexpr int kXrawOff = kXsOff + kWarps * kTileRows * 4;        // [warp][stage][32 rows] half
-constexpr int kBarOff = kXrawOff + kWarps * kStages * kTileRows * 2;   // [warp][stage] u64
-constexpr int kRedOff = kBarOff + kWarps * kStages * 8 + 64;     // [warp][512] f32
-constexpr int kPartOff = kRedOff + kWarps * kBandCols * 4;       // [512] f32
+constexpr int kRingBytes = kWarps * kStages * kTileBytes;                 // 48 KB
+constexpr int kRedBytes = kWarps * kBandCols * 4;                         // 8 KB, aliases the ring
+static_assert(kRedBytes <= kRingBytes, "reduction buffer reuses the ring");
+constexpr int kXsOff = kRingOff + kRingBytes;                             // [warp][16] half2
+constexpr int kXrawOff = kXsOff + kWarps * kTileRows * 4;                 // [warp][stage][16] half
+constexpr int kBarOff = kXrawOff + kWarps * kStages * kTileRows * 2;      // [warp][stage] u64
+constexpr int kPartOff = kBarOff + kWarps * kStages * 8 + 32;             // [512] f32
 constexpr int kSmemBytes = kPartOff + kBandCols * 4;
 
 struct Params {
@@ -73,10 +81,13 @@ struct Params {
   const __half* scales;
   const __half* bias;
   __half* y;
+  float* partials;   // [bands][kc][512]   (kc > 1)
+  int* tickets;      // [bands][c]         (kc > 1)
   int* dev_err;
   int K, N, W8, G;
-  int cluster;   // CTAs per band
-  int tiles;     // tiles per band = ceil(K / 32)
+  int cluster;       // c: CTAs per cluster
+  int kc;            // clusters per band
+  int tiles;         // tiles per band = ceil(K / 16)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -111,24 +122,29 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ float ld_dsmem_f32(const float* local, uint32_t rank) {
+__device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank) {
   uint32_t remote;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  return remote;
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
   float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
   return v;
 }
 __device__ __forceinline__ half2 h2(uint32_t u) { return *reinterpret_cast<half2*>(&u); }
 __device__ __forceinline__ uint32_t u32(half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 4)
     gemv_tma_kernel(const __grid_constant__ CUtensorMap tmap, const Params p) {
   extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ int s_last;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int c = p.cluster;
   const int rank = c > 1 ? (int)cluster_rank() : 0;
-  const int band = blockIdx.x / c;
-  const int wi = rank * kWarps + warp, nw = c * kWarps;
+  const int cluster_id = blockIdx.x / c;
+  const int band = cluster_id / p.kc, kidx = cluster_id % p.kc;
+  const int wi = (kidx * c + rank) * kWarps + warp, nw = p.kc * c * kWarps;
   const int t0 = (int)((long long)wi * p.tiles / nw);
   const int t1 = (int)((long long)(wi + 1) * p.tiles / nw);
   const int ntiles = t1 - t0;
@@ -149,17 +165,16 @@ __global__ void __launch_bounds__(kThreads, 2)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __syncwarp();
 
-  // Stage j % kStages receives tile t0 + j (8 KB of int4 words) and the tile's
-  // 32 activations (64 B), both counted on the stage's mbarrier.
-  auto x_bytes = [&](int j) { return (uint32_t)min(kTileRows, p.K - (t0 + j) * kTileRows) * 2u; };
+  // Stage j % kStages receives tile t0 + j (4 KB of int4 words) and the tile's
+  // 16 activations (32 B), both counted on the stage's mbarrier.
+  const uint32_t x_bytes = kTileRows * 2;   // K % 16 == 0: every tile has 16 rows
   auto issue_tile = [&](int j, bool with_x) {   // lane 0 only
     const int st = j % kStages;
     const uint32_t bar = bar0 + 8 * st;
     // the stage was last read through the generic proxy; order that before the TMA write
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     if (with_x)
-      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
-                   "r"(kTileBytes + x_bytes(j))
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(kTileBytes + x_bytes)
                    : "memory");
     else
       asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(kTileBytes) : "memory");
@@ -171,67 +186,66 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (with_x)
       asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                        xraw0 + st * kTileRows * 2),
-                   "l"(p.x + (size_t)(t0 + j) * kTileRows), "r"(x_bytes(j)), "r"(bar)
+                   "l"(p.x + (size_t)(t0 + j) * kTileRows), "r"(x_bytes), "r"(bar)
                    : "memory");
   };
   auto issue_x = [&](int j) {   // lane 0 only: activations of a tile whose weights are in flight
     const int st = j % kStages;
     const uint32_t bar = bar0 + 8 * st;
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(x_bytes(j)) : "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(x_bytes) : "memory");
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                      xraw0 + st * kTileRows * 2),
-                 "l"(p.x + (size_t)(t0 + j) * kTileRows), "r"(x_bytes(j)), "r"(bar)
+                 "l"(p.x + (size_t)(t0 + j) * kTileRows), "r"(x_bytes), "r"(bar)
                  : "memory");
   };
 
-  const int q = lane % 16, rg = lane / 16;         // 4 words of the band, 16-row half of the tile
-  const int w0 = band * kBandWords + q * 4;
+  const int w0 = band * kBandWords + lane * 2;   // this lane's 2 words = 16 columns
   const bool active = w0 < p.W8;
-  auto slot_row = [&](int j) { return (t0 + j) * kTileRows + 16 * rg; };
+  auto tile_row = [&](int j) { return (t0 + j) * kTileRows; };
 
-  float A[32], Y[32];
+  float A[16], Y[16];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) A[j] = Y[j] = 0.0f;
+  for (int j = 0; j < 16; ++j) A[j] = Y[j] = 0.0f;
   float Xg = 0.0f;
-  uint4 sc[4] = {}, zq = {}, nsc[4] = {}, nzq = {};
+  uint4 sc[2] = {}, nsc[2] = {};
+  uint2 zq = {}, nzq = {};
   uint32_t bad = 0;
   bool ok = true;
 
-  auto load_group = [&](int row, uint4* s4, uint4& z) {   // scales and zeros of the group of `row`
-    if (active && row < p.K) {
+  auto load_group = [&](int row, uint4* s2, uint2& z) {   // scales and zeros of the group of `row`
+    if (active) {
       const int g = row / p.G;
       const __half* sp = p.scales + (size_t)g * p.N + 8 * (size_t)w0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) s4[i] = __ldg(reinterpret_cast<const uint4*>(sp + 8 * i));
-      z = __ldg(reinterpret_cast<const uint4*>(p.qzeros + (size_t)g * p.W8 + w0));
+      s2[0] = __ldg(reinterpret_cast<const uint4*>(sp));
+      s2[1] = __ldg(reinterpret_cast<const uint4*>(sp + 8));
+      z = __ldg(reinterpret_cast<const uint2*>(p.qzeros + (size_t)g * p.W8 + w0));
     }
   };
-  auto check_group = [&](int row) {   // the slot that opens a group checks its scales, once
-    if (active && row < p.K && row % p.G == 0) {
+  auto check_group = [&](int row) {   // the tile that opens a group checks its scales, once
+    if (active && row % p.G == 0) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < 2; ++i)
         bad |= invalid_scale_pair(sc[i].x) | invalid_scale_pair(sc[i].y) | invalid_scale_pair(sc[i].z) |
                invalid_scale_pair(sc[i].w);
     }
   };
-
-  // y += s (A - z X) for the finished group; s, z of this lane's 32 columns
+  // y += s (A - z X) for the finished group, this lane's 16 columns
   auto flush_group = [&]() {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t zw = i == 0 ? zq.x : i == 1 ? zq.y : i == 2 ? zq.z : zq.w;
+    for (int i = 0; i < 2; ++i) {
+      const uint32_t zw = i == 0 ? zq.x : zq.y;
       const uint32_t sw[4] = {sc[i].x, sc[i].y, sc[i].z, sc[i].w};
-      // zero points as fp32 via the binary16 magic 1024 + z, pairs (0,1),(2,3),(4,5),(6,7)
+      // zero points via the binary16 magic 1024 + z, pairs (0,1),(2,3),(4,5),(6,7)
       const uint32_t zp[4] = {(zw & 0x000F000Fu) | 0x64006400u, ((zw >> 4) & 0x000F000Fu) | 0x64006400u,
                               ((zw >> 8) & 0x000F000Fu) | 0x64006400u, ((zw >> 12) & 0x000F000Fu) | 0x64006400u};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float2 s2 = __half22float2(h2(sw[e]));
         const float2 z2 = __half22float2(h2(zp[e]));
-        const float t0v = fmaf(-(z2.x - 1024.0f), Xg, A[i * 8 + 2 * e]);
-        const float t1v = fmaf(-(z2.y - 1024.0f), Xg, A[i * 8 + 2 * e + 1]);
-        Y[i * 8 + 2 * e] = fmaf(s2.x, t0v, Y[i * 8 + 2 * e]);
-        Y[i * 8 + 2 * e + 1] = fmaf(s2.y, t1v, Y[i * 8 + 2 * e + 1]);
+        const float a0 = fmaf(-(z2.x - 1024.0f), Xg, A[i * 8 + 2 * e]);
+        const float a1 = fmaf(-(z2.y - 1024.0f), Xg, A[i * 8 + 2 * e + 1]);
+        Y[i * 8 + 2 * e] = fmaf(s2.x, a0, Y[i * 8 + 2 * e]);
+        Y[i * 8 + 2 * e + 1] = fmaf(s2.y, a1, Y[i * 8 + 2 * e + 1]);
         A[i * 8 + 2 * e] = 0.0f;
         A[i * 8 + 2 * e + 1] = 0.0f;
       }
@@ -240,36 +254,33 @@ __global__ void __launch_bounds__(kThreads, 2)
   };
 
   // -- prologue: weights first (they do not depend on the previous kernel) ---
-  int issued = 0;
   const int pro = min(kStages - 1, ntiles);
   if (lane == 0)
     for (int j = 0; j < pro; ++j) issue_tile(j, false);
-  issued = pro;
-  if (ntiles > 0) load_group(slot_row(0), sc, zq);
+  int issued = pro;
+  if (ntiles > 0) load_group(tile_row(0), sc, zq);
   asm volatile("griddepcontrol.wait;" ::: "memory");   // x may come from the previous kernel
   if (lane == 0)
     for (int j = 0; j < pro; ++j) issue_x(j);
-  if (ntiles > 0) check_group(slot_row(0));
+  if (ntiles > 0) check_group(tile_row(0));
 
   for (int j = 0; j < ntiles; ++j) {
     if (issued < ntiles) {
       if (lane == 0) issue_tile(issued, true);
       ++issued;
     }
-    const bool next_group = j + 1 < ntiles && slot_row(j + 1) / p.G != slot_row(j) / p.G;
-    if (next_group) load_group(slot_row(j + 1), nsc, nzq);   // lands while this tile computes
+    const bool next_group = j + 1 < ntiles && tile_row(j + 1) / p.G != tile_row(j) / p.G;
+    if (next_group) load_group(tile_row(j + 1), nsc, nzq);   // lands while this tile computes
     const int st = j % kStages;
     const bool landed = mbar_wait_bounded(bar0 + 8 * st, (j / kStages) & 1);
     if (!__all_sync(0xffffffffu, landed)) {
       ok = false;
       break;
     }
-    // -- activations of the tile: lane l holds row l; a slot (16 rows) is 16 lanes
-    float Sxs, pow_lo;
+    // -- the tile's activations: lanes l and l + 16 both hold row l % 16
+    float Xt, pow_lo;
     {
-      static_assert(kTileRows == 32, "one activation row per lane");
-      const int kr = (t0 + j) * kTileRows + lane;
-      const float xf = kr < p.K ? __half2float(xraw[st * kTileRows + lane]) : 0.0f;
+      const float xf = __half2float(xraw[st * kTileRows + (lane & 15)]);
       float mx = fabsf(xf);
       float sum = xf;
 #pragma unroll
@@ -280,26 +291,23 @@ __global__ void __launch_bounds__(kThreads, 2)
       // |x| < 2^e with e the binary exponent of mx; scale by 2^(15 - e)
       const int e = mx > 0.0f ? ((__float_as_int(mx) >> 23) & 255) - 126 : 0;
       const int S = 15 - e;
-      const float f = __int_as_float((127 + S) << 23);
-      const half hs = __float2half_rn(xf * f);
-      xs[lane] = u32(__halves2half2(hs, hs));
-      // this thread's slot is rows 16 rg .. 16 rg + 15, held by lanes 16 rg .. 16 rg + 15
-      Sxs = __shfl_sync(0xffffffffu, sum, 16 * rg);
-      const int Smine = __shfl_sync(0xffffffffu, S, 16 * rg);
-      pow_lo = __int_as_float((127 + 24 - Smine) << 23);
+      const half hs = __float2half_rn(xf * __int_as_float((127 + S) << 23));
+      if (lane < 16) xs[lane] = u32(__halves2half2(hs, hs));
+      Xt = sum;
+      pow_lo = __int_as_float((127 + 24 - S) << 23);
     }
     __syncwarp();
-    const unsigned char* tile = ring + st * kTileBytes + (16 * rg) * (kBandWords * 4) + q * 16;
-    half2 part[16];
+    const unsigned char* tile = ring + st * kTileBytes + lane * 8;
+    half2 part[8];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) part[i] = __float2half2_rn(0.0f);
+    for (int i = 0; i < 8; ++i) part[i] = __float2half2_rn(0.0f);
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      const uint4 w = *reinterpret_cast<const uint4*>(tile + r * (kBandWords * 4));
-      const half2 xx = h2(xs[16 * rg + r]);
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    for (int r = 0; r < kTileRows; ++r) {
+      const uint2 w = *reinterpret_cast<const uint2*>(tile + r * (kBandWords * 4));
+      const half2 xx = h2(xs[r]);
+      const uint32_t ws[2] = {w.x, w.y};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < 2; ++i) {
         const uint32_t w8 = ws[i] >> 8;
         part[4 * i + 0] = __hfma2(xx, h2(ws[i] & 0x000F000Fu), part[4 * i + 0]);   // columns 0,1
         part[4 * i + 1] = __hfma2(xx, h2(ws[i] & 0x00F000F0u), part[4 * i + 1]);   // columns 2,3 (x16)
@@ -310,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncwarp();   // stage st and xs are free again
     const float pow_hi = pow_lo * 0.0625f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < 2; ++i)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float2 f2 = __half22float2(part[4 * i + e]);
@@ -318,67 +326,113 @@ __global__ void __launch_bounds__(kThreads, 2)
         A[i * 8 + 2 * e] = fmaf(f2.x, pw, A[i * 8 + 2 * e]);
         A[i * 8 + 2 * e + 1] = fmaf(f2.y, pw, A[i * 8 + 2 * e + 1]);
       }
-    Xg += Sxs;
+    Xg += Xt;
     if (next_group) {
       flush_group();
-#pragma unroll
-      for (int i = 0; i < 4; ++i) sc[i] = nsc[i];
+      sc[0] = nsc[0];
+      sc[1] = nsc[1];
       zq = nzq;
-      check_group(slot_row(j + 1));
+      check_group(tile_row(j + 1));
     }
   }
-  const bool ended_in_group = ntiles > 0;
-  if (ok && ended_in_group) flush_group();
+  if (ok && ntiles > 0) flush_group();
   if (!ok) {
     if (lane == 0 && p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_TIMEOUT);
     for (int j = max(0, issued - kStages); j < issued; ++j)
       mbar_wait_bounded(bar0 + 8 * (j % kStages), (j / kStages) & 1);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) Y[j] = 0.0f;
+    for (int j = 0; j < 16; ++j) Y[j] = 0.0f;
   }
   if (bad && p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_SCALE);
 
-  // -- reduce: the two row halves of the warp, then the warps, then the cluster
+  // -- reduce: warps (shared memory, reusing the ring), then the cluster (DSMEM),
+  //    then the kc clusters of the band (workspace)
+  __syncthreads();   // every warp is done with its ring
+  float* red = reinterpret_cast<float*>(smem + kRingOff);   // [warp][512]
 #pragma unroll
-  for (int j = 0; j < 32; ++j) Y[j] += __shfl_xor_sync(0xffffffffu, Y[j], 16);
-  float* red = reinterpret_cast<float*>(smem + kRedOff) + warp * kBandCols;
-  if (rg == 0) {
-#pragma unroll
-    for (int j = 0; j < 32; j += 4)
-      *reinterpret_cast<float4*>(red + q * 32 + j) = make_float4(Y[j], Y[j + 1], Y[j + 2], Y[j + 3]);
-  }
+  for (int j = 0; j < 16; j += 4)
+    *reinterpret_cast<float4*>(red + warp * kBandCols + lane * 16 + j) =
+        make_float4(Y[j], Y[j + 1], Y[j + 2], Y[j + 3]);
   __syncthreads();
   float* part = reinterpret_cast<float*>(smem + kPartOff);
   for (int col = threadIdx.x; col < kBandCols; col += kThreads) {
     float v = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) v += reinterpret_cast<const float*>(smem + kRedOff)[w * kBandCols + col];
+    for (int w = 0; w < kWarps; ++w) v += red[w * kBandCols + col];
     part[col] = v;
   }
-  const int col0 = band * kBandCols;
-  if (c == 1) {
+  if (c > 1)
+    cluster_sync();   // every CTA of the cluster reaches this, errors included
+  else
     __syncthreads();
-    for (int col = threadIdx.x; col < kBandCols; col += kThreads) {
-      if (col0 + col < p.N) {
-        float v = part[col];
-        if (p.bias) v += __half2float(p.bias[col0 + col]);
-        p.y[col0 + col] = __float2half_rn(v);
+  const int per = kBandCols / c;          // this CTA's column slice of the band
+  const int col0 = band * kBandCols + rank * per;
+  constexpr int kMaxPer = kBandCols / kThreads;   // up to 4 columns per thread (c == 1)
+  float v[kMaxPer];
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    v[i] = 0.0f;
+    const int t = threadIdx.x + i * kThreads;
+    if (t < per) {
+      if (c > 1) {
+        float r[kMaxCluster];
+#pragma unroll
+        for (int k = 0; k < kMaxCluster; ++k)   // all loads first, then the ordered sum
+          if (k < c) r[k] = ld_dsmem_f32(dsmem_addr(part + rank * per + t, (uint32_t)k));
+#pragma unroll
+        for (int k = 0; k < kMaxCluster; ++k)
+          if (k < c) v[i] += r[k];
+      } else {
+        v[i] = part[t];
       }
     }
-    return;
   }
-  cluster_sync();   // every CTA of the cluster reaches this point, errors included
-  const int per = kBandCols / c;
-  for (int t = threadIdx.x; t < per; t += kThreads) {
-    const int col = rank * per + t;
-    float v = 0.0f;
-    for (int r = 0; r < c; ++r) v += ld_dsmem_f32(part + col, (uint32_t)r);
-    if (col0 + col < p.N) {
-      if (p.bias) v += __half2float(p.bias[col0 + col]);
-      p.y[col0 + col] = __float2half_rn(v);
+  if (c > 1) cluster_sync();   // peers may still be reading this CTA's partial
+
+  if (p.kc > 1) {
+    float* slot = p.partials + ((size_t)band * p.kc + kidx) * kBandCols + rank * per;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      const int t = threadIdx.x + i * kThreads;
+      if (t < per) __stcg(slot + t, v[i]);
+    }
+    __threadfence();
+    __syncthreads();
+    int* ticket = p.tickets + band * c + rank;
+    if (threadIdx.x == 0) {
+      const int n = atomicAdd(ticket, 1);
+      s_last = n == p.kc - 1;
+      if (s_last) *ticket = 0;   // re-arm for the next launch
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const float* base = p.partials + (size_t)band * p.kc * kBandCols + rank * per;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      const int t = threadIdx.x + i * kThreads;
+      if (t < per) {
+        float r[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)   // kc <= 8: all loads first, then the ordered sum
+          if (k < p.kc) r[k] = __ldcg(base + (size_t)k * kBandCols + t);
+        float acc = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (k < p.kc) acc += r[k];
+        v[i] = acc;
+      }
     }
   }
-  cluster_sync();   // peers may still be reading this CTA's partial
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int t = threadIdx.x + i * kThreads;
+    if (t < per && col0 + t < p.N) {
+      float out = v[i];
+      if (p.bias) out += __half2float(p.bias[col0 + t]);
+      p.y[col0 + t] = __float2half_rn(out);
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -434,15 +488,66 @@ static const DeviceInfo* device_info() {
   return &g_dev[dev];
 }
 
-// Largest cluster size whose clusters (one per band) are all co-resident and
-// whose warps each get at least half a tile on average.
-int choose_cluster(int bands, int tiles, const DeviceInfo& d) {
+struct Plan {
+  int bands, tiles, c, kc;
+  size_t bytes;   // workspace bytes (counters included)
+};
+
+// Tuning aid: ANVILQ_GEMV_PLAN="c,kc" forces the cluster size and the number of
+// clusters per band (c a power of two <= 16, 1 <= kc <= 8), for sweeps.
+static bool plan_override(int* c, int* kc) {
+  static int oc = 0, okc = 0;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    const char* e = std::getenv("ANVILQ_GEMV_PLAN");
+    int a = 0, b = 0;
+    if (e && std::sscanf(e, "%d,%d", &a, &b) == 2 && a >= 1 && a <= kMaxCluster && (a & (a - 1)) == 0 && b >= 1 &&
+        b <= 8) {
+      oc = a;
+      okc = b;
+    }
+  });
+  if (!oc) return false;
+  *c = oc;
+  *kc = okc;
+  return true;
+}
+
+// Grid of bands x kc clusters of c CTAs.  Measured on B200: the workspace
+// fix-up of kc > 1 costs a few microseconds of tail, so the largest cluster
+// whose clusters are all co-resident wins (c = 16, kc = 1 for 7B-class
+// layers); only deep-K layers, where every warp would stream 16 or more tiles,
+// trade that tail for more warps (c = 8, kc = 3 on 28672 x 8192).
+static Plan make_plan(const DeviceInfo& d, int K, int N) {
+  Plan pl{};
+  const int W8 = N / 8;
+  pl.bands = (W8 + kBandWords - 1) / kBandWords;
+  pl.tiles = (K + kTileRows - 1) / kTileRows;
   int c = 1;
-  for (int i = 1; i < 5; ++i) {
+  for (int i = 4; i >= 1; --i) {
     const int cand = 1 << i;
-    if (d.max_clusters[i] >= bands && 2 * cand <= tiles) c = cand;
+    if (d.max_clusters[i] >= pl.bands && cand * kWarps <= pl.tiles) {
+      c = cand;
+      break;
+    }
   }
-  return c;
+  int kc = 1;
+  if (pl.tiles / (kWarps * c) >= 16) {
+    for (int cand_c : {8, 16}) {
+      const int i = cand_c == 8 ? 3 : 4;
+      for (int cand_kc = 3; cand_kc >= 2; --cand_kc)
+        if (kc == 1 && d.max_clusters[i] >= pl.bands * cand_kc && pl.bands * cand_c * cand_kc <= 4 * d.sms) {
+          c = cand_c;
+          kc = cand_kc;
+        }
+    }
+  }
+  pl.c = c;
+  pl.kc = kc;
+  plan_override(&pl.c, &pl.kc);
+  pl.bytes = ANVILQ_WORKSPACE_COUNTER_BYTES +
+             (pl.kc > 1 ? (size_t)pl.bands * pl.kc * kBandCols * sizeof(float) : 0);
+  return pl;
 }
 
 }  // namespace tma_gemv
@@ -454,13 +559,25 @@ bool gemv_tma_supported(const void* x, const int32_t* qweight, const int32_t* qz
          tma_gemv::encode_fn() != nullptr;
 }
 
+size_t gemv_tma_workspace_bytes(int K, int N) {
+  const tma_gemv::DeviceInfo* d = tma_gemv::device_info();
+  if (!d || d->sms <= 0) return 0;
+  return tma_gemv::make_plan(*d, K, N).bytes;
+}
+
 int launch_gemv_tma(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
-                    const uint16_t* bias, uint16_t* y, int K, int N, int G, int* dev_err, cudaStream_t stream,
-                    bool overlap_prior) {
+                    const uint16_t* bias, uint16_t* y, int K, int N, int G, void* workspace,
+                    size_t workspace_bytes, int* dev_err, cudaStream_t stream, bool overlap_prior) {
   using namespace tma_gemv;
   const DeviceInfo* d = device_info();
   auto encode = encode_fn();
   if (!d || d->sms <= 0 || !encode) return ANVILQ_ECUDA;
+  const Plan pl = make_plan(*d, K, N);
+  if (pl.kc > 1) {
+    if (!workspace || workspace_bytes < pl.bytes) return ANVILQ_EWORKSPACE;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 15u) != 0) return ANVILQ_EALIGN;
+    if ((size_t)pl.bands * pl.c * sizeof(int) > ANVILQ_WORKSPACE_COUNTER_BYTES) return ANVILQ_ESHAPE;
+  }
   const int W8 = N / 8;
   CUtensorMap map;
   const cuuint64_t dims[2] = {(cuuint64_t)W8, (cuuint64_t)K};
@@ -477,20 +594,24 @@ int launch_gemv_tma(const uint16_t* x, const int32_t* qweight, const int32_t* qz
   p.scales = reinterpret_cast<const __half*>(scales);
   p.bias = reinterpret_cast<const __half*>(bias);
   p.y = reinterpret_cast<__half*>(y);
+  p.tickets = reinterpret_cast<int*>(workspace);
+  p.partials = workspace ? reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) +
+                                                    ANVILQ_WORKSPACE_COUNTER_BYTES)
+                         : nullptr;
   p.dev_err = dev_err;
   p.K = K; p.N = N; p.W8 = W8; p.G = G;
-  const int bands = (W8 + kBandWords - 1) / kBandWords;
-  p.tiles = (K + kTileRows - 1) / kTileRows;
-  p.cluster = choose_cluster(bands, p.tiles, *d);
+  p.cluster = pl.c;
+  p.kc = pl.kc;
+  p.tiles = pl.tiles;
 
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(bands * p.cluster, 1, 1);
+  cfg.gridDim = dim3(pl.bands * pl.kc * pl.c, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = p.cluster;
+  attr[0].val.clusterDim.x = pl.c;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;

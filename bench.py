@@ -263,10 +263,12 @@ def anvilq_arm(args, world, rank, local):
     value = step_bytes * world * args.steps / (ms / 1e3) / 1e9
     per_launch_ms = ms_step / s.launches()
     achieved = step_bytes / s.launches() / (per_launch_ms / 1e3) / 1e9
-    traffic = None
+    traffic = None   # DRAM bytes per launch from the committed ncu capture (profiles/)
     prof = REPO / "profiles" / "traffic.json"
     if prof.exists():
-        traffic = json.loads(prof.read_text()).get(f"gemv_tma_kernel/{args.workload}")
+        entry = json.loads(prof.read_text()).get(f"gemv_tma_kernel/{args.workload}")
+        if entry:
+            traffic = int(step_bytes / s.launches() * entry["ratio_read_over_algorithmic"])
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
