@@ -29,15 +29,27 @@ class CheckpointError(ValueError):
 
 
 class ArrayCheckpoint:
-    def __init__(self, layers: dict):
-        """layers: {(layer, projection): AwqLayer}."""
+    def __init__(self, layers: dict, embedding=None, norms=None):
+        """layers: {(layer, projection): AwqLayer}; embedding fp16 [V, H] (kind 0,
+        also the tied lm_head); norms: {("input", layer) | ("post", layer) | ("final", 0): fp16 [H]}
+        (kinds 5, 6, 7)."""
         self.layers = dict(layers)
+        self.embedding = embedding
+        self.norms = dict(norms or {})
 
     # -- reference interface (official_weights.py:320-356) --------------------
     @staticmethod
     def resolve(kind, layer, projection, row, col):
         if not all(type(v) is int and v >= 0 for v in (kind, layer, projection, row, col)):
             raise CheckpointError("invalid public model address")
+        if kind == 0:
+            if layer or projection:
+                raise CheckpointError("embedding unused address fields")
+            return (0, 0, 0), (row, col)
+        if kind in (5, 6, 7):
+            if projection or row or (kind == 7 and layer):
+                raise CheckpointError("norm unused address fields")
+            return (kind, layer, 0), (col,)
         if kind not in (1, 2, 3, 4):
             raise CheckpointError(f"not an array checkpoint model kind: {kind}")
         if kind == 4:
@@ -48,6 +60,16 @@ class ArrayCheckpoint:
 
     def _array(self, name):
         kind, layer, projection = name
+        if kind == 0:
+            if self.embedding is None:
+                raise CheckpointError("checkpoint has no embedding")
+            return self.embedding
+        if kind in (5, 6, 7):
+            key = {5: ("input", layer), 6: ("post", layer), 7: ("final", 0)}[kind]
+            try:
+                return self.norms[key]
+            except KeyError as exc:
+                raise CheckpointError(f"no norm {key}") from exc
         try:
             t = self.layers[layer, projection]
         except KeyError as exc:

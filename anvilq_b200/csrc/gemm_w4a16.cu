@@ -600,8 +600,13 @@ int anvilq_w4a16_gemm_ex(const uint16_t* x, const int32_t* qweight, const int32_
     return launch_exact(x, qweight, qzeros, scales, bias, reinterpret_cast<__half*>(y), M, K, N, G,
                         dev_err, s);
   if (M == 1 && gemv_tma_supported(x, qweight, qzeros, scales, K, N, G))
-    return launch_gemv_tma(x, qweight, qzeros, scales, bias, y, K, N, G, workspace, workspace_bytes, dev_err, s,
+  {
+    GemvIo io;
+    io.x = x;
+    io.y = y;
+    return launch_gemv_tma(io, qweight, qzeros, scales, bias, K, N, G, workspace, workspace_bytes, dev_err, s,
                            (flags & ANVILQ_GEMM_OVERLAP_PRIOR) != 0);
+  }
   const DeviceInfo* d = device_info();
   if (!d) return ANVILQ_ECUDA;
   const Plan pl = plan_for(*d, M, K, N);
@@ -609,6 +614,31 @@ int anvilq_w4a16_gemm_ex(const uint16_t* x, const int32_t* qweight, const int32_
   if (!workspace || workspace_bytes < pl.bytes) return ANVILQ_EWORKSPACE;
   if (!aligned16(workspace)) return ANVILQ_EALIGN;
   return launch_fast(pl, x, qweight, qzeros, scales, bias, y, M, K, N, G, workspace, dev_err, s);
+}
+
+int anvilq_w4a16_gemv_fused(const void* x, int x_mode, const uint16_t* gamma, float eps,
+                            const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
+                            const uint16_t* bias, void* y, int y_mode, int K, int N, int G, void* workspace,
+                            size_t workspace_bytes, int* dev_err, unsigned flags, anvilq_stream_t stream) {
+  if (!x || !qweight || !qzeros || !scales || !y) return ANVILQ_EINVAL;
+  if (flags & ~(unsigned)ANVILQ_GEMM_OVERLAP_PRIOR) return ANVILQ_EINVAL;
+  if (x_mode < ANVILQ_GEMV_X_HALF || x_mode > ANVILQ_GEMV_X_SILU_MUL) return ANVILQ_EINVAL;
+  if (y_mode < ANVILQ_GEMV_Y_HALF || y_mode > ANVILQ_GEMV_Y_RESIDUAL) return ANVILQ_EINVAL;
+  if (x_mode == ANVILQ_GEMV_X_RMSNORM && (!gamma || !(eps >= 0.0f))) return ANVILQ_EINVAL;
+  if (!shape_ok(1, K, N, G)) return ANVILQ_EINVAL;
+  const bool a16 = aligned16(x) && aligned16(y) && (!gamma || aligned16(gamma));
+  if (!a16 || !gemv_tma_supported(x, qweight, qzeros, scales, K, N, G)) return ANVILQ_ESHAPE;
+  GemvIo io;
+  io.xmode = x_mode;
+  io.ymode = y_mode;
+  io.x = static_cast<const uint16_t*>(x);
+  io.xr = static_cast<const float*>(x);
+  io.gamma = gamma;
+  io.eps = eps;
+  io.y = static_cast<uint16_t*>(y);
+  io.yr = static_cast<float*>(y);
+  return launch_gemv_tma(io, qweight, qzeros, scales, bias, K, N, G, workspace, workspace_bytes, dev_err,
+                         reinterpret_cast<cudaStream_t>(stream), (flags & ANVILQ_GEMM_OVERLAP_PRIOR) != 0);
 }
 
 int anvilq_w4a16_gemm_exact(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,

@@ -27,15 +27,13 @@
 //   * q is used as a binary16 SUBNORMAL: (w & 0x000F000F) reinterpreted as
 //     half2 is exactly (q0, q1) * 2^-24, (w & 0x00F000F0) is 16 (q2, q3) 2^-24,
 //     and the same on w >> 8 for lanes 4..7.  One AND per column pair.
-//   * x is pre-scaled per tile by an exact power of two 2^S (S from the tile's
-//     largest |x|, so |x 2^S| < 2^15): products x q land in the normal binary16
-//     range and the 16-row partial acc = sum x 2^S q 2^-24 takes one HFMA2 per
-//     column pair per row.
-//   * The partial is folded into fp32 as A += acc * 2^(24-S) (/16 for the
-//     shifted pairs), an exact scaling.
-//   * The zero point is applied once per group through the tile sums of x,
+//   * Each product x * q 2^-24 is formed exactly and added into an fp32
+//     accumulator by the mixed-precision fma.rn.f32.f16 (binary16 operands,
+//     binary32 addend and result): one instruction per weight, one rounding,
+//     no binary16 partial sums.
+//   * Per group the accumulators hold 2^-24 sum x q (2^-20 for the shifted
+//     pairs); the zero point is applied once through the group's sum of x,
 //     sum x (q - z) = sum x q - z sum x, and the scale once: y += s (A - z X).
-//     Only the 16-product partials are binary16.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -69,18 +67,35 @@ constexpr int kRingOff = 0;
 constexpr int kRingBytes = kWarps * kStages * kTileBytes;                 // 48 KB
 constexpr int kRedBytes = kWarps * kBandCols * 4;                         // 8 KB, aliases the ring
 static_assert(kRedBytes <= kRingBytes, "reduction buffer reuses the ring");
-constexpr int kXsOff = kRingOff + kRingBytes;                             // [warp][16] half2
-constexpr int kXrawOff = kXsOff + kWarps * kTileRows * 4;                 // [warp][stage][16] half
-constexpr int kBarOff = kXrawOff + kWarps * kStages * kTileRows * 2;      // [warp][stage] u64
+constexpr int kXsOff = kRingOff + kRingBytes;                             // [warp][16] half (+pad)
+// per stage: 128 B of raw activation rows: [0, 64) primary (fp16 x, fp32 residual
+// or fp16 gate rows), [64, 128) secondary (fp16 gamma or fp16 up rows)
+constexpr int kXrawStage = 128;
+constexpr int kXrawOff = kXsOff + kWarps * kTileRows * 4;                 // [warp][stage][128 B]
+constexpr int kBarOff = kXrawOff + kWarps * kStages * kXrawStage;         // [warp][stage] u64
 constexpr int kPartOff = kBarOff + kWarps * kStages * 8 + 32;             // [512] f32
 constexpr int kSmemBytes = kPartOff + kBandCols * 4;
 
+// Where the GEMV's activation row k comes from (template parameter XMODE):
+//   kXHalf     x[k] (fp16)
+//   kXRmsNorm  fp16( r[k] * gamma[k] / sqrt(mean(r^2) + eps) ), r an fp32 residual stream
+//   kXSiluMul  fp16( silu(g[k]) * u[k] ), g = x[0:K], u = x[K:2K] (a fused gate/up output)
+// and where the result goes (YMODE):
+//   kYHalf     y[c] = fp16(result (+ bias))
+//   kYResidual r_out[c] += result (+ bias), fp32 in place
+enum XMode { kXHalf = 0, kXRmsNorm = 1, kXSiluMul = 2 };
+enum YMode { kYHalf = 0, kYResidual = 1 };
+
 struct Params {
-  const __half* x;
+  const __half* x;         // kXHalf, kXSiluMul
+  const float* xr;         // kXRmsNorm: fp32 residual [K]
+  const __half* gamma;     // kXRmsNorm: [K]
+  float eps;
   const int32_t* qzeros;
   const __half* scales;
   const __half* bias;
-  __half* y;
+  __half* y;               // kYHalf
+  float* yr;               // kYResidual: fp32 residual [N], updated in place
   float* partials;   // [bands][kc][512]   (kc > 1)
   int* tickets;      // [bands][c]         (kc > 1)
   int* dev_err;
@@ -135,10 +150,21 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
 __device__ __forceinline__ half2 h2(uint32_t u) { return *reinterpret_cast<half2*>(&u); }
 __device__ __forceinline__ uint32_t u32(half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
+// a0 += x * q.lo, a1 += x * q.hi with binary16 x and q, binary32 accumulators:
+// the products are exact and rounded once into the accumulators.
+__device__ __forceinline__ void fma_f32_f16x2(float& a0, float& a1, uint32_t q2, unsigned short x) {
+  asm("{\n .reg .f16 q0, q1;\n mov.b32 {q0, q1}, %2;\n"
+      " fma.rn.f32.f16 %0, %3, q0, %0;\n fma.rn.f32.f16 %1, %3, q1, %1;\n}"
+      : "+f"(a0), "+f"(a1)
+      : "r"(q2), "h"(x));
+}
+
+template <int XMODE, int YMODE>
 __global__ void __launch_bounds__(kThreads, 4)
     gemv_tma_kernel(const __grid_constant__ CUtensorMap tmap, const Params p) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_last;
+  __shared__ float s_norm[kWarps + 1];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int c = p.cluster;
   const int rank = c > 1 ? (int)cluster_rank() : 0;
@@ -151,8 +177,8 @@ __global__ void __launch_bounds__(kThreads, 4)
 
   unsigned char* ring = smem + kRingOff + warp * kStages * kTileBytes;
   uint32_t* xs = reinterpret_cast<uint32_t*>(smem + kXsOff) + warp * kTileRows;
-  const __half* xraw = reinterpret_cast<const __half*>(smem + kXrawOff) + warp * kStages * kTileRows;
-  const uint32_t xraw0 = smem_u32(smem + kXrawOff) + warp * kStages * kTileRows * 2;
+  const unsigned char* xraw = smem + kXrawOff + warp * kStages * kXrawStage;
+  const uint32_t xraw0 = smem_u32(smem + kXrawOff) + warp * kStages * kXrawStage;
   const uint32_t bar0 = smem_u32(smem + kBarOff + warp * kStages * 8);
   if (lane == 0) {
     for (int s = 0; s < kStages; ++s)
@@ -166,8 +192,28 @@ __global__ void __launch_bounds__(kThreads, 4)
   __syncwarp();
 
   // Stage j % kStages receives tile t0 + j (4 KB of int4 words) and the tile's
-  // 16 activations (32 B), both counted on the stage's mbarrier.
-  const uint32_t x_bytes = kTileRows * 2;   // K % 16 == 0: every tile has 16 rows
+  // 16 activation rows (one or two short bulk copies), all counted on the
+  // stage's mbarrier.  K % 16 == 0, so every tile has 16 rows.
+  constexpr uint32_t x_bytes = XMODE == kXRmsNorm ? 16 * 4 + 16 * 2 : XMODE == kXSiluMul ? 2 * 16 * 2 : 16 * 2;
+  auto copy_x = [&](int j, uint32_t bar) {
+    const int st = j % kStages;
+    const size_t r0 = (size_t)(t0 + j) * kTileRows;
+    const uint32_t dst = xraw0 + st * kXrawStage;
+    auto bulk = [&](uint32_t d, const void* src, uint32_t n) {
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(d),
+                   "l"(src), "r"(n), "r"(bar)
+                   : "memory");
+    };
+    if (XMODE == kXHalf) bulk(dst, p.x + r0, 32);
+    if (XMODE == kXRmsNorm) {
+      bulk(dst, p.xr + r0, 64);
+      bulk(dst + 64, p.gamma + r0, 32);
+    }
+    if (XMODE == kXSiluMul) {
+      bulk(dst, p.x + r0, 32);
+      bulk(dst + 64, p.x + p.K + r0, 32);
+    }
+  };
   auto issue_tile = [&](int j, bool with_x) {   // lane 0 only
     const int st = j % kStages;
     const uint32_t bar = bar0 + 8 * st;
@@ -183,20 +229,12 @@ __global__ void __launch_bounds__(kThreads, 4)
         "[%4];" ::"r"(smem_u32(ring + st * kTileBytes)),
         "l"(&tmap), "r"(band * kBandWords), "r"((t0 + j) * kTileRows), "r"(bar)
         : "memory");
-    if (with_x)
-      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                       xraw0 + st * kTileRows * 2),
-                   "l"(p.x + (size_t)(t0 + j) * kTileRows), "r"(x_bytes), "r"(bar)
-                   : "memory");
+    if (with_x) copy_x(j, bar);
   };
   auto issue_x = [&](int j) {   // lane 0 only: activations of a tile whose weights are in flight
-    const int st = j % kStages;
-    const uint32_t bar = bar0 + 8 * st;
+    const uint32_t bar = bar0 + 8 * (j % kStages);
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(x_bytes) : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     xraw0 + st * kTileRows * 2),
-                 "l"(p.x + (size_t)(t0 + j) * kTileRows), "r"(x_bytes), "r"(bar)
-                 : "memory");
+    copy_x(j, bar);
   };
 
   const int w0 = band * kBandWords + lane * 2;   // this lane's 2 words = 16 columns
@@ -242,8 +280,9 @@ __global__ void __launch_bounds__(kThreads, 4)
       for (int e = 0; e < 4; ++e) {
         const float2 s2 = __half22float2(h2(sw[e]));
         const float2 z2 = __half22float2(h2(zp[e]));
-        const float a0 = fmaf(-(z2.x - 1024.0f), Xg, A[i * 8 + 2 * e]);
-        const float a1 = fmaf(-(z2.y - 1024.0f), Xg, A[i * 8 + 2 * e + 1]);
+        const float pw = (e & 1) ? 1048576.0f : 16777216.0f;   // 2^20 (shifted pairs) or 2^24
+        const float a0 = fmaf(-(z2.x - 1024.0f), Xg, A[i * 8 + 2 * e] * pw);
+        const float a1 = fmaf(-(z2.y - 1024.0f), Xg, A[i * 8 + 2 * e + 1] * pw);
         Y[i * 8 + 2 * e] = fmaf(s2.x, a0, Y[i * 8 + 2 * e]);
         Y[i * 8 + 2 * e + 1] = fmaf(s2.y, a1, Y[i * 8 + 2 * e + 1]);
         A[i * 8 + 2 * e] = 0.0f;
@@ -262,6 +301,26 @@ __global__ void __launch_bounds__(kThreads, 4)
   asm volatile("griddepcontrol.wait;" ::: "memory");   // x may come from the previous kernel
   if (lane == 0)
     for (int j = 0; j < pro; ++j) issue_x(j);
+  float norm_inv = 1.0f;   // kXRmsNorm: 1 / sqrt(mean(r^2) + eps), computed by every CTA
+  if (XMODE == kXRmsNorm) {
+    float ss = 0.0f;
+    for (int k = threadIdx.x; k < p.K; k += kThreads) {
+      const float v = __ldcg(p.xr + k);
+      ss = fmaf(v, v, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) s_norm[warp] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) t += s_norm[w];
+      s_norm[kWarps] = 1.0f / sqrtf(t / (float)p.K + p.eps);
+    }
+    __syncthreads();
+    norm_inv = s_norm[kWarps];
+  }
   if (ntiles > 0) check_group(tile_row(0));
 
   for (int j = 0; j < ntiles; ++j) {
@@ -278,54 +337,52 @@ __global__ void __launch_bounds__(kThreads, 4)
       break;
     }
     // -- the tile's activations: lanes l and l + 16 both hold row l % 16
-    float Xt, pow_lo;
+    float Xt;
     {
-      const float xf = __half2float(xraw[st * kTileRows + (lane & 15)]);
-      float mx = fabsf(xf);
+      // this row's activation, rounded to binary16 (the A16 of W4A16)
+      const unsigned char* xr0 = xraw + st * kXrawStage;
+      const int r = lane & 15;
+      float xf;
+      if (XMODE == kXHalf) xf = __half2float(reinterpret_cast<const __half*>(xr0)[r]);
+      if (XMODE == kXRmsNorm) {
+        const float v = reinterpret_cast<const float*>(xr0)[r];
+        const float gm = __half2float(reinterpret_cast<const __half*>(xr0 + 64)[r]);
+        xf = __half2float(__float2half_rn(v * gm * norm_inv));
+      }
+      if (XMODE == kXSiluMul) {
+        const float g = __half2float(reinterpret_cast<const __half*>(xr0)[r]);
+        const float u = __half2float(reinterpret_cast<const __half*>(xr0 + 64)[r]);
+        const float e = expf(-fabsf(g));   // stable silu (official_weights.py:494-499)
+        const float sg = g >= 0.0f ? g / (1.0f + e) : (g * e) / (1.0f + e);
+        xf = __half2float(__float2half_rn(sg * u));
+      }
       float sum = xf;
 #pragma unroll
-      for (int o = 1; o < 16; o <<= 1) {
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      }
-      // |x| < 2^e with e the binary exponent of mx; scale by 2^(15 - e)
-      const int e = mx > 0.0f ? ((__float_as_int(mx) >> 23) & 255) - 126 : 0;
-      const int S = 15 - e;
-      const half hs = __float2half_rn(xf * __int_as_float((127 + S) << 23));
-      if (lane < 16) xs[lane] = u32(__halves2half2(hs, hs));
+      for (int o = 1; o < 16; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if (lane < 16) reinterpret_cast<__half*>(xs)[lane] = __float2half_rn(xf);
       Xt = sum;
-      pow_lo = __int_as_float((127 + 24 - S) << 23);
     }
     __syncwarp();
     const unsigned char* tile = ring + st * kTileBytes + lane * 8;
-    half2 part[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) part[i] = __float2half2_rn(0.0f);
+    for (int r = 0; r < kTileRows; r += 2) {
+      const uint32_t xpair = xs[r / 2];   // rows r, r + 1
+      const unsigned short xr_[2] = {(unsigned short)(xpair & 0xFFFFu), (unsigned short)(xpair >> 16)};
 #pragma unroll
-    for (int r = 0; r < kTileRows; ++r) {
-      const uint2 w = *reinterpret_cast<const uint2*>(tile + r * (kBandWords * 4));
-      const half2 xx = h2(xs[r]);
-      const uint32_t ws[2] = {w.x, w.y};
+      for (int rr = 0; rr < 2; ++rr) {
+        const uint2 w = *reinterpret_cast<const uint2*>(tile + (r + rr) * (kBandWords * 4));
+        const uint32_t ws[2] = {w.x, w.y};
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const uint32_t w8 = ws[i] >> 8;
-        part[4 * i + 0] = __hfma2(xx, h2(ws[i] & 0x000F000Fu), part[4 * i + 0]);   // columns 0,1
-        part[4 * i + 1] = __hfma2(xx, h2(ws[i] & 0x00F000F0u), part[4 * i + 1]);   // columns 2,3 (x16)
-        part[4 * i + 2] = __hfma2(xx, h2(w8 & 0x000F000Fu), part[4 * i + 2]);      // columns 4,5
-        part[4 * i + 3] = __hfma2(xx, h2(w8 & 0x00F000F0u), part[4 * i + 3]);      // columns 6,7 (x16)
+        for (int i = 0; i < 2; ++i) {
+          const uint32_t w8 = ws[i] >> 8;
+          fma_f32_f16x2(A[i * 8 + 0], A[i * 8 + 1], ws[i] & 0x000F000Fu, xr_[rr]);   // columns 0,1
+          fma_f32_f16x2(A[i * 8 + 2], A[i * 8 + 3], ws[i] & 0x00F000F0u, xr_[rr]);   // columns 2,3 (x16)
+          fma_f32_f16x2(A[i * 8 + 4], A[i * 8 + 5], w8 & 0x000F000Fu, xr_[rr]);      // columns 4,5
+          fma_f32_f16x2(A[i * 8 + 6], A[i * 8 + 7], w8 & 0x00F000F0u, xr_[rr]);      // columns 6,7 (x16)
+        }
       }
     }
     __syncwarp();   // stage st and xs are free again
-    const float pow_hi = pow_lo * 0.0625f;
-#pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f2 = __half22float2(part[4 * i + e]);
-        const float pw = (e & 1) ? pow_hi : pow_lo;
-        A[i * 8 + 2 * e] = fmaf(f2.x, pw, A[i * 8 + 2 * e]);
-        A[i * 8 + 2 * e + 1] = fmaf(f2.y, pw, A[i * 8 + 2 * e + 1]);
-      }
     Xg += Xt;
     if (next_group) {
       flush_group();
@@ -430,7 +487,8 @@ __global__ void __launch_bounds__(kThreads, 4)
     if (t < per && col0 + t < p.N) {
       float out = v[i];
       if (p.bias) out += __half2float(p.bias[col0 + t]);
-      p.y[col0 + t] = __float2half_rn(out);
+      if (YMODE == kYHalf) p.y[col0 + t] = __float2half_rn(out);
+      if (YMODE == kYResidual) p.yr[col0 + t] += out;
     }
   }
 }
@@ -459,14 +517,26 @@ struct DeviceInfo {
 static DeviceInfo g_dev[kMaxDevices];
 static std::once_flag g_dev_once[kMaxDevices];
 
+using KernelFn = void (*)(CUtensorMap, Params);
+static KernelFn kernel_for(int xmode, int ymode) {
+  static const KernelFn table[3][2] = {
+      {gemv_tma_kernel<kXHalf, kYHalf>, gemv_tma_kernel<kXHalf, kYResidual>},
+      {gemv_tma_kernel<kXRmsNorm, kYHalf>, gemv_tma_kernel<kXRmsNorm, kYResidual>},
+      {gemv_tma_kernel<kXSiluMul, kYHalf>, gemv_tma_kernel<kXSiluMul, kYResidual>}};
+  return table[xmode][ymode];
+}
+
 static const DeviceInfo* device_info() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
   std::call_once(g_dev_once[dev], [dev] {
     DeviceInfo& d = g_dev[dev];
     cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaFuncSetAttribute(gemv_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    cudaFuncSetAttribute(gemv_tma_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    for (int xm = 0; xm < 3; ++xm)
+      for (int ym = 0; ym < 2; ++ym) {
+        cudaFuncSetAttribute(kernel_for(xm, ym), cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        cudaFuncSetAttribute(kernel_for(xm, ym), cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      }
     for (int i = 0; i < 5; ++i) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(1u << i, 1, 1);
@@ -480,7 +550,7 @@ static const DeviceInfo* device_info() {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, gemv_tma_kernel, &cfg) != cudaSuccess) n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kernel_for(kXHalf, kYHalf), &cfg) != cudaSuccess) n = 0;
       d.max_clusters[i] = n;
     }
     cudaGetLastError();
@@ -565,13 +635,14 @@ size_t gemv_tma_workspace_bytes(int K, int N) {
   return tma_gemv::make_plan(*d, K, N).bytes;
 }
 
-int launch_gemv_tma(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
-                    const uint16_t* bias, uint16_t* y, int K, int N, int G, void* workspace,
-                    size_t workspace_bytes, int* dev_err, cudaStream_t stream, bool overlap_prior) {
+int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
+                    const uint16_t* bias, int K, int N, int G, void* workspace, size_t workspace_bytes, int* dev_err,
+                    cudaStream_t stream, bool overlap_prior) {
   using namespace tma_gemv;
   const DeviceInfo* d = device_info();
   auto encode = encode_fn();
   if (!d || d->sms <= 0 || !encode) return ANVILQ_ECUDA;
+  if (io.xmode < 0 || io.xmode > 2 || io.ymode < 0 || io.ymode > 1) return ANVILQ_EINVAL;
   const Plan pl = make_plan(*d, K, N);
   if (pl.kc > 1) {
     if (!workspace || workspace_bytes < pl.bytes) return ANVILQ_EWORKSPACE;
@@ -589,11 +660,15 @@ int launch_gemv_tma(const uint16_t* x, const int32_t* qweight, const int32_t* qz
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return ANVILQ_EALIGN;
   Params p;
-  p.x = reinterpret_cast<const __half*>(x);
+  p.x = reinterpret_cast<const __half*>(io.x);
+  p.xr = io.xr;
+  p.gamma = reinterpret_cast<const __half*>(io.gamma);
+  p.eps = io.eps;
   p.qzeros = qzeros;
   p.scales = reinterpret_cast<const __half*>(scales);
   p.bias = reinterpret_cast<const __half*>(bias);
-  p.y = reinterpret_cast<__half*>(y);
+  p.y = reinterpret_cast<__half*>(io.y);
+  p.yr = io.yr;
   p.tickets = reinterpret_cast<int*>(workspace);
   p.partials = workspace ? reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) +
                                                     ANVILQ_WORKSPACE_COUNTER_BYTES)
@@ -618,7 +693,7 @@ int launch_gemv_tma(const uint16_t* x, const int32_t* qweight, const int32_t* qz
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = overlap_prior ? 2 : 1;
-  if (cudaLaunchKernelEx(&cfg, gemv_tma_kernel, map, p) != cudaSuccess) {
+  if (cudaLaunchKernelEx(&cfg, kernel_for(io.xmode, io.ymode), map, p) != cudaSuccess) {
     cudaGetLastError();
     return ANVILQ_ECUDA;
   }

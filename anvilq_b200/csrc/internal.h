@@ -11,8 +11,20 @@ namespace anvilq {
 bool gemv_tma_supported(const void* x, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
                         int K, int N, int G);
 size_t gemv_tma_workspace_bytes(int K, int N);
-int launch_gemv_tma(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
-                    const uint16_t* bias, uint16_t* y, int K, int N, int G, void* workspace,
-                    size_t workspace_bytes, int* dev_err, cudaStream_t stream, bool overlap_prior);
+
+// Source of the activations and destination of the result of one GEMV launch
+// (modes as in ANVILQ_GEMV_X_* / ANVILQ_GEMV_Y_* of anvilq.h).
+struct GemvIo {
+  int xmode = 0, ymode = 0;
+  const uint16_t* x = nullptr;   // fp16 x [K] or fp16 [gate | up] [2K]
+  const float* xr = nullptr;     // fp32 residual [K]
+  const uint16_t* gamma = nullptr;
+  float eps = 0.0f;
+  uint16_t* y = nullptr;         // fp16 out [N]
+  float* yr = nullptr;           // fp32 residual [N], += result
+};
+int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
+                    const uint16_t* bias, int K, int N, int G, void* workspace, size_t workspace_bytes, int* dev_err,
+                    cudaStream_t stream, bool overlap_prior);
 
 }  // namespace anvilq

@@ -1,0 +1,234 @@
+"""Batch-1 greedy decode of a Qwen2-architecture W4A16 AWQ model on B200.
+
+The step follows FP32Model.token (anvil-q1/tests/official_weights.py:451-509)
+and QwenFP64.step (anvil-q1-fp/tests/fp64_reference.py:210-246):
+
+    x = E[token]                                   fp32 residual stream
+    per layer:  h = rmsnorm(x); q,k,v = h W_qkv + b; rope(q, k); cache k, v
+                a = attention(q, K, V); x += a W_o
+                h = rmsnorm(x); g, u = h W_gate, h W_up; x += (silu(g) u) W_down
+    logits = rmsnorm(x) E^T;  token = argmax (lowest index on ties)
+
+Kernels per token: 1 embedding + per layer 6 (QKV GEMV with RMSNorm prologue and
+bias, RoPE + KV append, attention, O GEMV with residual epilogue, gate/up GEMV
+with RMSNorm prologue, down GEMV with SiLU-product prologue and residual epilogue)
++ the lm_head/argmax + the token commit.  q/k/v and gate/up are each one GEMV
+over weights concatenated along N at load time (AWQ packs 8 columns per word,
+so concatenating N-blocks of multiples of 8 keeps the layout).  Token, position
+and caches live on the device, so one CUDA graph replays every step.
+
+Weights here are synthetic (seeded) with the reference's value distributions;
+no checkpoint is available offline.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import _lib, ops, synthetic
+from .checkpoint import ArrayCheckpoint
+
+# (L, H, I, QH, KVH, D, G, V, SEQ) as in official_weights.py:21 DEFAULT_SHAPE
+QWEN05B_SHAPE = (24, 896, 4864, 14, 2, 64, 128, 151936, 32768)
+ROPE_THETA = 1_000_000.0
+RMS_EPS = 1e-6
+FLAG_OVERLAP = 1   # ANVILQ_GEMM_OVERLAP_PRIOR
+
+
+@dataclass
+class DecoderWeights:
+    """Per-layer AWQ projections in the reference's numbering (0..6 = q,k,v,o,gate,up,down)."""
+    shape: tuple
+    layers: list                      # [L] of dict projection -> AwqLayer
+    norms: dict = field(default_factory=dict)   # ("input", l) / ("post", l) / ("final", 0) -> fp16 [H]
+    embedding: np.ndarray | None = None         # fp16 [V, H], tied lm_head
+
+    def checkpoint(self) -> ArrayCheckpoint:
+        flat = {(l, p): lay for l, projs in enumerate(self.layers) for p, lay in projs.items()}
+        return ArrayCheckpoint(flat, embedding=self.embedding, norms=self.norms)
+
+
+def synthetic_weights(shape=QWEN05B_SHAPE, seed: int = 17) -> DecoderWeights:
+    """Random-init weights of the given shape.  W4 tensors use the BASELINE
+    distributions (u4 uniform, scales |N(0,1)|*0.01+1e-3); biases N(0,1);
+    norm weights 1 + 0.1 N(0,1); embedding 0.5 N(0,1); all fp16."""
+    L, H, I, QH, KVH, D, G, V, _ = shape
+    rng = np.random.default_rng(seed)
+    dims = ((H, QH * D, True), (H, KVH * D, True), (H, KVH * D, True), (QH * D, H, False),
+            (H, I, False), (H, I, False), (I, H, False))
+    layers = []
+    norms = {}
+    for l in range(L):
+        layers.append({p: synthetic.awq_layer(K, N, G, rng=rng, bias=b) for p, (K, N, b) in enumerate(dims)})
+        for which in ("input", "post"):
+            norms[which, l] = (1.0 + 0.1 * rng.standard_normal(H, dtype=np.float32)).astype(np.float16)
+    norms["final", 0] = (1.0 + 0.1 * rng.standard_normal(H, dtype=np.float32)).astype(np.float16)
+    embedding = (0.5 * rng.standard_normal((V, H), dtype=np.float32)).astype(np.float16)
+    return DecoderWeights(shape, layers, norms, embedding)
+
+
+def _concat(layers):
+    """AWQ layers with equal K and G concatenated along N."""
+    cat = lambda name: np.concatenate([getattr(l, name) for l in layers], axis=1)
+    bias = None
+    if layers[0].bias is not None:
+        bias = np.concatenate([l.bias for l in layers])
+    return synthetic.AwqLayer(cat("qweight"), cat("qzeros"), cat("scales"), bias, layers[0].group)
+
+
+class Decoder:
+    """Device-resident greedy decoder; ``step`` enqueues one token, ``capture``
+    records it as a CUDA graph that every later step replays."""
+
+    def __init__(self, weights: DecoderWeights, device="cuda", max_seq: int = 2048, keep_logits: bool = False):
+        self.shape = weights.shape
+        L, H, I, QH, KVH, D, G, V, SEQ = self.shape
+        self.max_seq = min(max_seq, SEQ)
+        self.device = torch.device(device)
+        dev = self.device
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+        self.layers = []
+        for projs in weights.layers:
+            qkv = _concat([projs[0], projs[1], projs[2]])
+            gu = _concat([projs[4], projs[5]])
+            self.layers.append({
+                "qkv": tuple(t(a) for a in (qkv.qweight, qkv.qzeros, qkv.scales, qkv.bias)),
+                "o": tuple(t(a) for a in (projs[3].qweight, projs[3].qzeros, projs[3].scales)) + (None,),
+                "gu": tuple(t(a) for a in (gu.qweight, gu.qzeros, gu.scales)) + (None,),
+                "down": tuple(t(a) for a in (projs[6].qweight, projs[6].qzeros, projs[6].scales)) + (None,),
+            })
+        self.gamma_in = [t(weights.norms["input", l]) for l in range(L)]
+        self.gamma_post = [t(weights.norms["post", l]) for l in range(L)]
+        self.gamma_final = t(weights.norms["final", 0])
+        self.embedding = t(weights.embedding)
+        self.k_cache = torch.zeros((L, self.max_seq, KVH, D), dtype=torch.float16, device=dev)
+        self.v_cache = torch.zeros_like(self.k_cache)
+        self.x = torch.zeros(H, dtype=torch.float32, device=dev)
+        self.qkv = torch.empty((QH + 2 * KVH) * D, dtype=torch.float16, device=dev)
+        self.q = torch.empty((1, QH, D), dtype=torch.float16, device=dev)
+        self.attn = torch.empty((1, QH, D), dtype=torch.float16, device=dev)
+        self.gu = torch.empty(2 * I, dtype=torch.float16, device=dev)
+        self.token = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.seqlen = torch.ones(1, dtype=torch.int32, device=dev)
+        self.key = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.logits = torch.empty(V, dtype=torch.float32, device=dev) if keep_logits else None
+        self.dev_err = torch.zeros(1, dtype=torch.int32, device=dev)
+        lib = _lib.load()
+        ws_bytes = max(lib.anvilq_w4a16_gemm_workspace_size(1, K, N, G)
+                       for K, N in ((H, (QH + 2 * KVH) * D), (QH * D, H), (H, 2 * I), (I, H)))
+        ws_bytes = max(ws_bytes, lib.anvilq_gqa_decode_workspace_size(1, QH, KVH, D, self.max_seq))
+        self.workspace = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+        self.stream = torch.cuda.Stream(dev)
+        self.graph = None
+        # host staging for the end-to-end path
+        self.token_in = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.token_out = torch.zeros(1, dtype=torch.int32).pin_memory()
+
+    # -- one token -----------------------------------------------------------
+    def _gemv(self, w, x, x_mode, gamma, y, y_mode, K, N):
+        lib = _lib.load()
+        qweight, qzeros, scales, bias = w
+        _lib.check(lib.anvilq_w4a16_gemv_fused(
+            x.data_ptr(), x_mode, None if gamma is None else gamma.data_ptr(), RMS_EPS,
+            qweight.data_ptr(), qzeros.data_ptr(), scales.data_ptr(), None if bias is None else bias.data_ptr(),
+            y.data_ptr(), y_mode, K, N, self.shape[6], self.workspace.data_ptr(), self.workspace.numel(),
+            self.dev_err.data_ptr(), FLAG_OVERLAP, self.stream.cuda_stream), "anvilq_w4a16_gemv_fused")
+
+    def _enqueue(self, host_io: bool):
+        L, H, I, QH, KVH, D, G, V, _ = self.shape
+        lib = _lib.load()
+        s = self.stream.cuda_stream
+        if host_io:
+            self.token.copy_(self.token_in, non_blocking=True)
+        _lib.check(lib.anvilq_embed(self.embedding.data_ptr(), self.token.data_ptr(), self.x.data_ptr(), H, V,
+                                    self.key.data_ptr(), self.dev_err.data_ptr(), FLAG_OVERLAP, s), "anvilq_embed")
+        nqkv = (QH + 2 * KVH) * D
+        for l, w in enumerate(self.layers):
+            self._gemv(w["qkv"], self.x, 1, self.gamma_in[l], self.qkv, 0, H, nqkv)
+            _lib.check(lib.anvilq_rope_kv_append(
+                self.qkv.data_ptr(), self.pos.data_ptr(), self.q.data_ptr(), self.k_cache[l].data_ptr(),
+                self.v_cache[l].data_ptr(), self.seqlen.data_ptr(), QH, KVH, D, self.max_seq, ROPE_THETA,
+                self.dev_err.data_ptr(), FLAG_OVERLAP, s), "anvilq_rope_kv_append")
+            _lib.check(lib.anvilq_gqa_decode(
+                self.q.data_ptr(), self.k_cache[l].data_ptr(), self.v_cache[l].data_ptr(), self.seqlen.data_ptr(),
+                self.attn.data_ptr(), 1, QH, KVH, D, self.max_seq, 0.0, self.workspace.data_ptr(),
+                self.workspace.numel(), self.dev_err.data_ptr(), s), "anvilq_gqa_decode")
+            self._gemv(w["o"], self.attn, 0, None, self.x, 1, QH * D, H)
+            self._gemv(w["gu"], self.x, 1, self.gamma_post[l], self.gu, 0, H, 2 * I)
+            self._gemv(w["down"], self.gu, 2, None, self.x, 1, I, H)
+        _lib.check(lib.anvilq_lmhead_argmax(
+            self.x.data_ptr(), self.gamma_final.data_ptr(), RMS_EPS, self.embedding.data_ptr(),
+            None if self.logits is None else self.logits.data_ptr(), self.key.data_ptr(), H, V, FLAG_OVERLAP, s),
+            "anvilq_lmhead_argmax")
+        _lib.check(lib.anvilq_argmax_commit(self.key.data_ptr(), self.token.data_ptr(), self.pos.data_ptr(),
+                                            FLAG_OVERLAP, s), "anvilq_argmax_commit")
+        if host_io:
+            self.token_out.copy_(self.token, non_blocking=True)
+
+    def kernels_per_step(self) -> int:
+        return 1 + 6 * self.shape[0] + 2
+
+    def reset(self, token: int):
+        """Start a new sequence at position 0 with `token` as the first input."""
+        with torch.cuda.stream(self.stream):
+            self.pos.zero_()
+            self.token.fill_(int(token))
+            self.token_in.fill_(int(token))
+        self.stream.synchronize()
+
+    def capture(self, host_io: bool = False):
+        """Record one step as a CUDA graph (warming the kernels first)."""
+        self.host_io = host_io
+        save_pos = self.pos.clone()
+        save_tok = self.token.clone()
+        with torch.cuda.stream(self.stream):
+            self._enqueue(host_io)
+        self.stream.synchronize()
+        with torch.cuda.stream(self.stream):
+            self.pos.copy_(save_pos)
+            self.token.copy_(save_tok)
+        self.stream.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self._enqueue(host_io)
+        return self
+
+    def step(self):
+        """Enqueue one token on ``self.stream`` (the graph if captured)."""
+        with torch.cuda.stream(self.stream):
+            if self.graph is not None:
+                self.graph.replay()
+            else:
+                self._enqueue(False)
+
+    def generate(self, first_token: int, n: int):
+        """Greedy-decode n tokens after `first_token`; returns the n chosen ids."""
+        self.reset(first_token)
+        out = []
+        for _ in range(n):
+            self.step()
+            self.stream.synchronize()
+            out.append(int(self.token.item()))
+        self.check_errors()
+        return out
+
+    def check_errors(self):
+        v = int(self.dev_err.item())
+        if v:
+            self.dev_err.zero_()
+            raise _lib.AnvilqError(f"decode step device error bits 0x{v:x}")
+
+    def bytes_per_step(self, context: int) -> int:
+        """Algorithmic HBM bytes of one step at a given context length."""
+        L, H, I, QH, KVH, D, G, V, _ = self.shape
+        b = 0
+        for K, N, bias in ((H, (QH + 2 * KVH) * D, True), (QH * D, H, False), (H, 2 * I, False), (I, H, False)):
+            b += synthetic.gemv_bytes(1, K, N, G, bias)
+        b *= L
+        b += L * (context * KVH * D * 2 * 2)    # K and V read once per layer
+        b += V * H * 2                            # tied lm_head
+        return b

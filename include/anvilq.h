@@ -50,6 +50,7 @@ typedef struct CUstream_st* anvilq_stream_t; /* same type as cudaStream_t */
 #define ANVILQ_DEV_ERR_SCALE 1   /* an AWQ scale was negative-nonzero or nonfinite */
 #define ANVILQ_DEV_ERR_SEQLEN 2  /* a sequence length outside [1, Tmax] */
 #define ANVILQ_DEV_ERR_TIMEOUT 4 /* a bounded wait inside a kernel expired */
+#define ANVILQ_DEV_ERR_TOKEN 8   /* a token id outside [0, V) */
 
 /* Workspace layout shared by every entry point that takes one: the first
  * ANVILQ_WORKSPACE_COUNTER_BYTES hold arrival counters that must be zero
@@ -102,6 +103,32 @@ int anvilq_w4a16_gemm_ex(const uint16_t* x, const int32_t* qweight, const int32_
                          int M, int K, int N, int G,
                          void* workspace, size_t workspace_bytes,
                          int* dev_err, unsigned flags, anvilq_stream_t stream);
+
+/* Batch-1 W4A16 GEMV with the decode step's neighbouring operations fused in.
+ *
+ * Replaces FP32Model.linear (official_weights.py:418-437) together with the
+ * operation that produces its input and the one that consumes its output in
+ * FP32Model.token (official_weights.py:451-509):
+ *   x_mode ANVILQ_GEMV_X_HALF     input row k = x[k]            (x: fp16 [K])
+ *          ANVILQ_GEMV_X_RMSNORM  input row k = fp16( r[k] * gamma[k] / sqrt(mean(r^2) + eps) )
+ *                                 (x: fp32 residual r [K], gamma fp16 [K]; norm :411-416)
+ *          ANVILQ_GEMV_X_SILU_MUL input row k = fp16( silu(g[k]) * u[k] )
+ *                                 (x: fp16 [2K] = [g | u], a fused gate/up output; :493-501)
+ *   y_mode ANVILQ_GEMV_Y_HALF     y fp16 [N] = result (+ bias)
+ *          ANVILQ_GEMV_Y_RESIDUAL y fp32 [N] += result (+ bias), the residual add (:489, :503)
+ * Same weights, workspace and requirements as anvilq_w4a16_gemm with M = 1
+ * (fast-kernel shapes only: K % 16 == 0, G % 16 == 0, N % 32 == 0, 16-byte
+ * aligned pointers; ANVILQ_ESHAPE otherwise).  flags: ANVILQ_GEMM_OVERLAP_PRIOR. */
+#define ANVILQ_GEMV_X_HALF 0
+#define ANVILQ_GEMV_X_RMSNORM 1
+#define ANVILQ_GEMV_X_SILU_MUL 2
+#define ANVILQ_GEMV_Y_HALF 0
+#define ANVILQ_GEMV_Y_RESIDUAL 1
+int anvilq_w4a16_gemv_fused(const void* x, int x_mode, const uint16_t* gamma, float eps,
+                            const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
+                            const uint16_t* bias, void* y, int y_mode, int K, int N, int G,
+                            void* workspace, size_t workspace_bytes, int* dev_err, unsigned flags,
+                            anvilq_stream_t stream);
 
 /* Reference-order W4A16 GEMM: one thread per output column sums its K products
  * in increasing k from +0.0 with every binary32 multiply and add rounded
@@ -157,6 +184,42 @@ int anvilq_gqa_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t
                       const int32_t* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D, int Tmax,
                       float scale, void* workspace, size_t workspace_bytes, int* dev_err,
                       anvilq_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Decode-step operations around the GEMVs and the attention (batch 1).
+ * Replace the pieces of FP32Model.token (anvil-q1/tests/official_weights.py:451-509).
+ * flags: ANVILQ_GEMM_OVERLAP_PRIOR launches them as programmatic dependents
+ * of the preceding kernel (they wait for it before touching memory). */
+
+/* x (fp32 [H]) = E[*token] (fp16 table [V][H]); sets *argmax_key = 0 when given.
+ * Embedding lookup, official_weights.py:463.  A token outside [0, V) sets
+ * ANVILQ_DEV_ERR_TOKEN and row 0 is used. */
+int anvilq_embed(const uint16_t* table, const int32_t* token, float* x, int H, int V,
+                 unsigned long long* argmax_key, int* dev_err, unsigned flags, anvilq_stream_t stream);
+
+/* RoPE and KV-cache append for the current position *pos (device int):
+ * qkv fp16 [(Hq + 2 Hkv) * D] = [q | k | v]; q and k rotated in split halves,
+ * angle = pos * theta^(-2i/D) (official_weights.py:439-449); q_out fp16
+ * [Hq * D]; rotated k and v written to row *pos of k_cache / v_cache
+ * fp16 [Tmax][Hkv][D] (:470); *seqlen = *pos + 1 when seqlen is given. */
+int anvilq_rope_kv_append(const uint16_t* qkv, const int32_t* pos, uint16_t* q_out, uint16_t* k_cache,
+                          uint16_t* v_cache, int32_t* seqlen, int Hq, int Hkv, int D, int Tmax, float theta,
+                          int* dev_err, unsigned flags, anvilq_stream_t stream);
+
+/* Tied fp16 lm_head with the final RMSNorm and greedy argmax fused:
+ * h = x * gamma / sqrt(mean(x^2) + eps) in fp32 (official_weights.py:504),
+ * logits[v] = h . E[v] (:505-506; written when logits != NULL), and
+ * *argmax_key = max over v of an orderable (logit, lowest v) key, combined
+ * with atomicMax (the key must be 0 before the call: anvilq_embed clears it).
+ * H % 64 == 0, H <= 16384, table 16-byte aligned. */
+int anvilq_lmhead_argmax(const float* x, const uint16_t* gamma, float eps, const uint16_t* table, float* logits,
+                         unsigned long long* argmax_key, int H, int V, unsigned flags, anvilq_stream_t stream);
+
+/* *token = the row encoded in *argmax_key (greedy choice, lowest index on
+ * ties as in anvil-q4/tests/transformer_reference.py:212-217); *pos += 1
+ * when pos is given.  Keeps the autoregressive loop on the device. */
+int anvilq_argmax_commit(const unsigned long long* argmax_key, int32_t* token, int32_t* pos, unsigned flags,
+                         anvilq_stream_t stream);
 
 /* GQA decode attention that allocates nothing and takes no workspace.
  *

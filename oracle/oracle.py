@@ -275,3 +275,90 @@ def normalized_error(actual, reference):
     na, nr = float(np.linalg.norm(a)), float(np.linalg.norm(r))
     cos = float(a @ r / (na * nr)) if na and nr else None
     return err / norm, cos
+
+
+# ---------------------------------------------------------------- decode step
+class DecodeOracle:
+    """Greedy decode in binary64, restating FP32Model.token
+    (anvil-q1/tests/official_weights.py:451-509) and QwenFP64.step
+    (anvil-q1-fp/tests/fp64_reference.py:210-246) for any model shape
+    (L, H, I, QH, KVH, D, G, V, SEQ).
+
+    weights: an object with .shape, .layers[l][p] (AWQ layers, p = 0..6 =
+    q,k,v,o,gate,up,down), .norms[("input"|"post", l)], .norms[("final", 0)]
+    and .embedding (fp16 [V, H], tied lm_head).  W4 weights are dequantised
+    exactly (delta * scale) per layer when used.
+    """
+
+    def __init__(self, weights, theta=1e6, eps=1e-6, act16=False):
+        """act16: round to binary16 where a W4A16 datapath stores activations in
+        binary16 (GEMV inputs, q/k/v, rotated q/k, attention output, gate/up
+        outputs); the residual stream and all arithmetic stay binary64."""
+        self.w = weights
+        self.shape = weights.shape
+        self.theta, self.eps = theta, eps
+        self.act16 = act16
+        self.cache = {}
+        self.E = np.asarray(weights.embedding)   # fp16; rows widened to binary64 when used
+
+    def _w(self, l, p):
+        lay = self.w.layers[l][p]
+        _, wf, _, bad = dequant(lay.qweight, lay.qzeros, lay.scales_bits, lay.group)
+        if bad.any():
+            raise OracleError(_STATUS[-2])
+        b = None if lay.bias is None else np.asarray(lay.bias, np.float64)
+        return wf.astype(np.float64), b
+
+    def _linear(self, x, l, p):
+        w, b = self._w(l, p)
+        y = x @ w
+        return y + b if b is not None else y
+
+    def _norm(self, x, gamma):
+        return x * np.asarray(gamma, np.float64) / np.sqrt(np.mean(x * x) + self.eps)
+
+    def _rope(self, x, heads, pos):
+        _, _, _, _, _, D, _, _, _ = self.shape
+        x = x.reshape(heads, D).copy()
+        half = D // 2
+        ang = pos * np.power(self.theta, -2.0 * np.arange(half) / D)
+        c, s = np.cos(ang), np.sin(ang)
+        a, b = x[:, :half].copy(), x[:, half:].copy()
+        x[:, :half] = a * c - b * s
+        x[:, half:] = b * c + a * s
+        return x.reshape(-1)
+
+    def _r(self, a):
+        return a.astype(np.float16).astype(np.float64) if self.act16 else a
+
+    def step(self, token, pos):
+        L, H, I, QH, KVH, D, G, V, SEQ = self.shape
+        r = self._r
+        x = self.E[token].astype(np.float64)
+        for l in range(L):
+            h = r(self._norm(x, self.w.norms["input", l]))
+            q = r(self._rope(r(self._linear(h, l, 0)), QH, pos))
+            k = r(self._rope(r(self._linear(h, l, 1)), KVH, pos))
+            v = r(self._linear(h, l, 2))
+            self.cache[l, pos] = (k.reshape(KVH, D), v.reshape(KVH, D))
+            keys = np.stack([self.cache[l, t][0] for t in range(pos + 1)])
+            vals = np.stack([self.cache[l, t][1] for t in range(pos + 1)])
+            ctx = r(attention_f64(q.reshape(QH, D), keys, vals).reshape(-1))
+            x = x + self._linear(ctx, l, 3)
+            h = r(self._norm(x, self.w.norms["post", l]))
+            g, u = r(self._linear(h, l, 4)), r(self._linear(h, l, 5))
+            silu = g / (1.0 + np.exp(-g))
+            x = x + self._linear(r(silu * u), l, 6)
+        h = self._norm(x, self.w.norms["final", 0])
+        # vocabulary in chunks, as fp64_reference.py:238-242 does, so the binary64
+        # embedding never exists in full
+        logits = np.empty(self.E.shape[0], np.float64)
+        for r in range(0, self.E.shape[0], 8192):
+            logits[r:r + 8192] = self.E[r:r + 8192].astype(np.float64) @ h
+        return logits
+
+
+def greedy(logits):
+    """Lowest index among the maxima (anvil-q4/tests/transformer_reference.py:212-217)."""
+    logits = np.asarray(logits)
+    return int(np.flatnonzero(logits == logits.max())[0])

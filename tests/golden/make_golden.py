@@ -5,7 +5,7 @@ This script imports the reference's own Python golden models read-only from a
 checkout of aHappend/anvil-q (default /root/reference, or $ANVILQ_REFERENCE):
 
 * anvil-q1/tests/verify.py         dequant_cases / dequant / pack / rounded / sat / half_fixed
-* anvil-q1/tests/official_weights.py  FP32Model.linear, f32
+* anvil-q1/tests/official_weights.py  FP32Model.linear, FP32Model.token, f32
 * anvil-q1-fp/tests/awq_prepare.py    pack_lanes / unpack_lanes
 * anvil-q1-fp/tests/fp64_reference.py attention
 
@@ -232,18 +232,47 @@ def attention_fixture():
     return out
 
 
+DECODE_SHAPE = (2, 128, 256, 2, 1, 64, 128, 64, 8)   # (L,H,I,QH,KVH,D,G,V,SEQ)
+
+
+def decode_fixture():
+    """FP32Model.token (official_weights.py:451-509) greedy-decoding 4 tokens on a
+    small Qwen2-shaped model with synthetic weights (anvilq_b200.decoder.synthetic_weights,
+    seed 29), starting from token 5."""
+    import hashlib
+    from anvilq_b200 import decoder
+    w = decoder.synthetic_weights(DECODE_SHAPE, seed=29)
+    model = ow.FP32Model(w.checkpoint(), DECODE_SHAPE)
+    tokens, logits = [5], []
+    for pos in range(4):
+        out = model.token(tokens[-1], pos, new_sequence=(pos == 0))
+        logits.append(np.asarray(out, np.float32))
+        best = max(range(len(out)), key=lambda i: (out[i], -i))
+        tokens.append(best)
+    digest = hashlib.sha256()
+    for projs in w.layers:
+        for p in range(7):
+            digest.update(np.ascontiguousarray(projs[p].qweight).tobytes())
+    digest.update(w.embedding.tobytes())
+    return dict(shape=np.array(DECODE_SHAPE), tokens=np.array(tokens), logits=np.stack(logits),
+                weights_sha256=np.array(digest.hexdigest()))
+
+
 def main():
     t0 = time.time()
     only = set(sys.argv[1:])
     if only:
         if "attention" in only:
             np.savez_compressed(HERE / "attention.npz", **attention_fixture())
+        if "decode" in only:
+            np.savez_compressed(HERE / "decode_small.npz", **decode_fixture())
         return
     (HERE / "dequant_cases.json").write_text(json.dumps(dequant_fixture()))
     np.savez_compressed(HERE / "pack.npz", **pack_fixture())
     np.savez_compressed(HERE / "linear.npz", **linear_fixture())
     np.savez_compressed(HERE / "attention.npz", **attention_fixture())
     np.savez_compressed(HERE / "cfg0_gate_proj.npz", **cfg0_fixture())
+    np.savez_compressed(HERE / "decode_small.npz", **decode_fixture())
     print(f"golden fixtures written in {time.time() - t0:.1f}s")
 
 

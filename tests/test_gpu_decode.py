@@ -1,0 +1,182 @@
+"""GPU parity of the fused decode-step operations and of the whole greedy decode."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from anvilq_b200 import _lib, decoder, synthetic
+
+pytestmark = pytest.mark.gpu
+
+# Per-operator tolerance (anvil-q1-fp/design/SPEC.md:311-317) for single operations;
+# the 24-layer integration tolerance (same SPEC, :313-314) for whole decode steps:
+# final-logit cosine >= 0.999 and normalized max error <= 0.01.
+TOL_OP = (2e-3, 0.9999)
+TOL_DECODE = (1e-2, 0.999)
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda", 0)
+
+
+def T(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def check(y, ref, tol, what):
+    err, cos = oracle.normalized_error(y, ref)
+    assert err <= tol[0] and cos >= tol[1], (what, err, cos)
+
+
+def _fused(dev, x, x_mode, gamma, layer, y, y_mode, K, N, G=128):
+    lib = _lib.load()
+    ws = torch.zeros(lib.anvilq_w4a16_gemm_workspace_size(1, K, N, G), dtype=torch.uint8, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    bias = None if layer.bias is None else T(layer.bias, dev)
+    qw, qz, sc = T(layer.qweight, dev), T(layer.qzeros, dev), T(layer.scales, dev)
+    rc = lib.anvilq_w4a16_gemv_fused(x.data_ptr(), x_mode, None if gamma is None else gamma.data_ptr(), 1e-6,
+                                     qw.data_ptr(), qz.data_ptr(), sc.data_ptr(),
+                                     None if bias is None else bias.data_ptr(), y.data_ptr(), y_mode, K, N, G,
+                                     ws.data_ptr(), ws.numel(), err.data_ptr(), 0,
+                                     torch.cuda.current_stream(dev).cuda_stream)
+    assert rc == 0, lib.anvilq_strerror(rc)
+    torch.cuda.synchronize(dev)
+    assert int(err.item()) == 0
+
+
+@pytest.mark.parametrize("K,N", [(896, 1152), (896, 9728), (4096, 4096)])
+def test_gemv_rmsnorm_prologue(dev, K, N):
+    rng = np.random.default_rng(K + N)
+    r = (rng.standard_normal(K) * 3).astype(np.float32)
+    gamma = (1 + 0.1 * rng.standard_normal(K)).astype(np.float16)
+    layer = synthetic.awq_layer(K, N, 128, rng=rng, bias=True)
+    y = torch.empty(N, dtype=torch.float16, device=dev)
+    _fused(dev, T(r, dev), 1, T(gamma, dev), layer, y, 0, K, N)
+    h = r.astype(np.float64) * gamma / np.sqrt(np.mean(r.astype(np.float64) ** 2) + 1e-6)
+    ref = oracle.gemv_fp32(h.astype(np.float16).astype(np.float32)[None], layer.qweight, layer.qzeros,
+                           layer.scales_bits, layer.bias_bits, 128, threads=oracle.max_threads())
+    check(y.float().cpu().numpy(), ref[0], TOL_OP, (K, N))
+
+
+@pytest.mark.parametrize("K,N", [(4864, 896), (11008, 4096)])
+def test_gemv_silu_prologue_residual_epilogue(dev, K, N):
+    rng = np.random.default_rng(K)
+    gu = rng.standard_normal(2 * K).astype(np.float16)
+    resid = rng.standard_normal(N).astype(np.float32)
+    layer = synthetic.awq_layer(K, N, 128, rng=rng)
+    y = T(resid, dev)
+    _fused(dev, T(gu, dev), 2, None, layer, y, 1, K, N)
+    g, u = gu[:K].astype(np.float64), gu[K:].astype(np.float64)
+    a = (g / (1 + np.exp(-g)) * u).astype(np.float16).astype(np.float32)
+    ref = resid + oracle.gemv_fp32(a[None], layer.qweight, layer.qzeros, layer.scales_bits, None, 128,
+                                   threads=oracle.max_threads())[0]
+    check(y.cpu().numpy(), ref, TOL_OP, (K, N))
+
+
+def test_rope_kv_append(dev):
+    lib = _lib.load()
+    QH, KVH, D, Tmax, pos = 14, 2, 64, 64, 37
+    rng = np.random.default_rng(3)
+    qkv = rng.standard_normal((QH + 2 * KVH) * D).astype(np.float16)
+    q = torch.empty(QH * D, dtype=torch.float16, device=dev)
+    kc = torch.zeros((Tmax, KVH, D), dtype=torch.float16, device=dev)
+    vc = torch.zeros_like(kc)
+    p = T(np.array([pos], np.int32), dev)
+    sl = torch.zeros(1, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    rc = lib.anvilq_rope_kv_append(T(qkv, dev).data_ptr(), p.data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                   sl.data_ptr(), QH, KVH, D, Tmax, 1e6, err.data_ptr(), 0,
+                                   torch.cuda.current_stream(dev).cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize(dev)
+    o = oracle.DecodeOracle.__new__(oracle.DecodeOracle)
+    o.shape, o.theta = (1, QH * D, 1, QH, KVH, D, 128, 1, Tmax), 1e6
+    x = qkv.astype(np.float64)
+    q_ref = o._rope(x[:QH * D], QH, pos)
+    k_ref = o._rope(x[QH * D:(QH + KVH) * D], KVH, pos)
+    check(q.float().cpu().numpy(), q_ref, TOL_OP, "q")
+    check(kc[pos].float().cpu().numpy().ravel(), k_ref, TOL_OP, "k")
+    assert np.array_equal(vc[pos].cpu().numpy().ravel(), qkv[(QH + KVH) * D:])
+    assert int(sl.item()) == pos + 1 and int(err.item()) == 0
+
+
+def test_lmhead_argmax(dev):
+    lib = _lib.load()
+    H, V = 896, 151936
+    rng = np.random.default_rng(11)
+    x = (rng.standard_normal(H) * 5).astype(np.float32)
+    gamma = (1 + 0.1 * rng.standard_normal(H)).astype(np.float16)
+    E = (0.5 * rng.standard_normal((V, H), dtype=np.float32)).astype(np.float16)
+    logits = torch.empty(V, dtype=torch.float32, device=dev)
+    key = torch.zeros(1, dtype=torch.int64, device=dev)
+    tok = torch.zeros(1, dtype=torch.int32, device=dev)
+    s = torch.cuda.current_stream(dev).cuda_stream
+    Et = T(E, dev)
+    assert lib.anvilq_lmhead_argmax(T(x, dev).data_ptr(), T(gamma, dev).data_ptr(), 1e-6, Et.data_ptr(),
+                                    logits.data_ptr(), key.data_ptr(), H, V, 0, s) == 0
+    assert lib.anvilq_argmax_commit(key.data_ptr(), tok.data_ptr(), None, 0, s) == 0
+    torch.cuda.synchronize(dev)
+    h = x.astype(np.float64) * gamma / np.sqrt(np.mean(x.astype(np.float64) ** 2) + 1e-6)
+    ref = E.astype(np.float64) @ h
+    got = logits.cpu().numpy()
+    check(got, ref, (1e-5, 0.999999), "logits")
+    # the kernel's choice is the lowest-index maximum of the logits it computed
+    assert int(tok.item()) == oracle.greedy(got)
+    assert ref[int(tok.item())] >= ref.max() - 1e-3 * max(1.0, abs(ref.max()))
+
+
+def test_decode_matches_reference_token(dev, golden_dir):
+    """Greedy decode against FP32Model.token itself (tests/golden/decode_small.npz)."""
+    g = np.load(golden_dir / "decode_small.npz")
+    shape = tuple(int(v) for v in g["shape"])
+    w = decoder.synthetic_weights(shape, seed=29)
+    d = decoder.Decoder(w, dev, max_seq=shape[-1], keep_logits=True)
+    tokens = [int(t) for t in g["tokens"]]
+    d.reset(tokens[0])
+    for pos in range(len(g["logits"])):
+        d.step()
+        d.stream.synchronize()
+        d.check_errors()
+        check(d.logits.cpu().numpy(), g["logits"][pos], TOL_DECODE, pos)
+        assert int(d.token.item()) == tokens[pos + 1]
+
+
+def test_decode_graph_replay_matches_eager(dev):
+    shape = (2, 128, 256, 2, 1, 64, 128, 64, 16)
+    w = decoder.synthetic_weights(shape, seed=31)
+    eager = decoder.Decoder(w, dev, max_seq=16).generate(7, 8)
+    d = decoder.Decoder(w, dev, max_seq=16)
+    d.reset(7)
+    d.capture()
+    d.reset(7)
+    out = []
+    for _ in range(8):
+        d.step()
+        d.stream.synchronize()
+        out.append(int(d.token.item()))
+    d.check_errors()
+    assert out == eager
+
+
+def test_decode_qwen05b_shape(dev):
+    """Full Qwen2.5-0.5B shape (24 layers, vocab 151936) against the binary64 oracle
+    with binary16 rounding where the W4A16 datapath stores activations.  (Against
+    the unrounded oracle the 24 random layers amplify the binary16 activation
+    rounding to ~5e-2 normalized error; the small-shape test above checks the
+    unrounded reference itself.)"""
+    w = decoder.synthetic_weights(decoder.QWEN05B_SHAPE, seed=17)
+    d = decoder.Decoder(w, dev, max_seq=64, keep_logits=True)
+    o = oracle.DecodeOracle(w, act16=True)
+    token = 1000
+    d.reset(token)
+    for pos in range(3):
+        ref = o.step(token, pos)
+        d.step()
+        d.stream.synchronize()
+        d.check_errors()
+        check(d.logits.cpu().numpy(), ref, TOL_DECODE, pos)
+        token = int(d.token.item())
+        assert ref[token] >= ref.max() - 1e-2 * max(1.0, abs(ref.max()))
