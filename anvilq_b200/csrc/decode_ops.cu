@@ -44,15 +44,21 @@ __global__ void embed_kernel(const __half* __restrict__ table, const int* __rest
 }
 
 // qkv = [q (Hq*D) | k (Hkv*D) | v (Hkv*D)] fp16.  q and k are rotated in split
-// halves: for pair i < D/2, angle = pos * theta^(-2i/D) (binary64 product,
-// rounded to binary32 as the reference does), then
+// halves: for pair i < D/2, angle = pos * theta^(-2i/D) (binary64 product of the
+// host-computed frequency, rounded to binary32 as the reference does; sine and
+// cosine of that binary32 angle in binary32), then
 //   a' = a cos - b sin,  b' = b cos + a sin   (a = x[i], b = x[i + D/2]).
 // q goes to q_out, rotated k and raw v to row `pos` of the caches
 // [Tmax][Hkv][D]; seqlen = pos + 1.
+constexpr int kMaxRopePairs = 128;   // head_dim <= 256
+struct RopeFreq {
+  double inv[kMaxRopePairs];          // theta^(-2i/D), binary64, computed on the host
+};
+
 __global__ void rope_append_kernel(const __half* __restrict__ qkv, const int* __restrict__ pos_p,
                                    __half* __restrict__ q_out, __half* __restrict__ k_cache,
                                    __half* __restrict__ v_cache, int* __restrict__ seqlen, int Hq, int Hkv, int D,
-                                   int Tmax, double theta, int* dev_err) {
+                                   int Tmax, const __grid_constant__ RopeFreq freq, int* dev_err) {
   pdl_enter();
   const int pos = *pos_p;
   if (pos < 0 || pos >= Tmax) {
@@ -65,8 +71,9 @@ __global__ void rope_append_kernel(const __half* __restrict__ qkv, const int* __
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < rot + copies; i += gridDim.x * blockDim.x) {
     if (i < rot) {
       const int head = i / half_d, pair = i % half_d;
-      const float angle = (float)((double)pos * pow(theta, -2.0 * pair / D));
-      const float co = (float)cos((double)angle), si = (float)sin((double)angle);
+      const float angle = (float)((double)pos * freq.inv[pair]);
+      float si, co;
+      sincosf(angle, &si, &co);
       const int a = head * D + pair, b = a + half_d;
       const float xa = __half2float(qkv[a]), xb = __half2float(qkv[b]);
       const float ra = __fsub_rn(__fmul_rn(xa, co), __fmul_rn(xb, si));
@@ -255,13 +262,16 @@ int anvilq_rope_kv_append(const uint16_t* qkv, const int32_t* pos, uint16_t* q_o
                           int* dev_err, unsigned flags, anvilq_stream_t stream) {
   if (!qkv || !pos || !q_out || !k_cache || !v_cache) return ANVILQ_EINVAL;
   if (Hq < 1 || Hkv < 1 || Hq % Hkv || D < 2 || D % 2 || Tmax < 1 || !(theta > 0.0f)) return ANVILQ_EINVAL;
+  if (D / 2 > kMaxRopePairs) return ANVILQ_ESHAPE;
+  RopeFreq freq;
+  for (int i = 0; i < D / 2; ++i) freq.inv[i] = std::pow((double)theta, -2.0 * i / D);
   if (flags & ~(unsigned)ANVILQ_GEMM_OVERLAP_PRIOR) return ANVILQ_EINVAL;
   const int work = (Hq + Hkv) * (D / 2) + Hkv * D;
   const int threads = 256, blocks = std::min(32, (work + threads - 1) / threads);
   return launch(rope_append_kernel, dim3(blocks), dim3(threads), 0, reinterpret_cast<cudaStream_t>(stream), flags,
                 reinterpret_cast<const __half*>(qkv), (const int*)pos, reinterpret_cast<__half*>(q_out),
                 reinterpret_cast<__half*>(k_cache), reinterpret_cast<__half*>(v_cache), (int*)seqlen, Hq, Hkv, D,
-                Tmax, (double)theta, dev_err);
+                Tmax, freq, dev_err);
 }
 
 int anvilq_lmhead_argmax(const float* x, const uint16_t* gamma, float eps, const uint16_t* table, float* logits,

@@ -47,6 +47,7 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kTile = 16;          // tokens per tile
 constexpr int kStages = 4;         // ring depth per warp
 constexpr int kMaxGroup = 8;       // query heads per kv head handled by one CTA
+constexpr int kMaxSplits = 32;     // KV splits per (sequence, kv head)
 constexpr unsigned long long kWaitLimitNs = 1000000000ull;
 
 struct Params {
@@ -71,6 +72,7 @@ struct Layout {
   static constexpr int kBarOffset = kRingBytes;                // kWarps * kStages mbarriers
   static constexpr int kCombOffset = kBarOffset + kWarps * kStages * 8;
   static constexpr int kCombBytes = kWarps * kMaxGroup * (D + 2) * 4;
+  static_assert(kCombBytes >= (3 * kMaxSplits * kMaxGroup + kMaxGroup) * 4, "split merge fits the warp-merge area");
   static constexpr int kTotal = kCombOffset + kCombBytes;
 };
 
@@ -339,20 +341,41 @@ __global__ void __launch_bounds__(kThreads) gqa_decode_kernel(const Params p) {
   if (!s_flag) return;
   __threadfence();
   const float* parts = p.partials + (size_t)pair * p.splits * G * (D + 2);
+  // split statistics (running max, running sum) of every head, loaded in one
+  // parallel pass into shared memory (reusing the warp-merge area)
+  float* s_stat = comb;   // [splits][G][2]
+  for (int i = threadIdx.x; i < p.splits * G; i += blockDim.x) {
+    const float* row = parts + (size_t)i * (D + 2);
+    s_stat[2 * i] = __ldcg(row + D);
+    s_stat[2 * i + 1] = __ldcg(row + D + 1);
+  }
+  __syncthreads();
+  float* s_w = comb + 2 * kMaxSplits * kMaxGroup;   // [splits][G] merge weights, then [G] 1/L
+  for (int hh = threadIdx.x; hh < G; hh += blockDim.x) {
+    float M = -INFINITY;
+    for (int sp = 0; sp < p.splits; ++sp) M = fmaxf(M, s_stat[2 * (sp * G + hh)]);
+    float lsum = 0.0f;
+    for (int sp = 0; sp < p.splits; ++sp) {
+      const float f = M == -INFINITY ? 0.0f : exp2f(s_stat[2 * (sp * G + hh)] - M);
+      s_w[sp * G + hh] = f;
+      lsum += f * s_stat[2 * (sp * G + hh) + 1];
+    }
+    s_w[kMaxSplits * G + hh] = lsum > 0.0f ? 1.0f / lsum : 0.0f;
+  }
+  __syncthreads();
   for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
     const int hh = e / D, d = e % D;
-    float M = -INFINITY;
-    for (int sp = 0; sp < p.splits; ++sp) M = fmaxf(M, __ldcg(parts + ((size_t)sp * G + hh) * (D + 2) + D));
-    float acc = 0.0f, lsum = 0.0f;
-    if (M != -INFINITY) {
-      for (int sp = 0; sp < p.splits; ++sp) {
-        const float* row = parts + ((size_t)sp * G + hh) * (D + 2);
-        const float f = exp2f(__ldcg(row + D) - M);
-        lsum += f * __ldcg(row + D + 1);
-        acc += f * __ldcg(row + d);
-      }
+    float acc = 0.0f;
+    int sp = 0;
+    for (; sp + 8 <= p.splits; sp += 8) {   // independent loads, summed in split order
+      float o[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) o[k] = __ldcg(parts + ((size_t)(sp + k) * G + hh) * (D + 2) + d);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc += s_w[(sp + k) * G + hh] * o[k];
     }
-    p.out[((size_t)b * p.Hq + (size_t)h * G + hh) * D + d] = __float2half_rn(lsum > 0.0f ? acc / lsum : 0.0f);
+    for (; sp < p.splits; ++sp) acc += s_w[sp * G + hh] * __ldcg(parts + ((size_t)sp * G + hh) * (D + 2) + d);
+    p.out[((size_t)b * p.Hq + (size_t)h * G + hh) * D + d] = __float2half_rn(acc * s_w[kMaxSplits * G + hh]);
   }
 }
 
@@ -386,7 +409,7 @@ static Plan plan_for(int B, int Hq, int Hkv, int D, int Tmax, int sms) {
   const long long slots = (long long)std::max(sms, 1) * ctas_per_sm;
   // enough CTAs for about two full waves, each split holding >= one tile per warp
   long long want = (2 * slots + pairs - 1) / pairs;
-  const int max_splits = std::max(1, tiles / kWarps);
+  const int max_splits = std::max(1, std::min(kMaxSplits, tiles / kWarps));
   pl.splits = (int)std::max<long long>(1, std::min<long long>(want, max_splits));
   pl.tiles_per_split = (tiles + pl.splits - 1) / pl.splits;
   pl.splits = (tiles + pl.tiles_per_split - 1) / pl.tiles_per_split;

@@ -181,8 +181,15 @@ class Decoder:
         self.stream.synchronize()
 
     def capture(self, host_io: bool = False):
-        """Record one step as a CUDA graph (warming the kernels first)."""
-        self.host_io = host_io
+        """Record one step as a CUDA graph (warming the kernels first) and make it
+        the graph that ``step`` replays.  host_io=True puts the copy of the
+        input token from pinned host memory and of the chosen token back to it
+        inside the graph (``token_in`` / ``token_out``)."""
+        self.graph = self.record(host_io)
+        return self
+
+    def record(self, host_io: bool = False):
+        """A CUDA graph of one step; the decoder state (position, token) is left as it was."""
         save_pos = self.pos.clone()
         save_tok = self.token.clone()
         with torch.cuda.stream(self.stream):
@@ -192,10 +199,49 @@ class Decoder:
             self.pos.copy_(save_pos)
             self.token.copy_(save_tok)
         self.stream.synchronize()
-        self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph, stream=self.stream):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=self.stream):
             self._enqueue(host_io)
-        return self
+        return graph
+
+    def record_gemvs(self):
+        """A CUDA graph of only this step's W4A16 GEMVs (same weights, buffers and
+        fused modes, same order), for timing the GEMV kernel on its own."""
+        L, H, I, QH, KVH, D, G, V, _ = self.shape
+        nqkv = (QH + 2 * KVH) * D
+
+        def enqueue():
+            for l, w in enumerate(self.layers):
+                self._gemv(w["qkv"], self.x, 1, self.gamma_in[l], self.qkv, 0, H, nqkv)
+                self._gemv(w["o"], self.attn, 0, None, self.x, 1, QH * D, H)
+                self._gemv(w["gu"], self.x, 1, self.gamma_post[l], self.gu, 0, H, 2 * I)
+                self._gemv(w["down"], self.gu, 2, None, self.x, 1, I, H)
+
+        with torch.cuda.stream(self.stream):
+            enqueue()
+        self.stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=self.stream):
+            enqueue()
+        return graph
+
+    def gemv_bytes_per_step(self) -> int:
+        L, H, I, QH, KVH, D, G, V, _ = self.shape
+        b = 0
+        for K, N, bias in ((H, (QH + 2 * KVH) * D, True), (QH * D, H, False), (H, 2 * I, False), (I, H, False)):
+            b += synthetic.gemv_bytes(1, K, N, G, bias)
+        return b * L
+
+    def fill_context(self, length: int, seed: int = 0):
+        """Fill cache rows [0, length) with N(0,1) keys and values (a synthetic
+        context) and set the position to `length`."""
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed)
+        with torch.cuda.stream(self.stream):
+            self.k_cache[:, :length].normal_(generator=g)
+            self.v_cache[:, :length].normal_(generator=g)
+            self.pos.fill_(length)
+        self.stream.synchronize()
 
     def step(self):
         """Enqueue one token on ``self.stream`` (the graph if captured)."""

@@ -2,23 +2,28 @@
 """Benchmark of the W4A16 AWQ decode datapath on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl anvilq|reference]
-                    [--workload proj05b|proj7b]
+                    [--workload decode05b|proj05b|proj7b]
 
-One step = one pass of the W4A16 AWQ GEMV over every projection of every layer of
-a batch-1 decode step (each projection has its own weights; all resident in HBM),
-replayed as one CUDA graph.  Default workload: the Qwen2.5-0.5B decode-step
-projection set (24 layers x q,k,v,o,gate,up,down; 186 MB of int4 weights, larger
-than the 126 MB L2, so no L2 flush is needed between steps).
+decode05b (default): one step = one greedy decode token of a Qwen2.5-0.5B-shape
+W4A16 AWQ model (24 layers, hidden 896, 14/2 heads of 64, intermediate 4864,
+vocab 151936, tied fp16 lm_head; random-init weights with the reference's value
+distributions), batch 1, at context 1024, as one CUDA graph.  value = tokens/s;
+the step moves ~471 MB (186 MB int4 weights, 272 MB lm_head, 12.6 MB KV), larger
+than the 126 MB L2, so no flush is needed between steps.  The roofline object
+times the step's 96 W4A16 GEMVs (same weights, buffers and fused modes) as a
+graph of their own in the same run.  e2e drives the public Decoder API with the
+input token copied from pinned host memory and the chosen token copied back
+inside every step, and the host waiting for it.
 
-value  = algorithmic HBM bytes of all ranks' steps / max-over-ranks device time (GB/s)
-e2e    = same metric through the public ProjectionStream API with every
-         projection's activations copied from pinned host memory and every output
-         copied back inside the timed step.
-With N GPUs, each rank runs an independent replica (weak scaling, no collective).
+proj05b / proj7b: one step = the W4A16 GEMV over every projection of a decode
+step (Qwen2.5-0.5B or Llama-7B-class shapes), value in GB/s.
 
---impl reference times the CPU restatement of the reference's golden GEMV
-(FP32Model.linear, anvil-q1/tests/official_weights.py:418-437) on all host
-cores over a bounded column sample of the same projection set.
+With N GPUs each rank runs an independent replica (weak scaling, no collective).
+
+--impl reference times the CPU restatement of the reference's golden model on
+the host cores over a bounded sample of the same workload: FP32Model.token
+(anvil-q1/tests/official_weights.py:451-509, binary64 numpy port) for decode05b,
+FP32Model.linear (:418-437, C port, bit-exact) for the projection sets.
 """
 from __future__ import annotations
 
@@ -38,6 +43,10 @@ sys.path.insert(0, str(REPO))
 
 METRIC = "W4A16 GEMV HBM GB/s (% of B200 peak); decode tok/s at 0.5B/7B shapes"
 WORKLOADS = {
+    "decode05b": dict(name="Qwen2.5-0.5B-shape greedy decode step, batch 1, context 1024: 24 layers, hidden 896, "
+                           "14 q / 2 kv heads of 64, intermediate 4864, W4A16 AWQ G128 projections, RMSNorm eps 1e-6, "
+                           "RoPE theta 1e6, fp16 KV cache, tied fp16 lm_head [151936, 896], greedy argmax",
+                      context=1024),
     "proj05b": dict(name="Qwen2.5-0.5B decode-step W4A16 projections: 24 layers x (q 896x896+bias, "
                          "k,v 896x128+bias, o 896x896, gate,up 896x4864, down 4864x896), G128, M=1",
                     layers=24, projections="QWEN05B_PROJECTIONS"),
@@ -182,7 +191,164 @@ def dist_init():
     return world, rank, local
 
 
+# ------------------------------------------------------------ decode05b
+def _decode_oracle_sample(context, seed=17):
+    """One layer of the decode step plus 1/24 of the lm_head rows, in the binary64
+    oracle (the per-token CPU time is 24x this sample)."""
+    import numpy as np
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle
+    from anvilq_b200 import decoder
+    L, H, I, QH, KVH, D, G, V, SEQ = decoder.QWEN05B_SHAPE
+    shape = (1, H, I, QH, KVH, D, G, V // L, SEQ)
+    w = decoder.synthetic_weights(shape, seed=seed)
+    o = oracle.DecodeOracle(w)
+    rng = np.random.default_rng(seed)
+    for t in range(context):   # synthetic context in the cache
+        o.cache[0, t] = (rng.standard_normal((KVH, D)), rng.standard_normal((KVH, D)))
+    return o
+
+
+def _decode_cpu(o, context, steps):
+    t0 = time.perf_counter()
+    for i in range(steps):
+        o.step(5, context + i)
+    return time.perf_counter() - t0
+
+
+def decode_cpu_baseline(context, target_s=15.0):
+    o = _decode_oracle_sample(context)
+    dt = _decode_cpu(o, context, 1)
+    n = max(1, int(target_s / max(dt, 1e-3)))
+    dt = _decode_cpu(o, context + 1, n)
+    per_token = dt / n * 24
+    return {"value": round(1.0 / per_token, 5), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"oracle.DecodeOracle (binary64 numpy restatement of FP32Model.token) on 1 of 24 layers "
+                      f"+ 1/24 of the lm_head rows at context {context}, {n} steps in {dt:.1f} s, scaled x24; "
+                      f"numpy/BLAS threads as available"}
+
+
+def decode_reference_arm(args, world, rank):
+    if rank != 0:
+        return 0
+    wl = WORKLOADS["decode05b"]
+    ctx = wl["context"]
+    o = _decode_oracle_sample(ctx)
+    _decode_cpu(o, ctx, args.warmup)
+    dt = _decode_cpu(o, ctx + args.warmup, args.steps)
+    per_token = dt / args.steps * 24
+    value = 1.0 / per_token
+    sample = ("oracle.DecodeOracle (binary64 numpy restatement of FP32Model.token), per step 1 of 24 layers "
+              "+ 1/24 of the lm_head rows, token time = 24 x sample")
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_token * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (seeded; BASELINE value distributions)",
+            "config": {"workload": wl["name"], "sample": sample},
+            "cpu_baseline": {"value": round(value, 5), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 5), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def decode_arm(args, world, rank, local):
+    import torch
+    from anvilq_b200 import decoder
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    wl = WORKLOADS["decode05b"]
+    ctx = wl["context"]
+    peak, peak_kind = load_peaks()
+    w = decoder.synthetic_weights(decoder.QWEN05B_SHAPE, seed=17 + rank)
+    total_steps = 2 * (args.warmup + args.steps) + 4
+    d = decoder.Decoder(w, dev, max_seq=ctx + total_steps + 8)
+    d.fill_context(ctx, seed=rank)
+    d.token.fill_(1000)
+    d.token_in.fill_(1000)
+    g_dev = d.record(False)
+    g_e2e = d.record(True)
+    g_gemv = d.record_gemvs()
+
+    def timed(graph, steps, host_wait):
+        for _ in range(args.warmup):
+            with torch.cuda.stream(d.stream):
+                graph.replay()
+            if host_wait:
+                d.stream.synchronize()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(d.stream)
+        for _ in range(steps):
+            with torch.cuda.stream(d.stream):
+                graph.replay()
+            if host_wait:
+                d.stream.synchronize()   # the host reads the chosen token every step
+        end.record(d.stream)
+        torch.cuda.synchronize(dev)
+        ms = start.elapsed_time(end)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+            torch.distributed.barrier()
+        return ms
+
+    with ClockSampler(dev.index) as clocks:
+        ms = timed(g_dev, args.steps, False)
+    d.pos.fill_(ctx)
+    ms_e2e = timed(g_e2e, args.steps, True)
+    ms_gemv = timed(g_gemv, args.steps, False)
+    d.check_errors()
+
+    tok_s = world * args.steps / (ms / 1e3)
+    step_bytes = d.bytes_per_step(ctx + args.warmup + args.steps // 2)
+    gemv_bytes = d.gemv_bytes_per_step()
+    gemv_launches = 4 * decoder.QWEN05B_SHAPE[0]
+    per_launch_s = ms_gemv / 1e3 / args.steps / gemv_launches
+    achieved = gemv_bytes / gemv_launches / per_launch_s / 1e9
+    traffic = None
+    prof = REPO / "profiles" / "traffic.json"
+    if prof.exists():
+        entry = json.loads(prof.read_text()).get("gemv_tma_kernel/decode05b")
+        if entry:
+            traffic = int(gemv_bytes / gemv_launches * entry["ratio_read_over_algorithmic"])
+    line = {
+        "metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16 activations x int4 weights, fp32 accumulate; fp16 KV and lm_head",
+        "data": "synthetic (seeded random-init weights and context; BASELINE value distributions)",
+        "config": {"workload": wl["name"], "batch": 1, "context": ctx, "layers": decoder.QWEN05B_SHAPE[0],
+                   "step_bytes": step_bytes, "kernels_per_step": d.kernels_per_step(),
+                   "l2": "inputs larger than L2 (no flush)", "parallelism": f"replicas x{world}",
+                   "graph": "one CUDA graph per token"},
+        "hbm_gbs": round(step_bytes * tok_s / world / 1e9, 2),
+        "hbm_frac_of_measured_peak": round(step_bytes * tok_s / world / 1e9 / peak, 4),
+        "roofline": {"bound": "hbm", "kernel": "gemv_tma_kernel", "achieved": round(achieved, 2), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "frac_of_8tbs_nominal": round(achieved / 8000.0, 4), "traffic": traffic,
+                     "launch_avg_us": round(per_launch_s * 1e6, 4),
+                     "measured_on": "the step's 96 W4A16 GEMVs as their own CUDA graph, same run"},
+        "e2e": {"value": round(world * args.steps / (ms_e2e / 1e3), 2), "unit": "tok/s",
+                "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
+                "ms_per_step": round(ms_e2e / args.steps, 5)},
+        "gpu_launches": d.kernels_per_step() * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = decode_cpu_baseline(ctx)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def reference_arm(args, world, rank):
+    if args.workload == "decode05b":
+        return decode_reference_arm(args, world, rank)
     from anvilq_b200 import stream as st
     wl = WORKLOADS[args.workload]
     projections = getattr(st, wl["projections"])
@@ -299,10 +465,10 @@ def anvilq_arm(args, world, rank, local):
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("anvilq", "reference"), default="anvilq")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="proj05b")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode05b")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
     if args.warmup < 3:
@@ -313,6 +479,8 @@ def main(argv=None):
         return reference_arm(args, world, rank)
     world, rank, local = dist_init()
     try:
+        if args.workload == "decode05b":
+            return decode_arm(args, world, rank, local)
         return anvilq_arm(args, world, rank, local)
     finally:
         if world > 1:
