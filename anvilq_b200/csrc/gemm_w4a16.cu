@@ -576,8 +576,11 @@ size_t anvilq_w4a16_gemm_workspace_size(int M, int K, int N, int G) {
   if (!shape_ok(M, K, N, G)) return 0;
   const DeviceInfo* d = device_info();
   if (!d) return 0;
-  const size_t b = plan_for(*d, M, K, N).bytes;
-  return M == 1 ? std::max(b, gemv_tma_workspace_bytes(K, N)) : b;
+  size_t b = plan_for(*d, M, K, N).bytes;
+  if (M == 1) b = std::max(b, gemv_tma_workspace_bytes(K, N));
+  // the tensor-core path may serve any M (anvilq_w4a16_verify_gemm)
+  if (G == 128 && K % 128 == 0 && N % 32 == 0) b = std::max(b, verify_tc_workspace_bytes(M, K, N));
+  return b;
 }
 
 int anvilq_w4a16_gemm(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
@@ -607,6 +610,9 @@ int anvilq_w4a16_gemm_ex(const uint16_t* x, const int32_t* qweight, const int32_
     return launch_gemv_tma(io, qweight, qzeros, scales, bias, K, N, G, workspace, workspace_bytes, dev_err, s,
                            (flags & ANVILQ_GEMM_OVERLAP_PRIOR) != 0);
   }
+  if (M >= ANVILQ_VERIFY_TC_MIN_M && verify_tc_supported(x, qweight, qzeros, scales, M, K, N, G))
+    return launch_verify_tc(x, qweight, nullptr, qzeros, scales, bias, y, M, K, N, workspace, workspace_bytes,
+                            dev_err, s);
   const DeviceInfo* d = device_info();
   if (!d) return ANVILQ_ECUDA;
   const Plan pl = plan_for(*d, M, K, N);
@@ -614,6 +620,39 @@ int anvilq_w4a16_gemm_ex(const uint16_t* x, const int32_t* qweight, const int32_
   if (!workspace || workspace_bytes < pl.bytes) return ANVILQ_EWORKSPACE;
   if (!aligned16(workspace)) return ANVILQ_EALIGN;
   return launch_fast(pl, x, qweight, qzeros, scales, bias, y, M, K, N, G, workspace, dev_err, s);
+}
+
+int anvilq_w4a16_verify_gemm(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
+                             const uint16_t* scales, const uint16_t* bias, uint16_t* y,
+                             int M, int K, int N, int G, void* workspace, size_t workspace_bytes,
+                             int* dev_err, anvilq_stream_t stream) {
+  if (!x || !qweight || !qzeros || !scales || !y) return ANVILQ_EINVAL;
+  if (!shape_ok(M, K, N, G)) return ANVILQ_EINVAL;
+  if (!verify_tc_supported(x, qweight, qzeros, scales, M, K, N, G)) return ANVILQ_ESHAPE;
+  return launch_verify_tc(x, qweight, nullptr, qzeros, scales, bias, y, M, K, N, workspace, workspace_bytes,
+                          dev_err, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t anvilq_w4a16_tc_pack_size(int K, int N, int G) {
+  return G == 128 ? tc_pack_bytes(K, N) : 0;
+}
+
+int anvilq_w4a16_tc_pack(const int32_t* qweight, int32_t* packed, int K, int N, int G, anvilq_stream_t stream) {
+  if (!qweight || !packed) return ANVILQ_EINVAL;
+  if (!shape_ok(1, K, N, G)) return ANVILQ_EINVAL;
+  if (anvilq_w4a16_tc_pack_size(K, N, G) == 0) return ANVILQ_ESHAPE;
+  return launch_tc_pack(qweight, packed, K, N, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int anvilq_w4a16_verify_gemm_packed(const uint16_t* x, const int32_t* packed, const int32_t* qzeros,
+                                    const uint16_t* scales, const uint16_t* bias, uint16_t* y, int M, int K,
+                                    int N, int G, void* workspace, size_t workspace_bytes, int* dev_err,
+                                    anvilq_stream_t stream) {
+  if (!x || !packed || !qzeros || !scales || !y) return ANVILQ_EINVAL;
+  if (!shape_ok(M, K, N, G)) return ANVILQ_EINVAL;
+  if (!aligned16(packed) || !verify_tc_supported(x, packed, qzeros, scales, M, K, N, G)) return ANVILQ_ESHAPE;
+  return launch_verify_tc(x, nullptr, packed, qzeros, scales, bias, y, M, K, N, workspace, workspace_bytes,
+                          dev_err, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int anvilq_w4a16_gemv_fused(const void* x, int x_mode, const uint16_t* gamma, float eps,

@@ -27,4 +27,17 @@ int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qze
                     const uint16_t* bias, int K, int N, int G, void* workspace, size_t workspace_bytes, int* dev_err,
                     cudaStream_t stream, bool overlap_prior);
 
+// Small-M (speculative verify) GEMM on tcgen05 tensor cores (verify_gemm_tc.cu):
+// G == 128, K % 128 == 0, N % 32 == 0, 16-byte aligned operands; M rows in
+// launches of at most 64.
+bool verify_tc_supported(const void* x, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
+                         int M, int K, int N, int G);
+size_t verify_tc_workspace_bytes(int M, int K, int N);
+// qweight: AWQ layout, or null when `packed` (anvilq_w4a16_tc_pack layout) is given.
+int launch_verify_tc(const uint16_t* x, const int32_t* qweight, const int32_t* packed, const int32_t* qzeros,
+                     const uint16_t* scales, const uint16_t* bias, uint16_t* y, int M, int K, int N,
+                     void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t stream);
+size_t tc_pack_bytes(int K, int N);
+int launch_tc_pack(const int32_t* qweight, int32_t* packed, int K, int N, cudaStream_t stream);
+
 }  // namespace anvilq

@@ -94,7 +94,7 @@ GEMM_OVERLAP_PRIOR = 1
 
 
 def gemm(x, qweight, qzeros, scales, bias=None, group: int = 128, out=None, dev_err=None,
-         overlap_prior: bool = False):
+         overlap_prior: bool = False, tensor_cores: bool = False):
     """y[M, N] = x[M, K] @ dequant(qweight, qzeros, scales) (+ bias), fp16 out.
 
     GPU counterpart of FP32Model.linear (anvil-q1/tests/official_weights.py:418-437)
@@ -122,10 +122,64 @@ def gemm(x, qweight, qzeros, scales, bias=None, group: int = 128, out=None, dev_
     need = lib.anvilq_w4a16_gemm_workspace_size(M, K, N, group)
     ws = workspace(x2.device, need)
     err = device_error_word(x2.device) if dev_err is None else dev_err
+    if tensor_cores:
+        _lib.check(lib.anvilq_w4a16_verify_gemm(_ptr(x2), _ptr(qweight), _ptr(qzeros), _ptr(scales), _ptr(bias),
+                                                _ptr(out), M, K, N, group, _ptr(ws), ws.numel(), _ptr(err),
+                                                _stream_ptr(x2.device)), "anvilq_w4a16_verify_gemm")
+        return out.view(N) if squeeze else out
     flags = GEMM_OVERLAP_PRIOR if overlap_prior else 0
     _lib.check(lib.anvilq_w4a16_gemm_ex(_ptr(x2), _ptr(qweight), _ptr(qzeros), _ptr(scales), _ptr(bias),
                                         _ptr(out), M, K, N, group, _ptr(ws), ws.numel(), _ptr(err), flags,
                                         _stream_ptr(x2.device)), "anvilq_w4a16_gemm_ex")
+    return out.view(N) if squeeze else out
+
+
+def verify_gemm(x, qweight, qzeros, scales, bias=None, group: int = 128, out=None, dev_err=None):
+    """The speculative-verify GEMM forced onto the tcgen05 tensor-core kernel for any M.
+
+    ``gemm`` already picks it for M >= 16; this is for callers (and tests) that
+    want the tensor-core path at every M.  Needs group 128, K % 128 == 0, N % 32 == 0.
+    """
+    return gemm(x, qweight, qzeros, scales, bias, group, out, dev_err, tensor_cores=True)
+
+
+def tc_pack(qweight, group: int = 128):
+    """qweight int32 [K, N/8] (AWQ) -> the tensor-core kernel's resident layout (int32, 1-D).
+
+    One-time rewrite for weights that stay on the device (anvilq_w4a16_tc_pack);
+    use the result with ``verify_gemm_packed``.
+    """
+    if qweight.dtype != torch.int32 or qweight.dim() != 2 or not qweight.is_contiguous():
+        raise ValueError("qweight must be contiguous int32 [K, N/8]")
+    K, W8 = qweight.shape
+    lib = _lib.load()
+    nbytes = lib.anvilq_w4a16_tc_pack_size(K, W8 * 8, group)
+    if nbytes == 0:
+        raise ValueError("tensor-core layout needs group 128, K % 128 == 0 and N % 32 == 0")
+    out = torch.empty(nbytes // 4, dtype=torch.int32, device=qweight.device)
+    _lib.check(lib.anvilq_w4a16_tc_pack(_ptr(qweight), _ptr(out), K, W8 * 8, group, _stream_ptr(qweight.device)),
+               "anvilq_w4a16_tc_pack")
+    return out
+
+
+def verify_gemm_packed(x, packed, qzeros, scales, bias=None, group: int = 128, out=None, dev_err=None):
+    """``verify_gemm`` on weights rewritten by ``tc_pack``; qzeros/scales/bias as for ``gemm``."""
+    if qzeros.dtype != torch.int32 or scales.dtype != torch.float16 or scales.dim() != 2:
+        raise TypeError("qzeros int32 [K/G, N/8] and scales float16 [K/G, N] expected")
+    K, N = scales.shape[0] * group, scales.shape[1]
+    squeeze = x.dim() == 1
+    x2 = x.unsqueeze(0) if squeeze else x
+    if x2.dtype != torch.float16 or x2.dim() != 2 or x2.shape[1] != K or not x2.is_contiguous():
+        raise ValueError(f"x must be contiguous float16 [M, {K}]")
+    M = x2.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float16, device=x2.device)
+    lib = _lib.load()
+    ws = workspace(x2.device, lib.anvilq_w4a16_gemm_workspace_size(M, K, N, group))
+    err = device_error_word(x2.device) if dev_err is None else dev_err
+    _lib.check(lib.anvilq_w4a16_verify_gemm_packed(_ptr(x2), _ptr(packed), _ptr(qzeros), _ptr(scales), _ptr(bias),
+                                                   _ptr(out), M, K, N, group, _ptr(ws), ws.numel(), _ptr(err),
+                                                   _stream_ptr(x2.device)), "anvilq_w4a16_verify_gemm_packed")
     return out.view(N) if squeeze else out
 
 

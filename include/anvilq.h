@@ -104,6 +104,44 @@ int anvilq_w4a16_gemm_ex(const uint16_t* x, const int32_t* qweight, const int32_
                          void* workspace, size_t workspace_bytes,
                          int* dev_err, unsigned flags, anvilq_stream_t stream);
 
+/* The speculative-verify GEMM on the tensor cores: M token rows against one
+ * AWQ weight matrix with tcgen05.mma from shared memory into TMEM
+ * accumulators (integer deltas q - z on the tensor cores, the group scale
+ * applied in fp32 afterwards).  Replaces the M full weight passes of the
+ * reference's sequential verify (anvil-q4/rtl/anvil_q4_speculative.sv:57-92,
+ * anvil-q4/design/SPEC.md:271-272) and its 4-token batched projection
+ * (anvil-q3-ht2/design/SPEC.md:81-86); every row equals FP32Model.linear
+ * (official_weights.py:418-437) within the fp32 accumulation-order tolerance.
+ * anvilq_w4a16_gemm(_ex) routes M >= ANVILQ_VERIFY_TC_MIN_M here by itself;
+ * this entry point uses the tensor cores for any M >= 1 (launches of at most
+ * 64 rows).  Requires G == 128, K % 128 == 0, N % 32 == 0 and 16-byte aligned
+ * x, qweight, qzeros and scales (ANVILQ_ESHAPE otherwise).  Workspace: at
+ * least anvilq_w4a16_gemm_workspace_size(M, K, N, G) bytes. */
+#define ANVILQ_VERIFY_TC_MIN_M 16
+int anvilq_w4a16_verify_gemm(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
+                             const uint16_t* scales, const uint16_t* bias, uint16_t* y,
+                             int M, int K, int N, int G,
+                             void* workspace, size_t workspace_bytes,
+                             int* dev_err, anvilq_stream_t stream);
+
+/* Resident-weight form of the verify GEMM.  anvilq_w4a16_tc_pack rewrites an
+ * AWQ qweight [K][N/8] once (at model load) into the order the tensor-core
+ * kernel's dequantisers consume -- the same nibbles, regrouped per 128-column
+ * x 128-row unit so that each output column's 8 consecutive rows share one
+ * 32-bit word (8 KB per unit, anvilq_w4a16_tc_pack_size bytes in all; columns
+ * past N zero).  anvilq_w4a16_verify_gemm_packed then computes exactly what
+ * anvilq_w4a16_verify_gemm computes from the original layout, with qzeros,
+ * scales and bias unchanged.  G must be 128, K % 128 == 0, N % 32 == 0, and
+ * `packed` 16-byte aligned (ANVILQ_ESHAPE otherwise). */
+size_t anvilq_w4a16_tc_pack_size(int K, int N, int G);
+int anvilq_w4a16_tc_pack(const int32_t* qweight, int32_t* packed, int K, int N, int G,
+                         anvilq_stream_t stream);
+int anvilq_w4a16_verify_gemm_packed(const uint16_t* x, const int32_t* packed, const int32_t* qzeros,
+                                    const uint16_t* scales, const uint16_t* bias, uint16_t* y,
+                                    int M, int K, int N, int G,
+                                    void* workspace, size_t workspace_bytes,
+                                    int* dev_err, anvilq_stream_t stream);
+
 /* Batch-1 W4A16 GEMV with the decode step's neighbouring operations fused in.
  *
  * Replaces FP32Model.linear (official_weights.py:418-437) together with the
