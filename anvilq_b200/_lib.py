@@ -29,6 +29,8 @@ SIGNATURES = {
     "anvilq_w4a16_tc_pack_size": (SZ, [I, I, I]),
     "anvilq_w4a16_tc_pack": (I, [P, P, I, I, I, P]),
     "anvilq_w4a16_verify_gemm_packed": (I, [P, P, P, P, P, P, I, I, I, I, P, SZ, P, P]),
+    "anvilq_w4a16_gemm_q16_workspace_size": (SZ, [I, I, I, I]),
+    "anvilq_w4a16_gemm_q16": (I, [P, P, P, P, P, P, I, I, I, I, P, SZ, P, P]),
     "anvilq_awq_dequant": (I, [P, P, P, P, P, I, I, I, P, P]),
     "anvilq_awq_pack": (I, [P, P, I, I, P]),
     "anvilq_awq_unpack": (I, [P, P, I, I, P]),

@@ -1,0 +1,201 @@
+// gemv_q16.cu -- bit-accurate Q16.16 integer W4A16 GEMV: the integer golden
+// model's projection (anvil-q1/tests/official_weights.py:592-612) and the RTL
+// datapath it specifies (anvil-q1/design/SPEC.md:151-158, anvil_q1_w4a16_gemv.sv):
+//
+//   total = sum_k x[k] * (u4 q[k][c] - u4 z[k/G][c]) * round_away(scale[k/G][c] * 2^16)
+//   total += clip32(round_away(bias[c] * 2^16)) * 65536            (when bias is given)
+//   y[c] = clip32(round_away(total / 65536))
+//
+// with x and y signed Q16.16 int32 and `total` an exact signed integer
+// (the reference uses Python integers; it needs ~80 bits).  round_away is
+// round-half-away-from-zero (official_weights.py:511-514), the binary16 ->
+// Q16.16 conversion is exact integer arithmetic on the fields
+// (official_weights.py:521-529, verify.py:216-238).
+//
+// Exact integer arithmetic on the GPU: per group each thread keeps, for its 8
+// columns, sum x * (q - z) in int64 (|x| < 2^31 and |q - z| <= 15, so any group
+// of fewer than 2^28 rows stays below 2^63); at the group's end that sum times the
+// group's Q16.16 scale (< 2^33) is added into an __int128 total.  K is split
+// into chunks of whole groups across CTAs; the chunk totals are exact, so the
+// finishing kernel's sum is the same in any order (bit-identical, no
+// floating point anywhere).
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+#include "../../include/anvilq.h"
+#include "internal.h"
+
+namespace anvilq {
+namespace q16 {
+
+constexpr int kThreads = 64;          // one thread per qweight word (8 columns)
+constexpr int kMaxChunks = 16;
+// AWQ lane j of a packed word sits at bit (0,16,4,20,8,24,12,28)[j] (anvil-q1/tests/verify.py:38)
+__device__ __forceinline__ int awq_shift(int j) { return ((j & 1) << 4) | ((j >> 1) << 2); }
+
+// half_integer(raw, scale=...) (official_weights.py:521-529): round_away(value * 2^16)
+// from the binary16 fields; false for exponent 31.
+__device__ __forceinline__ bool half_q16(uint16_t raw, long long* out) {
+  const int exponent = (raw >> 10) & 31, mantissa = raw & 1023;
+  if (exponent == 31) return false;
+  const long long significand = exponent == 0 ? mantissa : mantissa + 1024;
+  const int power = exponent == 0 ? -8 : exponent - 9;
+  long long mag;
+  if (power >= 0) {
+    mag = significand << power;
+  } else {   // round half away from zero of significand / 2^-power (a non-negative value)
+    const int s = -power;
+    mag = (significand + (1ll << (s - 1))) >> s;
+  }
+  *out = (raw & 0x8000u) ? -mag : mag;
+  return true;
+}
+
+__device__ __forceinline__ long long clip32(__int128 v) {
+  return v > 2147483647 ? 2147483647ll : v < -2147483648ll ? -2147483648ll : (long long)v;
+}
+
+struct Params {
+  const int32_t* x;        // [K] Q16.16
+  const int32_t* qweight;  // [K][W8]
+  const int32_t* qzeros;   // [groups][W8]
+  const uint16_t* scales;  // [groups][N] binary16
+  const uint16_t* bias;    // [N] binary16 or null
+  int32_t* y;              // [N] Q16.16
+  __int128* partial;       // [chunks][N]
+  int* dev_err;
+  int K, N, W8, G, groups, gpc, chunks;
+};
+
+// grid (bands of kThreads words, chunks): exact per-chunk totals of 8 columns per thread
+__global__ void __launch_bounds__(kThreads) q16_partial_kernel(const Params p) {
+  const int w = blockIdx.x * kThreads + threadIdx.x;
+  if (w >= p.W8) return;
+  const int g0 = blockIdx.y * p.gpc, g1 = min(g0 + p.gpc, p.groups);
+  __int128 total[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) total[j] = 0;
+  bool bad = false;
+  for (int g = g0; g < g1; ++g) {
+    const uint32_t zw = (uint32_t)__ldg(p.qzeros + (size_t)g * p.W8 + w);
+    long long s16[8];
+    int z[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      z[j] = (zw >> awq_shift(j)) & 15;
+      const uint16_t h = __ldg(p.scales + (size_t)g * p.N + 8 * w + j);
+      // an AWQ scale must be finite and not negative-nonzero (official_weights.py:526)
+      if (!half_q16(h, &s16[j]) || ((h & 0x8000u) && (h & 0x7FFFu))) {
+        bad = true;
+        s16[j] = 0;
+      }
+    }
+    long long acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const int k1 = min((g + 1) * p.G, p.K);
+    for (int k = g * p.G; k < k1; ++k) {
+      const long long xv = __ldg(p.x + k);
+      const uint32_t qw = (uint32_t)__ldg(p.qweight + (size_t)k * p.W8 + w);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += xv * (long long)((int)((qw >> awq_shift(j)) & 15) - z[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) total[j] += (__int128)acc[j] * s16[j];
+  }
+  if (bad && p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_SCALE);
+  __int128* out = p.partial + (size_t)blockIdx.y * p.N + 8 * w;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) out[j] = total[j];
+}
+
+// one thread per column: chunk totals, bias, round_away(total / 65536), clip32
+__global__ void q16_finish_kernel(const Params p) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= p.N) return;
+  __int128 total = 0;
+  for (int i = 0; i < p.chunks; ++i) total += p.partial[(size_t)i * p.N + c];
+  if (p.bias) {
+    long long b16;
+    if (half_q16(p.bias[c], &b16)) {
+      total += (__int128)clip32(b16) * 65536;
+    } else if (p.dev_err) {
+      atomicOr(p.dev_err, ANVILQ_DEV_ERR_NONFINITE);
+    }
+  }
+  const __int128 mag = total < 0 ? -total : total;
+  const __int128 r = (mag + 32768) >> 16;   // (2|n| + d) / 2d with d = 2^16
+  p.y[c] = (int32_t)clip32(total < 0 ? -r : r);
+}
+
+struct Plan {
+  int groups, gpc, chunks, bands;
+};
+static Plan plan_for(int K, int N, int G) {
+  Plan pl;
+  pl.groups = (K + G - 1) / G;
+  const int want = std::min(pl.groups, kMaxChunks);
+  pl.gpc = (pl.groups + want - 1) / want;
+  pl.chunks = (pl.groups + pl.gpc - 1) / pl.gpc;
+  pl.bands = (N / 8 + kThreads - 1) / kThreads;
+  return pl;
+}
+
+}  // namespace q16
+
+size_t gemm_q16_workspace_bytes(int K, int N, int G) {
+  const q16::Plan pl = q16::plan_for(K, N, G);
+  return (size_t)pl.chunks * N * sizeof(__int128);
+}
+
+int launch_gemm_q16(const int32_t* x, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
+                    const uint16_t* bias, int32_t* y, int M, int K, int N, int G, void* workspace,
+                    size_t workspace_bytes, int* dev_err, cudaStream_t stream) {
+  using namespace q16;
+  const Plan pl = plan_for(K, N, G);
+  if (!workspace || workspace_bytes < gemm_q16_workspace_bytes(K, N, G)) return ANVILQ_EWORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 15u) != 0) return ANVILQ_EALIGN;
+  Params p;
+  p.qweight = qweight;
+  p.qzeros = qzeros;
+  p.scales = scales;
+  p.bias = bias;
+  p.partial = reinterpret_cast<__int128*>(workspace);
+  p.dev_err = dev_err;
+  p.K = K;
+  p.N = N;
+  p.W8 = N / 8;
+  p.G = G;
+  p.groups = pl.groups;
+  p.gpc = pl.gpc;
+  p.chunks = pl.chunks;
+  for (int m = 0; m < M; ++m) {   // one token row per pass (the reference's linear is per token)
+    p.x = x + (size_t)m * K;
+    p.y = y + (size_t)m * N;
+    q16_partial_kernel<<<dim3(pl.bands, pl.chunks), kThreads, 0, stream>>>(p);
+    q16_finish_kernel<<<(N + 127) / 128, 128, 0, stream>>>(p);
+  }
+  return cudaGetLastError() == cudaSuccess ? ANVILQ_OK : ANVILQ_ECUDA;
+}
+
+}  // namespace anvilq
+
+using namespace anvilq;
+
+extern "C" {
+
+size_t anvilq_w4a16_gemm_q16_workspace_size(int M, int K, int N, int G) {
+  if (M < 1 || K < 1 || N < 8 || N % 8 || G < 1) return 0;
+  return gemm_q16_workspace_bytes(K, N, G);
+}
+
+int anvilq_w4a16_gemm_q16(const int32_t* x_q16, const int32_t* qweight, const int32_t* qzeros,
+                          const uint16_t* scales, const uint16_t* bias, int32_t* y_q16, int M, int K, int N, int G,
+                          void* workspace, size_t workspace_bytes, int* dev_err, anvilq_stream_t stream) {
+  if (!x_q16 || !qweight || !qzeros || !scales || !y_q16) return ANVILQ_EINVAL;
+  if (M < 1 || K < 1 || N < 8 || N % 8 || G < 1) return ANVILQ_EINVAL;
+  return launch_gemm_q16(x_q16, qweight, qzeros, scales, bias, y_q16, M, K, N, G, workspace, workspace_bytes,
+                         dev_err, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -40,4 +40,10 @@ int launch_verify_tc(const uint16_t* x, const int32_t* qweight, const int32_t* p
 size_t tc_pack_bytes(int K, int N);
 int launch_tc_pack(const int32_t* qweight, int32_t* packed, int K, int N, cudaStream_t stream);
 
+// Bit-accurate Q16.16 integer GEMV (gemv_q16.cu).
+size_t gemm_q16_workspace_bytes(int K, int N, int G);
+int launch_gemm_q16(const int32_t* x, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
+                    const uint16_t* bias, int32_t* y, int M, int K, int N, int G, void* workspace,
+                    size_t workspace_bytes, int* dev_err, cudaStream_t stream);
+
 }  // namespace anvilq

@@ -55,6 +55,10 @@ def raise_device_errors(device=None):
             what.append("sequence length outside [1, Tmax]")
         if value & 4:
             what.append("bounded wait expired inside a kernel")
+        if value & 8:
+            what.append("token id outside [0, V)")
+        if value & 16:
+            what.append("nonfinite binary16 parameter (bias)")
         raise _lib.AnvilqError(f"device error bits 0x{value:x}: " + "; ".join(what))
 
 
@@ -141,6 +145,32 @@ def verify_gemm(x, qweight, qzeros, scales, bias=None, group: int = 128, out=Non
     want the tensor-core path at every M.  Needs group 128, K % 128 == 0, N % 32 == 0.
     """
     return gemm(x, qweight, qzeros, scales, bias, group, out, dev_err, tensor_cores=True)
+
+
+def gemm_q16(x_q16, qweight, qzeros, scales, bias=None, group: int = 128, out=None, dev_err=None):
+    """Integer golden projection on the GPU: Q16.16 int32 x [M, K] -> Q16.16 int32 y [M, N].
+
+    Bit-identical to the reference's integer model (anvil-q1/tests/official_weights.py:592-612):
+    exact integer sum of x * (q - z) * round_away(scale * 2^16), plus
+    clip32(round_away(bias * 2^16)) * 65536, then clip32(round_away(total / 65536)).
+    """
+    K, N = _check_awq(qweight, qzeros, scales, group)
+    squeeze = x_q16.dim() == 1
+    x2 = x_q16.unsqueeze(0) if squeeze else x_q16
+    if x2.dtype != torch.int32 or x2.dim() != 2 or x2.shape[1] != K or not x2.is_contiguous():
+        raise ValueError(f"x_q16 must be contiguous int32 [M, {K}]")
+    M = x2.shape[0]
+    if bias is not None and (bias.dtype != torch.float16 or bias.numel() != N):
+        raise ValueError("bias must be float16 [N]")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.int32, device=x2.device)
+    lib = _lib.load()
+    ws = workspace(x2.device, lib.anvilq_w4a16_gemm_q16_workspace_size(M, K, N, group))
+    err = device_error_word(x2.device) if dev_err is None else dev_err
+    _lib.check(lib.anvilq_w4a16_gemm_q16(_ptr(x2), _ptr(qweight), _ptr(qzeros), _ptr(scales), _ptr(bias),
+                                         _ptr(out), M, K, N, group, _ptr(ws), ws.numel(), _ptr(err),
+                                         _stream_ptr(x2.device)), "anvilq_w4a16_gemm_q16")
+    return out.view(N) if squeeze else out
 
 
 def tc_pack(qweight, group: int = 128):

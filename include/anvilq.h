@@ -51,6 +51,7 @@ typedef struct CUstream_st* anvilq_stream_t; /* same type as cudaStream_t */
 #define ANVILQ_DEV_ERR_SEQLEN 2  /* a sequence length outside [1, Tmax] */
 #define ANVILQ_DEV_ERR_TIMEOUT 4 /* a bounded wait inside a kernel expired */
 #define ANVILQ_DEV_ERR_TOKEN 8   /* a token id outside [0, V) */
+#define ANVILQ_DEV_ERR_NONFINITE 16 /* a binary16 parameter (bias) was Inf or NaN */
 
 /* Workspace layout shared by every entry point that takes one: the first
  * ANVILQ_WORKSPACE_COUNTER_BYTES hold arrival counters that must be zero
@@ -177,6 +178,24 @@ int anvilq_w4a16_gemv_fused(const void* x, int x_mode, const uint16_t* gamma, fl
 int anvilq_w4a16_gemm_exact(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
                             const uint16_t* scales, const uint16_t* bias, float* y32,
                             int M, int K, int N, int G, int* dev_err, anvilq_stream_t stream);
+
+/* Bit-accurate Q16.16 integer W4A16 GEMV: the integer golden model's projection
+ * (anvil-q1/tests/official_weights.py:592-612) and the RTL datapath it
+ * specifies (anvil-q1/design/SPEC.md:151-158):
+ *   total = sum_k x[k] * (q - z) * round_away(scale * 2^16)   (exact integer)
+ *   total += clip32(round_away(bias * 2^16)) * 65536           (bias may be NULL)
+ *   y = clip32(round_away(total / 65536))
+ * x_q16 int32 [M][K] and y_q16 int32 [M][N] are signed Q16.16; weights in the
+ * AWQ layout of anvilq_w4a16_gemm, any G >= 1 (a partial last group allowed).
+ * Results are bit-identical to the reference for every input.  Invalid scales
+ * set ANVILQ_DEV_ERR_SCALE, a nonfinite bias ANVILQ_DEV_ERR_NONFINITE.
+ * workspace: anvilq_w4a16_gemm_q16_workspace_size bytes, 16-byte aligned (need
+ * not be zeroed). */
+size_t anvilq_w4a16_gemm_q16_workspace_size(int M, int K, int N, int G);
+int anvilq_w4a16_gemm_q16(const int32_t* x_q16, const int32_t* qweight, const int32_t* qzeros,
+                          const uint16_t* scales, const uint16_t* bias, int32_t* y_q16,
+                          int M, int K, int N, int G, void* workspace, size_t workspace_bytes,
+                          int* dev_err, anvilq_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * AWQ dequantisation of a whole [K][N] matrix, using the same in-register
