@@ -18,6 +18,11 @@ inside every step, and the host waiting for it.
 proj05b / proj7b: one step = the W4A16 GEMV over every projection of a decode
 step (Qwen2.5-0.5B or Llama-7B-class shapes), value in GB/s.
 
+tp70b: one step = the three 70B-class layer projections, each column-split over
+the N GPUs (strong scaling) and all-gathered over NCCL, as one CUDA graph;
+value = full-layer algorithmic GB/s over the max-over-ranks time; --m sets the
+token rows (1 for the GEMV, 16/64 for the verify GEMM).
+
 With N GPUs each rank runs an independent replica (weak scaling, no collective).
 
 --impl reference times the CPU restatement of the reference's golden model on
@@ -53,6 +58,10 @@ WORKLOADS = {
     "proj7b": dict(name="Llama-7B-class decode-step W4A16 projections: 32 layers x (q,k,v,o 4096x4096, "
                         "gate,up 4096x11008, down 11008x4096), G128, M=1",
                    layers=32, projections="LLAMA7B_PROJECTIONS"),
+    "tp70b": dict(name="70B-class W4A16 AWQ layer projections (K,N) in (8192,8192), (8192,28672), (28672,8192), "
+                       "G128, column-split over the GPUs (rank r holds columns [rN/W, (r+1)N/W)), y all-gathered "
+                       "over NCCL after every projection",
+                  shapes=((8192, 8192), (8192, 28672), (28672, 8192))),
 }
 
 
@@ -351,7 +360,8 @@ def reference_arm(args, world, rank):
         return decode_reference_arm(args, world, rank)
     from anvilq_b200 import stream as st
     wl = WORKLOADS[args.workload]
-    projections = getattr(st, wl["projections"])
+    projections = (tuple((K, N, False) for K, N in wl["shapes"]) if "shapes" in wl
+                   else getattr(st, wl["projections"]))
     if rank != 0:
         return 0
     sys.path.insert(0, str(REPO / "oracle"))
@@ -369,8 +379,8 @@ def reference_arm(args, world, rank):
         total_b += b
         total_t += dt
     value = total_b / total_t / 1e9
-    sample = (f"oracle/awq_oracle.c FP32Model.linear restatement, one layer's 7 projections, all K rows x "
-              f"first {frac:.4f} of the columns per step, {threads} threads")
+    sample = (f"oracle/awq_oracle.c FP32Model.linear restatement, one layer's {len(projections)} projections, "
+              f"all K rows x first {frac:.4f} of the columns per step, {threads} threads")
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_t / args.steps * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -462,6 +472,136 @@ def anvilq_arm(args, world, rank, local):
     return 0
 
 
+# ------------------------------------------------------------ tp70b
+def tp_arm(args, world, rank, local):
+    """Column-split 70B-class projections: per step, each rank's GEMM on its N/W slice followed by
+    an NCCL all-gather of y, for the three layer shapes, as one CUDA graph (compute + collectives)."""
+    import torch
+    import torch.distributed as dist
+    from anvilq_b200 import ops, synthetic
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    wl = WORKLOADS[args.workload]
+    M = args.m
+    peak, peak_kind = load_peaks()
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    layers = []
+    full_bytes = 0
+    shard_bytes = 0
+    for K, N in wl["shapes"]:
+        n = N // world
+        qw = torch.randint(-2**31, 2**31 - 1, (K, n // 8), dtype=torch.int32, device=dev, generator=g)
+        qz = torch.randint(-2**31, 2**31 - 1, (K // 128, n // 8), dtype=torch.int32, device=dev, generator=g)
+        sc = (torch.randn(K // 128, n, device=dev, generator=g).abs() * 0.01 + 1e-3).half()
+        x = torch.randn(M, K, device=dev, generator=torch.Generator(device=dev).manual_seed(7)).half()
+        y = torch.empty(M, n, dtype=torch.float16, device=dev)
+        yg = torch.empty(world * M, n, dtype=torch.float16, device=dev)
+        layers.append((x, qw, qz, sc, y, yg, K, N))
+        full_bytes += synthetic.gemv_bytes(M, K, N)
+        shard_bytes += synthetic.gemv_bytes(M, K, n)
+    stream = torch.cuda.Stream(dev)
+
+    def step(gather=True):
+        for x, qw, qz, sc, y, yg, K, N in layers:
+            ops.gemm(x, qw, qz, sc, None, 128, out=y)
+            if gather and world > 1:
+                dist.all_gather_into_tensor(yg, y)
+
+    def capture(gather):
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                step(gather)
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                step(gather)
+        return graph
+
+    g_full, g_comp = capture(True), capture(False)
+
+    def timed(graph):
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    with torch.cuda.stream(stream):
+        with ClockSampler(dev.index) as clocks:
+            ms = timed(g_full)
+        ms_comp = timed(g_comp)
+        # e2e: activations from pinned host memory in, gathered outputs back to the host, every step
+        x_host = [torch.randn(M, l[6]).half().pin_memory() for l in layers]
+        y_host = [torch.empty(M, l[7], dtype=torch.float16).pin_memory() for l in layers]
+        h2d = sum(t.numel() * 2 for t in x_host)
+        d2h = sum(t.numel() * 2 for t in y_host)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            for (x, qw, qz, sc, y, yg, K, N), xh, yh in zip(layers, x_host, y_host):
+                x.copy_(xh, non_blocking=True)
+                ops.gemm(x, qw, qz, sc, None, 128, out=y)
+                if world > 1:
+                    dist.all_gather_into_tensor(yg, y)
+                    yh.copy_(yg.view(world, M, -1).permute(1, 0, 2).reshape(M, -1), non_blocking=True)
+                else:
+                    yh.copy_(y, non_blocking=True)
+            stream.synchronize()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms_e2e = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms_e2e], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_e2e = float(t.item())
+    ops.raise_device_errors(dev)
+    del g_full, g_comp
+    launches = 3
+    value = full_bytes * args.steps / (ms / 1e3) / 1e9
+    per_launch = ms_comp / args.steps / launches
+    achieved = shard_bytes / launches / (per_launch / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16 activations x int4 weights, fp32 accumulate",
+        "data": "synthetic (seeded; x~N(0,1), u4 uniform, scales |N(0,1)|*0.01+1e-3)",
+        "config": {"workload": wl["name"], "M": M, "group": 128, "full_bytes_per_step": full_bytes,
+                   "shard_bytes_per_rank": shard_bytes, "parallelism": f"tp{world} (column split)",
+                   "graph": "one CUDA graph per step: 3 GEMMs + 3 NCCL all-gathers",
+                   "l2": "weights larger than L2 (no flush)",
+                   "compute_only_ms_per_step": round(ms_comp / args.steps, 5)},
+        "roofline": {"bound": "hbm", "kernel": "gemv_tma_kernel" if M == 1 else "verify_tc_kernel",
+                     "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
+                     "launch_avg_us": round(per_launch * 1e3, 4)},
+        "e2e": {"value": round(full_bytes * args.steps / (ms_e2e / 1e3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(ms_e2e / args.steps, 5)},
+        "gpu_launches": launches * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -470,6 +610,7 @@ def main(argv=None):
     ap.add_argument("--impl", choices=("anvilq", "reference"), default="anvilq")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode05b")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--m", type=int, default=1, help="token rows per projection (tp70b)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -481,6 +622,8 @@ def main(argv=None):
     try:
         if args.workload == "decode05b":
             return decode_arm(args, world, rank, local)
+        if args.workload == "tp70b":
+            return tp_arm(args, world, rank, local)
         return anvilq_arm(args, world, rank, local)
     finally:
         if world > 1:
