@@ -145,7 +145,9 @@ static Plan plan_for(int K, int N, int G) {
 
 size_t gemm_q16_workspace_bytes(int K, int N, int G) {
   const q16::Plan pl = q16::plan_for(K, N, G);
-  return (size_t)pl.chunks * N * sizeof(__int128);
+  // the first ANVILQ_WORKSPACE_COUNTER_BYTES belong to the arrival counters of
+  // the other kernels sharing a workspace and are left untouched
+  return ANVILQ_WORKSPACE_COUNTER_BYTES + (size_t)pl.chunks * N * sizeof(__int128);
 }
 
 int launch_gemm_q16(const int32_t* x, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
@@ -160,7 +162,7 @@ int launch_gemm_q16(const int32_t* x, const int32_t* qweight, const int32_t* qze
   p.qzeros = qzeros;
   p.scales = scales;
   p.bias = bias;
-  p.partial = reinterpret_cast<__int128*>(workspace);
+  p.partial = reinterpret_cast<__int128*>(reinterpret_cast<char*>(workspace) + ANVILQ_WORKSPACE_COUNTER_BYTES);
   p.dev_err = dev_err;
   p.K = K;
   p.N = N;

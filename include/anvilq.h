@@ -189,8 +189,9 @@ int anvilq_w4a16_gemm_exact(const uint16_t* x, const int32_t* qweight, const int
  * AWQ layout of anvilq_w4a16_gemm, any G >= 1 (a partial last group allowed).
  * Results are bit-identical to the reference for every input.  Invalid scales
  * set ANVILQ_DEV_ERR_SCALE, a nonfinite bias ANVILQ_DEV_ERR_NONFINITE.
- * workspace: anvilq_w4a16_gemm_q16_workspace_size bytes, 16-byte aligned (need
- * not be zeroed). */
+ * workspace: anvilq_w4a16_gemm_q16_workspace_size bytes, 16-byte aligned, with
+ * the shared layout of ANVILQ_WORKSPACE_COUNTER_BYTES (the counter region is
+ * neither read nor written; the scratch after it need not be zeroed). */
 size_t anvilq_w4a16_gemm_q16_workspace_size(int M, int K, int N, int G);
 int anvilq_w4a16_gemm_q16(const int32_t* x_q16, const int32_t* qweight, const int32_t* qzeros,
                           const uint16_t* scales, const uint16_t* bias, int32_t* y_q16,

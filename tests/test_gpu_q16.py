@@ -106,3 +106,15 @@ def test_invalid_parameters_fail(dev):
                  128)
     with pytest.raises(AnvilqError):
         ops.raise_device_errors(dev)
+
+
+def test_shared_workspace_counters_stay_zero(dev):
+    """The Q16 kernel shares ops.workspace with the split-K kernels, whose arrival
+    counters (the first ANVILQ_WORKSPACE_COUNTER_BYTES) must stay zero between calls."""
+    from anvilq_b200 import ops
+    _, layer = synthetic.gemv_case(1, 4096, 4096, 128, 3)
+    x = T(_q16_activations(2, 4096, 4), dev)
+    ops.gemm_q16(x, T(layer.qweight, dev), T(layer.qzeros, dev), T(layer.scales, dev), None, 128)
+    ops.raise_device_errors(dev)
+    ws = ops.workspace(dev, 1)
+    assert int(ws[:65536].count_nonzero()) == 0
