@@ -20,7 +20,7 @@ step (Qwen2.5-0.5B or Llama-7B-class shapes), value in GB/s.
 
 tp70b: one step = the three 70B-class layer projections, each column-split over
 the N GPUs (strong scaling) and all-gathered over NCCL, as one CUDA graph;
-value = full-layer algorithmic GB/s over the max-over-ranks time; --m sets the
+value = full-layer algorithmic GB/s over the max-over-ranks time; --tokens sets the
 token rows (1 for the GEMV, 16/64 for the verify GEMM).
 
 With N GPUs each rank runs an independent replica (weak scaling, no collective).
@@ -482,7 +482,7 @@ def tp_arm(args, world, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     wl = WORKLOADS[args.workload]
-    M = args.m
+    M = args.tokens
     peak, peak_kind = load_peaks()
     g = torch.Generator(device=dev)
     g.manual_seed(1000 + rank)
@@ -610,7 +610,7 @@ def main(argv=None):
     ap.add_argument("--impl", choices=("anvilq", "reference"), default="anvilq")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode05b")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--m", type=int, default=1, help="token rows per projection (tp70b)")
+    ap.add_argument("--tokens", type=int, default=1, help="token rows per projection (tp70b)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
