@@ -9,32 +9,49 @@
 // form (running max, running sum, rescale by exp(m_old - m_new)) follows the
 // tiled contract of anvil-q1-ht3/design/SPEC.md:545-556.
 //
-// Design (one CTA = one (sequence, kv head, KV split); 4 warps):
+// Design (B200, latency first: a decode step calls this once per layer with
+// a few kv heads, so the critical path, not bandwidth, sets the time):
+//   * Grid (CTAs per pair, Hkv, B); a pair = (sequence, kv head).  The CTAs of
+//     a pair split its live tiles into contiguous ranges; up to 8 of them form
+//     one thread-block cluster and merge their partial softmax states through
+//     distributed shared memory (one cluster barrier, one DSMEM round trip),
+//     so a short context finishes with no global-memory handshake at all.
+//     Longer contexts give a pair several clusters; each writes one merged
+//     partial, and the cluster CTA that arrives last at the pair's ticket
+//     merges those partials in cluster order (deterministic, no spin-wait),
+//     loading every partial of its elements in one L2 round trip.
 //   * The query heads of a GQA group (<= 8) share every K/V row, so each row is
-//     read from HBM once per group.  Rows are moved by the TMA engine
-//     (cp.async.bulk, one 128/256-byte row per lane, 32 rows = one 16-token K
-//     tile + V tile per instruction round) into a per-warp ring of 4 stages
-//     guarded by mbarriers; each warp streams its own tiles, so no inter-warp
-//     handshake sits on the critical path.  Rows are padded by 16 bytes so the
-//     fragment loads below are bank-conflict free.
+//     read from HBM once per group.  A 16-token K tile and V tile arrive as
+//     TMA boxes of a 4-D tensor map over the cache (D, Hkv, Tmax, B): one box
+//     per 64 dims of each, 128-byte swizzled, into a per-warp ring guarded by
+//     mbarriers; each of the 8 warps streams its own tiles, so no inter-warp
+//     handshake sits on the critical path.  The fragment loads below undo the
+//     swizzle (16-byte chunk c of row r sits at c ^ (r % 8)).  Cache rows past
+//     the live length inside the last tile are not part of the sequence: their
+//     K scores are masked and their V rows zeroed in shared memory, so whatever
+//     they hold cannot reach the output.
 //   * S = Q K^T on the tensor cores (mma.m16n8k16, fp16 in, fp32 accumulate):
 //     the group's query heads are the 16-row A operand (rows >= group size are
 //     zero), 8 tokens per n-tile.  The S accumulator layout is exactly the B
 //     operand layout of O^T += V^T P^T, so P never leaves registers; V^T comes
 //     from ldmatrix.trans.
-//   * Online softmax in the log2 domain, per warp; warps are merged in shared
-//     memory, KV splits through a caller-provided workspace: the CTA that
-//     arrives last at a (sequence, kv head) ticket merges the splits in split
-//     order (deterministic, no spin-wait) and writes fp16 output.
+//   * Online softmax in the log2 domain, per warp; the 8 warps are merged in
+//     shared memory, then the cluster, then (long contexts) the clusters.
 //   * Every mbarrier wait is bounded (about one second of %globaltimer); on
 //     expiry the kernel sets ANVILQ_DEV_ERR_TIMEOUT, stops using its tiles and
-//     waits, again bounded, for its own copies before it exits.
-#include <cuda_runtime.h>
+//     waits, again bounded, for its own copies before it exits.  The cluster
+//     barriers are reached by every thread of every CTA on every path (there is
+//     no return before them), and a cluster's CTAs are co-scheduled by the
+//     hardware, so they always complete.
+#include <cuda.h>
 #include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 #include <stdint.h>
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <mutex>
 
 #include "../../include/anvilq.h"
@@ -42,12 +59,12 @@
 namespace anvilq {
 namespace attn {
 
-constexpr int kWarps = 4;
+constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTile = 16;          // tokens per tile
-constexpr int kStages = 4;         // ring depth per warp
 constexpr int kMaxGroup = 8;       // query heads per kv head handled by one CTA
-constexpr int kMaxSplits = 32;     // KV splits per (sequence, kv head)
+constexpr int kMaxCluster = 8;     // CTAs of a pair merged in one cluster (portable size)
+constexpr int kMaxClusters = 16;   // clusters per pair
 constexpr unsigned long long kWaitLimitNs = 1000000000ull;
 
 struct Params {
@@ -56,24 +73,38 @@ struct Params {
   const __half* v;
   const int* seqlens;   // [B]
   __half* out;          // [B][Hq][D]
-  float* partials;      // [B][Hkv][splits][group][D + 2]
+  float* partials;      // [B][Hkv][clusters][group][D + 4]: o[D], max, sum, pad
   int* tickets;         // [B][Hkv]
   int* dev_err;
-  int Hq, Hkv, Tmax, group, splits, tiles_per_split;
-  float scale_log2;     // softmax scale * log2(e)
+  int Hq, Hkv, Tmax, group;
+  int cluster, clusters;   // CTAs per cluster, clusters per pair (gridDim.x = their product)
+  float scale_log2;        // softmax scale * log2(e)
 };
 
 template <int D>
 struct Layout {
-  static constexpr int kRowBytes = D * 2 + 16;                 // padded row
-  static constexpr int kStageBytes = 2 * kTile * kRowBytes;    // K tile + V tile
+  static constexpr int kStages = 2;                            // ring depth per warp
+  static constexpr int kHalves = D / 64;                       // 128-byte boxes per row
+  static constexpr int kBoxBytes = kTile * 128;                // 16 rows x 64 dims, swizzled
+  static constexpr int kTileBytes = kHalves * kBoxBytes;       // [half][row][128 B]
+  static constexpr int kStageBytes = 2 * kTileBytes;           // K tile + V tile
   static constexpr int kWarpBytes = kStages * kStageBytes;
   static constexpr int kRingBytes = kWarps * kWarpBytes;
+  static constexpr int kRow = D + 2;                           // one head's state: o[D], max, sum
+  static constexpr int kStateBytes = kMaxGroup * kRow * 4;     // a warp's or a CTA's state
   static constexpr int kBarOffset = kRingBytes;                // kWarps * kStages mbarriers
-  static constexpr int kCombOffset = kBarOffset + kWarps * kStages * 8;
-  static constexpr int kCombBytes = kWarps * kMaxGroup * (D + 2) * 4;
-  static_assert(kCombBytes >= (3 * kMaxSplits * kMaxGroup + kMaxGroup) * 4, "split merge fits the warp-merge area");
-  static constexpr int kTotal = kCombOffset + kCombBytes;
+  static constexpr int kAuxOffset = kBarOffset + kWarps * kStages * 8;
+  static constexpr int kAuxBytes = (kMaxGroup * kWarps + 2 * kMaxGroup) * 4;   // warp weights, head max/sum
+  static constexpr int kSlotOffset = kAuxOffset + kAuxBytes;   // rank 0: one state per CTA of the cluster
+  static constexpr int kSlotBytes = kMaxCluster * kStateBytes;
+  static constexpr int kTotal = kSlotOffset + kSlotBytes + 1024;   // + slack to align the ring to 1024
+  static_assert(kBoxBytes % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
+  static_assert(kWarpBytes >= kStateBytes, "a warp's state fits its idle ring");
+  static_assert(kTotal <= 227 * 1024, "fits one SM's shared memory");
+  // byte offset of the 16-byte chunk c (of 8 dims) of row r inside a tile
+  __device__ static __forceinline__ int chunk(int r, int c) {
+    return (c >> 3) * kBoxBytes + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+  }
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -107,14 +138,34 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
     if ((i & 63u) == 63u && globaltimer() - t0 > kWaitLimitNs) return false;
   }
 }
-__device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+__device__ __forceinline__ void tma_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                       uint32_t bar) {
   asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-      "l"(src), "r"(bytes), "r"(bar)
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(dst),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
       : "memory");
 }
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// cluster barrier halves: arrive.release orders this thread's earlier
+// shared-memory writes (remote ones included) before the wait.acquire of the
+// others; a thread may exit after arriving
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+// address of the same shared-memory variable in CTA `rank` of this cluster
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_dsmem(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 __device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -142,45 +193,63 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(kThreads) gqa_decode_kernel(const Params p) {
+__global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
+    gqa_decode_kernel(const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv, const Params p) {
   using L = Layout<D>;
   constexpr int KS = D / 16;   // k-steps of QK, m-tiles of PV
-  extern __shared__ __align__(128) unsigned char smem[];
+  constexpr int kStages = L::kStages;
+  constexpr int R = L::kRow;
+  constexpr int RG = D + 4;    // a head's row in the global partials (16-byte multiple)
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ int s_flag;
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int C = p.cluster, rank = split % C, cl = split / C;
   const int seqlen = p.seqlens[b];
   const bool bad_len = seqlen < 1 || seqlen > p.Tmax;
   const int ntiles = bad_len ? 0 : (seqlen + kTile - 1) / kTile;
-  const int tb = split * p.tiles_per_split;
-  const int te = min(ntiles, tb + p.tiles_per_split);
+  // the live sequence is spread over all CTAs of the pair (the grid is sized for Tmax)
+  const int per_split = (ntiles + gridDim.x - 1) / gridDim.x;
+  const int tb = split * per_split;
+  const int te = min(ntiles, tb + per_split);
   // warp-local tiles: tb + warp + kWarps * j
   const int my_tiles = te > tb + warp ? (te - tb - warp + kWarps - 1) / kWarps : 0;
 
   unsigned char* ring = smem + warp * L::kWarpBytes;
   const uint32_t bar0 = smem_u32(smem + L::kBarOffset + warp * kStages * 8);
-  if (lane == 0)
+  if (lane == 0) {
     for (int s = 0; s < kStages; ++s) mbar_init(bar0 + 8 * s, 1);
+    if (warp == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&mk) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&mv) : "memory");
+    }
+  }
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   __syncwarp();
-
-  const size_t row_stride = (size_t)p.Hkv * D;   // elements between consecutive tokens
-  const __half* kbase = p.k + ((size_t)b * p.Tmax * p.Hkv + h) * D;
-  const __half* vbase = p.v + ((size_t)b * p.Tmax * p.Hkv + h) * D;
 
   auto issue = [&](int j) {   // tile j of this warp into stage j % kStages
     const int st = j % kStages;
     const uint32_t bar = bar0 + 8 * st;
-    if (lane == 0) mbar_expect_tx(bar, 2 * kTile * D * 2);
-    __syncwarp();
+    // the stage may hold zeros written through the generic proxy (tail rows)
     fence_proxy_async();
-    const int tok = min((tb + warp + kWarps * j) * kTile + (lane % kTile), seqlen - 1);
-    const __half* src = (lane < kTile ? kbase : vbase) + (size_t)tok * row_stride;
-    const uint32_t dst = smem_u32(ring + st * L::kStageBytes + (lane / kTile) * kTile * L::kRowBytes +
-                                  (lane % kTile) * L::kRowBytes);
-    bulk_copy_g2s(dst, src, D * 2, bar);
+    __syncwarp();
+    if (lane == 0) {
+      mbar_expect_tx(bar, 2 * kTile * D * 2);
+      const int t0 = (tb + warp + kWarps * j) * kTile;
+      const uint32_t kd = smem_u32(ring + st * L::kStageBytes);
+#pragma unroll
+      for (int hf = 0; hf < L::kHalves; ++hf) {
+        tma_4d(kd + hf * L::kBoxBytes, &mk, 64 * hf, h, t0, b, bar);
+        tma_4d(kd + L::kTileBytes + hf * L::kBoxBytes, &mv, 64 * hf, h, t0, b, bar);
+      }
+    }
+    __syncwarp();
   };
+
+  int issued = 0;
+  for (; issued < min(kStages - 1, my_tiles); ++issued) issue(issued);
 
   // Q as the A operand: row g = query head of the group (zero beyond the group).
   const int g = lane / 4;
@@ -200,9 +269,7 @@ __global__ void __launch_bounds__(kThreads) gqa_decode_kernel(const Params p) {
   for (int mt = 0; mt < KS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.0f;
   float m_run = -INFINITY, l_run = 0.0f;
   bool ok = true;
-  int issued = 0;
 
-  for (; issued < min(kStages - 1, my_tiles); ++issued) issue(issued);
   for (int j = 0; j < my_tiles && ok; ++j) {
     if (issued < my_tiles) issue(issued++);
     const int st = j % kStages;
@@ -213,8 +280,17 @@ __global__ void __launch_bounds__(kThreads) gqa_decode_kernel(const Params p) {
       break;
     }
     const unsigned char* kt = ring + st * L::kStageBytes;
-    const unsigned char* vt = kt + kTile * L::kRowBytes;
+    const unsigned char* vt = kt + L::kTileBytes;
     const int t0 = (tb + warp + kWarps * j) * kTile;
+    if (t0 + kTile > seqlen) {
+      // rows past the sequence: zero their V (scores are masked below)
+      unsigned char* vz = ring + st * L::kStageBytes + L::kTileBytes;
+      for (int e = lane; e < kTile * L::kHalves * 8; e += 32) {
+        const int r = e / (L::kHalves * 8), c = e % (L::kHalves * 8);
+        if (t0 + r >= seqlen) *reinterpret_cast<uint4*>(vz + L::chunk(r, c)) = make_uint4(0, 0, 0, 0);
+      }
+      __syncwarp();
+    }
 
     // S = Q K^T for tokens t0..t0+15 (two n-tiles of 8)
     float s[2][4];
@@ -224,7 +300,7 @@ __global__ void __launch_bounds__(kThreads) gqa_decode_kernel(const Params p) {
 #pragma unroll
       for (int ks = 0; ks < KS; ks += 2) {
         const int mj = lane / 8, r = lane % 8;
-        const uint32_t addr = smem_u32(kt + (nt * 8 + r) * L::kRowBytes + (16 * (ks + mj / 2) + 8 * (mj % 2)) * 2);
+        const uint32_t addr = smem_u32(kt + L::chunk(nt * 8 + r, 2 * (ks + mj / 2) + (mj % 2)));
         uint32_t b0, b1, b2, b3;
         ldmatrix_x4(addr, b0, b1, b2, b3);
         mma16816(s[nt], qa[ks][0], 0u, qa[ks][1], 0u, b0, b1);
@@ -261,7 +337,7 @@ __global__ void __launch_bounds__(kThreads) gqa_decode_kernel(const Params p) {
       o[mt][2] *= alpha_a;
       o[mt][3] *= alpha_b;
       const int mj = lane / 8, r = lane % 8;
-      const uint32_t addr = smem_u32(vt + (r + 8 * (mj / 2)) * L::kRowBytes + (16 * mt + 8 * (mj % 2)) * 2);
+      const uint32_t addr = smem_u32(vt + L::chunk(r + 8 * (mj / 2), 2 * mt + (mj % 2)));
       uint32_t a0, a1, a2, a3;
       ldmatrix_x4_trans(addr, a0, a1, a2, a3);
       mma16816(o[mt], a0, a1, a2, a3, pb0, pb1);
@@ -276,9 +352,8 @@ __global__ void __launch_bounds__(kThreads) gqa_decode_kernel(const Params p) {
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
 
-  // ---- merge the warps (shared memory) ----
-  float* comb = reinterpret_cast<float*>(smem + L::kCombOffset);   // [warp][head][D + 2]
-  float* mine = comb + (size_t)warp * kMaxGroup * (D + 2);
+  // ---- merge the warps: each warp's state goes to its own ring, idle now ----
+  float* mine = reinterpret_cast<float*>(ring);   // [head][R]
   if (!ok) {
     m_run = -INFINITY;
     l_run = 0.0f;
@@ -286,135 +361,237 @@ __global__ void __launch_bounds__(kThreads) gqa_decode_kernel(const Params p) {
 #pragma unroll
   for (int mt = 0; mt < KS; ++mt) {
     const int d = 16 * mt + lane / 4, hh = 2 * (lane % 4);
-    mine[hh * (D + 2) + d] = ok ? o[mt][0] : 0.0f;
-    mine[(hh + 1) * (D + 2) + d] = ok ? o[mt][1] : 0.0f;
-    mine[hh * (D + 2) + d + 8] = ok ? o[mt][2] : 0.0f;
-    mine[(hh + 1) * (D + 2) + d + 8] = ok ? o[mt][3] : 0.0f;
+    mine[hh * R + d] = ok ? o[mt][0] : 0.0f;
+    mine[(hh + 1) * R + d] = ok ? o[mt][1] : 0.0f;
+    mine[hh * R + d + 8] = ok ? o[mt][2] : 0.0f;
+    mine[(hh + 1) * R + d + 8] = ok ? o[mt][3] : 0.0f;
   }
   if (lane % 4 == 0) {
-    mine[g * (D + 2) + D] = m_run;
-    mine[g * (D + 2) + D + 1] = l_run;
+    mine[g * R + D] = m_run;
+    mine[g * R + D + 1] = l_run;
   }
   __syncthreads();
+  if (bad_len && threadIdx.x == 0) atomicOr(p.dev_err, ANVILQ_DEV_ERR_SEQLEN);
+
   const int G = p.group;
   const int pair = b * p.Hkv + h;
-  const bool single = p.splits == 1;
-  float* part = p.partials + ((size_t)pair * p.splits + split) * G * (D + 2);
-  for (int e = threadIdx.x; e < G * (D + 2); e += blockDim.x) {
-    const int hh = e / (D + 2), d = e % (D + 2);
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, comb[(w * kMaxGroup + hh) * (D + 2) + D]);
-    float acc = 0.0f, lsum = 0.0f;
-    if (M != -INFINITY) {
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
-        const float* row = comb + (w * kMaxGroup + hh) * (D + 2);
-        const float f = exp2f(row[D] - M);
-        lsum += f * row[D + 1];
-        if (d < D) acc += f * row[d];
-      }
-    }
-    const float val = d < D ? acc : (d == D ? M : lsum);
-    if (single) {
-      if (d < D) {
-        const float out = (lsum > 0.0f) ? acc / lsum : 0.0f;
-        p.out[((size_t)b * p.Hq + (size_t)h * G + hh) * D + d] = __float2half_rn(out);
-      }
-    } else {
-      __stcg(part + e, val);
+  const int S2 = p.clusters;
+  float* fw = reinterpret_cast<float*>(smem + L::kAuxOffset);   // [head][warp] weights
+  float* hstat = fw + kMaxGroup * kWarps;                        // [head]: max, sum
+  // weights of the warps per head: lanes (head, warp) of warps 0-1, tree sums
+  // over the 8 lanes of a head in a fixed order
+  if (threadIdx.x < kMaxGroup * kWarps) {
+    const int hh = threadIdx.x / kWarps, w = threadIdx.x % kWarps;
+    const float* st = reinterpret_cast<const float*>(smem + w * L::kWarpBytes) + hh * R;
+    const float mw = hh < G ? st[D] : -INFINITY;
+    const float lw = hh < G ? st[D + 1] : 0.0f;
+    float M = mw;
+    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 1));
+    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 2));
+    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 4));
+    const float f = M == -INFINITY ? 0.0f : exp2f(mw - M);
+    float ls = f * lw;
+    ls += __shfl_xor_sync(0xffffffffu, ls, 1);
+    ls += __shfl_xor_sync(0xffffffffu, ls, 2);
+    ls += __shfl_xor_sync(0xffffffffu, ls, 4);
+    fw[hh * kWarps + w] = f;
+    if (w == 0) {
+      hstat[2 * hh] = M;
+      hstat[2 * hh + 1] = ls;
     }
   }
-  if (bad_len && threadIdx.x == 0) atomicOr(p.dev_err, ANVILQ_DEV_ERR_SEQLEN);
-  if (single) return;
+  __syncthreads();
 
-  // ---- merge the KV splits: last CTA of the (sequence, kv head) pair ----
+  // The pair's merged state of element (hh, d): with one cluster it is the
+  // output, otherwise this cluster's partial.
+  auto finish = [&](int hh, int d, float M, float lsum, float acc) {
+    if (S2 == 1) {
+      const float out = lsum > 0.0f ? acc / lsum : 0.0f;
+      p.out[((size_t)b * p.Hq + (size_t)h * G + hh) * D + d] = __float2half_rn(out);
+    } else {
+      float* row = p.partials + (((size_t)pair * S2 + cl) * G + hh) * RG;
+      __stcg(row + d, acc);
+      if (d == 0) {
+        __stcg(row + D, M);
+        __stcg(row + D + 1, lsum);
+      }
+    }
+  };
+  // the CTA's state; with a cluster it goes to slot `rank` of the cluster's rank 0
+  const uint32_t slot0 = smem_u32(smem + L::kSlotOffset);
+  const uint32_t my_slot = C > 1 ? dsmem_addr(slot0 + rank * L::kStateBytes, 0) : 0u;
+  for (int e = threadIdx.x; e < G * D; e += kThreads) {
+    const int hh = e / D, d = e % D;
+    float acc = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w)
+      acc += fw[hh * kWarps + w] * reinterpret_cast<const float*>(smem + w * L::kWarpBytes)[hh * R + d];
+    const float M = hstat[2 * hh], lsum = hstat[2 * hh + 1];
+    if (C == 1) {
+      finish(hh, d, M, lsum, acc);
+    } else {
+      st_dsmem(my_slot + (hh * R + d) * 4, acc);
+      if (d == 0) {
+        st_dsmem(my_slot + (hh * R + D) * 4, M);
+        st_dsmem(my_slot + (hh * R + D + 1) * 4, lsum);
+      }
+    }
+  }
+
+  // ---- merge the cluster's CTAs on rank 0, in rank order ----
+  if (C > 1) {
+    cluster_arrive();
+    if (rank != 0) return;   // nothing reads this CTA's shared memory
+    cluster_wait();
+    const float* slots = reinterpret_cast<const float*>(smem + L::kSlotOffset);
+    for (int e = threadIdx.x; e < G * D; e += kThreads) {
+      const int hh = e / D, d = e % D;
+      float M = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < kMaxCluster; ++r)
+        if (r < C) M = fmaxf(M, slots[(r * kMaxGroup + hh) * R + D]);
+      float acc = 0.0f, lsum = 0.0f;
+      if (M != -INFINITY) {
+#pragma unroll
+        for (int r = 0; r < kMaxCluster; ++r) {
+          if (r < C) {
+            const float* row = slots + (r * kMaxGroup + hh) * R;
+            const float f = exp2f(row[D] - M);
+            lsum += f * row[D + 1];
+            acc += f * row[d];
+          }
+        }
+      }
+      finish(hh, d, M, lsum, acc);
+    }
+  }
+  if (S2 == 1) return;
+
+  // ---- merge the pair's clusters: the last rank 0 to arrive, in cluster order ----
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
     const int ticket = atomicAdd(p.tickets + pair, 1);
-    const bool last = ticket == p.splits - 1;
+    const bool last = ticket == S2 - 1;   // one arrival per cluster (its rank 0)
     if (last) p.tickets[pair] = 0;
     s_flag = last;
   }
   __syncthreads();
   if (!s_flag) return;
   __threadfence();
-  const float* parts = p.partials + (size_t)pair * p.splits * G * (D + 2);
-  // split statistics (running max, running sum) of every head, loaded in one
-  // parallel pass into shared memory (reusing the warp-merge area)
-  float* s_stat = comb;   // [splits][G][2]
-  for (int i = threadIdx.x; i < p.splits * G; i += blockDim.x) {
-    const float* row = parts + (size_t)i * (D + 2);
-    s_stat[2 * i] = __ldcg(row + D);
-    s_stat[2 * i + 1] = __ldcg(row + D + 1);
+  const float* parts = p.partials + (size_t)pair * S2 * G * RG;
+  // the clusters' (max, sum) of every head, loaded in one parallel pass into
+  // the slot area (free again: the cluster merge is behind the barriers above)
+  float* gstat = reinterpret_cast<float*>(smem + L::kSlotOffset);   // [cluster][head][2]
+  for (int i = threadIdx.x; i < S2 * G; i += kThreads) {
+    const float* row = parts + (size_t)i * RG;
+    gstat[2 * i] = __ldcg(row + D);
+    gstat[2 * i + 1] = __ldcg(row + D + 1);
   }
   __syncthreads();
-  float* s_w = comb + 2 * kMaxSplits * kMaxGroup;   // [splits][G] merge weights, then [G] 1/L
-  for (int hh = threadIdx.x; hh < G; hh += blockDim.x) {
+  // two consecutive dims of one head per thread; all their partials are loaded
+  // before any is used (one L2 round trip), summed in cluster order
+  for (int e = threadIdx.x; e < G * (D / 2); e += kThreads) {
+    const int hh = e / (D / 2), d2 = 2 * (e % (D / 2));
+    const float* col = parts + (size_t)hh * RG + d2;
+    float2 oc[kMaxClusters];
+#pragma unroll
+    for (int c = 0; c < kMaxClusters; ++c)
+      if (c < S2) oc[c] = __ldcg(reinterpret_cast<const float2*>(col + (size_t)c * G * RG));
     float M = -INFINITY;
-    for (int sp = 0; sp < p.splits; ++sp) M = fmaxf(M, s_stat[2 * (sp * G + hh)]);
+    for (int c = 0; c < S2; ++c) M = fmaxf(M, gstat[2 * (c * G + hh)]);
     float lsum = 0.0f;
-    for (int sp = 0; sp < p.splits; ++sp) {
-      const float f = M == -INFINITY ? 0.0f : exp2f(s_stat[2 * (sp * G + hh)] - M);
-      s_w[sp * G + hh] = f;
-      lsum += f * s_stat[2 * (sp * G + hh) + 1];
-    }
-    s_w[kMaxSplits * G + hh] = lsum > 0.0f ? 1.0f / lsum : 0.0f;
-  }
-  __syncthreads();
-  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
-    const int hh = e / D, d = e % D;
-    float acc = 0.0f;
-    int sp = 0;
-    for (; sp + 8 <= p.splits; sp += 8) {   // independent loads, summed in split order
-      float o[8];
+    float2 acc = make_float2(0.0f, 0.0f);
+    if (M != -INFINITY) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) o[k] = __ldcg(parts + ((size_t)(sp + k) * G + hh) * (D + 2) + d);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) acc += s_w[(sp + k) * G + hh] * o[k];
+      for (int c = 0; c < kMaxClusters; ++c) {
+        if (c < S2) {
+          const float f = exp2f(gstat[2 * (c * G + hh)] - M);
+          lsum += f * gstat[2 * (c * G + hh) + 1];
+          acc.x += f * oc[c].x;
+          acc.y += f * oc[c].y;
+        }
+      }
     }
-    for (; sp < p.splits; ++sp) acc += s_w[sp * G + hh] * __ldcg(parts + ((size_t)sp * G + hh) * (D + 2) + d);
-    p.out[((size_t)b * p.Hq + (size_t)h * G + hh) * D + d] = __float2half_rn(acc * s_w[kMaxSplits * G + hh]);
+    const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
+    *reinterpret_cast<__half2*>(p.out + ((size_t)b * p.Hq + (size_t)h * G + hh) * D + d2) =
+        __floats2half2_rn(acc.x * inv, acc.y * inv);
   }
 }
 
 // ---------------------------------------------------------------------------
 struct Plan {
-  int splits, tiles_per_split;
+  int cluster, clusters;   // CTAs per cluster, clusters per pair
   size_t partial_bytes, bytes;
 };
 
 constexpr int kMaxDevices = 64;
-static int g_sms[kMaxDevices];
+struct DeviceInfo {
+  int sms;
+  int max_clusters[2];   // co-resident clusters of kMaxCluster CTAs, head_dim 64 / 128
+};
+static DeviceInfo g_info[kMaxDevices];
 static std::once_flag g_once[kMaxDevices];
 
-static int sm_count() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
-  std::call_once(g_once[dev], [dev] {
-    cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    cudaFuncSetAttribute(gqa_decode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout<64>::kTotal);
-    cudaFuncSetAttribute(gqa_decode_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout<128>::kTotal);
-    cudaGetLastError();
-  });
-  return g_sms[dev];
+template <int D>
+static int max_active_clusters() {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kMaxCluster * 64);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = Layout<D>::kTotal;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kMaxCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gqa_decode_kernel<D>, &cfg) != cudaSuccess) n = 0;
+  return n;
 }
 
-static Plan plan_for(int B, int Hq, int Hkv, int D, int Tmax, int sms) {
+static const DeviceInfo* device_info() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::call_once(g_once[dev], [dev] {
+    DeviceInfo& in = g_info[dev];
+    cudaDeviceGetAttribute(&in.sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaFuncSetAttribute(gqa_decode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout<64>::kTotal);
+    cudaFuncSetAttribute(gqa_decode_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout<128>::kTotal);
+    in.max_clusters[0] = max_active_clusters<64>();
+    in.max_clusters[1] = max_active_clusters<128>();
+    cudaGetLastError();
+  });
+  return g_info[dev].sms > 0 ? &g_info[dev] : nullptr;
+}
+
+// CTAs per pair: one wave of the GPU, but no more than one tile per warp at
+// the cache's capacity.  Up to 8 of them form a cluster; beyond that, whole
+// clusters, as many as can be resident at once.
+static Plan plan_for(int B, int Hq, int Hkv, int D, int Tmax, const DeviceInfo& dev) {
   Plan pl{};
-  const int tiles = (Tmax + kTile - 1) / kTile;
+  const long long tiles = (Tmax + kTile - 1) / kTile;
   const long long pairs = (long long)B * Hkv;
-  const int ctas_per_sm = D == 64 ? 3 : 1;
-  const long long slots = (long long)std::max(sms, 1) * ctas_per_sm;
-  // enough CTAs for about two full waves, each split holding >= one tile per warp
-  long long want = (2 * slots + pairs - 1) / pairs;
-  const int max_splits = std::max(1, std::min(kMaxSplits, tiles / kWarps));
-  pl.splits = (int)std::max<long long>(1, std::min<long long>(want, max_splits));
-  pl.tiles_per_split = (tiles + pl.splits - 1) / pl.splits;
-  pl.splits = (tiles + pl.tiles_per_split - 1) / pl.tiles_per_split;
+  const int per_sm = D == 64 ? 2 : 1;   // shared memory per CTA: ~83 KB / ~165 KB
+  const long long slots = (long long)dev.sms * per_sm;
+  long long ctas = std::max<long long>(1, std::min<long long>(slots / pairs, (tiles + kWarps - 1) / kWarps));
+  // Tuning aid: ANVILQ_ATTN_SPLITS=n (1..128) forces the CTAs per pair, for sweeps.
+  static const int forced = [] {
+    const char* e = std::getenv("ANVILQ_ATTN_SPLITS");
+    const int v = e ? std::atoi(e) : 0;
+    return v >= 1 && v <= kMaxCluster * kMaxClusters ? v : 0;
+  }();
+  if (forced) ctas = forced;
+  const int max_clusters = dev.max_clusters[D == 64 ? 0 : 1];
+  pl.cluster = 1;
+  if (max_clusters >= 1)
+    while (pl.cluster * 2 <= std::min<long long>(ctas, kMaxCluster)) pl.cluster *= 2;
+  long long clusters = std::min<long long>(kMaxClusters, ctas / pl.cluster);
+  if (pl.cluster == kMaxCluster) clusters = std::min<long long>(clusters, max_clusters / pairs);
+  pl.clusters = (int)std::max<long long>(1, clusters);
   const int group = Hq / Hkv;
-  pl.partial_bytes = pl.splits > 1 ? (size_t)pairs * pl.splits * group * (D + 2) * sizeof(float) : 0;
+  pl.partial_bytes = pl.clusters > 1 ? (size_t)pairs * pl.clusters * group * (D + 4) * sizeof(float) : 0;
   pl.bytes = ANVILQ_WORKSPACE_COUNTER_BYTES + pl.partial_bytes;
   return pl;
 }
@@ -426,6 +603,64 @@ static bool args_ok(int B, int Hq, int Hkv, int D, int Tmax) {
 
 static bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+static std::once_flag g_encode_once;
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    cudaGetLastError();
+  });
+  return g_encode;
+}
+
+// The cache [B][Tmax][Hkv][D] fp16 as a 4-D tensor (D, Hkv, Tmax, B); one box
+// = 64 dims x 1 head x 16 tokens, 128-byte swizzled.
+static bool cache_map(CUtensorMap* map, const void* cache, int B, int Hkv, int D, int Tmax) {
+  auto encode = encode_fn();
+  if (!encode) return false;
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)Hkv, (cuuint64_t)Tmax, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)Hkv * D * 2, (cuuint64_t)Tmax * Hkv * D * 2};
+  const cuuint32_t box[4] = {64, 1, (cuuint32_t)kTile, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(cache), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Tensor maps for both caches, then one launch (clusters of p.cluster CTAs along x).
+template <int D>
+static cudaError_t launch_d(const CUtensorMap& mk, const CUtensorMap& mv, const Params& p, int B, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.cluster * p.clusters, p.Hkv, B);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = Layout<D>::kTotal;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gqa_decode_kernel<D>, mk, mv, p);
+}
+
+static int launch(const Params& p, int B, int D, const void* k_cache, const void* v_cache, cudaStream_t st) {
+  CUtensorMap mk, mv;
+  if (!cache_map(&mk, k_cache, B, p.Hkv, D, p.Tmax) || !cache_map(&mv, v_cache, B, p.Hkv, D, p.Tmax))
+    return ANVILQ_EALIGN;
+  const cudaError_t e = D == 64 ? launch_d<64>(mk, mv, p, B, st) : launch_d<128>(mk, mv, p, B, st);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return ANVILQ_ECUDA;
+  }
+  return cudaGetLastError() == cudaSuccess ? ANVILQ_OK : ANVILQ_ECUDA;
+}
+
 }  // namespace attn
 }  // namespace anvilq
 
@@ -435,9 +670,9 @@ extern "C" {
 
 size_t anvilq_gqa_decode_workspace_size(int B, int Hq, int Hkv, int D, int Tmax) {
   if (!args_ok(B, Hq, Hkv, D, Tmax)) return 0;
-  const int sms = sm_count();
-  if (sms <= 0) return 0;
-  return plan_for(B, Hq, Hkv, D, Tmax, sms).bytes;
+  const DeviceInfo* dev = device_info();
+  if (!dev) return 0;
+  return plan_for(B, Hq, Hkv, D, Tmax, *dev).bytes;
 }
 
 int anvilq_gqa_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* seqlens,
@@ -446,9 +681,9 @@ int anvilq_gqa_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t
   if (!q || !k_cache || !v_cache || !seqlens || !out || !dev_err) return ANVILQ_EINVAL;
   if (!args_ok(B, Hq, Hkv, D, Tmax)) return ANVILQ_ESHAPE;
   if (!a16(q) || !a16(k_cache) || !a16(v_cache) || !a16(out)) return ANVILQ_EALIGN;
-  const int sms = sm_count();
-  if (sms <= 0) return ANVILQ_ECUDA;
-  const Plan pl = plan_for(B, Hq, Hkv, D, Tmax, sms);
+  const DeviceInfo* dev = device_info();
+  if (!dev) return ANVILQ_ECUDA;
+  const Plan pl = plan_for(B, Hq, Hkv, D, Tmax, *dev);
   if (!workspace || workspace_bytes < pl.bytes) return ANVILQ_EWORKSPACE;
   if (!a16(workspace)) return ANVILQ_EALIGN;
   Params p;
@@ -461,16 +696,10 @@ int anvilq_gqa_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t
   p.partials = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + ANVILQ_WORKSPACE_COUNTER_BYTES);
   p.dev_err = dev_err;
   p.Hq = Hq; p.Hkv = Hkv; p.Tmax = Tmax; p.group = Hq / Hkv;
-  p.splits = pl.splits; p.tiles_per_split = pl.tiles_per_split;
+  p.cluster = pl.cluster; p.clusters = pl.clusters;
   const float s = scale > 0.0f ? scale : 1.0f / std::sqrt((float)D);
   p.scale_log2 = s * 1.4426950408889634f;
-  const dim3 grid(pl.splits, Hkv, B);
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (D == 64)
-    gqa_decode_kernel<64><<<grid, kThreads, Layout<64>::kTotal, st>>>(p);
-  else
-    gqa_decode_kernel<128><<<grid, kThreads, Layout<128>::kTotal, st>>>(p);
-  return cudaGetLastError() == cudaSuccess ? ANVILQ_OK : ANVILQ_ECUDA;
+  return launch(p, B, D, k_cache, v_cache, reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"
@@ -525,9 +754,9 @@ extern "C" int anvilq_gqa_decode_noalloc(const uint16_t* q, const uint16_t* k_ca
   if (!q || !k_cache || !v_cache || !seqlens || !out || !dev_err) return ANVILQ_EINVAL;
   if (!args_ok(B, Hq, Hkv, D, Tmax)) return ANVILQ_ESHAPE;
   if (!a16(q) || !a16(k_cache) || !a16(v_cache) || !a16(out)) return ANVILQ_EALIGN;
-  const int sms = sm_count();
-  if (sms <= 0) return ANVILQ_ECUDA;
-  const Plan pl = plan_for(B, Hq, Hkv, D, Tmax, sms);
+  const DeviceInfo* dev = device_info();
+  if (!dev) return ANVILQ_ECUDA;
+  const Plan pl = plan_for(B, Hq, Hkv, D, Tmax, *dev);
   if (pl.bytes > kNoAllocScratchBytes) return ANVILQ_ENOSCRATCH;
   void* ws = nullptr;
   const int rc = noalloc_scratch(&ws);
@@ -549,13 +778,8 @@ extern "C" int anvilq_gqa_decode_noalloc(const uint16_t* q, const uint16_t* k_ca
   p.partials = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + ANVILQ_WORKSPACE_COUNTER_BYTES);
   p.dev_err = dev_err;
   p.Hq = Hq; p.Hkv = Hkv; p.Tmax = Tmax; p.group = Hq / Hkv;
-  p.splits = pl.splits; p.tiles_per_split = pl.tiles_per_split;
+  p.cluster = pl.cluster; p.clusters = pl.clusters;
   const float s = scale > 0.0f ? scale : 1.0f / std::sqrt((float)D);
   p.scale_log2 = s * 1.4426950408889634f;
-  const dim3 grid(pl.splits, Hkv, B);
-  if (D == 64)
-    gqa_decode_kernel<64><<<grid, kThreads, Layout<64>::kTotal, st>>>(p);
-  else
-    gqa_decode_kernel<128><<<grid, kThreads, Layout<128>::kTotal, st>>>(p);
-  return cudaGetLastError() == cudaSuccess ? ANVILQ_OK : ANVILQ_ECUDA;
+  return launch(p, B, D, k_cache, v_cache, st);
 }

@@ -81,6 +81,34 @@ def test_ragged_lengths(dev, L):
     check(y[0], ref[0], L)
 
 
+# Each shape reaches one way of merging a pair's KV splits on a 148-SM B200:
+# one CTA per pair (no merge), one cluster (distributed shared memory), and
+# several clusters (cluster merge, then the global merge of their partials).
+@pytest.mark.parametrize("B,Hq,Hkv,D,Tmax,seqlens", [
+    (40, 16, 4, 64, 256, None),                 # 160 pairs: one CTA each
+    (1, 14, 2, 64, 300, [300]),                 # clusters of 2
+    (1, 14, 2, 64, 1090, [1050]),               # clusters of 8 (the 0.5B decode step)
+    (1, 14, 2, 64, 8192, [8192]),               # 8 clusters of 8
+    (2, 14, 2, 64, 8192, [40, 8191]),           # as above, most clusters of sequence 0 empty
+    (1, 8, 1, 128, 16384, [16384]),             # 16 clusters of 8, head_dim 128
+    (3, 12, 3, 128, 5000, [1, 4999, 2500]),     # group of 4
+])
+def test_split_merge_paths(dev, B, Hq, Hkv, D, Tmax, seqlens):
+    from anvilq_b200 import ops
+    q, k, v = synthetic.kv_case(B, Hq, Hkv, D, Tmax, seed=Tmax + B)
+    if seqlens is None:
+        seqlens = list(np.random.default_rng(B).integers(1, Tmax + 1, size=B))
+    args = (T(q, dev), T(k, dev), T(v, dev), T(np.asarray(seqlens, np.int32), dev))
+    a = ops.gqa_decode(*args).clone()
+    y = ops.gqa_decode(*args)
+    ops.raise_device_errors(dev)
+    assert torch.equal(a, y), "split merge is not run-to-run deterministic"
+    ref = oracle.decode_attention_f64(q, k, v, seqlens)
+    y = y.float().cpu().numpy()
+    for b in range(B):
+        check(y[b], ref[b], (B, Hq, Hkv, D, Tmax, b, seqlens[b]))
+
+
 def test_fp32_loop_agreement(dev):
     """Against the FP32 sequential loop of official_weights.py:471-486 as well."""
     q, k, v = synthetic.kv_case(1, 14, 2, 64, 300, seed=89)
