@@ -1,5 +1,5 @@
 // gemv_tma.cu -- batch-1 W4A16 AWQ GEMV for B200: TMA-staged int4 stream,
-// two-level split-K (thread-block cluster + workspace), DSMEM reduction.
+// two-level split-K (thread-block cluster + workspace), DSMEM push reduction.
 //
 // Reference semantics: FP32Model.linear (anvil-q1/tests/official_weights.py:418-437),
 //   y[c] = sum_k x[k] * (u4 q[k][c] - u4 z[k/G][c]) * scale[k/G][c]  (+ bias[c]).
@@ -16,8 +16,10 @@
 //
 // Split-K, two levels.  The c CTAs of a thread-block cluster and kc clusters
 // share one band; the band's tiles are split evenly over all their warps.
-// Warps are reduced in shared memory and the CTAs of a cluster through
-// distributed shared memory, in rank order.  With kc > 1 every cluster leaves
+// Warps are reduced in shared memory; the CTA of rank r owns column slice r
+// of the band, every CTA stores its sum of that slice straight into the
+// owner's shared memory (DSMEM), and after a single cluster barrier the owner
+// adds the c partials in rank order.  With kc > 1 every cluster leaves
 // one partial per column slice in the workspace and the CTA that arrives last
 // at the slice's ticket adds the kc partials in cluster order.  Every sum has a
 // fixed order, so results are bit-reproducible; there are no atomics on data
@@ -41,6 +43,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
@@ -134,18 +137,20 @@ __device__ __forceinline__ uint32_t cluster_rank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
-__device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank) {
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// the same shared-memory address in CTA `rank` of this cluster
+__device__ __forceinline__ uint32_t dsmem_addr_u32(uint32_t local, uint32_t rank) {
   uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(rank));
   return remote;
 }
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
+__device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 __device__ __forceinline__ half2 h2(uint32_t u) { return *reinterpret_cast<half2*>(&u); }
 __device__ __forceinline__ uint32_t u32(half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
@@ -159,9 +164,18 @@ __device__ __forceinline__ void fma_f32_f16x2(float& a0, float& a1, uint32_t q2,
       : "r"(q2), "h"(x));
 }
 
-template <int XMODE, int YMODE>
+template <int XMODE, int YMODE, int BW>
 __global__ void __launch_bounds__(kThreads, 4)
     gemv_tma_kernel(const __grid_constant__ CUtensorMap tmap, const Params p) {
+  // Band geometry: BW qweight words (8 BW columns) per band.  A lane owns PW
+  // consecutive words of a row; LPR lanes cover a row, and the warp's NRS row
+  // sets take the tile's rows in turn (row r belongs to row set r % NRS).
+  constexpr int PW = BW == 64 ? 2 : 1;
+  constexpr int LPR = BW / PW;
+  constexpr int NRS = 32 / LPR;
+  constexpr int kCols = BW * 8;
+  constexpr int kTileB = kTileRows * BW * 4;
+  static_assert(BW == 64 || BW == 32 || BW == 16, "bands of 512, 256 or 128 columns");
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_last;
   __shared__ float s_norm[kWarps + 1];
@@ -220,14 +234,14 @@ __global__ void __launch_bounds__(kThreads, 4)
     // the stage was last read through the generic proxy; order that before the TMA write
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     if (with_x)
-      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(kTileBytes + x_bytes)
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(kTileB + x_bytes)
                    : "memory");
     else
-      asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(kTileBytes) : "memory");
+      asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(kTileB) : "memory");
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
         "[%4];" ::"r"(smem_u32(ring + st * kTileBytes)),
-        "l"(&tmap), "r"(band * kBandWords), "r"((t0 + j) * kTileRows), "r"(bar)
+        "l"(&tmap), "r"(band * BW), "r"((t0 + j) * kTileRows), "r"(bar)
         : "memory");
     if (with_x) copy_x(j, bar);
   };
@@ -237,7 +251,8 @@ __global__ void __launch_bounds__(kThreads, 4)
     copy_x(j, bar);
   };
 
-  const int w0 = band * kBandWords + lane * 2;   // this lane's 2 words = 16 columns
+  const int lw = lane % LPR, rs = lane / LPR;   // word slot and row set of this lane
+  const int w0 = band * BW + lw * PW;             // this lane's PW words = 8 PW columns
   const bool active = w0 < p.W8;
   auto tile_row = [&](int j) { return (t0 + j) * kTileRows; };
 
@@ -250,27 +265,35 @@ __global__ void __launch_bounds__(kThreads, 4)
   uint32_t bad = 0;
   bool ok = true;
 
-  auto load_group = [&](int row, uint4* s2, uint2& z) {   // scales and zeros of the group of `row`
+  // scales and zeros of the group of `row`.  Volatile loads: issued here, a
+  // group ahead of their use (a plain read-only load may be sunk by the
+  // compiler to its use, putting a memory round trip on the critical path).
+  auto load_group = [&](int row, uint4* s2, uint2& z) {
     if (active) {
       const int g = row / p.G;
       const __half* sp = p.scales + (size_t)g * p.N + 8 * (size_t)w0;
-      s2[0] = __ldg(reinterpret_cast<const uint4*>(sp));
-      s2[1] = __ldg(reinterpret_cast<const uint4*>(sp + 8));
-      z = __ldg(reinterpret_cast<const uint2*>(p.qzeros + (size_t)g * p.W8 + w0));
+      s2[0] = ld_stream_v4(sp);
+      if (PW == 2) {
+        s2[1] = ld_stream_v4(sp + 8);
+        z = ld_stream_v2(p.qzeros + (size_t)g * p.W8 + w0);
+      } else {
+        z.x = ld_stream_u32(p.qzeros + (size_t)g * p.W8 + w0);
+      }
     }
   };
   auto check_group = [&](int row) {   // the tile that opens a group checks its scales, once
     if (active && row % p.G == 0) {
 #pragma unroll
-      for (int i = 0; i < 2; ++i)
+      for (int i = 0; i < PW; ++i)
         bad |= invalid_scale_pair(sc[i].x) | invalid_scale_pair(sc[i].y) | invalid_scale_pair(sc[i].z) |
                invalid_scale_pair(sc[i].w);
     }
   };
-  // y += s (A - z X) for the finished group, this lane's 16 columns
+  // y += s (A - z X) for the finished group, this lane's 8 PW columns (X: the
+  // group's activations summed over this lane's row set)
   auto flush_group = [&]() {
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < PW; ++i) {
       const uint32_t zw = i == 0 ? zq.x : zq.y;
       const uint32_t sw[4] = {sc[i].x, sc[i].y, sc[i].z, sc[i].w};
       // zero points via the binary16 magic 1024 + z, pairs (0,1),(2,3),(4,5),(6,7)
@@ -303,10 +326,23 @@ __global__ void __launch_bounds__(kThreads, 4)
     for (int j = 0; j < pro; ++j) issue_x(j);
   float norm_inv = 1.0f;   // kXRmsNorm: 1 / sqrt(mean(r^2) + eps), computed by every CTA
   if (XMODE == kXRmsNorm) {
+    // every CTA needs the whole row's norm: 8 vector loads per thread in
+    // flight at once (one L2 round trip per 4096 elements), summed in a fixed order
+    const float4* xr4 = reinterpret_cast<const float4*>(p.xr);
+    const int n4 = p.K / 4;
     float ss = 0.0f;
-    for (int k = threadIdx.x; k < p.K; k += kThreads) {
-      const float v = __ldcg(p.xr + k);
-      ss = fmaf(v, v, ss);
+    for (int base = threadIdx.x; base < n4; base += 8 * kThreads) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        v[u] = base + u * kThreads < n4 ? __ldcg(xr4 + base + u * kThreads) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        ss = fmaf(v[u].x, v[u].x, ss);
+        ss = fmaf(v[u].y, v[u].y, ss);
+        ss = fmaf(v[u].z, v[u].z, ss);
+        ss = fmaf(v[u].w, v[u].w, ss);
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -356,30 +392,47 @@ __global__ void __launch_bounds__(kThreads, 4)
         const float sg = g >= 0.0f ? g / (1.0f + e) : (g * e) / (1.0f + e);
         xf = __half2float(__float2half_rn(sg * u));
       }
+      // the sum of this lane's row set: all 16 rows (NRS 1), or the rows of one
+      // parity (xor 2..8), taken from lane rs, whose row has parity rs (NRS 2)
       float sum = xf;
 #pragma unroll
-      for (int o = 1; o < 16; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      for (int o = NRS; o < 16; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if (NRS == 2) sum = __shfl_sync(0xffffffffu, sum, rs);
       if (lane < 16) reinterpret_cast<__half*>(xs)[lane] = __float2half_rn(xf);
       Xt = sum;
     }
     __syncwarp();
-    const unsigned char* tile = ring + st * kTileBytes + lane * 8;
+    const unsigned char* tile = ring + st * kTileBytes + lw * PW * 4;
+    // one qweight word (8 columns) times one activation into A[8 i .. 8 i + 7]
+    auto word_fma = [&](int i, uint32_t wd, unsigned short xv) {
+      const uint32_t w8 = wd >> 8;
+      fma_f32_f16x2(A[i * 8 + 0], A[i * 8 + 1], wd & 0x000F000Fu, xv);   // columns 0,1
+      fma_f32_f16x2(A[i * 8 + 2], A[i * 8 + 3], wd & 0x00F000F0u, xv);   // columns 2,3 (x16)
+      fma_f32_f16x2(A[i * 8 + 4], A[i * 8 + 5], w8 & 0x000F000Fu, xv);   // columns 4,5
+      fma_f32_f16x2(A[i * 8 + 6], A[i * 8 + 7], w8 & 0x00F000F0u, xv);   // columns 6,7 (x16)
+    };
+    if (NRS == 1) {
 #pragma unroll
-    for (int r = 0; r < kTileRows; r += 2) {
-      const uint32_t xpair = xs[r / 2];   // rows r, r + 1
-      const unsigned short xr_[2] = {(unsigned short)(xpair & 0xFFFFu), (unsigned short)(xpair >> 16)};
+      for (int r = 0; r < kTileRows; r += 2) {
+        const uint32_t xpair = xs[r / 2];   // rows r, r + 1
+        const unsigned short xr_[2] = {(unsigned short)(xpair & 0xFFFFu), (unsigned short)(xpair >> 16)};
 #pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const uint2 w = *reinterpret_cast<const uint2*>(tile + (r + rr) * (kBandWords * 4));
-        const uint32_t ws[2] = {w.x, w.y};
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const uint32_t w8 = ws[i] >> 8;
-          fma_f32_f16x2(A[i * 8 + 0], A[i * 8 + 1], ws[i] & 0x000F000Fu, xr_[rr]);   // columns 0,1
-          fma_f32_f16x2(A[i * 8 + 2], A[i * 8 + 3], ws[i] & 0x00F000F0u, xr_[rr]);   // columns 2,3 (x16)
-          fma_f32_f16x2(A[i * 8 + 4], A[i * 8 + 5], w8 & 0x000F000Fu, xr_[rr]);      // columns 4,5
-          fma_f32_f16x2(A[i * 8 + 6], A[i * 8 + 7], w8 & 0x00F000F0u, xr_[rr]);      // columns 6,7 (x16)
+        for (int rr = 0; rr < 2; ++rr) {
+          if (PW == 2) {
+            const uint2 w = *reinterpret_cast<const uint2*>(tile + (r + rr) * (BW * 4));
+            word_fma(0, w.x, xr_[rr]);
+            word_fma(1, w.y, xr_[rr]);
+          } else {
+            word_fma(0, *reinterpret_cast<const uint32_t*>(tile + (r + rr) * (BW * 4)), xr_[rr]);
+          }
         }
+      }
+    } else {
+      const unsigned short* xh = reinterpret_cast<const unsigned short*>(xs);
+#pragma unroll
+      for (int i2 = 0; i2 < kTileRows / NRS; ++i2) {
+        const int r = NRS * i2 + rs;
+        word_fma(0, *reinterpret_cast<const uint32_t*>(tile + r * (BW * 4)), xh[r]);
       }
     }
     __syncwarp();   // stage st and xs are free again
@@ -401,53 +454,63 @@ __global__ void __launch_bounds__(kThreads, 4)
     for (int j = 0; j < 16; ++j) Y[j] = 0.0f;
   }
   if (bad && p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_SCALE);
+  if (NRS == 2) {   // the two row sets of a word slot: lanes l and l ^ 16
+#pragma unroll
+    for (int j = 0; j < 8; ++j) Y[j] += __shfl_xor_sync(0xffffffffu, Y[j], 16);
+  }
 
-  // -- reduce: warps (shared memory, reusing the ring), then the cluster (DSMEM),
-  //    then the kc clusters of the band (workspace)
+  // -- reduce: warps (shared memory, reusing the ring), then the cluster (pushed
+  //    over DSMEM to the slice owners), then the kc clusters of the band (workspace)
   __syncthreads();   // every warp is done with its ring
   float* red = reinterpret_cast<float*>(smem + kRingOff);   // [warp][512]
+  if (lane < LPR) {
 #pragma unroll
-  for (int j = 0; j < 16; j += 4)
-    *reinterpret_cast<float4*>(red + warp * kBandCols + lane * 16 + j) =
-        make_float4(Y[j], Y[j + 1], Y[j + 2], Y[j + 3]);
+    for (int j = 0; j < 8 * PW; j += 4)
+      *reinterpret_cast<float4*>(red + warp * kCols + lw * 8 * PW + j) =
+          make_float4(Y[j], Y[j + 1], Y[j + 2], Y[j + 3]);
+  }
   __syncthreads();
-  float* part = reinterpret_cast<float*>(smem + kPartOff);
-  for (int col = threadIdx.x; col < kBandCols; col += kThreads) {
+  // The band's columns are owned in slices of per = 512 / c columns, slice r
+  // by the CTA of rank r.  Each CTA sums its warps and pushes slice r of that
+  // sum into slot [its rank] of owner r (distributed shared memory); after one
+  // cluster barrier every owner holds all c partials of its slice locally.
+  float* slots = reinterpret_cast<float*>(smem + kPartOff);   // [c][per]
+  const int per = kCols / c;              // this CTA's column slice of the band
+  const int col0 = band * kCols + rank * per;
+  const uint32_t slots_u32 = smem_u32(slots);
+  for (int col = threadIdx.x; col < kCols; col += kThreads) {
     float v = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) v += red[w * kBandCols + col];
-    part[col] = v;
+    for (int w = 0; w < kWarps; ++w) v += red[w * kCols + col];
+    if (c > 1) {
+      const int owner = col / per;
+      st_dsmem_f32(dsmem_addr_u32(slots_u32 + (rank * per + col % per) * 4, owner), v);
+    } else {
+      slots[col] = v;
+    }
   }
-  if (c > 1)
-    cluster_sync();   // every CTA of the cluster reaches this, errors included
-  else
+  if (c > 1) {
+    // every CTA of the cluster reaches this, errors included; the release /
+    // acquire pair orders the pushes before the owners' reads
+    cluster_arrive_release();
+    cluster_wait_acquire();
+  } else {
     __syncthreads();
-  const int per = kBandCols / c;          // this CTA's column slice of the band
-  const int col0 = band * kBandCols + rank * per;
-  constexpr int kMaxPer = kBandCols / kThreads;   // up to 4 columns per thread (c == 1)
+  }
+  constexpr int kMaxPer = kCols / kThreads;   // up to 4 columns per thread (c == 1)
   float v[kMaxPer];
 #pragma unroll
   for (int i = 0; i < kMaxPer; ++i) {
     v[i] = 0.0f;
     const int t = threadIdx.x + i * kThreads;
     if (t < per) {
-      if (c > 1) {
-        float r[kMaxCluster];
-#pragma unroll
-        for (int k = 0; k < kMaxCluster; ++k)   // all loads first, then the ordered sum
-          if (k < c) r[k] = ld_dsmem_f32(dsmem_addr(part + rank * per + t, (uint32_t)k));
-#pragma unroll
-        for (int k = 0; k < kMaxCluster; ++k)
-          if (k < c) v[i] += r[k];
-      } else {
-        v[i] = part[t];
-      }
+      v[i] = slots[t];
+      for (int k = 1; k < c; ++k) v[i] += slots[k * per + t];   // in rank order
     }
   }
-  if (c > 1) cluster_sync();   // peers may still be reading this CTA's partial
 
   if (p.kc > 1) {
-    float* slot = p.partials + ((size_t)band * p.kc + kidx) * kBandCols + rank * per;
+    float* slot = p.partials + ((size_t)band * p.kc + kidx) * kCols + rank * per;
 #pragma unroll
     for (int i = 0; i < kMaxPer; ++i) {
       const int t = threadIdx.x + i * kThreads;
@@ -464,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, 4)
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    const float* base = p.partials + (size_t)band * p.kc * kBandCols + rank * per;
+    const float* base = p.partials + (size_t)band * p.kc * kCols + rank * per;
 #pragma unroll
     for (int i = 0; i < kMaxPer; ++i) {
       const int t = threadIdx.x + i * kThreads;
@@ -472,7 +535,7 @@ __global__ void __launch_bounds__(kThreads, 4)
         float r[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k)   // kc <= 8: all loads first, then the ordered sum
-          if (k < p.kc) r[k] = __ldcg(base + (size_t)k * kBandCols + t);
+          if (k < p.kc) r[k] = __ldcg(base + (size_t)k * kCols + t);
         float acc = 0.0f;
 #pragma unroll
         for (int k = 0; k < 8; ++k)
@@ -518,12 +581,16 @@ static DeviceInfo g_dev[kMaxDevices];
 static std::once_flag g_dev_once[kMaxDevices];
 
 using KernelFn = void (*)(CUtensorMap, Params);
-static KernelFn kernel_for(int xmode, int ymode) {
-  static const KernelFn table[3][2] = {
-      {gemv_tma_kernel<kXHalf, kYHalf>, gemv_tma_kernel<kXHalf, kYResidual>},
-      {gemv_tma_kernel<kXRmsNorm, kYHalf>, gemv_tma_kernel<kXRmsNorm, kYResidual>},
-      {gemv_tma_kernel<kXSiluMul, kYHalf>, gemv_tma_kernel<kXSiluMul, kYResidual>}};
-  return table[xmode][ymode];
+constexpr int kBandWidths[3] = {64, 32, 16};   // qweight words per band
+template <int XM, int YM>
+static KernelFn kernel_bw(int bw) {
+  return bw == 64 ? gemv_tma_kernel<XM, YM, 64> : bw == 32 ? gemv_tma_kernel<XM, YM, 32> : gemv_tma_kernel<XM, YM, 16>;
+}
+static KernelFn kernel_for(int xmode, int ymode, int bw) {
+  if (xmode == kXHalf) return ymode == kYHalf ? kernel_bw<kXHalf, kYHalf>(bw) : kernel_bw<kXHalf, kYResidual>(bw);
+  if (xmode == kXRmsNorm)
+    return ymode == kYHalf ? kernel_bw<kXRmsNorm, kYHalf>(bw) : kernel_bw<kXRmsNorm, kYResidual>(bw);
+  return ymode == kYHalf ? kernel_bw<kXSiluMul, kYHalf>(bw) : kernel_bw<kXSiluMul, kYResidual>(bw);
 }
 
 static const DeviceInfo* device_info() {
@@ -533,9 +600,10 @@ static const DeviceInfo* device_info() {
     DeviceInfo& d = g_dev[dev];
     cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
     for (int xm = 0; xm < 3; ++xm)
-      for (int ym = 0; ym < 2; ++ym) {
-        cudaFuncSetAttribute(kernel_for(xm, ym), cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-        cudaFuncSetAttribute(kernel_for(xm, ym), cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      for (int ym = 0; ym < 2; ++ym)
+        for (int bw : kBandWidths) {
+          cudaFuncSetAttribute(kernel_for(xm, ym, bw), cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+          cudaFuncSetAttribute(kernel_for(xm, ym, bw), cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
       }
     for (int i = 0; i < 5; ++i) {
       cudaLaunchConfig_t cfg = {};
@@ -550,7 +618,7 @@ static const DeviceInfo* device_info() {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, kernel_for(kXHalf, kYHalf), &cfg) != cudaSuccess) n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kernel_for(kXHalf, kYHalf, 64), &cfg) != cudaSuccess) n = 0;
       d.max_clusters[i] = n;
     }
     cudaGetLastError();
@@ -559,64 +627,108 @@ static const DeviceInfo* device_info() {
 }
 
 struct Plan {
-  int bands, tiles, c, kc;
+  int bw, bands, tiles, c, kc;
   size_t bytes;   // workspace bytes (counters included)
 };
 
-// Tuning aid: ANVILQ_GEMV_PLAN="c,kc" forces the cluster size and the number of
-// clusters per band (c a power of two <= 16, 1 <= kc <= 8), for sweeps.
-static bool plan_override(int* c, int* kc) {
-  static int oc = 0, okc = 0;
+// Tuning aid: ANVILQ_GEMV_PLAN="c,kc[,bw]" forces the cluster size, the number
+// of clusters per band and the band width in words (c a power of two <= 16,
+// 1 <= kc <= 8, bw 64, 32 or 16), for sweeps.
+static bool plan_override(int* c, int* kc, int* bw) {
+  static int oc = 0, okc = 0, obw = 0;
   static std::once_flag once;
   std::call_once(once, [] {
     const char* e = std::getenv("ANVILQ_GEMV_PLAN");
-    int a = 0, b = 0;
-    if (e && std::sscanf(e, "%d,%d", &a, &b) == 2 && a >= 1 && a <= kMaxCluster && (a & (a - 1)) == 0 && b >= 1 &&
-        b <= 8) {
+    int a = 0, b = 0, w = 0;
+    const int n = e ? std::sscanf(e, "%d,%d,%d", &a, &b, &w) : 0;
+    if (n >= 2 && a >= 1 && a <= kMaxCluster && (a & (a - 1)) == 0 && b >= 1 && b <= 8) {
       oc = a;
       okc = b;
+      obw = n == 3 && (w == 64 || w == 32 || w == 16) ? w : 0;
     }
   });
   if (!oc) return false;
   *c = oc;
   *kc = okc;
+  if (obw) *bw = obw;
   return true;
 }
 
-// Grid of bands x kc clusters of c CTAs.  Measured on B200: the workspace
-// fix-up of kc > 1 costs a few microseconds of tail, so the largest cluster
-// whose clusters are all co-resident wins (c = 16, kc = 1 for 7B-class
-// layers); only deep-K layers, where every warp would stream 16 or more tiles,
-// trade that tail for more warps (c = 8, kc = 3 on 28672 x 8192).
+// Grid of bands x kc clusters of c CTAs, in one of two regimes (measured on
+// B200 across the 0.5B, 7B and 70B projection shapes; each rule picks the
+// fastest plan or one within a few percent):
+//   * Latency bound (each warp would stream fewer than 8 tiles at two CTAs
+//     per SM; all decode projections up to 7B-class): a warp spends ~2.5
+//     instructions per weight and lane on a tile and a cluster's reduction
+//     costs a barrier, so the plan looks for many CTAs, all co-resident, none
+//     idle.  Among band widths of 512, 256 and 128 columns and cluster sizes
+//     up to 16 (clusters co-resident, at most half the warps without a tile)
+//     it takes the CTA count closest to two per SM; on a tie, the larger
+//     cluster, unless some of its warps would have no tile.
+//   * Bandwidth bound: 512-column bands (narrower boxes cost DRAM efficiency)
+//     and the largest co-resident cluster.  The workspace fix-up of kc > 1
+//     costs a few microseconds of tail; only deep-K layers, where every warp
+//     would stream 16 or more tiles, trade that tail for more warps (c = 8,
+//     kc = 3 on 28672 x 8192).
 static Plan make_plan(const DeviceInfo& d, int K, int N) {
   Plan pl{};
   const int W8 = N / 8;
-  pl.bands = (W8 + kBandWords - 1) / kBandWords;
   pl.tiles = (K + kTileRows - 1) / kTileRows;
-  int c = 1;
-  for (int i = 4; i >= 1; --i) {
-    const int cand = 1 << i;
-    if (d.max_clusters[i] >= pl.bands && cand * kWarps <= pl.tiles) {
-      c = cand;
-      break;
-    }
-  }
+  const double tiles_per_warp = (double)W8 * pl.tiles / (64.0 * 2.0 * d.sms * kWarps);
   int kc = 1;
-  if (pl.tiles / (kWarps * c) >= 16) {
-    for (int cand_c : {8, 16}) {
-      const int i = cand_c == 8 ? 3 : 4;
-      for (int cand_kc = 3; cand_kc >= 2; --cand_kc)
-        if (kc == 1 && d.max_clusters[i] >= pl.bands * cand_kc && pl.bands * cand_c * cand_kc <= 4 * d.sms) {
-          c = cand_c;
-          kc = cand_kc;
+  if (tiles_per_warp < 8.0) {
+    const double target = 2.0 * d.sms;
+    double best_score = 1e30;
+    int best_ctas = 0;
+    pl.bw = kBandWidths[0];
+    pl.c = 1;
+    for (int bw : kBandWidths) {
+      const int bands = (W8 + bw - 1) / bw;
+      for (int i = 4; i >= 0; --i) {
+        const int c = 1 << i;
+        if (d.max_clusters[i] < bands || c * kWarps > 2 * pl.tiles) continue;
+        const int ctas = bands * c;
+        const double score = std::fabs(std::log((double)ctas / target));
+        bool take = score < best_score - 1e-9;
+        if (!take && ctas == best_ctas) {   // a tie: the larger cluster, if all its warps stream
+          const bool full = c * kWarps <= pl.tiles, best_full = pl.c * kWarps <= pl.tiles;
+          take = (full && !best_full) || (full == best_full && c > pl.c);
         }
+        if (take) {
+          best_score = score;
+          best_ctas = ctas;
+          pl.bw = bw;
+          pl.c = c;
+        }
+      }
+    }
+    pl.bands = (W8 + pl.bw - 1) / pl.bw;
+  } else {
+    pl.bw = kBandWidths[0];
+    pl.bands = (W8 + pl.bw - 1) / pl.bw;
+    pl.c = 1;
+    for (int i = 4; i >= 1; --i) {
+      const int cand = 1 << i;
+      if (d.max_clusters[i] >= pl.bands && cand * kWarps <= pl.tiles) {
+        pl.c = cand;
+        break;
+      }
+    }
+    if (pl.tiles / (kWarps * pl.c) >= 16) {
+      for (int cand_c : {8, 16}) {
+        const int i = cand_c == 8 ? 3 : 4;
+        for (int cand_kc = 3; cand_kc >= 2; --cand_kc)
+          if (kc == 1 && d.max_clusters[i] >= pl.bands * cand_kc && pl.bands * cand_c * cand_kc <= 4 * d.sms) {
+            pl.c = cand_c;
+            kc = cand_kc;
+          }
+      }
     }
   }
-  pl.c = c;
   pl.kc = kc;
-  plan_override(&pl.c, &pl.kc);
+  if (plan_override(&pl.c, &pl.kc, &pl.bw)) pl.bands = (W8 + pl.bw - 1) / pl.bw;
   pl.bytes = ANVILQ_WORKSPACE_COUNTER_BYTES +
-             (pl.kc > 1 ? (size_t)pl.bands * pl.kc * kBandCols * sizeof(float) : 0);
+             (pl.kc > 1 ? (size_t)pl.bands * pl.kc * pl.bw * 8 * sizeof(float) : 0);
   return pl;
 }
 
@@ -653,7 +765,7 @@ int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qze
   CUtensorMap map;
   const cuuint64_t dims[2] = {(cuuint64_t)W8, (cuuint64_t)K};
   const cuuint64_t strides[1] = {(cuuint64_t)W8 * 4};
-  const cuuint32_t box[2] = {(cuuint32_t)kBandWords, (cuuint32_t)kTileRows};
+  const cuuint32_t box[2] = {(cuuint32_t)pl.bw, (cuuint32_t)kTileRows};
   const cuuint32_t estr[2] = {1, 1};
   if (encode(&map, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, const_cast<int32_t*>(qweight), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -693,7 +805,7 @@ int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qze
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = overlap_prior ? 2 : 1;
-  if (cudaLaunchKernelEx(&cfg, kernel_for(io.xmode, io.ymode), map, p) != cudaSuccess) {
+  if (cudaLaunchKernelEx(&cfg, kernel_for(io.xmode, io.ymode, pl.bw), map, p) != cudaSuccess) {
     cudaGetLastError();
     return ANVILQ_ECUDA;
   }

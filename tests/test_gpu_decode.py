@@ -76,6 +76,41 @@ def test_gemv_silu_prologue_residual_epilogue(dev, K, N):
     check(y.cpu().numpy(), ref, TOL_OP, (K, N))
 
 
+# On a 148-SM B200 the GEMV plan takes 128-column bands for (896, 1152) and
+# (4864, 896), 256-column bands for (896, 4864) and (4864, 2048); every
+# activation prologue and output epilogue runs on each.
+@pytest.mark.parametrize("x_mode", [0, 1, 2])
+@pytest.mark.parametrize("y_mode", [0, 1])
+@pytest.mark.parametrize("K,N", [(896, 1152), (896, 4864), (4864, 896), (4864, 2048)])
+def test_gemv_modes_on_every_band_width(dev, K, N, x_mode, y_mode):
+    rng = np.random.default_rng(K * 7 + N + 3 * x_mode + y_mode)
+    layer = synthetic.awq_layer(K, N, 128, rng=rng, bias=(x_mode == 1))
+    gamma = None
+    if x_mode == 0:
+        xin = rng.standard_normal(K).astype(np.float16)
+        a = xin.astype(np.float32)
+    elif x_mode == 1:
+        xin = (rng.standard_normal(K) * 3).astype(np.float32)
+        gamma = (1 + 0.1 * rng.standard_normal(K)).astype(np.float16)
+        h = xin.astype(np.float64) * gamma / np.sqrt(np.mean(xin.astype(np.float64) ** 2) + 1e-6)
+        a = h.astype(np.float16).astype(np.float32)
+    else:
+        xin = rng.standard_normal(2 * K).astype(np.float16)
+        g, u = xin[:K].astype(np.float64), xin[K:].astype(np.float64)
+        a = (g / (1 + np.exp(-g)) * u).astype(np.float16).astype(np.float32)
+    prod = oracle.gemv_fp32(a[None], layer.qweight, layer.qzeros, layer.scales_bits, layer.bias_bits, 128,
+                            threads=oracle.max_threads())[0]
+    if y_mode == 0:
+        y = torch.empty(N, dtype=torch.float16, device=dev)
+        ref = prod
+    else:
+        resid = rng.standard_normal(N).astype(np.float32)
+        y = T(resid, dev)
+        ref = resid + prod
+    _fused(dev, T(xin, dev), x_mode, None if gamma is None else T(gamma, dev), layer, y, y_mode, K, N)
+    check(y.float().cpu().numpy(), ref, TOL_OP, (K, N, x_mode, y_mode))
+
+
 def test_rope_kv_append(dev):
     lib = _lib.load()
     QH, KVH, D, Tmax, pos = 14, 2, 64, 64, 37
