@@ -227,6 +227,10 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
     }
   }
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  // a kernel launched after this one with programmatic dependent launch (the
+  // next projection) may start now and stream its weights; it still waits
+  // for this grid to complete before it reads the attention output
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __syncwarp();
 
   auto issue = [&](int j) {   // tile j of this warp into stage j % kStages
