@@ -38,6 +38,8 @@ SIGNATURES = {
     "anvilq_gqa_decode": (I, [P, P, P, P, P, I, I, I, I, I, F, P, SZ, P, P]),
     "anvilq_gqa_decode_noalloc": (I, [P, P, P, P, P, I, I, I, I, I, F, P, P]),
     "anvilq_w4a16_gemv_fused": (I, [P, I, P, F, P, P, P, P, P, I, I, I, I, P, SZ, P, ctypes.c_uint, P]),
+    "anvilq_w4a16_gemv_qkv_rope": (I, [P, I, P, F, P, P, P, P, I, I, P, P, P, P, P, I, I, I, I, F, P, SZ, P,
+                                       ctypes.c_uint, P]),
     "anvilq_embed": (I, [P, P, P, I, I, P, P, ctypes.c_uint, P]),
     "anvilq_rope_kv_append": (I, [P, P, P, P, P, P, I, I, I, I, F, P, ctypes.c_uint, P]),
     "anvilq_lmhead_argmax": (I, [P, P, F, P, P, P, I, I, ctypes.c_uint, P]),

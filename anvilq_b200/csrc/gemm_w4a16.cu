@@ -680,6 +680,44 @@ int anvilq_w4a16_gemv_fused(const void* x, int x_mode, const uint16_t* gamma, fl
                          reinterpret_cast<cudaStream_t>(stream), (flags & ANVILQ_GEMM_OVERLAP_PRIOR) != 0);
 }
 
+int anvilq_w4a16_gemv_qkv_rope(const void* x, int x_mode, const uint16_t* gamma, float eps,
+                               const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
+                               const uint16_t* bias, int K, int G, const int32_t* pos, uint16_t* q_out,
+                               uint16_t* k_cache, uint16_t* v_cache, int32_t* seqlen, int Hq, int Hkv, int D,
+                               int Tmax, float theta, void* workspace, size_t workspace_bytes, int* dev_err,
+                               unsigned flags, anvilq_stream_t stream) {
+  if (!x || !qweight || !qzeros || !scales || !pos || !q_out || !k_cache || !v_cache) return ANVILQ_EINVAL;
+  if (flags & ~(unsigned)ANVILQ_GEMM_OVERLAP_PRIOR) return ANVILQ_EINVAL;
+  if (x_mode < ANVILQ_GEMV_X_HALF || x_mode > ANVILQ_GEMV_X_SILU_MUL) return ANVILQ_EINVAL;
+  if (x_mode == ANVILQ_GEMV_X_RMSNORM && (!gamma || !(eps >= 0.0f))) return ANVILQ_EINVAL;
+  if (Hq < 1 || Hkv < 1 || Hq % Hkv || D < 2 || D % 2 || Tmax < 1 || !(theta > 0.0f)) return ANVILQ_EINVAL;
+  const long long n = (long long)(Hq + 2 * Hkv) * D;
+  if (n > (1 << 24)) return ANVILQ_ESHAPE;
+  const int N = (int)n;
+  if (!shape_ok(1, K, N, G)) return ANVILQ_EINVAL;
+  const bool a16 = aligned16(x) && (!gamma || aligned16(gamma));
+  if (!a16 || !gemv_tma_supported(x, qweight, qzeros, scales, K, N, G)) return ANVILQ_ESHAPE;
+  GemvIo io;
+  io.xmode = x_mode;
+  io.ymode = 2;
+  io.x = static_cast<const uint16_t*>(x);
+  io.xr = static_cast<const float*>(x);
+  io.gamma = gamma;
+  io.eps = eps;
+  io.rope_pos = pos;
+  io.q_out = q_out;
+  io.k_cache = k_cache;
+  io.v_cache = v_cache;
+  io.seqlen = seqlen;
+  io.Hq = Hq;
+  io.Hkv = Hkv;
+  io.D = D;
+  io.Tmax = Tmax;
+  io.theta = theta;
+  return launch_gemv_tma(io, qweight, qzeros, scales, bias, K, N, G, workspace, workspace_bytes, dev_err,
+                         reinterpret_cast<cudaStream_t>(stream), (flags & ANVILQ_GEMM_OVERLAP_PRIOR) != 0);
+}
+
 int anvilq_w4a16_gemm_exact(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
                             const uint16_t* scales, const uint16_t* bias, float* y32,
                             int M, int K, int N, int G, int* dev_err, anvilq_stream_t stream) {

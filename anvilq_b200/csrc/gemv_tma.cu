@@ -86,8 +86,15 @@ constexpr int kSmemBytes = kPartOff + kBandCols * 4;
 // and where the result goes (YMODE):
 //   kYHalf     y[c] = fp16(result (+ bias))
 //   kYResidual r_out[c] += result (+ bias), fp32 in place
+//   kYRope     the QKV projection of a decode step: y = fp16(result (+ bias))
+//              is never stored; its q and k heads are rotated (split-half RoPE
+//              at position *pos) into q_out and row *pos of the K cache, its
+//              v heads copied to row *pos of the V cache, *seqlen = *pos + 1
+//              -- the same operations, in the same precision, as the separate
+//              RoPE/append kernel applied to the stored y.
 enum XMode { kXHalf = 0, kXRmsNorm = 1, kXSiluMul = 2 };
-enum YMode { kYHalf = 0, kYResidual = 1 };
+enum YMode { kYHalf = 0, kYResidual = 1, kYRope = 2 };
+constexpr int kMaxRopePairs = 64;   // head_dim <= 128 in the fused RoPE epilogue
 
 struct Params {
   const __half* x;         // kXHalf, kXSiluMul
@@ -106,6 +113,14 @@ struct Params {
   int cluster;       // c: CTAs per cluster
   int kc;            // clusters per band
   int tiles;         // tiles per band = ceil(K / 16)
+  // kYRope only
+  const int* rope_pos;     // position of the token
+  __half* q_out;           // [Hq][D]
+  __half* k_cache;         // [Tmax][Hkv][D]
+  __half* v_cache;
+  int* seqlen;             // optional
+  int Hq, Hkv, D, Tmax;
+  double rope_inv[kMaxRopePairs];   // theta^(-2i/D), binary64, computed on the host
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -478,15 +493,23 @@ __global__ void __launch_bounds__(kThreads, 4)
   const int per = kCols / c;              // this CTA's column slice of the band
   const int col0 = band * kCols + rank * per;
   const uint32_t slots_u32 = smem_u32(slots);
+  // slot position L of a band column: the column itself, or for kYRope the
+  // pair order (head, i, half) that gives every owner both columns i and
+  // i + D/2 of the heads' dims it owns (bands hold whole heads)
+  auto slot_of = [&](int col) {
+    if (YMODE != kYRope) return col;
+    const int hd = p.D / 2, head = col / p.D, j = col % p.D;
+    return 2 * (head * hd + j % hd) + (j >= hd ? 1 : 0);
+  };
   for (int col = threadIdx.x; col < kCols; col += kThreads) {
     float v = 0.0f;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) v += red[w * kCols + col];
+    const int L = slot_of(col);
     if (c > 1) {
-      const int owner = col / per;
-      st_dsmem_f32(dsmem_addr_u32(slots_u32 + (rank * per + col % per) * 4, owner), v);
+      st_dsmem_f32(dsmem_addr_u32(slots_u32 + (rank * per + L % per) * 4, L / per), v);
     } else {
-      slots[col] = v;
+      slots[L] = v;
     }
   }
   if (c > 1) {
@@ -496,6 +519,50 @@ __global__ void __launch_bounds__(kThreads, 4)
     cluster_wait_acquire();
   } else {
     __syncthreads();
+  }
+  if (YMODE == kYRope) {   // kc == 1 (the host plan guarantees it)
+    const int hd = p.D / 2;
+    const int pos = *p.rope_pos;
+    const bool pos_ok = pos >= 0 && pos < p.Tmax;
+    if (!pos_ok) {
+      if (band == 0 && rank == 0 && threadIdx.x == 0 && p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_SEQLEN);
+      return;
+    }
+    for (int q2 = threadIdx.x; q2 < per / 2; q2 += kThreads) {
+      float va = slots[2 * q2], vb = slots[2 * q2 + 1];
+      for (int k = 1; k < c; ++k) {   // in rank order, as for the stored projection
+        va += slots[k * per + 2 * q2];
+        vb += slots[k * per + 2 * q2 + 1];
+      }
+      const int pr = (rank * per) / 2 + q2;   // pair index within the band
+      const int i = pr % hd;
+      const int ca = band * kCols + (pr / hd) * p.D + i, cb = ca + hd;
+      if (ca >= p.N) continue;
+      if (p.bias) {
+        va += __half2float(p.bias[ca]);
+        vb += __half2float(p.bias[cb]);
+      }
+      const __half ha = __float2half_rn(va), hb = __float2half_rn(vb);
+      const int head = ca / p.D;
+      if (head < p.Hq + p.Hkv) {
+        const float angle = (float)((double)pos * p.rope_inv[i]);
+        float si, co;
+        sincosf(angle, &si, &co);
+        const float xa = __half2float(ha), xb = __half2float(hb);
+        const float ra = __fsub_rn(__fmul_rn(xa, co), __fmul_rn(xb, si));
+        const float rb = __fadd_rn(__fmul_rn(xb, co), __fmul_rn(xa, si));
+        __half* dst = head < p.Hq ? p.q_out + (size_t)head * p.D
+                                  : p.k_cache + ((size_t)pos * p.Hkv + (head - p.Hq)) * p.D;
+        dst[i] = __float2half_rn(ra);
+        dst[i + hd] = __float2half_rn(rb);
+      } else {
+        __half* dst = p.v_cache + ((size_t)pos * p.Hkv + (head - p.Hq - p.Hkv)) * p.D;
+        dst[i] = ha;
+        dst[i + hd] = hb;
+      }
+    }
+    if (p.seqlen && band == 0 && rank == 0 && threadIdx.x == 0) *p.seqlen = pos + 1;
+    return;
   }
   constexpr int kMaxPer = kCols / kThreads;   // up to 4 columns per thread (c == 1)
   float v[kMaxPer];
@@ -586,11 +653,14 @@ template <int XM, int YM>
 static KernelFn kernel_bw(int bw) {
   return bw == 64 ? gemv_tma_kernel<XM, YM, 64> : bw == 32 ? gemv_tma_kernel<XM, YM, 32> : gemv_tma_kernel<XM, YM, 16>;
 }
+template <int XM>
+static KernelFn kernel_y(int ymode, int bw) {
+  return ymode == kYHalf ? kernel_bw<XM, kYHalf>(bw) : ymode == kYResidual ? kernel_bw<XM, kYResidual>(bw)
+                                                                         : kernel_bw<XM, kYRope>(bw);
+}
 static KernelFn kernel_for(int xmode, int ymode, int bw) {
-  if (xmode == kXHalf) return ymode == kYHalf ? kernel_bw<kXHalf, kYHalf>(bw) : kernel_bw<kXHalf, kYResidual>(bw);
-  if (xmode == kXRmsNorm)
-    return ymode == kYHalf ? kernel_bw<kXRmsNorm, kYHalf>(bw) : kernel_bw<kXRmsNorm, kYResidual>(bw);
-  return ymode == kYHalf ? kernel_bw<kXSiluMul, kYHalf>(bw) : kernel_bw<kXSiluMul, kYResidual>(bw);
+  return xmode == kXHalf ? kernel_y<kXHalf>(ymode, bw) : xmode == kXRmsNorm ? kernel_y<kXRmsNorm>(ymode, bw)
+                                                                           : kernel_y<kXSiluMul>(ymode, bw);
 }
 
 static const DeviceInfo* device_info() {
@@ -600,7 +670,7 @@ static const DeviceInfo* device_info() {
     DeviceInfo& d = g_dev[dev];
     cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
     for (int xm = 0; xm < 3; ++xm)
-      for (int ym = 0; ym < 2; ++ym)
+      for (int ym = 0; ym < 3; ++ym)
         for (int bw : kBandWidths) {
           cudaFuncSetAttribute(kernel_for(xm, ym, bw), cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
           cudaFuncSetAttribute(kernel_for(xm, ym, bw), cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
@@ -754,8 +824,25 @@ int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qze
   const DeviceInfo* d = device_info();
   auto encode = encode_fn();
   if (!d || d->sms <= 0 || !encode) return ANVILQ_ECUDA;
-  if (io.xmode < 0 || io.xmode > 2 || io.ymode < 0 || io.ymode > 1) return ANVILQ_EINVAL;
-  const Plan pl = make_plan(*d, K, N);
+  if (io.xmode < 0 || io.xmode > 2 || io.ymode < 0 || io.ymode > 2) return ANVILQ_EINVAL;
+  Plan pl = make_plan(*d, K, N);
+  if (io.ymode == kYRope) {
+    // the epilogue needs whole heads in a band and one cluster per band; the
+    // usual plan of every decode QKV shape qualifies, anything else falls back
+    // to 512-column bands
+    if (io.D < 2 || io.D % 2 || io.D / 2 > kMaxRopePairs || (kBandWidths[0] * 8) % io.D) return ANVILQ_ESHAPE;
+    if (pl.kc > 1 || (pl.bw * 8) % io.D) {
+      pl.bw = kBandWidths[0];
+      pl.bands = (N / 8 + pl.bw - 1) / pl.bw;
+      pl.c = 1;
+      for (int i = 4; i >= 1; --i)
+        if (d->max_clusters[i] >= pl.bands && (1 << i) * kWarps <= pl.tiles) {
+          pl.c = 1 << i;
+          break;
+        }
+      pl.kc = 1;
+    }
+  }
   if (pl.kc > 1) {
     if (!workspace || workspace_bytes < pl.bytes) return ANVILQ_EWORKSPACE;
     if ((reinterpret_cast<uintptr_t>(workspace) & 15u) != 0) return ANVILQ_EALIGN;
@@ -787,6 +874,14 @@ int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qze
                          : nullptr;
   p.dev_err = dev_err;
   p.K = K; p.N = N; p.W8 = W8; p.G = G;
+  p.rope_pos = io.rope_pos;
+  p.q_out = reinterpret_cast<__half*>(io.q_out);
+  p.k_cache = reinterpret_cast<__half*>(io.k_cache);
+  p.v_cache = reinterpret_cast<__half*>(io.v_cache);
+  p.seqlen = io.seqlen;
+  p.Hq = io.Hq; p.Hkv = io.Hkv; p.D = io.D; p.Tmax = io.Tmax;
+  for (int i = 0; i < kMaxRopePairs; ++i)
+    p.rope_inv[i] = io.ymode == kYRope && i < io.D / 2 ? std::pow((double)io.theta, -2.0 * i / io.D) : 0.0;
   p.cluster = pl.c;
   p.kc = pl.kc;
   p.tiles = pl.tiles;

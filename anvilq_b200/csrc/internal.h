@@ -22,6 +22,14 @@ struct GemvIo {
   float eps = 0.0f;
   uint16_t* y = nullptr;         // fp16 out [N]
   float* yr = nullptr;           // fp32 residual [N], += result
+  // ymode 2 (QKV projection with RoPE and the KV-cache append)
+  const int32_t* rope_pos = nullptr;
+  uint16_t* q_out = nullptr;
+  uint16_t* k_cache = nullptr;
+  uint16_t* v_cache = nullptr;
+  int32_t* seqlen = nullptr;
+  int Hq = 0, Hkv = 0, D = 0, Tmax = 0;
+  float theta = 0.0f;
 };
 int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
                     const uint16_t* bias, int K, int N, int G, void* workspace, size_t workspace_bytes, int* dev_err,

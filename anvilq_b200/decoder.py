@@ -9,10 +9,10 @@ and QwenFP64.step (anvil-q1-fp/tests/fp64_reference.py:210-246):
                 h = rmsnorm(x); g, u = h W_gate, h W_up; x += (silu(g) u) W_down
     logits = rmsnorm(x) E^T;  token = argmax (lowest index on ties)
 
-Kernels per token: 1 embedding + per layer 6 (QKV GEMV with RMSNorm prologue and
-bias, RoPE + KV append, attention, O GEMV with residual epilogue, gate/up GEMV
-with RMSNorm prologue, down GEMV with SiLU-product prologue and residual epilogue)
-+ the lm_head/argmax + the token commit.  q/k/v and gate/up are each one GEMV
+Kernels per token: 1 embedding + per layer 5 (QKV GEMV with RMSNorm prologue,
+bias and a RoPE + KV-append epilogue, attention, O GEMV with residual
+epilogue, gate/up GEMV with RMSNorm prologue, down GEMV with SiLU-product
+prologue and residual epilogue) + the lm_head/argmax + the token commit.  q/k/v and gate/up are each one GEMV
 over weights concatenated along N at load time (AWQ packs 8 columns per word,
 so concatenating N-blocks of multiples of 8 keeps the layout).  Token, position
 and caches live on the device, so one CUDA graph replays every step.
@@ -107,7 +107,6 @@ class Decoder:
         self.k_cache = torch.zeros((L, self.max_seq, KVH, D), dtype=torch.float16, device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
         self.x = torch.zeros(H, dtype=torch.float32, device=dev)
-        self.qkv = torch.empty((QH + 2 * KVH) * D, dtype=torch.float16, device=dev)
         self.q = torch.empty((1, QH, D), dtype=torch.float16, device=dev)
         self.attn = torch.empty((1, QH, D), dtype=torch.float16, device=dev)
         self.gu = torch.empty(2 * I, dtype=torch.float16, device=dev)
@@ -138,6 +137,18 @@ class Decoder:
             y.data_ptr(), y_mode, K, N, self.shape[6], self.workspace.data_ptr(), self.workspace.numel(),
             self.dev_err.data_ptr(), FLAG_OVERLAP, self.stream.cuda_stream), "anvilq_w4a16_gemv_fused")
 
+    def _qkv_rope(self, l, w):
+        """QKV projection of layer l with RoPE and the KV-cache append in its epilogue."""
+        L, H, I, QH, KVH, D, G, V, _ = self.shape
+        lib = _lib.load()
+        qweight, qzeros, scales, bias = w["qkv"]
+        _lib.check(lib.anvilq_w4a16_gemv_qkv_rope(
+            self.x.data_ptr(), 1, self.gamma_in[l].data_ptr(), RMS_EPS, qweight.data_ptr(), qzeros.data_ptr(),
+            scales.data_ptr(), None if bias is None else bias.data_ptr(), H, G, self.pos.data_ptr(),
+            self.q.data_ptr(), self.k_cache[l].data_ptr(), self.v_cache[l].data_ptr(), self.seqlen.data_ptr(),
+            QH, KVH, D, self.max_seq, ROPE_THETA, self.workspace.data_ptr(), self.workspace.numel(),
+            self.dev_err.data_ptr(), FLAG_OVERLAP, self.stream.cuda_stream), "anvilq_w4a16_gemv_qkv_rope")
+
     def _enqueue(self, host_io: bool):
         L, H, I, QH, KVH, D, G, V, _ = self.shape
         lib = _lib.load()
@@ -146,13 +157,8 @@ class Decoder:
             self.token.copy_(self.token_in, non_blocking=True)
         _lib.check(lib.anvilq_embed(self.embedding.data_ptr(), self.token.data_ptr(), self.x.data_ptr(), H, V,
                                     self.key.data_ptr(), self.dev_err.data_ptr(), FLAG_OVERLAP, s), "anvilq_embed")
-        nqkv = (QH + 2 * KVH) * D
         for l, w in enumerate(self.layers):
-            self._gemv(w["qkv"], self.x, 1, self.gamma_in[l], self.qkv, 0, H, nqkv)
-            _lib.check(lib.anvilq_rope_kv_append(
-                self.qkv.data_ptr(), self.pos.data_ptr(), self.q.data_ptr(), self.k_cache[l].data_ptr(),
-                self.v_cache[l].data_ptr(), self.seqlen.data_ptr(), QH, KVH, D, self.max_seq, ROPE_THETA,
-                self.dev_err.data_ptr(), FLAG_OVERLAP, s), "anvilq_rope_kv_append")
+            self._qkv_rope(l, w)
             _lib.check(lib.anvilq_gqa_decode(
                 self.q.data_ptr(), self.k_cache[l].data_ptr(), self.v_cache[l].data_ptr(), self.seqlen.data_ptr(),
                 self.attn.data_ptr(), 1, QH, KVH, D, self.max_seq, 0.0, self.workspace.data_ptr(),
@@ -170,7 +176,7 @@ class Decoder:
             self.token_out.copy_(self.token, non_blocking=True)
 
     def kernels_per_step(self) -> int:
-        return 1 + 6 * self.shape[0] + 2
+        return 1 + 5 * self.shape[0] + 2
 
     def reset(self, token: int):
         """Start a new sequence at position 0 with `token` as the first input."""
@@ -208,11 +214,10 @@ class Decoder:
         """A CUDA graph of only this step's W4A16 GEMVs (same weights, buffers and
         fused modes, same order), for timing the GEMV kernel on its own."""
         L, H, I, QH, KVH, D, G, V, _ = self.shape
-        nqkv = (QH + 2 * KVH) * D
 
         def enqueue():
             for l, w in enumerate(self.layers):
-                self._gemv(w["qkv"], self.x, 1, self.gamma_in[l], self.qkv, 0, H, nqkv)
+                self._qkv_rope(l, w)
                 self._gemv(w["o"], self.attn, 0, None, self.x, 1, QH * D, H)
                 self._gemv(w["gu"], self.x, 1, self.gamma_post[l], self.gu, 0, H, 2 * I)
                 self._gemv(w["down"], self.gu, 2, None, self.x, 1, I, H)

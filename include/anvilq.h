@@ -169,6 +169,26 @@ int anvilq_w4a16_gemv_fused(const void* x, int x_mode, const uint16_t* gamma, fl
                             void* workspace, size_t workspace_bytes, int* dev_err, unsigned flags,
                             anvilq_stream_t stream);
 
+/* The decode step's QKV projection with RoPE and the KV-cache append fused
+ * into its epilogue: y = the GEMV of anvilq_w4a16_gemv_fused (same x_mode
+ * inputs; N = (Hq + 2 Hkv) * D) rounded to fp16 (y_mode ANVILQ_GEMV_Y_HALF),
+ * then exactly anvilq_rope_kv_append on that y -- q heads rotated into q_out,
+ * k heads rotated into row *pos of k_cache, v heads copied to row *pos of
+ * v_cache, *seqlen = *pos + 1 -- without y ever being stored.  Results are
+ * bit-identical to the two calls whenever the GEMV plan keeps whole heads in
+ * a band and one cluster per band (every decode QKV shape; otherwise equal
+ * within the GEMV tolerance).  Replaces FP32Model.linear for the q/k/v
+ * projections with the rotation and cache write that follow it
+ * (official_weights.py:418-437, 439-449, 466-470).  D even, D <= 128; a *pos
+ * outside [0, Tmax) sets ANVILQ_DEV_ERR_SEQLEN and writes nothing.
+ * flags: ANVILQ_GEMM_OVERLAP_PRIOR. */
+int anvilq_w4a16_gemv_qkv_rope(const void* x, int x_mode, const uint16_t* gamma, float eps,
+                               const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
+                               const uint16_t* bias, int K, int G, const int32_t* pos, uint16_t* q_out,
+                               uint16_t* k_cache, uint16_t* v_cache, int32_t* seqlen, int Hq, int Hkv, int D,
+                               int Tmax, float theta, void* workspace, size_t workspace_bytes, int* dev_err,
+                               unsigned flags, anvilq_stream_t stream);
+
 /* Reference-order W4A16 GEMM: one thread per output column sums its K products
  * in increasing k from +0.0 with every binary32 multiply and add rounded
  * separately (no FMA), exactly as FP32Model.linear does

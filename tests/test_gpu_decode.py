@@ -111,6 +111,64 @@ def test_gemv_modes_on_every_band_width(dev, K, N, x_mode, y_mode):
     check(y.float().cpu().numpy(), ref, TOL_OP, (K, N, x_mode, y_mode))
 
 
+def _qkv_two_calls_and_fused(dev, K, Hq, Hkv, D, Tmax, pos, seed):
+    lib = _lib.load()
+    N = (Hq + 2 * Hkv) * D
+    rng = np.random.default_rng(seed)
+    r = (rng.standard_normal(K) * 3).astype(np.float32)
+    gamma = (1 + 0.1 * rng.standard_normal(K)).astype(np.float16)
+    layer = synthetic.awq_layer(K, N, 128, rng=rng, bias=True)
+    s = torch.cuda.current_stream(dev).cuda_stream
+    ws = torch.zeros(lib.anvilq_w4a16_gemm_workspace_size(1, K, N, 128), dtype=torch.uint8, device=dev)
+    xr, gm = T(r, dev), T(gamma, dev)
+    qw, qz, sc, b = T(layer.qweight, dev), T(layer.qzeros, dev), T(layer.scales, dev), T(layer.bias, dev)
+    p = T(np.array([pos], np.int32), dev)
+    outs = []
+    for fused in (False, True):
+        q = torch.zeros(Hq * D, dtype=torch.float16, device=dev)
+        kc = torch.zeros((Tmax, Hkv, D), dtype=torch.float16, device=dev)
+        vc = torch.zeros_like(kc)
+        sl = torch.zeros(1, dtype=torch.int32, device=dev)
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        if fused:
+            rc = lib.anvilq_w4a16_gemv_qkv_rope(xr.data_ptr(), 1, gm.data_ptr(), 1e-6, qw.data_ptr(), qz.data_ptr(),
+                                                sc.data_ptr(), b.data_ptr(), K, 128, p.data_ptr(), q.data_ptr(),
+                                                kc.data_ptr(), vc.data_ptr(), sl.data_ptr(), Hq, Hkv, D, Tmax, 1e6,
+                                                ws.data_ptr(), ws.numel(), err.data_ptr(), 0, s)
+            assert rc == 0, lib.anvilq_strerror(rc)
+        else:
+            qkv = torch.empty(N, dtype=torch.float16, device=dev)
+            assert lib.anvilq_w4a16_gemv_fused(xr.data_ptr(), 1, gm.data_ptr(), 1e-6, qw.data_ptr(), qz.data_ptr(),
+                                               sc.data_ptr(), b.data_ptr(), qkv.data_ptr(), 0, K, N, 128,
+                                               ws.data_ptr(), ws.numel(), err.data_ptr(), 0, s) == 0
+            assert lib.anvilq_rope_kv_append(qkv.data_ptr(), p.data_ptr(), q.data_ptr(), kc.data_ptr(),
+                                             vc.data_ptr(), sl.data_ptr(), Hq, Hkv, D, Tmax, 1e6, err.data_ptr(),
+                                             0, s) == 0
+        torch.cuda.synchronize(dev)
+        outs.append((q, kc, vc, int(sl.item()), int(err.item())))
+    return outs
+
+
+@pytest.mark.parametrize("K,Hq,Hkv,D", [(896, 14, 2, 64), (3584, 28, 4, 128), (4096, 32, 8, 128),
+                                        (2048, 16, 16, 128), (1024, 8, 1, 64)])
+@pytest.mark.parametrize("pos", [0, 37, 95])
+def test_qkv_rope_fused_bit_identical_to_two_calls(dev, K, Hq, Hkv, D, pos):
+    """The fused QKV projection + RoPE + cache append equals the GEMV (fp16 y)
+    followed by anvilq_rope_kv_append, bit for bit."""
+    (qa, ka, va, sa, ea), (qb, kb, vb, sb, eb) = _qkv_two_calls_and_fused(dev, K, Hq, Hkv, D, 96, pos, K + pos)
+    assert ea == 0 and eb == 0
+    assert torch.equal(qa, qb) and torch.equal(ka, kb) and torch.equal(va, vb)
+    assert sa == sb == pos + 1
+    assert int(kb[pos].ne(0).sum()) > 0 and int(kb.ne(0).sum()) == int(kb[pos].ne(0).sum())
+
+
+def test_qkv_rope_fused_rejects_position_past_cache(dev):
+    outs = _qkv_two_calls_and_fused(dev, 896, 14, 2, 64, 32, 32, 5)
+    for q, kc, vc, sl, err in outs:
+        assert err & 2 and sl == 0
+        assert int(kc.ne(0).sum()) == 0 and int(vc.ne(0).sum()) == 0
+
+
 def test_rope_kv_append(dev):
     lib = _lib.load()
     QH, KVH, D, Tmax, pos = 14, 2, 64, 64, 37
