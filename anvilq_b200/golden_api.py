@@ -6,6 +6,9 @@
   projection numbering (0..6 = q,k,v,o,gate,up,down), bias added for q/k/v,
   list of floats out, and a CheckpointError-style exception on an invalid
   scale.  Activations are rounded to binary16 (the W4A16 contract).
+* ``GpuLinear(...).linear_q16(x_q16, layer, projection)`` is the integer model's
+  projection (the ``linear`` inside FixedModel.token, official_weights.py:592-612):
+  Q16.16 ints in and out, bit-identical.
 * ``dequant(qw, qz, h, lane)`` mirrors verify.dequant (anvil-q1/tests/verify.py:241-250)
   for one lane of one word, computed on the GPU by the GEMM kernels' unpack.
 * ``pack(values)`` mirrors verify.pack (verify.py:252-253).
@@ -80,6 +83,20 @@ class GpuLinear:
         except AnvilqError as exc:
             raise CheckpointError(str(exc)) from exc
         return [float(v) for v in y.float().cpu().numpy()]
+
+    def linear_q16(self, x_q16, layer, projection):
+        """The integer model's projection (the ``linear`` of FixedModel.token,
+        official_weights.py:592-612): Q16.16 int activations in, Q16.16 ints out,
+        exact sum of x * (q - z) * round_away(scale * 2^16), bias * 2^16 added for
+        q/k/v, round-half-away >> 16, saturated to int32; bit-identical."""
+        qweight, qzeros, scales, bias = self.weights(layer, projection)
+        xt = torch.tensor(np.asarray(x_q16, np.int64).astype(np.int32), device=self.device)
+        try:
+            y = ops.gemm_q16(xt, qweight, qzeros, scales, bias, self.shape[6])
+            ops.raise_device_errors(self.device)
+        except AnvilqError as exc:
+            raise CheckpointError(str(exc)) from exc
+        return [int(v) for v in y.cpu().numpy().reshape(-1)]
 
 
 SHIFTS = (0, 16, 4, 20, 8, 24, 12, 28)

@@ -2,7 +2,7 @@
 """Benchmark of the W4A16 AWQ decode datapath on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl anvilq|reference]
-                    [--workload decode05b|proj05b|proj7b]
+                    [--workload decode05b|proj05b|proj7b|attn|tp70b]
 
 decode05b (default): one step = one greedy decode token of a Qwen2.5-0.5B-shape
 W4A16 AWQ model (24 layers, hidden 896, 14/2 heads of 64, intermediate 4864,
@@ -17,6 +17,12 @@ inside every step, and the host waiting for it.
 
 proj05b / proj7b: one step = the W4A16 GEMV over every projection of a decode
 step (Qwen2.5-0.5B or Llama-7B-class shapes), value in GB/s.
+
+attn: one step = one decode-attention launch over the rank's share of a
+64-sequence batch at context 32768 (32/8 heads of 128); value = KV bytes
+streamed per second over all ranks (strong scaling, batch-sharded, no
+collective).  e2e copies q from pinned host memory and the output back
+every step.
 
 tp70b: one step = the three 70B-class layer projections, each column-split over
 the N GPUs (strong scaling) and all-gathered over NCCL, as one CUDA graph;
@@ -58,6 +64,10 @@ WORKLOADS = {
     "proj7b": dict(name="Llama-7B-class decode-step W4A16 projections: 32 layers x (q,k,v,o 4096x4096, "
                         "gate,up 4096x11008, down 11008x4096), G128, M=1",
                    layers=32, projections="LLAMA7B_PROJECTIONS"),
+    "attn": dict(name="GQA decode attention over an fp16 KV cache: 32 q / 8 kv heads of 128, global batch 64 at "
+                      "context 32768 (every sequence full), scale 1/sqrt(128); the batch is sharded over the GPUs "
+                      "(rank r holds sequences [64r/W, 64(r+1)/W)), no collective",
+                 batch=64, context=32768, hq=32, hkv=8, d=128),
     "tp70b": dict(name="70B-class W4A16 AWQ layer projections (K,N) in (8192,8192), (8192,28672), (28672,8192), "
                        "G128, column-split over the GPUs (rank r holds columns [rN/W, (r+1)N/W)), y all-gathered "
                        "over NCCL after every projection",
@@ -355,9 +365,42 @@ def decode_arm(args, world, rank, local):
     return 0
 
 
+def attn_reference_arm(args, world, rank):
+    if rank != 0:
+        return 0
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle
+    wl = WORKLOADS["attn"]
+    T, Hq, Hkv, D = wl["context"], wl["hq"], wl["hkv"], wl["d"]
+    q, k, v, n = attn_cpu(args.steps + args.warmup, wl, 60.0)
+    for _ in range(args.warmup):
+        for _ in range(n):
+            oracle.attention_f64(q[0], k[0], v[0])
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for _ in range(n):
+            oracle.attention_f64(q[0], k[0], v[0])
+    dt = time.perf_counter() - t0
+    value = args.steps * n * attn_bytes(1, T, Hq, Hkv, D) / dt / 1e9
+    sample = (f"oracle.attention_f64 (fp64 numpy restatement of fp64_reference.attention) on {n} whole "
+              f"sequences of context {T} per step; numpy/BLAS threads as available")
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (seeded; q, K, V ~ N(0,1) fp16)",
+            "config": {"workload": wl["name"], "sample": "whole sequences, see cpu_baseline"},
+            "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def reference_arm(args, world, rank):
     if args.workload == "decode05b":
         return decode_reference_arm(args, world, rank)
+    if args.workload == "attn":
+        return attn_reference_arm(args, world, rank)
     from anvilq_b200 import stream as st
     wl = WORKLOADS[args.workload]
     projections = (tuple((K, N, False) for K, N in wl["shapes"]) if "shapes" in wl
@@ -467,6 +510,125 @@ def anvilq_arm(args, world, rank, local):
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(projections)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------ attn
+def attn_bytes(B, T, Hq, Hkv, D):
+    """Algorithmic HBM bytes of one decode-attention launch: K and V once, q in, out."""
+    return B * T * Hkv * D * 2 * 2 + 2 * B * Hq * D * 2
+
+
+def attn_cpu(args_steps, wl, target_s):
+    """fp64 numpy restatement of attention() (fp64_reference.py:164-170) on whole
+    sequences of the workload; returns (bytes, seconds, sequences per step)."""
+    import numpy as np
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle
+    from anvilq_b200 import synthetic
+    T, Hq, Hkv, D = wl["context"], wl["hq"], wl["hkv"], wl["d"]
+    q, k, v = synthetic.kv_case(1, Hq, Hkv, D, T, seed=17)
+    t0 = time.perf_counter()
+    oracle.attention_f64(q[0], k[0], v[0])
+    dt = time.perf_counter() - t0
+    n = max(1, int(target_s / max(args_steps, 1) / max(dt, 1e-3)))
+    return q, k, v, n
+
+
+def attn_arm(args, world, rank, local):
+    import torch
+    from anvilq_b200 import ops
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    wl = WORKLOADS["attn"]
+    Bg, T, Hq, Hkv, D = wl["batch"], wl["context"], wl["hq"], wl["hkv"], wl["d"]
+    if Bg % world:
+        raise SystemExit(f"batch {Bg} does not split over {world} GPUs")
+    B = Bg // world
+    peak, peak_kind = load_peaks()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(17 + rank)
+    k = torch.randn((B, T, Hkv, D), generator=gen, device=dev, dtype=torch.float16)
+    v = torch.randn((B, T, Hkv, D), generator=gen, device=dev, dtype=torch.float16)
+    q = torch.randn((B, Hq, D), generator=gen, device=dev, dtype=torch.float16)
+    out = torch.empty_like(q)
+    seqlens = torch.full((B,), T, dtype=torch.int32, device=dev)
+    q_host = q.cpu().pin_memory()
+    out_host = torch.empty(q.shape, dtype=torch.float16).pin_memory()
+    stream = torch.cuda.Stream(dev)
+    step_bytes = attn_bytes(B, T, Hq, Hkv, D)
+
+    def step(host_io):
+        if host_io:
+            q.copy_(q_host, non_blocking=True)
+        ops.gqa_decode(q, k, v, seqlens, out=out)
+        if host_io:
+            out_host.copy_(out, non_blocking=True)
+
+    def timed(host_io):
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                step(host_io)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(args.steps):
+                step(host_io)
+                if host_io:
+                    stream.synchronize()
+            end.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = start.elapsed_time(end)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+            torch.distributed.barrier()
+        return ms
+
+    with ClockSampler(dev.index) as clocks:
+        ms = timed(False)
+    ms_e2e = timed(True)
+    ops.raise_device_errors(dev)
+    ms_step = ms / args.steps
+    value = step_bytes * world * args.steps / (ms / 1e3) / 1e9
+    achieved = step_bytes / (ms_step / 1e3) / 1e9   # one launch per step
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f16 q/K/V, fp32 scores and softmax",
+        "data": "synthetic (seeded; q, K, V ~ N(0,1) fp16)",
+        "config": {"workload": wl["name"], "batch": Bg, "batch_per_gpu": B, "context": T, "q_heads": Hq,
+                   "kv_heads": Hkv, "head_dim": D, "step_bytes_per_gpu": step_bytes,
+                   "l2": "KV per GPU larger than L2 (no flush)", "parallelism": f"batch-sharded x{world}"},
+        "roofline": {"bound": "hbm", "kernel": "gqa_decode_kernel", "achieved": round(achieved, 2), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
+                     "launch_avg_us": round(ms_step * 1e3, 3)},
+        "e2e": {"value": round(step_bytes * world * args.steps / (ms_e2e / 1e3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": q.numel() * 2, "d2h_bytes_per_step": out.numel() * 2,
+                "ms_per_step": round(ms_e2e / args.steps, 5)},
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, str(REPO / "oracle"))
+        import oracle
+        qc, kc, vc, n = attn_cpu(1, wl, 12.0)
+        t0 = time.perf_counter()
+        for _ in range(n):
+            oracle.attention_f64(qc[0], kc[0], vc[0])
+        dt = time.perf_counter() - t0
+        line["cpu_baseline"] = {
+            "value": round(n * attn_bytes(1, T, Hq, Hkv, D) / dt / 1e9, 4), "unit": "GB/s",
+            "cores": os.cpu_count(), "kind": "port",
+            "sample": f"oracle.attention_f64 (fp64 numpy restatement of fp64_reference.attention) on {n} whole "
+                      f"sequences of context {T}, {dt:.1f} s; numpy/BLAS threads as available"}
     if rank == 0:
         print(json.dumps(line), flush=True)
     return 0
@@ -624,6 +786,8 @@ def main(argv=None):
             return decode_arm(args, world, rank, local)
         if args.workload == "tp70b":
             return tp_arm(args, world, rank, local)
+        if args.workload == "attn":
+            return attn_arm(args, world, rank, local)
         return anvilq_arm(args, world, rank, local)
     finally:
         if world > 1:

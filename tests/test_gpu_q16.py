@@ -118,3 +118,15 @@ def test_shared_workspace_counters_stay_zero(dev):
     ops.raise_device_errors(dev)
     ws = ops.workspace(dev, 1)
     assert int(ws[:65536].count_nonzero()) == 0
+
+
+def test_golden_api_linear_q16(dev):
+    """GpuLinear.linear_q16: the integer model's projection over the checkpoint, bit-identical."""
+    from anvilq_b200.checkpoint import ArrayCheckpoint, gemv_shape
+    from anvilq_b200.golden_api import GpuLinear
+    _, layer = synthetic.gemv_case(1, 512, 128, 128, 61, bias=True)
+    x = _q16_activations(1, 512, 62)[0]
+    ckpt = ArrayCheckpoint({(0, 0): layer})
+    y = GpuLinear(ckpt, gemv_shape(512, 128, 128, 0)).linear_q16([int(v) for v in x], 0, 0)
+    ref = oracle.gemv_q16(x[None], layer.qweight, layer.qzeros, layer.scales_bits, layer.bias_bits, 128)
+    assert y == [int(v) for v in ref[0]]
