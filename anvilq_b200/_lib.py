@@ -37,9 +37,16 @@ SIGNATURES = {
     "anvilq_gqa_decode_workspace_size": (SZ, [I, I, I, I, I]),
     "anvilq_gqa_decode": (I, [P, P, P, P, P, I, I, I, I, I, F, P, SZ, P, P]),
     "anvilq_gqa_decode_noalloc": (I, [P, P, P, P, P, I, I, I, I, I, F, P, P]),
+    "anvilq_kv_int8_store": (I, [P, I, I, I, I, I, I, P, P, P, P, P, P]),
+    "anvilq_gqa_decode_int8": (I, [P, P, P, P, P, P, P, P, P, I, I, I, I, I, F, P, SZ, P, P]),
     "anvilq_w4a16_gemv_fused": (I, [P, I, P, F, P, P, P, P, P, I, I, I, I, P, SZ, P, ctypes.c_uint, P]),
     "anvilq_w4a16_gemv_qkv_rope": (I, [P, I, P, F, P, P, P, P, I, I, P, P, P, P, P, I, I, I, I, F, P, SZ, P,
                                        ctypes.c_uint, P]),
+    "anvilq_peer_handle_size": (SZ, []),
+    "anvilq_peer_export": (I, [P, P, ctypes.POINTER(ctypes.c_size_t)]),
+    "anvilq_peer_import": (I, [P, SZ, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)]),
+    "anvilq_peer_close": (I, [P]),
+    "anvilq_w4a16_gemv_allgather": (I, [P, P, P, P, P, I, I, I, I, I, I, I, P, P, P, P, SZ, P, ctypes.c_uint, P]),
     "anvilq_embed": (I, [P, P, P, I, I, P, P, ctypes.c_uint, P]),
     "anvilq_rope_kv_append": (I, [P, P, P, P, P, P, I, I, I, I, F, P, ctypes.c_uint, P]),
     "anvilq_lmhead_argmax": (I, [P, P, F, P, P, P, I, I, ctypes.c_uint, P]),

@@ -92,9 +92,15 @@ constexpr int kSmemBytes = kPartOff + kBandCols * 4;
 //              v heads copied to row *pos of the V cache, *seqlen = *pos + 1
 //              -- the same operations, in the same precision, as the separate
 //              RoPE/append kernel applied to the stored y.
+//   kYPeer     one rank's column slice of a tensor-parallel split: y = fp16(result
+//              (+ bias)) stored at columns [col0, col0 + N) of every rank's
+//              full-width output (peer memory over NVLink), then the ranks'
+//              completion flags exchanged, so that when the kernel completes
+//              the full row is present on every rank (the all-gather fused in).
 enum XMode { kXHalf = 0, kXRmsNorm = 1, kXSiluMul = 2 };
-enum YMode { kYHalf = 0, kYResidual = 1, kYRope = 2 };
+enum YMode { kYHalf = 0, kYResidual = 1, kYRope = 2, kYPeer = 3 };
 constexpr int kMaxRopePairs = 64;   // head_dim <= 128 in the fused RoPE epilogue
+constexpr int kMaxPeers = 8;        // ranks of a fused all-gather
 
 struct Params {
   const __half* x;         // kXHalf, kXSiluMul
@@ -121,6 +127,11 @@ struct Params {
   int* seqlen;             // optional
   int Hq, Hkv, D, Tmax;
   double rope_inv[kMaxRopePairs];   // theta^(-2i/D), binary64, computed on the host
+  // kYPeer only
+  __half* peer_y[kMaxPeers];         // every rank's full-width y [n_full] (this rank's included)
+  unsigned* peer_flags[kMaxPeers];   // every rank's flag array [kMaxPeers]
+  unsigned* epoch;                   // this rank's count of fused calls (device)
+  int world, tp_rank, col_base;      // col_base: first column of this rank's slice
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -166,6 +177,15 @@ __device__ __forceinline__ uint32_t dsmem_addr_u32(uint32_t local, uint32_t rank
 }
 __device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+// system-scope flag accesses between GPUs of the node
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 __device__ __forceinline__ half2 h2(uint32_t u) { return *reinterpret_cast<half2*>(&u); }
 __device__ __forceinline__ uint32_t u32(half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
@@ -520,6 +540,43 @@ __global__ void __launch_bounds__(kThreads, 4)
   } else {
     __syncthreads();
   }
+  if (YMODE == kYPeer) {   // kc == 1 (the host plan guarantees it)
+    for (int t = threadIdx.x; t < per; t += kThreads) {
+      if (col0 + t >= p.N) continue;
+      float out = slots[t];
+      for (int k = 1; k < c; ++k) out += slots[k * per + t];   // in rank order, as for kYHalf
+      if (p.bias) out += __half2float(p.bias[col0 + t]);
+      const __half h = __float2half_rn(out);
+      for (int r = 0; r < p.world; ++r) p.peer_y[r][p.col_base + col0 + t] = h;
+    }
+    // every CTA's stores are ordered before its ticket; the last CTA to arrive
+    // raises this rank's flag in every rank, then waits (bounded) for all flags
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const int n = atomicAdd_system(p.tickets, 1);
+      s_last = n == (int)gridDim.x - 1;
+      if (s_last) p.tickets[0] = 0;   // re-armed for the next launch
+    }
+    __syncthreads();
+    if (!s_last || threadIdx.x != 0) return;
+    __threadfence_system();
+    const unsigned e = *p.epoch + 1;
+    for (int r = 0; r < p.world; ++r) st_release_sys(p.peer_flags[r] + p.tp_rank, e);
+    const unsigned* mine = p.peer_flags[p.tp_rank];
+    const unsigned long long t_start = globaltimer();
+    bool done = false;
+    for (uint32_t i = 0; !done; ++i) {
+      done = true;
+      for (int r = 0; r < p.world; ++r) done &= (int)(ld_acquire_sys(mine + r) - e) >= 0;
+      if (!done && (i & 63u) == 63u && globaltimer() - t_start > kWaitLimitNs) {
+        if (p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_TIMEOUT);
+        break;
+      }
+    }
+    *p.epoch = e;
+    return;
+  }
   if (YMODE == kYRope) {   // kc == 1 (the host plan guarantees it)
     const int hd = p.D / 2;
     const int pos = *p.rope_pos;
@@ -655,6 +712,10 @@ static KernelFn kernel_bw(int bw) {
 }
 template <int XM>
 static KernelFn kernel_y(int ymode, int bw) {
+  if (ymode == kYPeer) {   // the fused all-gather takes fp16 activations
+    if constexpr (XM == kXHalf) return kernel_bw<kXHalf, kYPeer>(bw);
+    return nullptr;
+  }
   return ymode == kYHalf ? kernel_bw<XM, kYHalf>(bw) : ymode == kYResidual ? kernel_bw<XM, kYResidual>(bw)
                                                                          : kernel_bw<XM, kYRope>(bw);
 }
@@ -670,8 +731,9 @@ static const DeviceInfo* device_info() {
     DeviceInfo& d = g_dev[dev];
     cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
     for (int xm = 0; xm < 3; ++xm)
-      for (int ym = 0; ym < 3; ++ym)
+      for (int ym = 0; ym < 4; ++ym)
         for (int bw : kBandWidths) {
+          if (!kernel_for(xm, ym, bw)) continue;
           cudaFuncSetAttribute(kernel_for(xm, ym, bw), cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
           cudaFuncSetAttribute(kernel_for(xm, ym, bw), cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
       }
@@ -824,8 +886,14 @@ int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qze
   const DeviceInfo* d = device_info();
   auto encode = encode_fn();
   if (!d || d->sms <= 0 || !encode) return ANVILQ_ECUDA;
-  if (io.xmode < 0 || io.xmode > 2 || io.ymode < 0 || io.ymode > 2) return ANVILQ_EINVAL;
+  if (io.xmode < 0 || io.xmode > 2 || io.ymode < 0 || io.ymode > 3) return ANVILQ_EINVAL;
+  if (io.ymode == kYPeer && io.xmode != kXHalf) return ANVILQ_EINVAL;
   Plan pl = make_plan(*d, K, N);
+  if (io.ymode == kYPeer) {
+    if (io.world < 1 || io.world > kMaxPeers || io.tp_rank < 0 || io.tp_rank >= io.world || !io.epoch)
+      return ANVILQ_EINVAL;
+    if (pl.kc > 1) pl.kc = 1;   // one completion ticket per launch: no workspace fix-up
+  }
   if (io.ymode == kYRope) {
     // the epilogue needs whole heads in a band and one cluster per band; the
     // usual plan of every decode QKV shape qualifies, anything else falls back
@@ -847,6 +915,10 @@ int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qze
     if (!workspace || workspace_bytes < pl.bytes) return ANVILQ_EWORKSPACE;
     if ((reinterpret_cast<uintptr_t>(workspace) & 15u) != 0) return ANVILQ_EALIGN;
     if ((size_t)pl.bands * pl.c * sizeof(int) > ANVILQ_WORKSPACE_COUNTER_BYTES) return ANVILQ_ESHAPE;
+  }
+  if (io.ymode == kYPeer) {   // the launch's completion ticket lives in the counter region
+    if (!workspace || workspace_bytes < ANVILQ_WORKSPACE_COUNTER_BYTES) return ANVILQ_EWORKSPACE;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 15u) != 0) return ANVILQ_EALIGN;
   }
   const int W8 = N / 8;
   CUtensorMap map;
@@ -880,6 +952,14 @@ int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qze
   p.v_cache = reinterpret_cast<__half*>(io.v_cache);
   p.seqlen = io.seqlen;
   p.Hq = io.Hq; p.Hkv = io.Hkv; p.D = io.D; p.Tmax = io.Tmax;
+  for (int r = 0; r < kMaxPeers; ++r) {
+    p.peer_y[r] = r < io.world ? reinterpret_cast<__half*>(io.peer_y[r]) : nullptr;
+    p.peer_flags[r] = r < io.world ? io.peer_flags[r] : nullptr;
+  }
+  p.epoch = io.epoch;
+  p.world = io.world;
+  p.tp_rank = io.tp_rank;
+  p.col_base = io.col_base;
   for (int i = 0; i < kMaxRopePairs; ++i)
     p.rope_inv[i] = io.ymode == kYRope && i < io.D / 2 ? std::pow((double)io.theta, -2.0 * i / io.D) : 0.0;
   p.cluster = pl.c;

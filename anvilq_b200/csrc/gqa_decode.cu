@@ -79,16 +79,29 @@ struct Params {
   int Hq, Hkv, Tmax, group;
   int cluster, clusters;   // CTAs per cluster, clusters per pair (gridDim.x = their product)
   float scale_log2;        // softmax scale * log2(e)
+  // INT8 cache only: fp32 payloads of escaped (token, kv head) rows, [B][Tmax][Hkv][D] (may be NULL)
+  const float* k_escape;
+  const float* v_escape;
 };
 
-template <int D>
+constexpr uint32_t kEscapeMarker = 0x7FC00000u;   // INT8-cache metadata of an escaped row
+
+// Q8: the cache holds INT8 codes with per-(token, kv head) scales (kv_int8.cu);
+// a stage then carries the K and V code tiles and their 16 metadata words, and
+// each warp stages them into fp16 tiles of the same swizzled layout for the MMAs.
+template <int D, bool Q8 = false>
 struct Layout {
   static constexpr int kStages = 2;                            // ring depth per warp
   static constexpr int kHalves = D / 64;                       // 128-byte boxes per row
   static constexpr int kBoxBytes = kTile * 128;                // 16 rows x 64 dims, swizzled
-  static constexpr int kTileBytes = kHalves * kBoxBytes;       // [half][row][128 B]
-  static constexpr int kStageBytes = 2 * kTileBytes;           // K tile + V tile
-  static constexpr int kWarpBytes = kStages * kStageBytes;
+  static constexpr int kTileBytes = kHalves * kBoxBytes;       // fp16 tile: [half][row][128 B]
+  static constexpr int kCodeBytes = kTile * D;                 // INT8 tile: [row][D]
+  static constexpr int kMetaBytes = kTile * 4;                 // 16 metadata words (one TMA box)
+  static constexpr int kMetaSlot = 128;                        // a TMA destination is 128-byte aligned
+  static constexpr int kStageBytes = Q8 ? 2 * kCodeBytes + 2 * kMetaSlot : 2 * kTileBytes;
+  static constexpr int kStageTx = Q8 ? 2 * kCodeBytes + 2 * kMetaBytes : 2 * kTileBytes;   // bytes landed
+  static constexpr int kStagingOffset = kStages * kStageBytes; // Q8: fp16 K tile + V tile, per warp
+  static constexpr int kWarpBytes = kStagingOffset + (Q8 ? 2 * kTileBytes : 0);
   static constexpr int kRingBytes = kWarps * kWarpBytes;
   static constexpr int kRow = D + 2;                           // one head's state: o[D], max, sum
   static constexpr int kStateBytes = kMaxGroup * kRow * 4;     // a warp's or a CTA's state
@@ -99,6 +112,8 @@ struct Layout {
   static constexpr int kSlotBytes = kMaxCluster * kStateBytes;
   static constexpr int kTotal = kSlotOffset + kSlotBytes + 1024;   // + slack to align the ring to 1024
   static_assert(kBoxBytes % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
+  static_assert(kStageBytes % 128 == 0 && kWarpBytes % 128 == 0 && kCodeBytes % 128 == 0,
+                "stages, warp areas and every TMA destination stay 128-byte aligned");
   static_assert(kWarpBytes >= kStateBytes, "a warp's state fits its idle ring");
   static_assert(kTotal <= 227 * 1024, "fits one SM's shared memory");
   // byte offset of the 16-byte chunk c (of 8 dims) of row r inside a tile
@@ -146,6 +161,13 @@ __device__ __forceinline__ void tma_4d(uint32_t dst, const CUtensorMap* map, int
       "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
       : "memory");
 }
+__device__ __forceinline__ void tma_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(dst),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+      : "memory");
+}
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -191,11 +213,22 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
 }
+// four INT8 codes (ascending bytes) as four fp16 values (exact: |code| <= 127)
+__device__ __forceinline__ uint2 codes_to_half4(uint32_t w) {
+  return make_uint2(pack_half2((float)(int8_t)(w & 0xFFu), (float)(int8_t)((w >> 8) & 0xFFu)),
+                    pack_half2((float)(int8_t)((w >> 16) & 0xFFu), (float)(int8_t)(w >> 24)));
+}
+// a row's scale from its metadata word (1 for an escaped row, whose payload is the value itself)
+__device__ __forceinline__ float meta_scale(uint32_t m) { return m == kEscapeMarker ? 1.0f : __uint_as_float(m); }
 
-template <int D>
+// mk / mv: the K / V cache (fp16, or Q8: INT8 codes); mkm / mvm (Q8 only): their
+// metadata [B][Hkv][Tmax] uint32.
+template <int D, bool Q8>
 __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
-    gqa_decode_kernel(const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv, const Params p) {
-  using L = Layout<D>;
+    gqa_decode_kernel(const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv,
+                      const __grid_constant__ CUtensorMap mkm, const __grid_constant__ CUtensorMap mvm,
+                      const Params p) {
+  using L = Layout<D, Q8>;
   constexpr int KS = D / 16;   // k-steps of QK, m-tiles of PV
   constexpr int kStages = L::kStages;
   constexpr int R = L::kRow;
@@ -224,6 +257,10 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
     if (warp == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(&mk) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(&mv) : "memory");
+      if (Q8) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&mkm) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&mvm) : "memory");
+      }
     }
   }
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -240,13 +277,21 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
     fence_proxy_async();
     __syncwarp();
     if (lane == 0) {
-      mbar_expect_tx(bar, 2 * kTile * D * 2);
       const int t0 = (tb + warp + kWarps * j) * kTile;
       const uint32_t kd = smem_u32(ring + st * L::kStageBytes);
+      if (Q8) {
+        mbar_expect_tx(bar, L::kStageTx);
+        tma_4d(kd, &mk, 0, h, t0, b, bar);
+        tma_4d(kd + L::kCodeBytes, &mv, 0, h, t0, b, bar);
+        tma_3d(kd + 2 * L::kCodeBytes, &mkm, t0, h, b, bar);
+        tma_3d(kd + 2 * L::kCodeBytes + L::kMetaSlot, &mvm, t0, h, b, bar);
+      } else {
+        mbar_expect_tx(bar, 2 * kTile * D * 2);
 #pragma unroll
-      for (int hf = 0; hf < L::kHalves; ++hf) {
-        tma_4d(kd + hf * L::kBoxBytes, &mk, 64 * hf, h, t0, b, bar);
-        tma_4d(kd + L::kTileBytes + hf * L::kBoxBytes, &mv, 64 * hf, h, t0, b, bar);
+        for (int hf = 0; hf < L::kHalves; ++hf) {
+          tma_4d(kd + hf * L::kBoxBytes, &mk, 64 * hf, h, t0, b, bar);
+          tma_4d(kd + L::kTileBytes + hf * L::kBoxBytes, &mv, 64 * hf, h, t0, b, bar);
+        }
       }
     }
     __syncwarp();
@@ -273,6 +318,9 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
   for (int mt = 0; mt < KS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.0f;
   float m_run = -INFINITY, l_run = 0.0f;
   bool ok = true;
+  // Q8: o holds the output divided by F, the largest V scale of the last tile
+  // (the V scales are folded into P, normalised per tile to stay clear of fp16 underflow)
+  float F = 1.0f;
 
   for (int j = 0; j < my_tiles && ok; ++j) {
     if (issued < my_tiles) issue(issued++);
@@ -283,10 +331,46 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
       ok = false;
       break;
     }
+    const int t0 = (tb + warp + kWarps * j) * kTile;
     const unsigned char* kt = ring + st * L::kStageBytes;
     const unsigned char* vt = kt + L::kTileBytes;
-    const int t0 = (tb + warp + kWarps * j) * kTile;
-    if (t0 + kTile > seqlen) {
+    const uint32_t* km = reinterpret_cast<const uint32_t*>(kt + 2 * L::kCodeBytes);   // Q8 metadata
+    const uint32_t* vm = reinterpret_cast<const uint32_t*>(kt + 2 * L::kCodeBytes + L::kMetaSlot);
+    if (Q8) {
+      // codes -> fp16 tiles in the swizzled layout; escaped rows from their fp32
+      // payload; rows past the sequence zero
+      unsigned char* sk = ring + L::kStagingOffset;
+      unsigned char* sv = sk + L::kTileBytes;
+      for (int e = lane; e < kTile * D / 4; e += 32) {
+        const int r = e / (D / 4), d = 4 * (e % (D / 4));
+        const int tok = t0 + r;
+        uint2 hk = make_uint2(0, 0), hv = make_uint2(0, 0);
+        if (tok < seqlen) {
+          const size_t esc_at = (((size_t)b * p.Tmax + tok) * p.Hkv + h) * D + d;
+          if (km[r] != kEscapeMarker) {
+            hk = codes_to_half4(*reinterpret_cast<const uint32_t*>(kt + r * D + d));
+          } else if (p.k_escape) {
+            const float4 f = *reinterpret_cast<const float4*>(p.k_escape + esc_at);
+            hk = make_uint2(pack_half2(f.x, f.y), pack_half2(f.z, f.w));
+          } else if (d == 0) {
+            atomicOr(p.dev_err, ANVILQ_DEV_ERR_NONFINITE);
+          }
+          if (vm[r] != kEscapeMarker) {
+            hv = codes_to_half4(*reinterpret_cast<const uint32_t*>(kt + L::kCodeBytes + r * D + d));
+          } else if (p.v_escape) {
+            const float4 f = *reinterpret_cast<const float4*>(p.v_escape + esc_at);
+            hv = make_uint2(pack_half2(f.x, f.y), pack_half2(f.z, f.w));
+          } else if (d == 0) {
+            atomicOr(p.dev_err, ANVILQ_DEV_ERR_NONFINITE);
+          }
+        }
+        *reinterpret_cast<uint2*>(sk + L::chunk(r, d >> 3) + (d & 7) * 2) = hk;
+        *reinterpret_cast<uint2*>(sv + L::chunk(r, d >> 3) + (d & 7) * 2) = hv;
+      }
+      __syncwarp();
+      kt = sk;
+      vt = sv;
+    } else if (t0 + kTile > seqlen) {
       // rows past the sequence: zero their V (scores are masked below)
       unsigned char* vz = ring + st * L::kStageBytes + L::kTileBytes;
       for (int e = lane; e < kTile * L::kHalves * 8; e += 32) {
@@ -318,7 +402,8 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int tok = t0 + nt * 8 + 2 * (lane % 4) + e;
-        x[nt * 2 + e] = tok < seqlen ? s[nt][e] * p.scale_log2 : -INFINITY;
+        const float ks = Q8 && tok < seqlen ? meta_scale(km[tok - t0]) : 1.0f;   // Q8: code scale of K
+        x[nt * 2 + e] = tok < seqlen ? s[nt][e] * ks * p.scale_log2 : -INFINITY;
       }
     float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -330,10 +415,25 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
     for (int e = 0; e < 4; ++e) pr[e] = exp2f(x[e] - m_new);
     l_run = l_run * alpha + (pr[0] + pr[1]) + (pr[2] + pr[3]);
     m_run = m_new;
+    float rescale = 1.0f;   // Q8: F_old / F_new on top of the softmax rescale
+    if (Q8) {
+      // P times each token's V scale over the tile's largest one
+      float vs = lane < kTile && t0 + lane < seqlen ? meta_scale(vm[lane]) : 0.0f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) vs = fmaxf(vs, __shfl_xor_sync(0xffffffffu, vs, o));
+      const float inv = 1.0f / vs;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = (e >> 1) * 8 + 2 * (lane % 4) + (e & 1);
+        pr[e] = t0 + r < seqlen ? pr[e] * (meta_scale(vm[r]) * inv) : 0.0f;
+      }
+      rescale = F * inv;
+      F = vs;
+    }
     const uint32_t pb0 = pack_half2(pr[0], pr[1]);   // tokens 2(l%4), +1   (k rows 0..7)
     const uint32_t pb1 = pack_half2(pr[2], pr[3]);   // tokens 8 + 2(l%4)   (k rows 8..15)
-    const float alpha_a = __shfl_sync(0xffffffffu, alpha, 8 * (lane % 4));
-    const float alpha_b = __shfl_sync(0xffffffffu, alpha, 8 * (lane % 4) + 4);
+    const float alpha_a = __shfl_sync(0xffffffffu, alpha, 8 * (lane % 4)) * rescale;
+    const float alpha_b = __shfl_sync(0xffffffffu, alpha, 8 * (lane % 4) + 4) * rescale;
 #pragma unroll
     for (int mt = 0; mt < KS; ++mt) {
       o[mt][0] *= alpha_a;
@@ -362,13 +462,14 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
     m_run = -INFINITY;
     l_run = 0.0f;
   }
+  if (!Q8) F = 1.0f;
 #pragma unroll
   for (int mt = 0; mt < KS; ++mt) {
     const int d = 16 * mt + lane / 4, hh = 2 * (lane % 4);
-    mine[hh * R + d] = ok ? o[mt][0] : 0.0f;
-    mine[(hh + 1) * R + d] = ok ? o[mt][1] : 0.0f;
-    mine[hh * R + d + 8] = ok ? o[mt][2] : 0.0f;
-    mine[(hh + 1) * R + d + 8] = ok ? o[mt][3] : 0.0f;
+    mine[hh * R + d] = ok ? o[mt][0] * F : 0.0f;
+    mine[(hh + 1) * R + d] = ok ? o[mt][1] * F : 0.0f;
+    mine[hh * R + d + 8] = ok ? o[mt][2] * F : 0.0f;
+    mine[(hh + 1) * R + d + 8] = ok ? o[mt][3] * F : 0.0f;
   }
   if (lane % 4 == 0) {
     mine[g * R + D] = m_run;
@@ -542,7 +643,7 @@ static int max_active_clusters() {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(kMaxCluster * 64);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = Layout<D>::kTotal;
+  cfg.dynamicSmemBytes = Layout<D, false>::kTotal;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = kMaxCluster;
@@ -551,7 +652,7 @@ static int max_active_clusters() {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, gqa_decode_kernel<D>, &cfg) != cudaSuccess) n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gqa_decode_kernel<D, false>, &cfg) != cudaSuccess) n = 0;
   return n;
 }
 
@@ -561,8 +662,14 @@ static const DeviceInfo* device_info() {
   std::call_once(g_once[dev], [dev] {
     DeviceInfo& in = g_info[dev];
     cudaDeviceGetAttribute(&in.sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaFuncSetAttribute(gqa_decode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout<64>::kTotal);
-    cudaFuncSetAttribute(gqa_decode_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout<128>::kTotal);
+    cudaFuncSetAttribute(gqa_decode_kernel<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         Layout<64, false>::kTotal);
+    cudaFuncSetAttribute(gqa_decode_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         Layout<128, false>::kTotal);
+    cudaFuncSetAttribute(gqa_decode_kernel<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         Layout<64, true>::kTotal);
+    cudaFuncSetAttribute(gqa_decode_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         Layout<128, true>::kTotal);
     in.max_clusters[0] = max_active_clusters<64>();
     in.max_clusters[1] = max_active_clusters<128>();
     cudaGetLastError();
@@ -635,13 +742,41 @@ static bool cache_map(CUtensorMap* map, const void* cache, int B, int Hkv, int D
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Tensor maps for both caches, then one launch (clusters of p.cluster CTAs along x).
-template <int D>
-static cudaError_t launch_d(const CUtensorMap& mk, const CUtensorMap& mv, const Params& p, int B, cudaStream_t st) {
+// INT8 codes [B][Tmax][Hkv][D] as a 4-D tensor (D, Hkv, Tmax, B); one box = a
+// 16-token tile of one kv head, unswizzled.
+static bool code_map(CUtensorMap* map, const void* codes, int B, int Hkv, int D, int Tmax) {
+  auto encode = encode_fn();
+  if (!encode) return false;
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)Hkv, (cuuint64_t)Tmax, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)D, (cuuint64_t)Hkv * D, (cuuint64_t)Tmax * Hkv * D};
+  const cuuint32_t box[4] = {(cuuint32_t)D, 1, (cuuint32_t)kTile, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(codes), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Metadata [B][Hkv][Tmax] uint32 as (Tmax, Hkv, B); one box = 16 tokens' words.
+static bool meta_map(CUtensorMap* map, const void* meta, int B, int Hkv, int Tmax) {
+  auto encode = encode_fn();
+  if (!encode) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)Tmax, (cuuint64_t)Hkv, (cuuint64_t)B};
+  const cuuint64_t strides[2] = {(cuuint64_t)Tmax * 4, (cuuint64_t)Hkv * Tmax * 4};
+  const cuuint32_t box[3] = {(cuuint32_t)kTile, 1, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void*>(meta), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// One launch, clusters of p.cluster CTAs along x.
+template <int D, bool Q8>
+static cudaError_t launch_d(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mkm,
+                            const CUtensorMap& mvm, const Params& p, int B, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.cluster * p.clusters, p.Hkv, B);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = Layout<D>::kTotal;
+  cfg.dynamicSmemBytes = Layout<D, Q8>::kTotal;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -650,19 +785,35 @@ static cudaError_t launch_d(const CUtensorMap& mk, const CUtensorMap& mv, const 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gqa_decode_kernel<D>, mk, mv, p);
+  return cudaLaunchKernelEx(&cfg, gqa_decode_kernel<D, Q8>, mk, mv, mkm, mvm, p);
 }
 
-static int launch(const Params& p, int B, int D, const void* k_cache, const void* v_cache, cudaStream_t st) {
-  CUtensorMap mk, mv;
-  if (!cache_map(&mk, k_cache, B, p.Hkv, D, p.Tmax) || !cache_map(&mv, v_cache, B, p.Hkv, D, p.Tmax))
-    return ANVILQ_EALIGN;
-  const cudaError_t e = D == 64 ? launch_d<64>(mk, mv, p, B, st) : launch_d<128>(mk, mv, p, B, st);
+static int finish_launch(cudaError_t e) {
   if (e != cudaSuccess) {
     cudaGetLastError();
     return ANVILQ_ECUDA;
   }
   return cudaGetLastError() == cudaSuccess ? ANVILQ_OK : ANVILQ_ECUDA;
+}
+
+// fp16 caches: tensor maps for both, then one launch.
+static int launch(const Params& p, int B, int D, const void* k_cache, const void* v_cache, cudaStream_t st) {
+  CUtensorMap mk, mv;
+  if (!cache_map(&mk, k_cache, B, p.Hkv, D, p.Tmax) || !cache_map(&mv, v_cache, B, p.Hkv, D, p.Tmax))
+    return ANVILQ_EALIGN;
+  return finish_launch(D == 64 ? launch_d<64, false>(mk, mv, mk, mv, p, B, st)
+                               : launch_d<128, false>(mk, mv, mk, mv, p, B, st));
+}
+
+// INT8 caches: code and metadata tensor maps, then one launch.
+static int launch_q8(const Params& p, int B, int D, const void* k_codes, const void* k_meta, const void* v_codes,
+                     const void* v_meta, cudaStream_t st) {
+  CUtensorMap mk, mv, mkm, mvm;
+  if (!code_map(&mk, k_codes, B, p.Hkv, D, p.Tmax) || !code_map(&mv, v_codes, B, p.Hkv, D, p.Tmax) ||
+      !meta_map(&mkm, k_meta, B, p.Hkv, p.Tmax) || !meta_map(&mvm, v_meta, B, p.Hkv, p.Tmax))
+    return ANVILQ_EALIGN;
+  return finish_launch(D == 64 ? launch_d<64, true>(mk, mv, mkm, mvm, p, B, st)
+                               : launch_d<128, true>(mk, mv, mkm, mvm, p, B, st));
 }
 
 }  // namespace attn
@@ -703,7 +854,40 @@ int anvilq_gqa_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t
   p.cluster = pl.cluster; p.clusters = pl.clusters;
   const float s = scale > 0.0f ? scale : 1.0f / std::sqrt((float)D);
   p.scale_log2 = s * 1.4426950408889634f;
+  p.k_escape = p.v_escape = nullptr;
   return launch(p, B, D, k_cache, v_cache, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int anvilq_gqa_decode_int8(const uint16_t* q, const int8_t* k_codes, const uint32_t* k_meta, const float* k_escape,
+                           const int8_t* v_codes, const uint32_t* v_meta, const float* v_escape,
+                           const int32_t* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D, int Tmax,
+                           float scale, void* workspace, size_t workspace_bytes, int* dev_err,
+                           anvilq_stream_t stream) {
+  if (!q || !k_codes || !k_meta || !v_codes || !v_meta || !seqlens || !out || !dev_err) return ANVILQ_EINVAL;
+  if (!args_ok(B, Hq, Hkv, D, Tmax) || Tmax % kTile) return ANVILQ_ESHAPE;
+  if (!a16(q) || !a16(k_codes) || !a16(v_codes) || !a16(k_meta) || !a16(v_meta) || !a16(out) ||
+      (k_escape && !a16(k_escape)) || (v_escape && !a16(v_escape)))
+    return ANVILQ_EALIGN;
+  const DeviceInfo* dev = device_info();
+  if (!dev) return ANVILQ_ECUDA;
+  const Plan pl = plan_for(B, Hq, Hkv, D, Tmax, *dev);
+  if (!workspace || workspace_bytes < pl.bytes) return ANVILQ_EWORKSPACE;
+  if (!a16(workspace)) return ANVILQ_EALIGN;
+  Params p;
+  p.q = reinterpret_cast<const __half*>(q);
+  p.k = p.v = nullptr;
+  p.seqlens = seqlens;
+  p.out = reinterpret_cast<__half*>(out);
+  p.tickets = reinterpret_cast<int*>(workspace);
+  p.partials = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + ANVILQ_WORKSPACE_COUNTER_BYTES);
+  p.dev_err = dev_err;
+  p.Hq = Hq; p.Hkv = Hkv; p.Tmax = Tmax; p.group = Hq / Hkv;
+  p.cluster = pl.cluster; p.clusters = pl.clusters;
+  const float s = scale > 0.0f ? scale : 1.0f / std::sqrt((float)D);
+  p.scale_log2 = s * 1.4426950408889634f;
+  p.k_escape = k_escape;
+  p.v_escape = v_escape;
+  return launch_q8(p, B, D, k_codes, k_meta, v_codes, v_meta, reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"
@@ -785,5 +969,6 @@ extern "C" int anvilq_gqa_decode_noalloc(const uint16_t* q, const uint16_t* k_ca
   p.cluster = pl.cluster; p.clusters = pl.clusters;
   const float s = scale > 0.0f ? scale : 1.0f / std::sqrt((float)D);
   p.scale_log2 = s * 1.4426950408889634f;
+  p.k_escape = p.v_escape = nullptr;
   return launch(p, B, D, k_cache, v_cache, st);
 }

@@ -30,6 +30,11 @@ struct GemvIo {
   int32_t* seqlen = nullptr;
   int Hq = 0, Hkv = 0, D = 0, Tmax = 0;
   float theta = 0.0f;
+  // ymode 3 (column slice of a tensor-parallel split, all-gather fused in)
+  uint16_t* peer_y[8] = {};
+  unsigned* peer_flags[8] = {};
+  unsigned* epoch = nullptr;
+  int world = 0, tp_rank = 0, col_base = 0;
 };
 int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
                     const uint16_t* bias, int K, int N, int G, void* workspace, size_t workspace_bytes, int* dev_err,

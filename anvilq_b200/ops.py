@@ -306,3 +306,59 @@ def gqa_decode(q, k_cache, v_cache, seqlens, scale: float = 0.0, out=None, dev_e
                                      Hkv, D, Tmax, float(scale), _ptr(ws), ws.numel(), _ptr(err),
                                      _stream_ptr(q.device)), "anvilq_gqa_decode")
     return out
+
+
+def kv_int8_store(src, codes, meta, escape=None, start=None, dev_err=None):
+    """Encode K or V rows src [B, T, H, D] (fp16 or fp32) into an INT8 cache:
+    codes int8 [B, Tmax, H, D], meta int32 [B, H, Tmax] (uint32 scale bits or the
+    escape marker 0x7FC00000), escape fp32 [B, Tmax, H, D] or None; rows go to
+    positions start[b] + t (start: int32 CUDA tensor [B], or None for 0).
+
+    The Anvil-Q4 per-head INT8 cache with FP32 escape (anvil-q4/tests/cache_reference.py:54-83)."""
+    if src.dim() != 4 or src.dtype not in (torch.float16, torch.float32) or not src.is_contiguous():
+        raise ValueError("src must be contiguous fp16/fp32 [B, T, H, D]")
+    B, T, H, D = src.shape
+    if codes.dtype != torch.int8 or codes.dim() != 4 or codes.shape[0] != B or codes.shape[2:] != (H, D):
+        raise ValueError("codes must be int8 [B, Tmax, H, D]")
+    Tmax = codes.shape[1]
+    if meta.dtype != torch.int32 or tuple(meta.shape) != (B, H, Tmax):
+        raise ValueError("meta must be int32 [B, H, Tmax]")
+    if escape is not None and (escape.dtype != torch.float32 or escape.shape != codes.shape):
+        raise ValueError("escape must be float32 with the shape of codes")
+    if start is not None and (start.dtype != torch.int32 or start.numel() != B or not start.is_cuda):
+        raise ValueError("start must be an int32 CUDA tensor [B]")
+    lib = _lib.load()
+    err = device_error_word(src.device) if dev_err is None else dev_err
+    _lib.check(lib.anvilq_kv_int8_store(_ptr(src), 1 if src.dtype == torch.float16 else 0, B, T, H, D, Tmax,
+                                        _ptr(start), _ptr(codes), _ptr(meta), _ptr(escape), _ptr(err),
+                                        _stream_ptr(src.device)), "anvilq_kv_int8_store")
+
+
+def gqa_decode_int8(q, k_codes, k_meta, v_codes, v_meta, seqlens, k_escape=None, v_escape=None, scale: float = 0.0,
+                    out=None, dev_err=None):
+    """gqa_decode over INT8 caches (kv_int8_store's format); returns fp16 [B, Hq, D]."""
+    if q.dtype != torch.float16 or q.dim() != 3 or not q.is_contiguous():
+        raise TypeError("q must be contiguous float16 [B, Hq, D]")
+    B, Hq, D = q.shape
+    if k_codes.dtype != torch.int8 or k_codes.dim() != 4 or v_codes.shape != k_codes.shape:
+        raise ValueError("k_codes/v_codes must be int8 [B, Tmax, Hkv, D]")
+    _, Tmax, Hkv, Dk = k_codes.shape
+    if Dk != D or k_codes.shape[0] != B:
+        raise ValueError("batch or head_dim of q and the caches differ")
+    if k_meta.dtype != torch.int32 or tuple(k_meta.shape) != (B, Hkv, Tmax) or v_meta.shape != k_meta.shape:
+        raise ValueError("k_meta/v_meta must be int32 [B, Hkv, Tmax]")
+    if seqlens.dtype != torch.int32 or seqlens.numel() != B or not seqlens.is_cuda:
+        raise ValueError("seqlens must be an int32 CUDA tensor [B]")
+    if out is None:
+        out = torch.empty_like(q)
+    lib = _lib.load()
+    need = lib.anvilq_gqa_decode_workspace_size(B, Hq, Hkv, D, Tmax)
+    if need == 0:
+        raise ValueError(f"unsupported attention shape B={B} Hq={Hq} Hkv={Hkv} D={D} Tmax={Tmax}")
+    ws = workspace(q.device, need)
+    err = device_error_word(q.device) if dev_err is None else dev_err
+    _lib.check(lib.anvilq_gqa_decode_int8(_ptr(q), _ptr(k_codes), _ptr(k_meta), _ptr(k_escape), _ptr(v_codes),
+                                          _ptr(v_meta), _ptr(v_escape), _ptr(seqlens), _ptr(out), B, Hq, Hkv, D,
+                                          Tmax, float(scale), _ptr(ws), ws.numel(), _ptr(err),
+                                          _stream_ptr(q.device)), "anvilq_gqa_decode_int8")
+    return out

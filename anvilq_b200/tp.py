@@ -11,8 +11,16 @@ kernels, and one all-gather (NCCL on GPUs) assembles y.
 The exchange is the only collective: ranks share no partial sums (the K
 reduction is complete inside each rank), so results are bit-identical to the
 single-GPU call on the same slice of columns.
+
+At M = 1 the all-gather can be fused into the GEMV itself
+(``FusedTPLinear``): each rank's kernel stores its slice straight into every
+rank's full-width output over NVLink (CUDA IPC buffers, ``PeerOutputs``) and
+the ranks exchange completion flags, so one kernel per projection replaces the
+GEMV + NCCL all-gather pair.
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -74,3 +82,97 @@ class TPLinear:
         x2 = x.unsqueeze(0) if x.dim() == 1 else x
         y = gather_columns(self.local(x2), self.world, self.pg)
         return y.view(self.N) if x.dim() == 1 else y
+
+
+class PeerOutputs:
+    """Full-width fp16 outputs that every rank of the group writes directly
+    (peer stores over NVLink into CUDA IPC buffers), ``slots`` of them, plus the
+    flag array and the call counter of the fused all-gather.  Collective: every
+    rank constructs it with the same arguments, and closes it."""
+
+    _FLAGS = 256   # bytes reserved for the 8 flags at the start of the buffer
+
+    def __init__(self, n_full: int, slots: int = 2, device=None, process_group=None):
+        from . import _lib
+        self.lib = _lib.load()
+        self.pg = process_group
+        self.world = dist.get_world_size(process_group)
+        self.rank = dist.get_rank(process_group)
+        if not 1 <= self.world <= 8:
+            raise ValueError("the fused all-gather spans 1 to 8 ranks")
+        self.n_full, self.slots = n_full, slots
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.slot_bytes = -(-n_full * 2 // 256) * 256
+        self.buf = torch.zeros(self._FLAGS + slots * self.slot_bytes, dtype=torch.uint8, device=self.device)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=self.device)
+        torch.cuda.synchronize(self.device)
+        handle = (ctypes.c_char * self.lib.anvilq_peer_handle_size())()
+        offset = ctypes.c_size_t()
+        _lib.check(self.lib.anvilq_peer_export(self.buf.data_ptr(), handle, ctypes.byref(offset)),
+                   "anvilq_peer_export")
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, (bytes(handle), offset.value), group=process_group)
+        self._opened, ptrs = [], []
+        for r, (h, off) in enumerate(everyone):
+            if r == self.rank:
+                ptrs.append(self.buf.data_ptr())
+                continue
+            base, ptr = ctypes.c_void_p(), ctypes.c_void_p()
+            _lib.check(self.lib.anvilq_peer_import(h, off, ctypes.byref(base), ctypes.byref(ptr)),
+                       "anvilq_peer_import")
+            self._opened.append(base.value)
+            ptrs.append(ptr.value)
+        self.flag_ptrs = (ctypes.c_void_p * self.world)(*ptrs)
+        self.y_ptrs = [(ctypes.c_void_p * self.world)(*[q + self._FLAGS + s * self.slot_bytes for q in ptrs])
+                       for s in range(slots)]
+        dist.barrier(group=process_group)   # every rank holds every buffer before anyone writes
+
+    def output(self, slot: int, n: int | None = None):
+        """This rank's full-width output of one slot (a view, fp16 [n_full])."""
+        off = self._FLAGS + slot * self.slot_bytes
+        return self.buf[off:off + 2 * (n or self.n_full)].view(torch.float16)
+
+    def close(self):
+        """Collective: release the imported peer buffers (after all fused calls completed)."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.pg)
+        for base in self._opened:
+            self.lib.anvilq_peer_close(base)
+        self._opened = []
+
+
+class FusedTPLinear:
+    """``TPLinear`` at M = 1 with the all-gather fused into the GEMV: one kernel
+    per call computes this rank's slice and stores it in every rank's output
+    slot, then waits for every rank's completion flag.  Returns the full row
+    (a view of ``outputs.output(slot)``); slots must alternate between calls
+    (see anvilq_w4a16_gemv_allgather)."""
+
+    def __init__(self, qweight, qzeros, scales, bias, group_size: int, outputs: PeerOutputs, slot: int,
+                 sharded: bool = False):
+        """Full AWQ tensors of the projection, or (``sharded``) this rank's slice already."""
+        self.out = outputs
+        self.slot = slot
+        self.N = qweight.shape[1] * 8 * (outputs.world if sharded else 1)
+        if self.N > outputs.n_full:
+            raise ValueError("projection wider than the peer outputs")
+        self.col_base = column_range(self.N, outputs.rank, outputs.world)[0]
+        self.shard = ((qweight, qzeros, scales, bias) if sharded
+                      else shard_awq(qweight, qzeros, scales, bias, outputs.rank, outputs.world))
+        self.group_size = group_size
+        self.K = qweight.shape[0]
+
+    def __call__(self, x, flags: int = 0):
+        from . import _lib, ops
+        lib = self.out.lib
+        qw, qz, sc, b = self.shard
+        n = qw.shape[1] * 8
+        ws = ops.workspace(x.device, lib.anvilq_w4a16_gemm_workspace_size(1, self.K, n, self.group_size))
+        err = ops.device_error_word(x.device)
+        _lib.check(lib.anvilq_w4a16_gemv_allgather(
+            x.data_ptr(), qw.data_ptr(), qz.data_ptr(), sc.data_ptr(), None if b is None else b.data_ptr(),
+            self.K, n, self.group_size, self.out.rank, self.out.world, self.col_base, self.N,
+            ctypes.cast(self.out.y_ptrs[self.slot], ctypes.c_void_p), ctypes.cast(self.out.flag_ptrs, ctypes.c_void_p),
+            self.out.epoch.data_ptr(), ws.data_ptr(), ws.numel(), err.data_ptr(), flags,
+            torch.cuda.current_stream(x.device).cuda_stream), "anvilq_w4a16_gemv_allgather")
+        return self.out.output(self.slot, self.N)

@@ -25,11 +25,15 @@ collective).  e2e copies q from pinned host memory and the output back
 every step.
 
 tp70b: one step = the three 70B-class layer projections, each column-split over
-the N GPUs (strong scaling) and all-gathered over NCCL, as one CUDA graph;
-value = full-layer algorithmic GB/s over the max-over-ranks time; --tokens sets the
-token rows (1 for the GEMV, 16/64 for the verify GEMM).
+the N GPUs (strong scaling) and all-gathered, as one CUDA graph; at M = 1 on
+several GPUs the all-gather is fused into each GEMV (every rank stores its slice
+into every rank's output over NVLink and the ranks exchange completion flags),
+otherwise NCCL all-gathers follow the GEMMs; value = full-layer algorithmic GB/s
+over the max-over-ranks time; --tokens sets the token rows (1 for the GEMV, 16/64
+for the verify GEMM).
 
-With N GPUs each rank runs an independent replica (weak scaling, no collective).
+With N GPUs, decode05b and the projection sets run one independent replica per
+rank (weak scaling, no collective); attn shards its batch (no collective).
 
 --impl reference times the CPU restatement of the reference's golden model on
 the host cores over a bounded sample of the same workload: FP32Model.token
@@ -681,6 +685,26 @@ def tp_arm(args, world, rank, local):
         return graph
 
     g_full, g_comp = capture(True), capture(False)
+    # at M = 1 on several GPUs: the all-gather fused into each GEMV (peer stores over NVLink)
+    fused = world > 1 and M == 1
+    g_fused = outs = None
+    if fused:
+        from anvilq_b200 import tp
+        outs = tp.PeerOutputs(max(l[7] for l in layers), slots=len(layers), device=dev)
+        flins = [tp.FusedTPLinear(qw, qz, sc, None, 128, outs, i, sharded=True)
+                 for i, (x, qw, qz, sc, y, yg, K, N) in enumerate(layers)]
+
+        def step_fused():
+            for lin, l in zip(flins, layers):
+                lin(l[0][0])
+
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                step_fused()
+            stream.synchronize()
+            g_fused = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_fused, stream=stream):
+                step_fused()
 
     def timed(graph):
         for _ in range(args.warmup):
@@ -704,7 +728,9 @@ def tp_arm(args, world, rank, local):
 
     with torch.cuda.stream(stream):
         with ClockSampler(dev.index) as clocks:
-            ms = timed(g_full)
+            ms = ms_nccl = timed(g_full)
+            if fused:
+                ms = timed(g_fused)
         ms_comp = timed(g_comp)
         # e2e: activations from pinned host memory in, gathered outputs back to the host, every step
         x_host = [torch.randn(M, l[6]).half().pin_memory() for l in layers]
@@ -717,8 +743,11 @@ def tp_arm(args, world, rank, local):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(args.steps):
-            for (x, qw, qz, sc, y, yg, K, N), xh, yh in zip(layers, x_host, y_host):
+            for i, ((x, qw, qz, sc, y, yg, K, N), xh, yh) in enumerate(zip(layers, x_host, y_host)):
                 x.copy_(xh, non_blocking=True)
+                if fused:
+                    yh.copy_(flins[i](x[0]).view(1, -1), non_blocking=True)
+                    continue
                 ops.gemm(x, qw, qz, sc, None, 128, out=y)
                 if world > 1:
                     dist.all_gather_into_tensor(yg, y)
@@ -734,7 +763,9 @@ def tp_arm(args, world, rank, local):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms_e2e = float(t.item())
     ops.raise_device_errors(dev)
-    del g_full, g_comp
+    del g_full, g_comp, g_fused
+    if outs is not None:
+        outs.close()
     launches = 3
     value = full_bytes * args.steps / (ms / 1e3) / 1e9
     per_launch = ms_comp / args.steps / launches
@@ -746,7 +777,10 @@ def tp_arm(args, world, rank, local):
         "data": "synthetic (seeded; x~N(0,1), u4 uniform, scales |N(0,1)|*0.01+1e-3)",
         "config": {"workload": wl["name"], "M": M, "group": 128, "full_bytes_per_step": full_bytes,
                    "shard_bytes_per_rank": shard_bytes, "parallelism": f"tp{world} (column split)",
-                   "graph": "one CUDA graph per step: 3 GEMMs + 3 NCCL all-gathers",
+                   "graph": ("one CUDA graph per step: 3 GEMVs, each storing its slice into every rank's "
+                             "output over NVLink and exchanging completion flags (all-gather fused in)" if fused
+                             else "one CUDA graph per step: 3 GEMMs + 3 NCCL all-gathers"),
+                   "nccl_allgather_ms_per_step": round(ms_nccl / args.steps, 5),
                    "l2": "weights larger than L2 (no flush)",
                    "compute_only_ms_per_step": round(ms_comp / args.steps, 5)},
         "roofline": {"bound": "hbm", "kernel": "gemv_tma_kernel" if M == 1 else "verify_tc_kernel",

@@ -284,6 +284,42 @@ int anvilq_rope_kv_append(const uint16_t* qkv, const int32_t* pos, uint16_t* q_o
                           uint16_t* v_cache, int32_t* seqlen, int Hq, int Hkv, int D, int Tmax, float theta,
                           int* dev_err, unsigned flags, anvilq_stream_t stream);
 
+/* ---- tensor-parallel column split with the all-gather fused in ---------------
+ *
+ * Replaces the column-split projection followed by its all-gather (SURVEY
+ * cfg4: rank r of W holds output columns [r N/W, (r+1) N/W); reference analog:
+ * the column interleave of anvil-q2/rtl/anvil_q2_gemv_lane.sv:117,187).
+ *
+ * Peer buffers: a rank exports any device pointer (e.g. a tensor's) as an IPC
+ * handle (anvilq_peer_handle_size() bytes) plus its offset within its
+ * allocation; the other ranks of the node import it and write into it with
+ * plain stores over NVLink.  No multicast object is involved. */
+size_t anvilq_peer_handle_size(void);
+int anvilq_peer_export(const void* dev_ptr, void* handle_out, size_t* offset_out);
+int anvilq_peer_import(const void* handle, size_t offset, void** base_out, void** dev_ptr_out);
+int anvilq_peer_close(void* base);
+
+/* This rank's slice of y = x W (+ bias) for an M = 1 projection (x fp16 [K],
+ * the rank's qweight/qzeros/scales/bias of N columns as anvilq_w4a16_gemm)
+ * stored as fp16 at columns [col_base, col_base + N) of every rank's full-width
+ * output peer_y[r] (fp16 [n_full]; host array of `world` device pointers,
+ * this rank's own included).  After all its stores the rank raises its flag,
+ * value = its count of fused calls, in every rank's flag array peer_flags[r]
+ * (unsigned [8] each, zero-initialised, host array of device pointers) and
+ * waits, bounded by ~1 s (ANVILQ_DEV_ERR_TIMEOUT), until every rank's flag
+ * has reached that count; *epoch (device, this rank's, starts at 0) advances
+ * by one.  When the call completes on `stream` the full row is in
+ * peer_y[rank].  Every rank must make the same sequence of calls, and a
+ * peer_y buffer must not be written again until every rank has passed a
+ * later fused call (alternate two or more buffers).  The workspace is as for
+ * anvilq_w4a16_gemm (its counter region holds the completion ticket).
+ * flags: ANVILQ_GEMM_OVERLAP_PRIOR. */
+int anvilq_w4a16_gemv_allgather(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
+                                const uint16_t* scales, const uint16_t* bias, int K, int N, int G, int rank,
+                                int world, int col_base, int n_full, uint16_t* const* peer_y,
+                                unsigned int* const* peer_flags, unsigned int* epoch, void* workspace,
+                                size_t workspace_bytes, int* dev_err, unsigned flags, anvilq_stream_t stream);
+
 /* Tied fp16 lm_head with the final RMSNorm and greedy argmax fused:
  * h = x * gamma / sqrt(mean(x^2) + eps) in fp32 (official_weights.py:504),
  * logits[v] = h . E[v] (:505-506; written when logits != NULL), and
@@ -322,6 +358,40 @@ int anvilq_argmax_commit(const unsigned long long* argmax_key, int32_t* token, i
 int anvilq_gqa_decode_noalloc(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
                               const int32_t* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D,
                               int Tmax, float scale, int* dev_err, anvilq_stream_t stream);
+
+/* ---- INT8 KV cache (Anvil-Q4 per-head encoding with FP32 escape) ------------
+ *
+ * Format (anvil-q4/design/SPEC.md:209-235, rational model
+ * anvil-q4/tests/cache_reference.py:54-83), one (token, kv head) row of D values
+ * at a time: scale = fp32(maxabs / 127) (1.0 for an all-+0 row), code =
+ * clamp(round-half-even(|fp32(v / scale)|), 127) with v's sign, value =
+ * fp32(code * scale); a row holding NaN, +-inf or -0.0, or whose scale
+ * underflows to 0, escapes: metadata 0x7FC00000, codes 0, and its values (NaN
+ * made 0x7FC00000) in the fp32 escape payload.  Layout:
+ *   codes    int8   [B][Tmax][Hkv][D]
+ *   meta     uint32 [B][Hkv][Tmax]   (scale bits or 0x7FC00000)
+ *   escape   float  [B][Tmax][Hkv][D] (optional; zero for ordinary rows)
+ *
+ * anvilq_kv_int8_store encodes rows src [B][T][H][D] (fp16 when src_half, else
+ * fp32) into positions start[b] + t of sequence b (start: device int32 [B], or
+ * NULL for 0); codes and metadata are bit-identical to the rational model.
+ * Without an escape buffer an escaped row sets ANVILQ_DEV_ERR_NONFINITE.
+ * D <= 256; a position outside [0, Tmax) sets ANVILQ_DEV_ERR_SEQLEN. */
+int anvilq_kv_int8_store(const void* src, int src_half, int B, int T, int H, int D, int Tmax,
+                         const int32_t* start, int8_t* codes, uint32_t* meta, float* escape, int* dev_err,
+                         anvilq_stream_t stream);
+
+/* anvilq_gqa_decode over INT8 caches of the format above: scores use each K row's
+ * scale (escaped rows their fp32 payload, rounded to fp16 for the tensor cores),
+ * the V scales are folded into the probabilities.  Same q, seqlens, out, scale
+ * and workspace (anvilq_gqa_decode_workspace_size) as anvilq_gqa_decode;
+ * Tmax % 16 == 0; all pointers 16-byte aligned.  An escaped row without an
+ * escape payload sets ANVILQ_DEV_ERR_NONFINITE and counts as zeros. */
+int anvilq_gqa_decode_int8(const uint16_t* q, const int8_t* k_codes, const uint32_t* k_meta, const float* k_escape,
+                           const int8_t* v_codes, const uint32_t* v_meta, const float* v_escape,
+                           const int32_t* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D, int Tmax,
+                           float scale, void* workspace, size_t workspace_bytes, int* dev_err,
+                           anvilq_stream_t stream);
 
 #ifdef __cplusplus
 }

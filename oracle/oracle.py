@@ -266,6 +266,53 @@ def decode_attention_f64(q, k_cache, v_cache, seqlens):
 
 
 # ---------------------------------------------------------------- metrics
+KV_ESCAPE_MARKER = 0x7FC00000
+
+
+def kv_int8_encode(bits):
+    """Per-head INT8 KV-cache encoding with FP32 escape, restating
+    anvil-q4/tests/cache_reference.py:54-83 (format anvil-q4/design/SPEC.md:209-235)
+    on float32 bit patterns [..., D] (one head per last axis).
+
+    Ordinary head: scale = fp32(maxabs / 127) (1.0 for an all-+0 head), code =
+    clamp(round-half-even(|fp32(v / scale)|), 127) with v's sign, reconstruction
+    fp32(code * scale).  A head holding NaN, +-inf or -0.0, or whose scale
+    underflows to 0, escapes: metadata 0x7FC00000, codes 0, payload = the values
+    with every NaN made 0x7FC00000.  Every step is one IEEE binary32 operation
+    (division, round to integer, product), which numpy float32 performs exactly.
+    Returns (scale_bits uint32 [...], codes int8 [..., D], recon_bits uint32 [..., D],
+    escape_bits uint32 [..., D] (zero for ordinary heads))."""
+    bits = np.ascontiguousarray(bits, np.uint32)
+    nonfinite = (bits & 0x7F800000) == 0x7F800000
+    esc = np.any(nonfinite | (bits == 0x80000000), axis=-1)
+    with np.errstate(all="ignore"):
+        v = bits.view(np.float32)
+        maxabs = np.where(esc[..., None], np.float32(0), np.abs(v)).max(axis=-1).astype(np.float32)
+        scale = np.where(maxabs > 0, maxabs / np.float32(127), np.float32(1)).astype(np.float32)
+        esc = esc | (scale == 0)
+        safe = np.where(esc, np.float32(1), scale).astype(np.float32)
+        ratio = (np.where(esc[..., None], np.float32(0), v) / safe[..., None]).astype(np.float32)
+        mag = np.minimum(np.rint(np.abs(ratio)), np.float32(127))
+        code = np.where(ratio < 0, -mag, mag).astype(np.int8)
+        recon = (code.astype(np.float32) * safe[..., None]).astype(np.float32)
+    canon = np.where(nonfinite & ((bits & 0x7FFFFF) != 0), np.uint32(KV_ESCAPE_MARKER), bits)
+    scale_bits = np.where(esc, np.uint32(KV_ESCAPE_MARKER), scale.view(np.uint32)).astype(np.uint32)
+    codes = np.where(esc[..., None], np.int8(0), code).astype(np.int8)
+    recon_bits = np.where(esc[..., None], canon, recon.view(np.uint32)).astype(np.uint32)
+    escape_bits = np.where(esc[..., None], canon, np.uint32(0)).astype(np.uint32)
+    return scale_bits, codes, recon_bits, escape_bits
+
+
+def kv_int8_decode(scale_bits, codes, escape_bits):
+    """Reconstruction of kv_int8_encode's output as float32: fp32(code * scale),
+    or the escape payload for marker heads (SPEC.md:221-229)."""
+    scale_bits = np.asarray(scale_bits, np.uint32)
+    esc = scale_bits == KV_ESCAPE_MARKER
+    scale = np.where(esc, np.uint32(0x3F800000), scale_bits).view(np.float32)
+    recon = (np.asarray(codes, np.int8).astype(np.float32) * scale[..., None]).astype(np.float32)
+    return np.where(esc[..., None], np.asarray(escape_bits, np.uint32).view(np.float32), recon)
+
+
 def normalized_error(actual, reference):
     """anvil-q1-fp/design/SPEC.md:311-317: max|a-r| / max(1, max|r|) and cosine."""
     a = np.asarray(actual, np.float64).ravel()

@@ -8,6 +8,7 @@ checkout of aHappend/anvil-q (default /root/reference, or $ANVILQ_REFERENCE):
 * anvil-q1/tests/official_weights.py  FP32Model.linear, FP32Model.token, f32
 * anvil-q1-fp/tests/awq_prepare.py    pack_lanes / unpack_lanes
 * anvil-q1-fp/tests/fp64_reference.py attention
+* anvil-q4/tests/cache_reference.py  encode_head (per-head INT8 KV cache with FP32 escape)
 
 and writes their outputs on seeded inputs.  The tests only read the fixtures;
 nothing at test time needs the reference.  Run from the repository root:
@@ -258,6 +259,37 @@ def decode_fixture():
                 weights_sha256=np.array(digest.hexdigest()))
 
 
+def kv_int8_fixture():
+    """cache_reference.encode_head on its own CASES and on seeded heads (ordinary
+    N(0,1)-scaled values, tiny magnitudes near the scale underflow, -0.0 / inf / NaN
+    escapes), D = 2..128."""
+    cr = _load("anvilq_q4_cache_reference", REF / "anvil-q4" / "tests" / "cache_reference.py")
+    heads = [list(v) for v in cr.CASES.values()]
+    rng = np.random.default_rng(170043)
+    for d in (2, 8, 64, 128):
+        for kind in range(6):
+            v = (rng.standard_normal(d) * (10.0 ** rng.integers(-4, 4))).astype(np.float32).view(np.uint32)
+            if kind == 1:
+                v = rng.integers(0, 80, size=d).astype(np.uint32)            # subnormal units around 63/64
+            if kind == 2:
+                v[rng.integers(0, d)] = 0x80000000                           # negative zero
+            if kind == 3:
+                v[rng.integers(0, d)] = (0x7F800000, 0xFF800000)[int(rng.integers(0, 2))]
+            if kind == 4:
+                v[rng.integers(0, d)] = 0x7F800000 | int(rng.integers(1, 1 << 23)) | (int(rng.integers(0, 2)) << 31)
+            if kind == 5:
+                v = np.zeros(d, np.uint32)
+            heads.append([int(b) for b in v])
+    out = {"count": np.array(len(heads))}
+    for i, h in enumerate(heads):
+        scale, codes, recon = cr.encode_head(h)
+        out[f"h{i}_in"] = np.array(h, np.uint32)
+        out[f"h{i}_scale"] = np.array(scale, np.uint32)
+        out[f"h{i}_codes"] = np.array(codes, np.uint8)
+        out[f"h{i}_recon"] = np.array(recon, np.uint32)
+    return out
+
+
 def main():
     t0 = time.time()
     only = set(sys.argv[1:])
@@ -266,6 +298,8 @@ def main():
             np.savez_compressed(HERE / "attention.npz", **attention_fixture())
         if "decode" in only:
             np.savez_compressed(HERE / "decode_small.npz", **decode_fixture())
+        if "kv_int8" in only:
+            np.savez_compressed(HERE / "kv_int8.npz", **kv_int8_fixture())
         return
     (HERE / "dequant_cases.json").write_text(json.dumps(dequant_fixture()))
     np.savez_compressed(HERE / "pack.npz", **pack_fixture())
@@ -273,6 +307,7 @@ def main():
     np.savez_compressed(HERE / "attention.npz", **attention_fixture())
     np.savez_compressed(HERE / "cfg0_gate_proj.npz", **cfg0_fixture())
     np.savez_compressed(HERE / "decode_small.npz", **decode_fixture())
+    np.savez_compressed(HERE / "kv_int8.npz", **kv_int8_fixture())
     print(f"golden fixtures written in {time.time() - t0:.1f}s")
 
 

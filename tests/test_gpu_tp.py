@@ -69,3 +69,43 @@ def test_tp2_matches_single_gpu_slices(tmp_path, M):
                            128, threads=oracle.max_threads())
     err, cos = oracle.normalized_error(y_tp.astype(np.float32), ref)
     assert err <= TOL_ERR and cos >= TOL_COS
+
+
+def _fused_rank_main(rank, world, port, K, N, out_path):
+    import datetime
+    from anvilq_b200 import ops, tp
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        x, layer = synthetic.gemv_case(1, K, N, 128, 37, bias=True)
+        to = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+        full = (to(layer.qweight), to(layer.qzeros), to(layer.scales), to(layer.bias))
+        outs = tp.PeerOutputs(N, slots=2, device=dev)
+        fused = [tp.FusedTPLinear(*full, 128, outs, s) for s in (0, 1)]
+        nccl = tp.TPLinear(*full, 128)
+        same = []
+        for i in range(5):   # alternating slots, a different x every call
+            xi = to((x[0].astype(np.float32) * (1.0 + 0.25 * i)).astype(np.float16))
+            y = fused[i % 2](xi).clone()
+            same.append(bool(torch.equal(y, nccl(xi))))
+        ops.raise_device_errors(dev)
+        torch.cuda.synchronize(dev)
+        outs.close()
+        if rank == 0:
+            np.save(out_path, np.array(same))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_fused_allgather_matches_nccl(tmp_path):
+    """The GEMV with the all-gather fused into its epilogue (peer stores over
+    NVLink, flag exchange) returns the same full row, bit for bit, as the
+    GEMV + NCCL all-gather, call after call."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = tmp_path / "same.npy"
+    mp.spawn(_fused_rank_main, args=(2, _free_port(), 4096, 11008, str(out)), nprocs=2, join=True)
+    assert np.load(out).all()

@@ -146,3 +146,18 @@ def test_invalid_scale_raises():
             oracle.gemv_fp32(x, qw, qz, sc, None, 8)
     sc = np.full((1, 8), 0x8000, np.uint16)      # negative zero is valid
     assert (oracle.gemv_fp32(x, qw, qz, sc, None, 8) == 0).all()
+
+
+def test_kv_int8_encoding_matches_reference(golden_dir):
+    """oracle.kv_int8_encode reproduces anvil-q4's cache_reference.encode_head (rational
+    model) on its own cases and on seeded heads, escapes included, bit for bit."""
+    g = np.load(golden_dir / "kv_int8.npz")
+    n = int(g["count"])
+    assert n >= 30
+    for i in range(n):
+        scale, codes, recon, esc = oracle.kv_int8_encode(g[f"h{i}_in"][None])
+        assert int(scale[0]) == int(g[f"h{i}_scale"]), i
+        assert np.array_equal(codes[0].view(np.uint8), g[f"h{i}_codes"]), i
+        assert np.array_equal(recon[0], g[f"h{i}_recon"]), i
+        if int(scale[0]) == oracle.KV_ESCAPE_MARKER:
+            assert np.array_equal(esc[0], g[f"h{i}_recon"]), i
