@@ -186,6 +186,16 @@ class Decoder:
             self.token_in.fill_(int(token))
         self.stream.synchronize()
 
+    def set_position(self, token: int, pos: int):
+        """Make the next step run `token` at position `pos` of the current
+        sequence: cache rows [0, pos) are kept, row pos is (re)written."""
+        if not 0 <= int(pos) < self.max_seq:
+            raise ValueError(f"position {pos} outside the cache [0, {self.max_seq})")
+        with torch.cuda.stream(self.stream):
+            self.pos.fill_(int(pos))
+            self.token.fill_(int(token))
+            self.token_in.fill_(int(token))
+
     def capture(self, host_io: bool = False):
         """Record one step as a CUDA graph (warming the kernels first) and make it
         the graph that ``step`` replays.  host_io=True puts the copy of the

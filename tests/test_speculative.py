@@ -1,0 +1,124 @@
+"""Two-token greedy speculative verification: the controller's decisions
+(anvil-q4/rtl/anvil_q4_speculative.sv:1-94) against a host-side fake target.
+
+The fake target is a fixed greedy "model": after token t at position p it
+predicts (7 t + p) mod V, and it records every run, so the tests can check both
+the answer and which target runs the verifier spent."""
+import pytest
+
+from anvilq_b200 import _lib
+from anvilq_b200.speculative import SpeculativeVerifier
+
+
+class FakeTarget:
+    def __init__(self, vocabulary=50, capacity=16, fail_at=None, bad_argmax_at=None):
+        self.vocabulary = vocabulary
+        self.context_capacity = capacity
+        self.runs = []
+        self.fail_at = fail_at
+        self.bad_argmax_at = bad_argmax_at
+
+    def next(self, token, pos):
+        return (7 * token + pos) % self.vocabulary
+
+    def run(self, token, pos):
+        self.runs.append((token, pos))
+        if self.fail_at == pos:
+            raise _lib.AnvilqError("target fault")
+        if self.bad_argmax_at == pos:
+            return self.vocabulary
+        return self.next(token, pos)
+
+
+def test_new_sequence_accepts_both_tokens_when_the_draft_is_greedy():
+    t = FakeTarget()
+    v = SpeculativeVerifier(t)
+    t1 = t.next(3, 0)
+    r = v.verify(3, t1, 0, new_sequence=True)
+    assert (r.accepted, r.error, r.commit_length, r.target_runs) == (2, False, 2, 2)
+    assert r.prediction == t.next(t1, 1)
+    assert t.runs == [(3, 0), (t1, 1)]
+    assert (v.committed_tokens, v.prediction, v.sequence_valid) == (2, t.next(t1, 1), True)
+
+
+def test_mismatching_second_token_accepts_one_and_skips_the_second_run():
+    t = FakeTarget()
+    v = SpeculativeVerifier(t)
+    wrong = (t.next(3, 0) + 1) % t.vocabulary
+    r = v.verify(3, wrong, 0, new_sequence=True)
+    assert (r.accepted, r.error, r.commit_length, r.prediction) == (1, False, 1, t.next(3, 0))
+    assert t.runs == [(3, 0)]
+    assert v.committed_tokens == 1
+
+
+def test_continuation_whose_first_token_misses_the_prediction_accepts_nothing():
+    t = FakeTarget()
+    v = SpeculativeVerifier(t)
+    v.verify(3, 0, 0, new_sequence=True)              # commits 1, prediction p
+    p = v.prediction
+    n = len(t.runs)
+    r = v.verify((p + 1) % t.vocabulary, 0, 1)
+    assert (r.accepted, r.error, r.commit_length, r.prediction, r.target_runs) == (0, False, 0, p, 0)
+    assert len(t.runs) == n and v.committed_tokens == 1 and v.prediction == p
+
+
+def test_continuation_chain_commits_the_greedy_sequence():
+    """Drafting the true greedy continuation commits two tokens per verification,
+    and the committed tokens are exactly the plain greedy decode."""
+    t = FakeTarget(vocabulary=97, capacity=64)
+    v = SpeculativeVerifier(t)
+    seq = [5]
+    for p in range(20):
+        seq.append(t.next(seq[-1], p))
+    r = v.verify(seq[0], seq[1], 0, new_sequence=True)
+    assert r.accepted == 2 and v.prediction == seq[2]
+    while v.committed_tokens < 16:
+        pos = v.committed_tokens
+        # the draft: the standing prediction (= seq[pos]) and its greedy successor
+        r = v.verify(v.prediction, t.next(v.prediction, pos), pos)
+        assert r.accepted == 2 and not r.error and r.target_runs == 2
+        # tokens [0, pos + 2) committed; the prediction is the next greedy token
+        assert v.committed_tokens == pos + 2 and v.prediction == seq[pos + 2]
+    assert t.runs == [(seq[p], p) for p in range(16)]
+
+
+@pytest.mark.parametrize("draft", [
+    (50, 0, 0, True),        # token0 outside the vocabulary
+    (0, 50, 0, True),        # token1 outside the vocabulary
+    (1, 2, 3, True),         # a new sequence must start at 0
+    (1, 2, 0, False),        # continuation without a valid sequence
+    (1, 2, 15, True),        # pos >= capacity - 1
+    (1, 2, -1, True),
+])
+def test_invalid_drafts_are_errors_that_run_nothing(draft):
+    t = FakeTarget()
+    v = SpeculativeVerifier(t)
+    r = v.verify(*draft[:3], new_sequence=draft[3])
+    assert (r.accepted, r.error, r.commit_length, r.target_runs) == (0, True, 0, 0)
+    assert t.runs == [] and v.committed_tokens == 0 and not v.sequence_valid
+
+
+def test_continuation_at_the_wrong_position_is_an_error():
+    t = FakeTarget()
+    v = SpeculativeVerifier(t)
+    v.verify(3, 0, 0, new_sequence=True)
+    r = v.verify(v.prediction, 0, v.committed_tokens + 1)
+    assert r.error and r.accepted == 0 and v.committed_tokens == 1
+
+
+def test_degenerate_vocabulary_and_capacity_are_errors():
+    for vocab, cap in ((0, 16), (50, 1)):
+        t = FakeTarget(vocabulary=vocab, capacity=cap)
+        r = SpeculativeVerifier(t).verify(0, 0, 0, new_sequence=True)
+        assert r.error and t.runs == []
+
+
+@pytest.mark.parametrize("kind", ["fault", "argmax"])
+@pytest.mark.parametrize("at", [0, 1])
+def test_target_failure_in_either_run_commits_nothing(kind, at):
+    t = FakeTarget(**({"fail_at": at} if kind == "fault" else {"bad_argmax_at": at}))
+    v = SpeculativeVerifier(t)
+    r = v.verify(3, t.next(3, 0), 0, new_sequence=True)
+    assert (r.accepted, r.error, r.commit_length) == (0, True, 0)
+    assert len(t.runs) == at + 1
+    assert v.committed_tokens == 0 and not v.sequence_valid and v.prediction is None
