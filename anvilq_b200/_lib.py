@@ -51,6 +51,7 @@ SIGNATURES = {
     "anvilq_rope_kv_append": (I, [P, P, P, P, P, P, I, I, I, I, F, P, ctypes.c_uint, P]),
     "anvilq_lmhead_argmax": (I, [P, P, F, P, P, P, I, I, ctypes.c_uint, P]),
     "anvilq_argmax_commit": (I, [P, P, P, ctypes.c_uint, P]),
+    "anvilq_gqa_decode_paged": (I, [P, P, P, P, P, P, I, I, I, I, I, I, I, F, P, SZ, P, P]),
 }
 
 _lib = None

@@ -82,6 +82,12 @@ struct Params {
   // INT8 cache only: fp32 payloads of escaped (token, kv head) rows, [B][Tmax][Hkv][D] (may be NULL)
   const float* k_escape;
   const float* v_escape;
+  // paged fp16 cache only (else NULL): logical page j of sequence b lives in
+  // physical page page_table[b][j] (bit 31 valid, bits 30:0 the page) of a
+  // pool [num_pages][page_tokens][Hkv][D]; the tensor maps then cover the
+  // pool as one sequence of num_pages * page_tokens rows
+  const uint32_t* page_table;   // [B][max_pages]
+  int page_tokens, max_pages, num_pages;
 };
 
 constexpr uint32_t kEscapeMarker = 0x7FC00000u;   // INT8-cache metadata of an escaped row
@@ -279,6 +285,20 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
     if (lane == 0) {
       const int t0 = (tb + warp + kWarps * j) * kTile;
       const uint32_t kd = smem_u32(ring + st * L::kStageBytes);
+      int row = t0, seq = b;   // the tile's coordinates in the tensor maps
+      if (!Q8 && p.page_table) {
+        // a 16-token tile never straddles a page (page_tokens % 16 == 0); an
+        // absent or out-of-range page is an error, and the copy then reads
+        // physical page 0 so that it stays inside the pool
+        const uint32_t e = p.page_table[(size_t)b * p.max_pages + t0 / p.page_tokens];
+        uint32_t page = e & 0x7FFFFFFFu;
+        if (!(e >> 31) || page >= (uint32_t)p.num_pages) {
+          atomicOr(p.dev_err, ANVILQ_DEV_ERR_PAGE);
+          page = 0;
+        }
+        row = (int)page * p.page_tokens + t0 % p.page_tokens;
+        seq = 0;
+      }
       if (Q8) {
         mbar_expect_tx(bar, L::kStageTx);
         tma_4d(kd, &mk, 0, h, t0, b, bar);
@@ -289,8 +309,8 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
         mbar_expect_tx(bar, 2 * kTile * D * 2);
 #pragma unroll
         for (int hf = 0; hf < L::kHalves; ++hf) {
-          tma_4d(kd + hf * L::kBoxBytes, &mk, 64 * hf, h, t0, b, bar);
-          tma_4d(kd + L::kTileBytes + hf * L::kBoxBytes, &mv, 64 * hf, h, t0, b, bar);
+          tma_4d(kd + hf * L::kBoxBytes, &mk, 64 * hf, h, row, seq, bar);
+          tma_4d(kd + L::kTileBytes + hf * L::kBoxBytes, &mv, 64 * hf, h, row, seq, bar);
         }
       }
     }
@@ -841,7 +861,7 @@ int anvilq_gqa_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t
   const Plan pl = plan_for(B, Hq, Hkv, D, Tmax, *dev);
   if (!workspace || workspace_bytes < pl.bytes) return ANVILQ_EWORKSPACE;
   if (!a16(workspace)) return ANVILQ_EALIGN;
-  Params p;
+  Params p{};   // value-initialised: no page table, no escape payloads unless set
   p.q = reinterpret_cast<const __half*>(q);
   p.k = reinterpret_cast<const __half*>(k_cache);
   p.v = reinterpret_cast<const __half*>(v_cache);
@@ -873,7 +893,7 @@ int anvilq_gqa_decode_int8(const uint16_t* q, const int8_t* k_codes, const uint3
   const Plan pl = plan_for(B, Hq, Hkv, D, Tmax, *dev);
   if (!workspace || workspace_bytes < pl.bytes) return ANVILQ_EWORKSPACE;
   if (!a16(workspace)) return ANVILQ_EALIGN;
-  Params p;
+  Params p{};   // value-initialised: no page table, no escape payloads unless set
   p.q = reinterpret_cast<const __half*>(q);
   p.k = p.v = nullptr;
   p.seqlens = seqlens;
@@ -888,6 +908,49 @@ int anvilq_gqa_decode_int8(const uint16_t* q, const int8_t* k_codes, const uint3
   p.k_escape = k_escape;
   p.v_escape = v_escape;
   return launch_q8(p, B, D, k_codes, k_meta, v_codes, v_meta, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int anvilq_gqa_decode_paged(const uint16_t* q, const uint16_t* k_pool, const uint16_t* v_pool,
+                            const uint32_t* page_table, const int32_t* seqlens, uint16_t* out, int B, int Hq, int Hkv,
+                            int D, int page_tokens, int max_pages, int num_pages, float scale, void* workspace,
+                            size_t workspace_bytes, int* dev_err, anvilq_stream_t stream) {
+  if (!q || !k_pool || !v_pool || !page_table || !seqlens || !out || !dev_err) return ANVILQ_EINVAL;
+  if (page_tokens < kTile || page_tokens % kTile || max_pages < 1 || num_pages < 1 ||
+      (long long)page_tokens * max_pages > (1LL << 30) || (long long)page_tokens * num_pages > (1LL << 30))
+    return ANVILQ_ESHAPE;
+  const int Tmax = page_tokens * max_pages;   // logical capacity of a sequence
+  if (!args_ok(B, Hq, Hkv, D, Tmax)) return ANVILQ_ESHAPE;
+  if (!a16(q) || !a16(k_pool) || !a16(v_pool) || !a16(out)) return ANVILQ_EALIGN;
+  const DeviceInfo* dev = device_info();
+  if (!dev) return ANVILQ_ECUDA;
+  const Plan pl = plan_for(B, Hq, Hkv, D, Tmax, *dev);
+  if (!workspace || workspace_bytes < pl.bytes) return ANVILQ_EWORKSPACE;
+  if (!a16(workspace)) return ANVILQ_EALIGN;
+  Params p{};
+  p.q = reinterpret_cast<const __half*>(q);
+  p.k = reinterpret_cast<const __half*>(k_pool);
+  p.v = reinterpret_cast<const __half*>(v_pool);
+  p.seqlens = seqlens;
+  p.out = reinterpret_cast<__half*>(out);
+  p.tickets = reinterpret_cast<int*>(workspace);
+  p.partials = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + ANVILQ_WORKSPACE_COUNTER_BYTES);
+  p.dev_err = dev_err;
+  p.Hq = Hq; p.Hkv = Hkv; p.Tmax = Tmax; p.group = Hq / Hkv;
+  p.cluster = pl.cluster; p.clusters = pl.clusters;
+  const float s = scale > 0.0f ? scale : 1.0f / std::sqrt((float)D);
+  p.scale_log2 = s * 1.4426950408889634f;
+  p.page_table = page_table;
+  p.page_tokens = page_tokens;
+  p.max_pages = max_pages;
+  p.num_pages = num_pages;
+  // the pool as one sequence of num_pages * page_tokens rows
+  CUtensorMap mk, mv;
+  if (!cache_map(&mk, k_pool, 1, Hkv, D, page_tokens * num_pages) ||
+      !cache_map(&mv, v_pool, 1, Hkv, D, page_tokens * num_pages))
+    return ANVILQ_EALIGN;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return finish_launch(D == 64 ? launch_d<64, false>(mk, mv, mk, mv, p, B, st)
+                               : launch_d<128, false>(mk, mv, mk, mv, p, B, st));
 }
 
 }  // extern "C"
@@ -956,7 +1019,7 @@ extern "C" int anvilq_gqa_decode_noalloc(const uint16_t* q, const uint16_t* k_ca
     cudaGetLastError();
     return ANVILQ_ECUDA;
   }
-  Params p;
+  Params p{};   // value-initialised: no page table, no escape payloads unless set
   p.q = reinterpret_cast<const __half*>(q);
   p.k = reinterpret_cast<const __half*>(k_cache);
   p.v = reinterpret_cast<const __half*>(v_cache);

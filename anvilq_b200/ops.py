@@ -59,6 +59,8 @@ def raise_device_errors(device=None):
             what.append("token id outside [0, V)")
         if value & 16:
             what.append("nonfinite binary16 parameter (bias)")
+        if value & 32:
+            what.append("page-table entry of a live page absent or out of range")
         raise _lib.AnvilqError(f"device error bits 0x{value:x}: " + "; ".join(what))
 
 
@@ -305,6 +307,46 @@ def gqa_decode(q, k_cache, v_cache, seqlens, scale: float = 0.0, out=None, dev_e
     _lib.check(lib.anvilq_gqa_decode(_ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(seqlens), _ptr(out), B, Hq,
                                      Hkv, D, Tmax, float(scale), _ptr(ws), ws.numel(), _ptr(err),
                                      _stream_ptr(q.device)), "anvilq_gqa_decode")
+    return out
+
+
+def gqa_decode_paged(q, k_pool, v_pool, page_table, seqlens, max_pages: int | None = None, scale: float = 0.0,
+                     out=None, dev_err=None):
+    """gqa_decode over a paged fp16 cache: pools [num_pages, page_tokens, Hkv, D],
+    page_table int32 [B, max_pages] (uint32 entries: bit 31 valid, bits 30:0 the
+    physical page; the Anvil-Q4 page table, anvil-q4/design/SPEC.md:205-208).
+    Logical position t of sequence b is row t % page_tokens of page
+    page_table[b, t // page_tokens].  Returns fp16 [B, Hq, D]."""
+    if q.dtype != torch.float16 or k_pool.dtype != torch.float16 or v_pool.dtype != torch.float16:
+        raise TypeError("q and the KV pools must be float16")
+    if q.dim() != 3 or k_pool.dim() != 4 or v_pool.shape != k_pool.shape:
+        raise ValueError("q [B, Hq, D], k_pool/v_pool [num_pages, page_tokens, Hkv, D]")
+    B, Hq, D = q.shape
+    num_pages, page_tokens, Hkv, Dk = k_pool.shape
+    if Dk != D:
+        raise ValueError("head_dim of q and the pools differ")
+    if page_table.dtype != torch.int32 or page_table.dim() != 2 or page_table.shape[0] != B or not page_table.is_cuda:
+        raise ValueError("page_table must be an int32 CUDA tensor [B, max_pages]")
+    if seqlens.dtype != torch.int32 or seqlens.numel() != B or not seqlens.is_cuda:
+        raise ValueError("seqlens must be an int32 CUDA tensor [B]")
+    for t in (q, k_pool, v_pool, page_table, seqlens):
+        if not t.is_contiguous():
+            raise ValueError("inputs must be contiguous")
+    max_pages = page_table.shape[1] if max_pages is None else int(max_pages)
+    if max_pages != page_table.shape[1]:
+        raise ValueError("max_pages must equal page_table.shape[1]")
+    if out is None:
+        out = torch.empty_like(q)
+    lib = _lib.load()
+    need = lib.anvilq_gqa_decode_workspace_size(B, Hq, Hkv, D, page_tokens * max_pages)
+    if need == 0:
+        raise ValueError(f"unsupported attention shape B={B} Hq={Hq} Hkv={Hkv} D={D}")
+    ws = workspace(q.device, need)
+    err = device_error_word(q.device) if dev_err is None else dev_err
+    _lib.check(lib.anvilq_gqa_decode_paged(_ptr(q), _ptr(k_pool), _ptr(v_pool), _ptr(page_table), _ptr(seqlens),
+                                           _ptr(out), B, Hq, Hkv, D, page_tokens, max_pages, num_pages,
+                                           float(scale), _ptr(ws), ws.numel(), _ptr(err),
+                                           _stream_ptr(q.device)), "anvilq_gqa_decode_paged")
     return out
 
 

@@ -52,6 +52,7 @@ typedef struct CUstream_st* anvilq_stream_t; /* same type as cudaStream_t */
 #define ANVILQ_DEV_ERR_TIMEOUT 4 /* a bounded wait inside a kernel expired */
 #define ANVILQ_DEV_ERR_TOKEN 8   /* a token id outside [0, V) */
 #define ANVILQ_DEV_ERR_NONFINITE 16 /* a binary16 parameter (bias) was Inf or NaN */
+#define ANVILQ_DEV_ERR_PAGE 32     /* a page-table entry of a live page was absent or out of range */
 
 /* Workspace layout shared by every entry point that takes one: the first
  * ANVILQ_WORKSPACE_COUNTER_BYTES hold arrival counters that must be zero
@@ -392,6 +393,23 @@ int anvilq_gqa_decode_int8(const uint16_t* q, const int8_t* k_codes, const uint3
                            const int32_t* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D, int Tmax,
                            float scale, void* workspace, size_t workspace_bytes, int* dev_err,
                            anvilq_stream_t stream);
+
+/* anvilq_gqa_decode over a PAGED fp16 cache (the Anvil-Q4 page table,
+ * anvil-q4/design/SPEC.md:205-208: an entry's bit 31 marks it valid, bits 30:0
+ * give the physical page).  Logical position t of sequence b lives in row
+ * t % page_tokens of physical page page_table[b][t / page_tokens] of the pools
+ *   k_pool / v_pool fp16 [num_pages][page_tokens][Hkv][D],
+ *   page_table uint32 [B][max_pages] (device).
+ * A sequence holds at most Tmax = page_tokens * max_pages positions; q, seqlens,
+ * out, scale and the workspace (anvilq_gqa_decode_workspace_size(B, Hq, Hkv, D,
+ * Tmax)) are as for anvilq_gqa_decode, whose result this equals bit for bit
+ * for the same logical cache contents.  page_tokens % 16 == 0.  A live page
+ * whose entry is not valid or names a page >= num_pages sets
+ * ANVILQ_DEV_ERR_PAGE (the output is then not to be used). */
+int anvilq_gqa_decode_paged(const uint16_t* q, const uint16_t* k_pool, const uint16_t* v_pool,
+                            const uint32_t* page_table, const int32_t* seqlens, uint16_t* out, int B, int Hq, int Hkv,
+                            int D, int page_tokens, int max_pages, int num_pages, float scale, void* workspace,
+                            size_t workspace_bytes, int* dev_err, anvilq_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,57 @@
+"""Two-token speculative verification with the GPU decoder as the target.
+
+What the verifier commits must be the plain greedy decode of the same model,
+bit for bit (same kernels, same cache), whether a draft is accepted whole,
+cut after its first token (its second token's cache row then gets rewritten
+by the next run) or rejected without a target run."""
+import pytest
+import torch
+
+from anvilq_b200 import decoder
+from anvilq_b200.speculative import DecoderTarget, SpeculativeVerifier
+
+pytestmark = pytest.mark.gpu
+
+SHAPE = (2, 128, 256, 2, 1, 64, 128, 64, 32)   # (L, H, I, QH, KVH, D, G, V, SEQ)
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda", 0)
+
+
+def _greedy(w, dev, first, n):
+    return [first] + decoder.Decoder(w, dev, max_seq=32).generate(first, n)
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_verifier_commits_the_greedy_decode(dev, graph):
+    w = decoder.synthetic_weights(SHAPE, seed=41)
+    seq = _greedy(w, dev, 9, 20)                  # seq[p] is the token at position p
+    d = decoder.Decoder(w, dev, max_seq=32)
+    if graph:
+        d.reset(9)
+        d.capture()
+    v = SpeculativeVerifier(DecoderTarget(d))
+    r = v.verify(seq[0], seq[1], 0, new_sequence=True)
+    assert (r.accepted, r.error, r.prediction) == (2, False, seq[2])
+    wrong = lambda t: (t + 1) % SHAPE[7]
+    pos, i = 2, 0
+    while pos < 18:
+        case = i % 3
+        i += 1
+        if case == 0:         # a draft whose second token is wrong: one token accepted
+            r = v.verify(seq[pos], wrong(seq[pos + 1]), pos)
+            assert (r.accepted, r.error, r.target_runs, r.prediction) == (1, False, 1, seq[pos + 1])
+        elif case == 1:       # a draft that misses the prediction: nothing runs
+            r = v.verify(wrong(seq[pos]), seq[pos + 1], pos)
+            assert (r.accepted, r.error, r.target_runs) == (0, False, 0)
+            r = v.verify(seq[pos], seq[pos + 1], pos)
+            assert (r.accepted, r.error) == (2, False)
+        else:
+            r = v.verify(seq[pos], seq[pos + 1], pos)
+            assert (r.accepted, r.error, r.target_runs) == (2, False, 2)
+        pos = v.committed_tokens
+        assert v.prediction == seq[pos], pos
