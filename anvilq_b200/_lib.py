@@ -52,6 +52,8 @@ SIGNATURES = {
     "anvilq_lmhead_argmax": (I, [P, P, F, P, P, P, I, I, ctypes.c_uint, P]),
     "anvilq_argmax_commit": (I, [P, P, P, ctypes.c_uint, P]),
     "anvilq_gqa_decode_paged": (I, [P, P, P, P, P, P, I, I, I, I, I, I, I, F, P, SZ, P, P]),
+    "anvilq_tree_attention_workspace_size": (SZ, [I, I, I, I, I]),
+    "anvilq_tree_attention": (I, [P, P, P, P, I, P, I, I, I, I, I, F, P, SZ, P, P]),
 }
 
 _lib = None

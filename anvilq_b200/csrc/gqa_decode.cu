@@ -55,6 +55,7 @@
 #include <mutex>
 
 #include "../../include/anvilq.h"
+#include "internal.h"
 
 namespace anvilq {
 namespace attn {
@@ -88,6 +89,10 @@ struct Params {
   // pool as one sequence of num_pages * page_tokens rows
   const uint32_t* page_table;   // [B][max_pages]
   int page_tokens, max_pages, num_pages;
+  // optional [B][Hq]: each head's log-sum-exp of its scaled scores in the log2
+  // domain, log2(sum_t 2^(q.k_t scale log2(e))) (-inf for an empty sequence),
+  // so that a caller can merge this softmax with scores over further keys
+  float* lse;
 };
 
 constexpr uint32_t kEscapeMarker = 0x7FC00000u;   // INT8-cache metadata of an escaped row
@@ -533,6 +538,7 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
     if (S2 == 1) {
       const float out = lsum > 0.0f ? acc / lsum : 0.0f;
       p.out[((size_t)b * p.Hq + (size_t)h * G + hh) * D + d] = __float2half_rn(out);
+      if (p.lse && d == 0) p.lse[(size_t)b * p.Hq + (size_t)h * G + hh] = lsum > 0.0f ? M + log2f(lsum) : -INFINITY;
     } else {
       float* row = p.partials + (((size_t)pair * S2 + cl) * G + hh) * RG;
       __stcg(row + d, acc);
@@ -641,6 +647,7 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
     const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
     *reinterpret_cast<__half2*>(p.out + ((size_t)b * p.Hq + (size_t)h * G + hh) * D + d2) =
         __floats2half2_rn(acc.x * inv, acc.y * inv);
+    if (p.lse && d2 == 0) p.lse[(size_t)b * p.Hq + (size_t)h * G + hh] = lsum > 0.0f ? M + log2f(lsum) : -INFINITY;
   }
 }
 
@@ -839,6 +846,62 @@ static int launch_q8(const Params& p, int B, int D, const void* k_codes, const v
 }  // namespace attn
 }  // namespace anvilq
 
+namespace anvilq {
+
+size_t gqa_decode_workspace_bytes(int B, int Hq, int Hkv, int D, int Tmax) {
+  using namespace attn;
+  if (!args_ok(B, Hq, Hkv, D, Tmax)) return 0;
+  const DeviceInfo* dev = device_info();
+  if (!dev) return 0;
+  return plan_for(B, Hq, Hkv, D, Tmax, *dev).bytes;
+}
+
+int launch_gqa_decode_paged(const uint16_t* q, const uint16_t* k_pool, const uint16_t* v_pool,
+                            const uint32_t* page_table, const int32_t* seqlens, uint16_t* out, float* lse, int B,
+                            int Hq, int Hkv, int D, int page_tokens, int max_pages, int num_pages, float scale,
+                            void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t st) {
+  using namespace attn;
+  if (!q || !k_pool || !v_pool || !page_table || !seqlens || !out || !dev_err) return ANVILQ_EINVAL;
+  if (page_tokens < kTile || page_tokens % kTile || max_pages < 1 || num_pages < 1 ||
+      (long long)page_tokens * max_pages > (1LL << 30) || (long long)page_tokens * num_pages > (1LL << 30))
+    return ANVILQ_ESHAPE;
+  const int Tmax = page_tokens * max_pages;   // logical capacity of a sequence
+  if (!args_ok(B, Hq, Hkv, D, Tmax)) return ANVILQ_ESHAPE;
+  if (!a16(q) || !a16(k_pool) || !a16(v_pool) || !a16(out)) return ANVILQ_EALIGN;
+  const DeviceInfo* dev = device_info();
+  if (!dev) return ANVILQ_ECUDA;
+  const Plan pl = plan_for(B, Hq, Hkv, D, Tmax, *dev);
+  if (!workspace || workspace_bytes < pl.bytes) return ANVILQ_EWORKSPACE;
+  if (!a16(workspace)) return ANVILQ_EALIGN;
+  Params p{};
+  p.q = reinterpret_cast<const __half*>(q);
+  p.k = reinterpret_cast<const __half*>(k_pool);
+  p.v = reinterpret_cast<const __half*>(v_pool);
+  p.seqlens = seqlens;
+  p.out = reinterpret_cast<__half*>(out);
+  p.tickets = reinterpret_cast<int*>(workspace);
+  p.partials = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + ANVILQ_WORKSPACE_COUNTER_BYTES);
+  p.dev_err = dev_err;
+  p.Hq = Hq; p.Hkv = Hkv; p.Tmax = Tmax; p.group = Hq / Hkv;
+  p.cluster = pl.cluster; p.clusters = pl.clusters;
+  const float s = scale > 0.0f ? scale : 1.0f / std::sqrt((float)D);
+  p.scale_log2 = s * 1.4426950408889634f;
+  p.page_table = page_table;
+  p.page_tokens = page_tokens;
+  p.max_pages = max_pages;
+  p.num_pages = num_pages;
+  p.lse = lse;
+  // the pool as one sequence of num_pages * page_tokens rows
+  CUtensorMap mk, mv;
+  if (!cache_map(&mk, k_pool, 1, Hkv, D, page_tokens * num_pages) ||
+      !cache_map(&mv, v_pool, 1, Hkv, D, page_tokens * num_pages))
+    return ANVILQ_EALIGN;
+  return finish_launch(D == 64 ? launch_d<64, false>(mk, mv, mk, mv, p, B, st)
+                               : launch_d<128, false>(mk, mv, mk, mv, p, B, st));
+}
+
+}  // namespace anvilq
+
 using namespace anvilq::attn;
 
 extern "C" {
@@ -914,43 +977,9 @@ int anvilq_gqa_decode_paged(const uint16_t* q, const uint16_t* k_pool, const uin
                             const uint32_t* page_table, const int32_t* seqlens, uint16_t* out, int B, int Hq, int Hkv,
                             int D, int page_tokens, int max_pages, int num_pages, float scale, void* workspace,
                             size_t workspace_bytes, int* dev_err, anvilq_stream_t stream) {
-  if (!q || !k_pool || !v_pool || !page_table || !seqlens || !out || !dev_err) return ANVILQ_EINVAL;
-  if (page_tokens < kTile || page_tokens % kTile || max_pages < 1 || num_pages < 1 ||
-      (long long)page_tokens * max_pages > (1LL << 30) || (long long)page_tokens * num_pages > (1LL << 30))
-    return ANVILQ_ESHAPE;
-  const int Tmax = page_tokens * max_pages;   // logical capacity of a sequence
-  if (!args_ok(B, Hq, Hkv, D, Tmax)) return ANVILQ_ESHAPE;
-  if (!a16(q) || !a16(k_pool) || !a16(v_pool) || !a16(out)) return ANVILQ_EALIGN;
-  const DeviceInfo* dev = device_info();
-  if (!dev) return ANVILQ_ECUDA;
-  const Plan pl = plan_for(B, Hq, Hkv, D, Tmax, *dev);
-  if (!workspace || workspace_bytes < pl.bytes) return ANVILQ_EWORKSPACE;
-  if (!a16(workspace)) return ANVILQ_EALIGN;
-  Params p{};
-  p.q = reinterpret_cast<const __half*>(q);
-  p.k = reinterpret_cast<const __half*>(k_pool);
-  p.v = reinterpret_cast<const __half*>(v_pool);
-  p.seqlens = seqlens;
-  p.out = reinterpret_cast<__half*>(out);
-  p.tickets = reinterpret_cast<int*>(workspace);
-  p.partials = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + ANVILQ_WORKSPACE_COUNTER_BYTES);
-  p.dev_err = dev_err;
-  p.Hq = Hq; p.Hkv = Hkv; p.Tmax = Tmax; p.group = Hq / Hkv;
-  p.cluster = pl.cluster; p.clusters = pl.clusters;
-  const float s = scale > 0.0f ? scale : 1.0f / std::sqrt((float)D);
-  p.scale_log2 = s * 1.4426950408889634f;
-  p.page_table = page_table;
-  p.page_tokens = page_tokens;
-  p.max_pages = max_pages;
-  p.num_pages = num_pages;
-  // the pool as one sequence of num_pages * page_tokens rows
-  CUtensorMap mk, mv;
-  if (!cache_map(&mk, k_pool, 1, Hkv, D, page_tokens * num_pages) ||
-      !cache_map(&mv, v_pool, 1, Hkv, D, page_tokens * num_pages))
-    return ANVILQ_EALIGN;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  return finish_launch(D == 64 ? launch_d<64, false>(mk, mv, mk, mv, p, B, st)
-                               : launch_d<128, false>(mk, mv, mk, mv, p, B, st));
+  return anvilq::launch_gqa_decode_paged(q, k_pool, v_pool, page_table, seqlens, out, nullptr, B, Hq, Hkv, D,
+                                         page_tokens, max_pages, num_pages, scale, workspace, workspace_bytes,
+                                         dev_err, reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -59,4 +59,13 @@ int launch_gemm_q16(const int32_t* x, const int32_t* qweight, const int32_t* qze
                     const uint16_t* bias, int32_t* y, int M, int K, int N, int G, void* workspace,
                     size_t workspace_bytes, int* dev_err, cudaStream_t stream);
 
+// Decode attention over a paged fp16 cache (gqa_decode.cu), as
+// anvilq_gqa_decode_paged, optionally also writing each head's log2-domain
+// log-sum-exp to lse [B][Hq] (null: not written).
+size_t gqa_decode_workspace_bytes(int B, int Hq, int Hkv, int D, int Tmax);
+int launch_gqa_decode_paged(const uint16_t* q, const uint16_t* k_pool, const uint16_t* v_pool,
+                            const uint32_t* page_table, const int32_t* seqlens, uint16_t* out, float* lse, int B,
+                            int Hq, int Hkv, int D, int page_tokens, int max_pages, int num_pages, float scale,
+                            void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t stream);
+
 }  // namespace anvilq

@@ -61,6 +61,8 @@ def raise_device_errors(device=None):
             what.append("nonfinite binary16 parameter (bias)")
         if value & 32:
             what.append("page-table entry of a live page absent or out of range")
+        if value & 64:
+            what.append("draft-node ancestor mask breaks the tree contract")
         raise _lib.AnvilqError(f"device error bits 0x{value:x}: " + "; ".join(what))
 
 
@@ -347,6 +349,41 @@ def gqa_decode_paged(q, k_pool, v_pool, page_table, seqlens, max_pages: int | No
                                            _ptr(out), B, Hq, Hkv, D, page_tokens, max_pages, num_pages,
                                            float(scale), _ptr(ws), ws.numel(), _ptr(err),
                                            _stream_ptr(q.device)), "anvilq_gqa_decode_paged")
+    return out
+
+
+def tree_attention(q, k_cache, v_cache, ancestors, prefix_len: int, scale: float = 0.0, out=None, dev_err=None):
+    """Attention of M speculative draft nodes: q [M, Hq, D], one sequence's caches
+    [Tmax, Hkv, D] fp16 holding the committed prefix in rows [0, prefix_len) and
+    draft node j in row prefix_len + j, ancestors int32 [M] (bit j of entry m:
+    node m sees node j; itself included).  Returns fp16 [M, Hq, D].
+
+    Per-node causal tree attention (anvil-q3-ht2/design/SPEC.md:71-86, ancestor
+    contract anvil-q1-ht3/design/SPEC.md:528-533)."""
+    if q.dtype != torch.float16 or k_cache.dtype != torch.float16 or v_cache.dtype != torch.float16:
+        raise TypeError("q and the caches must be float16")
+    if q.dim() != 3 or k_cache.dim() != 3 or v_cache.shape != k_cache.shape:
+        raise ValueError("q [M, Hq, D], k_cache/v_cache [Tmax, Hkv, D]")
+    M, Hq, D = q.shape
+    Tmax, Hkv, Dk = k_cache.shape
+    if Dk != D:
+        raise ValueError("head_dim of q and the caches differ")
+    if ancestors.dtype != torch.int32 or ancestors.numel() != M or not ancestors.is_cuda:
+        raise ValueError("ancestors must be an int32 CUDA tensor [M]")
+    for t in (q, k_cache, v_cache, ancestors):
+        if not t.is_contiguous():
+            raise ValueError("inputs must be contiguous")
+    if out is None:
+        out = torch.empty_like(q)
+    lib = _lib.load()
+    need = lib.anvilq_tree_attention_workspace_size(M, Hq, Hkv, D, Tmax)
+    if need == 0:
+        raise ValueError(f"unsupported tree attention shape M={M} Hq={Hq} Hkv={Hkv} D={D} Tmax={Tmax}")
+    ws = workspace(q.device, need)
+    err = device_error_word(q.device) if dev_err is None else dev_err
+    _lib.check(lib.anvilq_tree_attention(_ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(ancestors), int(prefix_len),
+                                         _ptr(out), M, Hq, Hkv, D, Tmax, float(scale), _ptr(ws), ws.numel(),
+                                         _ptr(err), _stream_ptr(q.device)), "anvilq_tree_attention")
     return out
 
 

@@ -53,6 +53,7 @@ typedef struct CUstream_st* anvilq_stream_t; /* same type as cudaStream_t */
 #define ANVILQ_DEV_ERR_TOKEN 8   /* a token id outside [0, V) */
 #define ANVILQ_DEV_ERR_NONFINITE 16 /* a binary16 parameter (bias) was Inf or NaN */
 #define ANVILQ_DEV_ERR_PAGE 32     /* a page-table entry of a live page was absent or out of range */
+#define ANVILQ_DEV_ERR_TREE 64     /* a draft node's ancestor mask broke the tree contract */
 
 /* Workspace layout shared by every entry point that takes one: the first
  * ANVILQ_WORKSPACE_COUNTER_BYTES hold arrival counters that must be zero
@@ -410,6 +411,30 @@ int anvilq_gqa_decode_paged(const uint16_t* q, const uint16_t* k_pool, const uin
                             const uint32_t* page_table, const int32_t* seqlens, uint16_t* out, int B, int Hq, int Hkv,
                             int D, int page_tokens, int max_pages, int num_pages, float scale, void* workspace,
                             size_t workspace_bytes, int* dev_err, anvilq_stream_t stream);
+
+/* ---- tree attention of speculative draft nodes -----------------------------
+ *
+ * Replaces the per-node causal tree attention of the batched draft-tree decoder
+ * (anvil-q3-ht2/design/SPEC.md:71-86) under the ancestor contract of
+ * anvil-q1-ht3/design/SPEC.md:528-533.  Draft node m (0 <= m < M <= 32) attends
+ * to cache rows [0, prefix_len) -- the committed prefix -- and to the rows
+ * prefix_len + j of the nodes j whose bit is set in ancestors[m] (device
+ * uint32 [M]); node j's K/V must already be in those rows.  A mask must hold
+ * bit m, no bit above m, and every ancestor's own mask (else
+ * ANVILQ_DEV_ERR_TREE; the output is then not to be used).
+ *   q fp16 [M][Hq][D], k_cache / v_cache fp16 [Tmax][Hkv][D] (one sequence),
+ *   out fp16 [M][Hq][D]; prefix_len + M <= Tmax, Tmax % 16 == 0,
+ *   Hq % Hkv == 0, Hq / Hkv <= 8, D in {64, 128}, 16-byte aligned pointers.
+ * scale <= 0 selects 1/sqrt(D).  workspace: at least
+ * anvilq_tree_attention_workspace_size(M, Hq, Hkv, D, Tmax) bytes, layout as
+ * described at ANVILQ_WORKSPACE_COUNTER_BYTES.  No counterpart function in the
+ * reference's Python goldens: the golden is attention() of
+ * anvil-q1-fp/tests/fp64_reference.py:164-170 over each node's key rows. */
+size_t anvilq_tree_attention_workspace_size(int M, int Hq, int Hkv, int D, int Tmax);
+int anvilq_tree_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                          const uint32_t* ancestors, int prefix_len, uint16_t* out, int M, int Hq, int Hkv, int D,
+                          int Tmax, float scale, void* workspace, size_t workspace_bytes, int* dev_err,
+                          anvilq_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -242,6 +242,31 @@ def attention_f64(q, keys, values):
     return np.einsum("kgt,tkd->kgd", p, values).reshape(hq, d)
 
 
+def tree_attention_f64(q, k_cache, v_cache, ancestors, prefix_len):
+    """Per-node tree attention: node m attends to rows [0, prefix_len) and the
+    rows prefix_len + j of its ancestors j (bit j of ancestors[m]), prefix
+    first, then the nodes in ascending order (anvil-q1-ht3/design/SPEC.md:528-538),
+    each through attention() of fp64_reference.py:164-170.
+    q [M, Hq, D], caches [Tmax, Hkv, D]."""
+    out = []
+    for m in range(len(q)):
+        rows = list(range(prefix_len)) + [prefix_len + j for j in range(32) if (int(ancestors[m]) >> j) & 1]
+        out.append(attention_f64(q[m], k_cache[rows], v_cache[rows]))
+    return np.stack(out)
+
+
+def tree_is_valid(ancestors):
+    """The ancestor contract of anvil-q1-ht3/design/SPEC.md:528-533: node m sees
+    itself, no later node, and the ancestors of each of its ancestors."""
+    a = [int(x) & 0xFFFFFFFF for x in ancestors]
+    for m, mask in enumerate(a):
+        if not (mask >> m) & 1 or mask >> (m + 1):
+            return False
+        if any((mask >> j) & 1 and a[j] & ~mask for j in range(m)):
+            return False
+    return True
+
+
 def attention_fp32(q_bits, k_bits, v_bits):
     """official_weights.py:471-486 FP32 loop for one sequence; inputs are binary16 bits."""
     q_bits = _c(q_bits, np.uint16)
