@@ -54,6 +54,11 @@ SIGNATURES = {
     "anvilq_gqa_decode_paged": (I, [P, P, P, P, P, P, I, I, I, I, I, I, I, F, P, SZ, P, P]),
     "anvilq_tree_attention_workspace_size": (SZ, [I, I, I, I, I]),
     "anvilq_tree_attention": (I, [P, P, P, P, I, P, I, I, I, I, I, F, P, SZ, P, P]),
+    "anvilq_rmsnorm_rows": (I, [P, P, F, P, I, I, ctypes.c_uint, P]),
+    "anvilq_residual_add_rows": (I, [P, P, I, I, ctypes.c_uint, P]),
+    "anvilq_silu_mul_rows": (I, [P, P, I, I, ctypes.c_uint, P]),
+    "anvilq_legacy_kv_encode": (I, [P, P, P, I, I, I, I, I, P]),
+    "anvilq_legacy_kv_decode": (I, [P, P, P, I, I, I, I, I, P, P]),
 }
 
 _lib = None

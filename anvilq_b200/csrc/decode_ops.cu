@@ -207,6 +207,54 @@ __global__ void commit_kernel(const unsigned long long* __restrict__ key, int* _
   if (pos) *pos += 1;
 }
 
+// ---- M-row forms of the GEMV prologues / epilogues (the batched verification
+// pass, where the projections run as M-row GEMMs) --------------------------
+
+// out[m] = fp16(x[m] * gamma / sqrt(mean(x[m]^2) + eps)): one CTA per row, the
+// same binary32 expression as the RMSNorm prologue of the batch-1 GEMV.
+constexpr int kRowThreads = 256;
+__global__ void __launch_bounds__(kRowThreads) rmsnorm_rows_kernel(const float* __restrict__ x,
+                                                                   const __half* __restrict__ gamma, float eps,
+                                                                   __half* __restrict__ out, int H) {
+  pdl_enter();
+  __shared__ float s_part[kRowThreads / 32];
+  const float* xr = x + (size_t)blockIdx.x * H;
+  float ss = 0.0f;
+  for (int c = threadIdx.x; c < H; c += kRowThreads) ss = fmaf(xr[c], xr[c], ss);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (threadIdx.x % 32 == 0) s_part[threadIdx.x / 32] = ss;
+  __syncthreads();
+  float t = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kRowThreads / 32; ++w) t += s_part[w];
+  const float inv = 1.0f / sqrtf(t / (float)H + eps);
+  for (int c = threadIdx.x; c < H; c += kRowThreads)
+    out[(size_t)blockIdx.x * H + c] = __float2half_rn(xr[c] * __half2float(gamma[c]) * inv);
+}
+
+// x[i] += y[i] (fp32 residual stream plus an fp16 projection output)
+__global__ void add_rows_kernel(float* __restrict__ x, const __half* __restrict__ y, long long n) {
+  pdl_enter();
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    x[i] += __half2float(y[i]);
+}
+
+// out[m][i] = fp16(silu(g) * u), g = gu[m][i], u = gu[m][I + i]: the stable
+// SiLU of the batch-1 GEMV prologue (official_weights.py:494-499)
+__global__ void silu_mul_rows_kernel(const __half* __restrict__ gu, __half* __restrict__ out, int M, int I) {
+  pdl_enter();
+  const long long n = (long long)M * I;
+  for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += (long long)gridDim.x * blockDim.x) {
+    const long long m = t / I, i = t % I;
+    const float g = __half2float(gu[m * 2 * I + i]);
+    const float u = __half2float(gu[m * 2 * I + I + i]);
+    const float e = expf(-fabsf(g));
+    const float sg = g >= 0.0f ? g / (1.0f + e) : (g * e) / (1.0f + e);
+    out[t] = __float2half_rn(sg * u);
+  }
+}
+
 constexpr int kMaxDevices = 64;
 static int g_sms[kMaxDevices];
 static std::once_flag g_once[kMaxDevices];
@@ -295,6 +343,32 @@ int anvilq_argmax_commit(const unsigned long long* argmax_key, int32_t* token, i
   if (flags & ~(unsigned)ANVILQ_GEMM_OVERLAP_PRIOR) return ANVILQ_EINVAL;
   return launch(commit_kernel, dim3(1), dim3(1), 0, reinterpret_cast<cudaStream_t>(stream), flags, argmax_key,
                 (int*)token, (int*)pos);
+}
+
+int anvilq_rmsnorm_rows(const float* x, const uint16_t* gamma, float eps, uint16_t* out, int M, int H,
+                        unsigned flags, anvilq_stream_t stream) {
+  if (!x || !gamma || !out || M < 1 || H < 1) return ANVILQ_EINVAL;
+  if (flags & ~(unsigned)ANVILQ_GEMM_OVERLAP_PRIOR) return ANVILQ_EINVAL;
+  return launch(rmsnorm_rows_kernel, dim3(M), dim3(kRowThreads), 0, reinterpret_cast<cudaStream_t>(stream), flags,
+                x, reinterpret_cast<const __half*>(gamma), eps, reinterpret_cast<__half*>(out), H);
+}
+
+int anvilq_residual_add_rows(float* x, const uint16_t* y, int M, int H, unsigned flags, anvilq_stream_t stream) {
+  if (!x || !y || M < 1 || H < 1) return ANVILQ_EINVAL;
+  if (flags & ~(unsigned)ANVILQ_GEMM_OVERLAP_PRIOR) return ANVILQ_EINVAL;
+  const long long n = (long long)M * H;
+  const int blocks = (int)std::min<long long>((n + 255) / 256, 4096);
+  return launch(add_rows_kernel, dim3(blocks), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), flags, x,
+                reinterpret_cast<const __half*>(y), n);
+}
+
+int anvilq_silu_mul_rows(const uint16_t* gu, uint16_t* out, int M, int I, unsigned flags, anvilq_stream_t stream) {
+  if (!gu || !out || M < 1 || I < 1) return ANVILQ_EINVAL;
+  if (flags & ~(unsigned)ANVILQ_GEMM_OVERLAP_PRIOR) return ANVILQ_EINVAL;
+  const long long n = (long long)M * I;
+  const int blocks = (int)std::min<long long>((n + 255) / 256, 4096);
+  return launch(silu_mul_rows_kernel, dim3(blocks), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), flags,
+                reinterpret_cast<const __half*>(gu), reinterpret_cast<__half*>(out), M, I);
 }
 
 }  // extern "C"

@@ -283,6 +283,79 @@ class Decoder:
             self.dev_err.zero_()
             raise _lib.AnvilqError(f"decode step device error bits 0x{v:x}")
 
+    # -- M draft tokens in one pass (speculative verification) -----------------
+    def _verify_buffers(self, M: int):
+        bufs = getattr(self, "_vbufs", {})
+        if M not in bufs:
+            L, H, I, QH, KVH, D, G, V, _ = self.shape
+            dev = self.device
+            z = lambda shape, dt: torch.zeros(shape, dtype=dt, device=dev)
+            bufs[M] = dict(
+                tok=z(M, torch.int32), pos=z(M, torch.int32), key=z(M, torch.int64), out=z(M, torch.int32),
+                x=z((M, H), torch.float32), h=z((M, H), torch.float16), y=z((M, H), torch.float16),
+                qkv=z((M, (QH + 2 * KVH) * D), torch.float16), q=z((M, QH, D), torch.float16),
+                attn=z((M, QH, D), torch.float16), gu=z((M, 2 * I), torch.float16), act=z((M, I), torch.float16),
+                anc=torch.tensor([(1 << (m + 1)) - 1 for m in range(M)], dtype=torch.int32, device=dev))
+            self._vbufs = bufs
+        return bufs[M]
+
+    def verify_tokens(self, tokens, pos: int):
+        """Run M draft tokens at positions pos .. pos + M - 1 through the model in
+        one pass and return the greedy choice after each of them.
+
+        The batched counterpart of M decode steps (FP32Model.token per token,
+        official_weights.py:451-509): every projection is one M-row W4A16 GEMM,
+        so the weights stream once for all M tokens; each token's K/V row is
+        written at its position and token m attends to the cache rows [0, pos)
+        and the draft tokens 0..m (tree attention with a chain of ancestors).
+        Rows pos + m of the caches are overwritten.  The decoder's own token and
+        position are left unchanged."""
+        L, H, I, QH, KVH, D, G, V, _ = self.shape
+        M = len(tokens)
+        if M < 1 or M > 32 or pos < 0 or pos + M > self.max_seq:
+            raise ValueError(f"{M} draft tokens at position {pos} do not fit the cache of {self.max_seq}")
+        lib = _lib.load()
+        b = self._verify_buffers(M)
+        s = self.stream.cuda_stream
+        chk = _lib.check
+        with torch.cuda.stream(self.stream):
+            b["tok"].copy_(torch.tensor([int(t) for t in tokens], dtype=torch.int32), non_blocking=False)
+            b["pos"].copy_(torch.arange(pos, pos + M, dtype=torch.int32), non_blocking=False)
+            for m in range(M):
+                chk(lib.anvilq_embed(self.embedding.data_ptr(), b["tok"][m:].data_ptr(), b["x"][m].data_ptr(), H, V,
+                                     b["key"][m:].data_ptr(), self.dev_err.data_ptr(), 0, s), "anvilq_embed")
+            for l, w in enumerate(self.layers):
+                chk(lib.anvilq_rmsnorm_rows(b["x"].data_ptr(), self.gamma_in[l].data_ptr(), RMS_EPS,
+                                            b["h"].data_ptr(), M, H, 0, s), "anvilq_rmsnorm_rows")
+                ops.gemm(b["h"], *w["qkv"], G, out=b["qkv"], dev_err=self.dev_err)
+                for m in range(M):
+                    chk(lib.anvilq_rope_kv_append(b["qkv"][m].data_ptr(), b["pos"][m:].data_ptr(), b["q"][m].data_ptr(),
+                                                  self.k_cache[l].data_ptr(), self.v_cache[l].data_ptr(), None, QH,
+                                                  KVH, D, self.max_seq, ROPE_THETA, self.dev_err.data_ptr(), 0, s),
+                        "anvilq_rope_kv_append")
+                ops.tree_attention(b["q"], self.k_cache[l], self.v_cache[l], b["anc"], pos, out=b["attn"],
+                                   dev_err=self.dev_err)
+                ops.gemm(b["attn"].view(M, QH * D), *w["o"][:3], None, G, out=b["y"], dev_err=self.dev_err)
+                chk(lib.anvilq_residual_add_rows(b["x"].data_ptr(), b["y"].data_ptr(), M, H, 0, s),
+                    "anvilq_residual_add_rows")
+                chk(lib.anvilq_rmsnorm_rows(b["x"].data_ptr(), self.gamma_post[l].data_ptr(), RMS_EPS,
+                                            b["h"].data_ptr(), M, H, 0, s), "anvilq_rmsnorm_rows")
+                ops.gemm(b["h"], *w["gu"][:3], None, G, out=b["gu"], dev_err=self.dev_err)
+                chk(lib.anvilq_silu_mul_rows(b["gu"].data_ptr(), b["act"].data_ptr(), M, I, 0, s),
+                    "anvilq_silu_mul_rows")
+                ops.gemm(b["act"], *w["down"][:3], None, G, out=b["y"], dev_err=self.dev_err)
+                chk(lib.anvilq_residual_add_rows(b["x"].data_ptr(), b["y"].data_ptr(), M, H, 0, s),
+                    "anvilq_residual_add_rows")
+            for m in range(M):
+                chk(lib.anvilq_lmhead_argmax(b["x"][m].data_ptr(), self.gamma_final.data_ptr(), RMS_EPS,
+                                             self.embedding.data_ptr(), None, b["key"][m:].data_ptr(), H, V, 0, s),
+                    "anvilq_lmhead_argmax")
+                chk(lib.anvilq_argmax_commit(b["key"][m:].data_ptr(), b["out"][m:].data_ptr(), None, 0, s),
+                    "anvilq_argmax_commit")
+        self.stream.synchronize()
+        self.check_errors()
+        return [int(t) for t in b["out"].cpu()]
+
     def bytes_per_step(self, context: int) -> int:
         """Algorithmic HBM bytes of one step at a given context length."""
         L, H, I, QH, KVH, D, G, V, _ = self.shape

@@ -63,6 +63,8 @@ def raise_device_errors(device=None):
             what.append("page-table entry of a live page absent or out of range")
         if value & 64:
             what.append("draft-node ancestor mask breaks the tree contract")
+        if value & 128:
+            what.append("legacy cache block with a forbidden code, padding or metadata")
         raise _lib.AnvilqError(f"device error bits 0x{value:x}: " + "; ".join(what))
 
 
@@ -384,6 +386,43 @@ def tree_attention(q, k_cache, v_cache, ancestors, prefix_len: int, scale: float
     _lib.check(lib.anvilq_tree_attention(_ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(ancestors), int(prefix_len),
                                          _ptr(out), M, Hq, Hkv, D, Tmax, float(scale), _ptr(ws), ws.numel(),
                                          _ptr(err), _stream_ptr(q.device)), "anvilq_tree_attention")
+    return out
+
+
+def legacy_kv_shape(H: int, D: int, block: int, fmt: int):
+    """(blocks per head B, words per block W) of the legacy cache layout."""
+    bits = 8 if fmt == 1 else 4
+    return (D + block - 1) // block, (block * bits + 31) // 32
+
+
+def legacy_kv_encode(values, H: int, D: int, block: int, fmt: int):
+    """Q16.16 rows int32 [R, H*D] -> (payload int32 [R, H*B*W], metadata int32
+    [R, H*B]) in the legacy cache format fmt (1 INT8 symmetric, 2 INT4
+    symmetric, 3 INT4 asymmetric; anvil-q4/tests/legacy_reference.py:71-97);
+    uint32 words are held as int32."""
+    if values.dtype != torch.int32 or values.dim() != 2 or values.shape[1] != H * D or not values.is_contiguous():
+        raise ValueError("values must be contiguous int32 [R, H*D]")
+    R = values.shape[0]
+    B, W = legacy_kv_shape(H, D, block, fmt)
+    payload = torch.empty((R, H * B * W), dtype=torch.int32, device=values.device)
+    meta = torch.empty((R, H * B), dtype=torch.int32, device=values.device)
+    lib = _lib.load()
+    _lib.check(lib.anvilq_legacy_kv_encode(_ptr(values), _ptr(payload), _ptr(meta), R, H, D, block, fmt,
+                                           _stream_ptr(values.device)), "anvilq_legacy_kv_encode")
+    return payload, meta
+
+
+def legacy_kv_decode(payload, meta, H: int, D: int, block: int, fmt: int, dev_err=None):
+    """The legacy cache rows back to Q16.16 int32 [R, H*D]: sat32((code - z) 2^e)."""
+    R = payload.shape[0]
+    B, W = legacy_kv_shape(H, D, block, fmt)
+    if payload.dtype != torch.int32 or tuple(payload.shape) != (R, H * B * W) or tuple(meta.shape) != (R, H * B):
+        raise ValueError("payload int32 [R, H*B*W] and metadata int32 [R, H*B] expected")
+    out = torch.empty((R, H * D), dtype=torch.int32, device=payload.device)
+    lib = _lib.load()
+    err = device_error_word(payload.device) if dev_err is None else dev_err
+    _lib.check(lib.anvilq_legacy_kv_decode(_ptr(payload), _ptr(meta), _ptr(out), R, H, D, block, fmt, _ptr(err),
+                                           _stream_ptr(payload.device)), "anvilq_legacy_kv_decode")
     return out
 
 

@@ -44,7 +44,7 @@ class Verification:
     error: bool            # verify_error: nothing accepted, nothing committed
     commit_length: int     # tokens committed to the sequence (== accepted unless error)
     prediction: int        # commit_prediction: greedy token after the committed prefix (when committed)
-    target_runs: int       # target decode steps spent
+    target_runs: int       # target passes spent (decode steps, or batched two-token passes)
 
 
 class DecoderTarget:
@@ -63,6 +63,18 @@ class DecoderTarget:
         d.stream.synchronize()
         d.check_errors()
         return int(d.token.item())
+
+
+class BatchedDecoderTarget(DecoderTarget):
+    """The target as ONE pass over both draft tokens (``Decoder.verify_tokens``):
+    token0 at pos and token1 at pos + 1 through M = 2 row GEMMs, so the weights
+    stream once for the pair.  run_pair returns the greedy choice after each;
+    the verifier uses the second only when the first equals token1, which is
+    exactly when the reference's controller would have run it."""
+
+    def run_pair(self, token0: int, token1: int, pos: int):
+        a0, a1 = self.dec.verify_tokens([token0, token1], pos)
+        return a0, a1
 
 
 class SpeculativeVerifier:
@@ -96,6 +108,16 @@ class SpeculativeVerifier:
             return self._commit(pos, 0, prediction, 0)
         runs = 0
         try:
+            if hasattr(self.target, "run_pair"):   # both target runs in one batched pass
+                runs = 1
+                a0, a1 = self.target.run_pair(token0, token1, pos)
+                if not 0 <= a0 < self.vocabulary:
+                    return Verification(0, True, 0, 0, runs)
+                if a0 != token1:
+                    return self._commit(pos, 1, a0, runs)
+                if not 0 <= a1 < self.vocabulary:
+                    return Verification(0, True, 0, 0, runs)
+                return self._commit(pos, 2, a1, runs)
             runs += 1
             a0 = self.target.run(token0, pos)
             if not 0 <= a0 < self.vocabulary:
@@ -120,4 +142,4 @@ class SpeculativeVerifier:
         return Verification(accepted, False, accepted, 0 if prediction is None else int(prediction), runs)
 
 
-__all__ = ["Verification", "DecoderTarget", "SpeculativeVerifier"]
+__all__ = ["Verification", "DecoderTarget", "BatchedDecoderTarget", "SpeculativeVerifier"]

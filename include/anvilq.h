@@ -54,6 +54,7 @@ typedef struct CUstream_st* anvilq_stream_t; /* same type as cudaStream_t */
 #define ANVILQ_DEV_ERR_NONFINITE 16 /* a binary16 parameter (bias) was Inf or NaN */
 #define ANVILQ_DEV_ERR_PAGE 32     /* a page-table entry of a live page was absent or out of range */
 #define ANVILQ_DEV_ERR_TREE 64     /* a draft node's ancestor mask broke the tree contract */
+#define ANVILQ_DEV_ERR_CODEC 128   /* a legacy cache block held a forbidden code, padding or metadata */
 
 /* Workspace layout shared by every entry point that takes one: the first
  * ANVILQ_WORKSPACE_COUNTER_BYTES hold arrival counters that must be zero
@@ -435,6 +436,40 @@ int anvilq_tree_attention(const uint16_t* q, const uint16_t* k_cache, const uint
                           const uint32_t* ancestors, int prefix_len, uint16_t* out, int M, int Hq, int Hkv, int D,
                           int Tmax, float scale, void* workspace, size_t workspace_bytes, int* dev_err,
                           anvilq_stream_t stream);
+
+/* ---- M-row decode operations (the batched verification of M draft tokens) ----
+ *
+ * The prologues / epilogues that the batch-1 GEMV fuses, for M rows whose
+ * projections run as M-row GEMMs (official_weights.py:466-503 per token):
+ * anvilq_rmsnorm_rows: out fp16 [M][H] = x * gamma / sqrt(mean(x^2) + eps), x fp32 [M][H];
+ * anvilq_residual_add_rows: x fp32 [M][H] += y fp16 [M][H];
+ * anvilq_silu_mul_rows: out fp16 [M][I] = silu(g) * u with [g | u] = gu fp16 [M][2I].
+ * flags: ANVILQ_GEMM_OVERLAP_PRIOR. */
+int anvilq_rmsnorm_rows(const float* x, const uint16_t* gamma, float eps, uint16_t* out, int M, int H,
+                        unsigned flags, anvilq_stream_t stream);
+int anvilq_residual_add_rows(float* x, const uint16_t* y, int M, int H, unsigned flags, anvilq_stream_t stream);
+int anvilq_silu_mul_rows(const uint16_t* gu, uint16_t* out, int M, int I, unsigned flags, anvilq_stream_t stream);
+
+/* ---- legacy KV-cache codecs of the Q16.16 datapath ---------------------------
+ *
+ * The legacy quantised caches of the Anvil-Q chips (anvil-q4/design/SPEC.md:250-262;
+ * model anvil-q4/tests/legacy_reference.py:71-97 cache_block, payload layout
+ * :186-203): format 1 INT8 symmetric, 2 INT4 symmetric, 3 INT4 asymmetric, one
+ * power-of-two exponent (and for format 3 a zero point) per block of `block`
+ * consecutive Q16.16 values of a head (1 <= block <= 64; a head's last block may
+ * be shorter).  Rows of H heads x D values:
+ *   values   int32  [rows][H * D]        Q16.16
+ *   payload  uint32 [rows][H * B * W]    B = ceil(D / block), W = ceil(block * bits / 32),
+ *                                        codes in ascending bytes / nibbles, padding zero
+ *   metadata uint32 [rows][H * B]        exponent | (zero point & 15) << 8
+ * Encoding is bit-identical to the reference model; decoding gives
+ * sat32((code - z) 2^e) and sets ANVILQ_DEV_ERR_CODEC for an exponent past
+ * the format's range, reserved metadata bits, the forbidden symmetric codes
+ * (-128, -8) or nonzero padding. */
+int anvilq_legacy_kv_encode(const int32_t* values, uint32_t* payload, uint32_t* metadata, int rows, int H, int D,
+                            int block, int format, anvilq_stream_t stream);
+int anvilq_legacy_kv_decode(const uint32_t* payload, const uint32_t* metadata, int32_t* values, int rows, int H,
+                            int D, int block, int format, int* dev_err, anvilq_stream_t stream);
 
 #ifdef __cplusplus
 }

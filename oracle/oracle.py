@@ -242,6 +242,86 @@ def attention_f64(q, keys, values):
     return np.einsum("kgt,tkd->kgd", p, values).reshape(hq, d)
 
 
+# ---- legacy symmetric / asymmetric KV-cache codecs over Q16.16 values --------
+# anvil-q4/tests/legacy_reference.py:71-97 (cache_block) and the payload layout
+# of :186-203 / anvil-q4/design/SPEC.md:250-262.  Formats: 1 INT8 symmetric,
+# 2 INT4 symmetric, 3 INT4 asymmetric.
+
+LEGACY_LIMITS = {1: (127, 25), 2: (7, 29)}    # (largest code, largest exponent)
+LEGACY_EMAX = {1: 25, 2: 29, 3: 32}
+
+
+def _round_away_shift(v: int, e: int) -> int:
+    """v / 2^e rounded half away from zero (signed magnitude)."""
+    if e == 0:
+        return v
+    m = (abs(v) + (1 << (e - 1))) >> e
+    return -m if v < 0 else m
+
+
+def _sat32(v: int) -> int:
+    return max(-(1 << 31), min((1 << 31) - 1, v))
+
+
+def legacy_kv_block(values, fmt):
+    """One block of Q16.16 values -> (metadata, codes, decoded).
+
+    Symmetric (fmt 1/2): the exponent is the smallest e <= Emax with
+    max|v| <= L 2^e (on the unrounded magnitude), codes round v / 2^e half away
+    from zero and clamp to [-L, L].  Asymmetric (fmt 3): the first e in 0..32 for
+    which the rounded extrema plus a zero point z in [-8, 7] fit [-8, 7]; z is
+    the fitting value closest to 0.  Metadata = e | (z & 15) << 8; decoded =
+    sat32((code - z) 2^e)."""
+    vals = [int(v) for v in values]
+    if fmt == 3:
+        for e in range(33):
+            r = [_round_away_shift(v, e) for v in vals]
+            low, high = max(-8, -8 - min(r)), min(7, 7 - max(r))
+            if low <= high:
+                z = low if low > 0 else (high if high < 0 else 0)
+                codes = [x + z for x in r]
+                break
+        else:
+            raise AssertionError("no exponent fits the asymmetric range")
+    else:
+        limit, emax = LEGACY_LIMITS[fmt]
+        a = max(abs(v) for v in vals)
+        e = next(k for k in range(emax + 1) if a <= limit << k)
+        z = 0
+        codes = [min(limit, max(-limit, _round_away_shift(v, e))) for v in vals]
+    return e | ((z & 15) << 8), codes, [_sat32((c - z) << e) for c in codes]
+
+
+def legacy_kv_encode(values, H, D, block, fmt):
+    """Rows of H heads x D Q16.16 values [R, H*D] -> payload uint32 [R, H*B*W],
+    metadata uint32 [R, H*B], decoded int32 [R, H*D]; B = ceil(D / block) blocks
+    per head, W = ceil(block * bits / 32) words per block, codes in ascending
+    bytes (INT8) or nibbles (INT4) of each word, padding zero."""
+    values = np.asarray(values, np.int64)
+    R = values.shape[0]
+    bits = 8 if fmt == 1 else 4
+    per = 32 // bits
+    B = (D + block - 1) // block
+    W = (block * bits + 31) // 32
+    payload = np.zeros((R, H * B * W), np.uint32)
+    meta = np.zeros((R, H * B), np.uint32)
+    decoded = np.zeros((R, H * D), np.int32)
+    for r in range(R):
+        for h in range(H):
+            for b in range(B):
+                lo, hi = h * D + b * block, h * D + min(D, (b + 1) * block)
+                m, codes, dec = legacy_kv_block(values[r, lo:hi], fmt)
+                meta[r, h * B + b] = m
+                decoded[r, lo:hi] = dec
+                padded = codes + [0] * (W * per - len(codes))
+                for w in range(W):
+                    word = 0
+                    for k in range(per):
+                        word |= (padded[w * per + k] & ((1 << bits) - 1)) << (k * bits)
+                    payload[r, (h * B + b) * W + w] = word
+    return payload, meta, decoded
+
+
 def tree_attention_f64(q, k_cache, v_cache, ancestors, prefix_len):
     """Per-node tree attention: node m attends to rows [0, prefix_len) and the
     rows prefix_len + j of its ancestors j (bit j of ancestors[m]), prefix

@@ -9,6 +9,8 @@ checkout of aHappend/anvil-q (default /root/reference, or $ANVILQ_REFERENCE):
 * anvil-q1-fp/tests/awq_prepare.py    pack_lanes / unpack_lanes
 * anvil-q1-fp/tests/fp64_reference.py attention
 * anvil-q4/tests/cache_reference.py  encode_head (per-head INT8 KV cache with FP32 escape)
+* anvil-q4/tests/legacy_reference.py cache_block (legacy symmetric INT8/INT4 and asymmetric INT4
+                                     KV-cache codecs over Q16.16 values)
 
 and writes their outputs on seeded inputs.  The tests only read the fixtures;
 nothing at test time needs the reference.  Run from the repository root:
@@ -290,6 +292,36 @@ def kv_int8_fixture():
     return out
 
 
+def legacy_kv_fixture():
+    """legacy_reference.cache_block for the three legacy cache formats (1: INT8
+    symmetric, 2: INT4 symmetric, 3: INT4 asymmetric) on the SPEC's worked
+    values, int32 extremes, zero and one-sided blocks, and seeded Q16.16 blocks
+    of lengths 1..64 over magnitudes 2^0..2^31."""
+    sys.path.insert(0, str(REF / "anvil-q4" / "tests"))
+    lr = _load("anvilq_q4_legacy_reference", REF / "anvil-q4" / "tests" / "legacy_reference.py")
+    lo, hi = -(1 << 31), (1 << 31) - 1
+    blocks = [[509, -509, 3, 0], [29, -29, 1], [0] * 8, [lo, hi, 0, 1], [lo] * 5, [hi] * 3, [-1, -2, -3],
+              [1, 2, 3, 4, 5, 6, 7, 8], [-7, 7, 8, -8], [hi, -hi], [(1 << 30) + 12345, -5], [127, -127, 128],
+              [7, -7, 8], [254, 255, 256, -1]]
+    rng = np.random.default_rng(20250417)
+    for n in (1, 2, 7, 8, 24, 32, 63, 64):
+        for _ in range(6):
+            mag = 1 << int(rng.integers(0, 32))
+            v = rng.integers(-mag, mag, size=n, dtype=np.int64)
+            if rng.integers(0, 4) == 0:
+                v = np.abs(v) + int(rng.integers(0, 1000))      # one-sided (asymmetric zero point)
+            blocks.append([int(min(hi, max(lo, x))) for x in v])
+    out = {"count": np.array(len(blocks))}
+    for i, b in enumerate(blocks):
+        out[f"b{i}_in"] = np.array(b, np.int32)
+        for fmt in (1, 2, 3):
+            meta, codes, decoded = lr.cache_block(b, fmt)
+            out[f"b{i}_f{fmt}_meta"] = np.array(meta, np.int32)
+            out[f"b{i}_f{fmt}_codes"] = np.array(codes, np.int8)
+            out[f"b{i}_f{fmt}_decoded"] = np.array(decoded, np.int32)
+    return out
+
+
 def main():
     t0 = time.time()
     only = set(sys.argv[1:])
@@ -300,6 +332,8 @@ def main():
             np.savez_compressed(HERE / "decode_small.npz", **decode_fixture())
         if "kv_int8" in only:
             np.savez_compressed(HERE / "kv_int8.npz", **kv_int8_fixture())
+        if "legacy_kv" in only:
+            np.savez_compressed(HERE / "legacy_kv.npz", **legacy_kv_fixture())
         return
     (HERE / "dequant_cases.json").write_text(json.dumps(dequant_fixture()))
     np.savez_compressed(HERE / "pack.npz", **pack_fixture())
@@ -308,6 +342,7 @@ def main():
     np.savez_compressed(HERE / "cfg0_gate_proj.npz", **cfg0_fixture())
     np.savez_compressed(HERE / "decode_small.npz", **decode_fixture())
     np.savez_compressed(HERE / "kv_int8.npz", **kv_int8_fixture())
+    np.savez_compressed(HERE / "legacy_kv.npz", **legacy_kv_fixture())
     print(f"golden fixtures written in {time.time() - t0:.1f}s")
 
 

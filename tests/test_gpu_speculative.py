@@ -8,7 +8,7 @@ import pytest
 import torch
 
 from anvilq_b200 import decoder
-from anvilq_b200.speculative import DecoderTarget, SpeculativeVerifier
+from anvilq_b200.speculative import BatchedDecoderTarget, DecoderTarget, SpeculativeVerifier
 
 pytestmark = pytest.mark.gpu
 
@@ -26,15 +26,15 @@ def _greedy(w, dev, first, n):
     return [first] + decoder.Decoder(w, dev, max_seq=32).generate(first, n)
 
 
-@pytest.mark.parametrize("graph", [False, True])
-def test_verifier_commits_the_greedy_decode(dev, graph):
+@pytest.mark.parametrize("graph,batched", [(False, False), (True, False), (False, True)])
+def test_verifier_commits_the_greedy_decode(dev, graph, batched):
     w = decoder.synthetic_weights(SHAPE, seed=41)
     seq = _greedy(w, dev, 9, 20)                  # seq[p] is the token at position p
     d = decoder.Decoder(w, dev, max_seq=32)
     if graph:
         d.reset(9)
         d.capture()
-    v = SpeculativeVerifier(DecoderTarget(d))
+    v = SpeculativeVerifier(BatchedDecoderTarget(d) if batched else DecoderTarget(d))
     r = v.verify(seq[0], seq[1], 0, new_sequence=True)
     assert (r.accepted, r.error, r.prediction) == (2, False, seq[2])
     wrong = lambda t: (t + 1) % SHAPE[7]
@@ -45,6 +45,7 @@ def test_verifier_commits_the_greedy_decode(dev, graph):
         if case == 0:         # a draft whose second token is wrong: one token accepted
             r = v.verify(seq[pos], wrong(seq[pos + 1]), pos)
             assert (r.accepted, r.error, r.target_runs, r.prediction) == (1, False, 1, seq[pos + 1])
+            # the rejected token's cache row (written by the batched pass) is rewritten by the next run
         elif case == 1:       # a draft that misses the prediction: nothing runs
             r = v.verify(wrong(seq[pos]), seq[pos + 1], pos)
             assert (r.accepted, r.error, r.target_runs) == (0, False, 0)
@@ -52,6 +53,27 @@ def test_verifier_commits_the_greedy_decode(dev, graph):
             assert (r.accepted, r.error) == (2, False)
         else:
             r = v.verify(seq[pos], seq[pos + 1], pos)
-            assert (r.accepted, r.error, r.target_runs) == (2, False, 2)
+            assert (r.accepted, r.error, r.target_runs) == (2, False, 1 if batched else 2)
         pos = v.committed_tokens
         assert v.prediction == seq[pos], pos
+
+
+@pytest.mark.parametrize("M", [1, 2, 4, 8])
+def test_verify_tokens_equal_sequential_decode_steps(dev, M):
+    """One batched pass over M tokens gives the greedy choice after each token,
+    as M decode steps do, and leaves the cache ready for the next step."""
+    w = decoder.synthetic_weights(SHAPE, seed=43)
+    seq = _greedy(w, dev, 5, 24)
+    d = decoder.Decoder(w, dev, max_seq=32)
+    P = 6
+    d.reset(seq[0])
+    for _ in range(P):                 # commit tokens 0 .. P-1 by plain steps
+        d.step()
+    d.stream.synchronize()
+    got = d.verify_tokens(seq[P:P + M], P)
+    assert got == seq[P + 1:P + M + 1]
+    # continue with a plain step after the verified tokens
+    d.set_position(seq[P + M], P + M)
+    d.step()
+    d.stream.synchronize()
+    assert int(d.token.item()) == seq[P + M + 1]

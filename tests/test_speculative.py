@@ -122,3 +122,34 @@ def test_target_failure_in_either_run_commits_nothing(kind, at):
     assert (r.accepted, r.error, r.commit_length) == (0, True, 0)
     assert len(t.runs) == at + 1
     assert v.committed_tokens == 0 and not v.sequence_valid and v.prediction is None
+
+
+class FakePairTarget(FakeTarget):
+    """A target that runs both draft tokens in one batched pass."""
+
+    def run_pair(self, token0, token1, pos):
+        self.runs.append(((token0, pos), (token1, pos + 1)))
+        a0 = self.vocabulary if self.bad_argmax_at == pos else self.next(token0, pos)
+        a1 = self.vocabulary if self.bad_argmax_at == pos + 1 else self.next(token1, pos + 1)
+        return a0, a1
+
+
+def test_batched_target_gives_the_same_commits_in_one_pass():
+    t = FakePairTarget()
+    v = SpeculativeVerifier(t)
+    t1 = t.next(3, 0)
+    r = v.verify(3, t1, 0, new_sequence=True)
+    assert (r.accepted, r.error, r.prediction, r.target_runs) == (2, False, t.next(t1, 1), 1)
+    r = v.verify(v.prediction, (t.next(v.prediction, 2) + 1) % t.vocabulary, 2)
+    assert (r.accepted, r.prediction, r.target_runs) == (1, t.next(t.next(t1, 1), 2), 1)
+    assert len(t.runs) == 2
+
+
+def test_batched_target_ignores_the_second_choice_when_the_first_misses():
+    # an out-of-vocabulary second choice only matters when token1 was accepted
+    t = FakePairTarget(bad_argmax_at=1)
+    r = SpeculativeVerifier(t).verify(3, (t.next(3, 0) + 1) % 50, 0, new_sequence=True)
+    assert (r.accepted, r.error) == (1, False)
+    t = FakePairTarget(bad_argmax_at=1)
+    r = SpeculativeVerifier(t).verify(3, t.next(3, 0), 0, new_sequence=True)
+    assert (r.accepted, r.error) == (0, True)
