@@ -60,24 +60,29 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kBandWords = 64;                          // 256 B per row, 512 columns
 constexpr int kBandCols = kBandWords * 8;
 constexpr int kTileRows = 16;
-constexpr int kStages = 3;
+constexpr int kMinStages = 3, kMaxStages = 4;   // ring depth per warp (template parameter S)
 constexpr int kTileBytes = kTileRows * kBandWords * 4;  // 4 KB
 constexpr int kMaxCluster = 16;
 constexpr unsigned long long kWaitLimitNs = 1000000000ull;
 
-// dynamic shared memory layout
-constexpr int kRingOff = 0;
-constexpr int kRingBytes = kWarps * kStages * kTileBytes;                 // 48 KB
-constexpr int kRedBytes = kWarps * kBandCols * 4;                         // 8 KB, aliases the ring
-static_assert(kRedBytes <= kRingBytes, "reduction buffer reuses the ring");
-constexpr int kXsOff = kRingOff + kRingBytes;                             // [warp][16] half (+pad)
-// per stage: 128 B of raw activation rows: [0, 64) primary (fp16 x, fp32 residual
-// or fp16 gate rows), [64, 128) secondary (fp16 gamma or fp16 up rows)
-constexpr int kXrawStage = 128;
-constexpr int kXrawOff = kXsOff + kWarps * kTileRows * 4;                 // [warp][stage][128 B]
-constexpr int kBarOff = kXrawOff + kWarps * kStages * kXrawStage;         // [warp][stage] u64
-constexpr int kPartOff = kBarOff + kWarps * kStages * 8 + 32;             // [512] f32
-constexpr int kSmemBytes = kPartOff + kBandCols * 4;
+// dynamic shared memory layout for a ring of S stages per warp: S = 3 fits
+// four CTAs on an SM, S = 4 three (each warp with a third more bytes in flight)
+template <int S>
+struct Smem {
+  static constexpr int kRingOff = 0;
+  static constexpr int kRingBytes = kWarps * S * kTileBytes;                 // 48 / 64 KB
+  static constexpr int kXsOff = kRingOff + kRingBytes;                       // [warp][16] half (+pad)
+  // per stage: 128 B of raw activation rows: [0, 64) primary (fp16 x, fp32 residual
+  // or fp16 gate rows), [64, 128) secondary (fp16 gamma or fp16 up rows)
+  static constexpr int kXrawStage = 128;
+  static constexpr int kXrawOff = kXsOff + kWarps * kTileRows * 4;           // [warp][stage][128 B]
+  static constexpr int kBarOff = kXrawOff + kWarps * S * kXrawStage;         // [warp][stage] u64
+  static constexpr int kPartOff = kBarOff + kWarps * S * 8 + 32;             // [512] f32
+  static constexpr int kBytes = kPartOff + kBandCols * 4;
+};
+constexpr int kRedBytes = kWarps * kBandCols * 4;                            // 8 KB, aliases the ring
+static_assert(kRedBytes <= Smem<kMinStages>::kRingBytes, "reduction buffer reuses the ring");
+constexpr int smem_bytes(int stages) { return stages == 3 ? Smem<3>::kBytes : Smem<4>::kBytes; }
 
 // Where the GEMV's activation row k comes from (template parameter XMODE):
 //   kXHalf     x[k] (fp16)
@@ -199,9 +204,12 @@ __device__ __forceinline__ void fma_f32_f16x2(float& a0, float& a1, uint32_t q2,
       : "r"(q2), "h"(x));
 }
 
-template <int XMODE, int YMODE, int BW>
+template <int XMODE, int YMODE, int BW, int kStages>
 __global__ void __launch_bounds__(kThreads, 4)
     gemv_tma_kernel(const __grid_constant__ CUtensorMap tmap, const Params p) {
+  using L = Smem<kStages>;
+  constexpr int kRingOff = L::kRingOff, kXsOff = L::kXsOff, kXrawStage = L::kXrawStage, kXrawOff = L::kXrawOff,
+                kBarOff = L::kBarOff, kPartOff = L::kPartOff;
   // Band geometry: BW qweight words (8 BW columns) per band.  A lane owns PW
   // consecutive words of a row; LPR lanes cover a row, and the warp's NRS row
   // sets take the tile's rows in turn (row r belongs to row set r % NRS).
@@ -699,29 +707,35 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   int sms = 0;
-  int max_clusters[5] = {0, 0, 0, 0, 0};   // co-resident clusters of size 1, 2, 4, 8, 16
+  // co-resident clusters of size 1, 2, 4, 8, 16, for each ring depth
+  int max_clusters[kMaxStages - kMinStages + 1][5] = {};
 };
 static DeviceInfo g_dev[kMaxDevices];
 static std::once_flag g_dev_once[kMaxDevices];
 
 using KernelFn = void (*)(CUtensorMap, Params);
 constexpr int kBandWidths[3] = {64, 32, 16};   // qweight words per band
-template <int XM, int YM>
+template <int XM, int YM, int S>
 static KernelFn kernel_bw(int bw) {
-  return bw == 64 ? gemv_tma_kernel<XM, YM, 64> : bw == 32 ? gemv_tma_kernel<XM, YM, 32> : gemv_tma_kernel<XM, YM, 16>;
+  return bw == 64 ? gemv_tma_kernel<XM, YM, 64, S> : bw == 32 ? gemv_tma_kernel<XM, YM, 32, S>
+                                                              : gemv_tma_kernel<XM, YM, 16, S>;
 }
-template <int XM>
+template <int XM, int S>
 static KernelFn kernel_y(int ymode, int bw) {
   if (ymode == kYPeer) {   // the fused all-gather takes fp16 activations
-    if constexpr (XM == kXHalf) return kernel_bw<kXHalf, kYPeer>(bw);
+    if constexpr (XM == kXHalf) return kernel_bw<kXHalf, kYPeer, S>(bw);
     return nullptr;
   }
-  return ymode == kYHalf ? kernel_bw<XM, kYHalf>(bw) : ymode == kYResidual ? kernel_bw<XM, kYResidual>(bw)
-                                                                         : kernel_bw<XM, kYRope>(bw);
+  return ymode == kYHalf ? kernel_bw<XM, kYHalf, S>(bw) : ymode == kYResidual ? kernel_bw<XM, kYResidual, S>(bw)
+                                                                            : kernel_bw<XM, kYRope, S>(bw);
 }
-static KernelFn kernel_for(int xmode, int ymode, int bw) {
-  return xmode == kXHalf ? kernel_y<kXHalf>(ymode, bw) : xmode == kXRmsNorm ? kernel_y<kXRmsNorm>(ymode, bw)
-                                                                           : kernel_y<kXSiluMul>(ymode, bw);
+template <int S>
+static KernelFn kernel_s(int xmode, int ymode, int bw) {
+  return xmode == kXHalf ? kernel_y<kXHalf, S>(ymode, bw) : xmode == kXRmsNorm ? kernel_y<kXRmsNorm, S>(ymode, bw)
+                                                                              : kernel_y<kXSiluMul, S>(ymode, bw);
+}
+static KernelFn kernel_for(int xmode, int ymode, int bw, int stages) {
+  return stages == 3 ? kernel_s<3>(xmode, ymode, bw) : kernel_s<4>(xmode, ymode, bw);
 }
 
 static const DeviceInfo* device_info() {
@@ -730,18 +744,21 @@ static const DeviceInfo* device_info() {
   std::call_once(g_dev_once[dev], [dev] {
     DeviceInfo& d = g_dev[dev];
     cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
-    for (int xm = 0; xm < 3; ++xm)
-      for (int ym = 0; ym < 4; ++ym)
-        for (int bw : kBandWidths) {
-          if (!kernel_for(xm, ym, bw)) continue;
-          cudaFuncSetAttribute(kernel_for(xm, ym, bw), cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-          cudaFuncSetAttribute(kernel_for(xm, ym, bw), cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-      }
+    for (int st = kMinStages; st <= kMaxStages; ++st)
+      for (int xm = 0; xm < 3; ++xm)
+        for (int ym = 0; ym < 4; ++ym)
+          for (int bw : kBandWidths) {
+            KernelFn k = kernel_for(xm, ym, bw, st);
+            if (!k) continue;
+            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(st));
+            cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+          }
+    for (int st = kMinStages; st <= kMaxStages; ++st)
     for (int i = 0; i < 5; ++i) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(1u << i, 1, 1);
       cfg.blockDim = dim3(kThreads, 1, 1);
-      cfg.dynamicSmemBytes = kSmemBytes;
+      cfg.dynamicSmemBytes = smem_bytes(st);
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
       attr[0].val.clusterDim.x = 1u << i;
@@ -750,8 +767,8 @@ static const DeviceInfo* device_info() {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, kernel_for(kXHalf, kYHalf, 64), &cfg) != cudaSuccess) n = 0;
-      d.max_clusters[i] = n;
+      if (cudaOccupancyMaxActiveClusters(&n, kernel_for(kXHalf, kYHalf, 64, st), &cfg) != cudaSuccess) n = 0;
+      d.max_clusters[st - kMinStages][i] = n;
     }
     cudaGetLastError();
   });
@@ -759,7 +776,7 @@ static const DeviceInfo* device_info() {
 }
 
 struct Plan {
-  int bw, bands, tiles, c, kc;
+  int bw, bands, tiles, c, kc, stages;
   size_t bytes;   // workspace bytes (counters included)
 };
 
@@ -802,8 +819,10 @@ static bool plan_override(int* c, int* kc, int* bw) {
 //     costs a few microseconds of tail; only deep-K layers, where every warp
 //     would stream 16 or more tiles, trade that tail for more warps (c = 8,
 //     kc = 3 on 28672 x 8192).
-static Plan make_plan(const DeviceInfo& d, int K, int N) {
+static Plan make_plan(const DeviceInfo& d, int K, int N, int stages) {
   Plan pl{};
+  pl.stages = stages;
+  const int* max_clusters = d.max_clusters[stages - kMinStages];
   const int W8 = N / 8;
   pl.tiles = (K + kTileRows - 1) / kTileRows;
   const double tiles_per_warp = (double)W8 * pl.tiles / (64.0 * 2.0 * d.sms * kWarps);
@@ -818,7 +837,7 @@ static Plan make_plan(const DeviceInfo& d, int K, int N) {
       const int bands = (W8 + bw - 1) / bw;
       for (int i = 4; i >= 0; --i) {
         const int c = 1 << i;
-        if (d.max_clusters[i] < bands || c * kWarps > 2 * pl.tiles) continue;
+        if (max_clusters[i] < bands || c * kWarps > 2 * pl.tiles) continue;
         const int ctas = bands * c;
         const double score = std::fabs(std::log((double)ctas / target));
         bool take = score < best_score - 1e-9;
@@ -841,7 +860,7 @@ static Plan make_plan(const DeviceInfo& d, int K, int N) {
     pl.c = 1;
     for (int i = 4; i >= 1; --i) {
       const int cand = 1 << i;
-      if (d.max_clusters[i] >= pl.bands && cand * kWarps <= pl.tiles) {
+      if (max_clusters[i] >= pl.bands && cand * kWarps <= pl.tiles) {
         pl.c = cand;
         break;
       }
@@ -850,7 +869,7 @@ static Plan make_plan(const DeviceInfo& d, int K, int N) {
       for (int cand_c : {8, 16}) {
         const int i = cand_c == 8 ? 3 : 4;
         for (int cand_kc = 3; cand_kc >= 2; --cand_kc)
-          if (kc == 1 && d.max_clusters[i] >= pl.bands * cand_kc && pl.bands * cand_c * cand_kc <= 4 * d.sms) {
+          if (kc == 1 && max_clusters[i] >= pl.bands * cand_kc && pl.bands * cand_c * cand_kc <= 4 * d.sms) {
             pl.c = cand_c;
             kc = cand_kc;
           }
@@ -861,6 +880,25 @@ static Plan make_plan(const DeviceInfo& d, int K, int N) {
   if (plan_override(&pl.c, &pl.kc, &pl.bw)) pl.bands = (W8 + pl.bw - 1) / pl.bw;
   pl.bytes = ANVILQ_WORKSPACE_COUNTER_BYTES +
              (pl.kc > 1 ? (size_t)pl.bands * pl.kc * pl.bw * 8 * sizeof(float) : 0);
+  return pl;
+}
+
+// Ring depth: four stages give every warp a third more bytes in flight but fit
+// three CTAs on an SM instead of four.  Measured on B200 (CUDA graphs of
+// distinct-weight launches), four stages are 6-14 % faster wherever the plan
+// keeps its CTA count (4096x11008, 4096x22016, 11008x4096, 8192x8192,
+// 28672x8192, 4864x896, 896x1152) and equal elsewhere, but 30 % slower on
+// 8192x28672, where 56 bands of 8-CTA clusters no longer fit co-resident and
+// the plan halves its CTAs.  So: four stages unless that plan launches fewer CTAs.
+static Plan choose_plan(const DeviceInfo& d, int K, int N) {
+  const Plan p3 = make_plan(d, K, N, kMinStages);
+  const Plan p4 = make_plan(d, K, N, kMaxStages);
+  const long long c3 = (long long)p3.bands * p3.kc * p3.c, c4 = (long long)p4.bands * p4.kc * p4.c;
+  const Plan& pl = c4 >= c3 ? p4 : p3;
+  static const bool log = std::getenv("ANVILQ_GEMV_PLAN_LOG") != nullptr;
+  if (log)
+    std::fprintf(stderr, "anvilq gemv plan K=%d N=%d: bw=%d bands=%d c=%d kc=%d stages=%d (CTAs %lld at 3 stages, "
+                 "%lld at 4)\n", K, N, pl.bw, pl.bands, pl.c, pl.kc, pl.stages, c3, c4);
   return pl;
 }
 
@@ -876,7 +914,7 @@ bool gemv_tma_supported(const void* x, const int32_t* qweight, const int32_t* qz
 size_t gemv_tma_workspace_bytes(int K, int N) {
   const tma_gemv::DeviceInfo* d = tma_gemv::device_info();
   if (!d || d->sms <= 0) return 0;
-  return tma_gemv::make_plan(*d, K, N).bytes;
+  return tma_gemv::choose_plan(*d, K, N).bytes;
 }
 
 int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
@@ -888,7 +926,8 @@ int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qze
   if (!d || d->sms <= 0 || !encode) return ANVILQ_ECUDA;
   if (io.xmode < 0 || io.xmode > 2 || io.ymode < 0 || io.ymode > 3) return ANVILQ_EINVAL;
   if (io.ymode == kYPeer && io.xmode != kXHalf) return ANVILQ_EINVAL;
-  Plan pl = make_plan(*d, K, N);
+  Plan pl = choose_plan(*d, K, N);
+  const int* max_clusters = d->max_clusters[pl.stages - kMinStages];
   if (io.ymode == kYPeer) {
     if (io.world < 1 || io.world > kMaxPeers || io.tp_rank < 0 || io.tp_rank >= io.world || !io.epoch)
       return ANVILQ_EINVAL;
@@ -904,7 +943,7 @@ int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qze
       pl.bands = (N / 8 + pl.bw - 1) / pl.bw;
       pl.c = 1;
       for (int i = 4; i >= 1; --i)
-        if (d->max_clusters[i] >= pl.bands && (1 << i) * kWarps <= pl.tiles) {
+        if (max_clusters[i] >= pl.bands && (1 << i) * kWarps <= pl.tiles) {
           pl.c = 1 << i;
           break;
         }
@@ -969,7 +1008,7 @@ int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qze
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.bands * pl.kc * pl.c, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.dynamicSmemBytes = smem_bytes(pl.stages);
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -980,7 +1019,7 @@ int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qze
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = overlap_prior ? 2 : 1;
-  if (cudaLaunchKernelEx(&cfg, kernel_for(io.xmode, io.ymode, pl.bw), map, p) != cudaSuccess) {
+  if (cudaLaunchKernelEx(&cfg, kernel_for(io.xmode, io.ymode, pl.bw, pl.stages), map, p) != cudaSuccess) {
     cudaGetLastError();
     return ANVILQ_ECUDA;
   }
