@@ -12,6 +12,12 @@
 * ``dequant(qw, qz, h, lane)`` mirrors verify.dequant (anvil-q1/tests/verify.py:241-250)
   for one lane of one word, computed on the GPU by the GEMM kernels' unpack.
 * ``pack(values)`` mirrors verify.pack (verify.py:252-253).
+* ``encode_head(values)`` mirrors cache_reference.encode_head
+  (anvil-q4/tests/cache_reference.py:54-71): the per-head INT8 KV encoding with
+  FP32 escape, encoded on the GPU by the cache-store kernel.
+* ``cache_block(values, cache_format)`` mirrors legacy_reference.cache_block
+  (anvil-q4/tests/legacy_reference.py:71-92): the legacy INT8/INT4 codecs of
+  the Q16.16 datapath, encoded and decoded on the GPU.
 """
 from __future__ import annotations
 
@@ -136,3 +142,60 @@ def dequant(qw, qz, h, lane, device="cuda"):
     num, den = significand << max(power + 16, 0), 1 << max(-(power + 16), 0)
     s16 = (2 * num + den) // (2 * den)
     return d * sign * s16, 0
+
+
+ESCAPE_MARKER = 0x7FC00000
+
+
+def encode_head(values, device="cuda"):
+    """cache_reference.encode_head signature: binary32 bit patterns of one
+    (token, kv head) row -> (scale bits or the escape marker, codes as unsigned
+    bytes, reconstructed binary32 bit patterns).  Codes and scale come from the
+    GPU encoder (anvilq_kv_int8_store); an ordinary row reconstructs as
+    fp32(code * scale), an escaped row as its canonical payload."""
+    bits = np.array([int(v) & 0xFFFFFFFF for v in values], np.uint32)
+    D = bits.size
+    dev = torch.device(device)
+    src = torch.from_numpy(bits.view(np.float32).reshape(1, 1, 1, D).copy()).to(dev)
+    codes = torch.zeros((1, 1, 1, D), dtype=torch.int8, device=dev)
+    meta = torch.zeros((1, 1, 1), dtype=torch.int32, device=dev)
+    escape = torch.zeros((1, 1, 1, D), dtype=torch.float32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ops.kv_int8_store(src, codes, meta, escape=escape, dev_err=err)
+    if int(err.item()):
+        raise AnvilqError(f"kv_int8_store device error bits 0x{int(err.item()):x}")
+    scale = int(meta.cpu().numpy().view(np.uint32)[0, 0, 0])
+    c = codes.cpu().numpy().reshape(D)
+    if scale == ESCAPE_MARKER:
+        payload = escape.cpu().numpy().reshape(D).view(np.uint32)
+        return scale, [int(x) & 255 for x in c], [int(x) for x in payload]
+    s32 = np.array([scale], np.uint32).view(np.float32)[0]
+    recon = (c.astype(np.float32) * s32).astype(np.float32).view(np.uint32)
+    return scale, [int(x) & 255 for x in c], [int(x) for x in recon]
+
+
+def cache_block(values, cache_format, device="cuda"):
+    """legacy_reference.cache_block signature: one block of Q16.16 ints and the
+    cache format (1 INT8 symmetric, 2 INT4 symmetric, 3 INT4 asymmetric) ->
+    (metadata, codes, decoded), encoded and decoded on the GPU
+    (anvilq_legacy_kv_encode / anvilq_legacy_kv_decode)."""
+    if cache_format not in (1, 2, 3):
+        raise ValueError("cache_format must be 1, 2 or 3")
+    n = len(values)
+    if not 1 <= n <= 64:
+        raise ValueError("a block holds 1..64 values")
+    dev = torch.device(device)
+    x = torch.tensor([[int(v) for v in values]], dtype=torch.int32, device=dev)
+    payload, meta = ops.legacy_kv_encode(x, 1, n, n, cache_format)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    decoded = ops.legacy_kv_decode(payload, meta, 1, n, n, cache_format, dev_err=err)
+    if int(err.item()):
+        raise AnvilqError(f"legacy cache decode device error bits 0x{int(err.item()):x}")
+    bits = 8 if cache_format == 1 else 4
+    words = payload.cpu().numpy().view(np.uint32).reshape(-1)
+    per = 32 // bits
+    codes = []
+    for i in range(n):
+        raw = (int(words[i // per]) >> ((i % per) * bits)) & ((1 << bits) - 1)
+        codes.append(raw - (1 << bits) if raw >= 1 << (bits - 1) else raw)
+    return int(meta.cpu().numpy().view(np.uint32)[0, 0]), codes, [int(v) for v in decoded.cpu().numpy()[0]]

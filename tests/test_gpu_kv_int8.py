@@ -134,3 +134,15 @@ def test_attention_int8_escape_without_payload_flags_error(dev):
     ops.gqa_decode_int8(T(q, dev), kc, km, vc, vm, T(np.array([64], np.int32), dev))   # no escape buffers
     with pytest.raises(AnvilqError):
         ops.raise_device_errors(dev)
+
+
+def test_golden_api_encode_head_matches_reference(dev, golden_dir):
+    """golden_api.encode_head (the reference's signature, GPU encoder) returns the
+    reference's own (scale, codes, reconstructed) for every fixture head."""
+    from anvilq_b200 import golden_api
+    g = np.load(golden_dir / "kv_int8.npz")
+    for i in range(int(g["count"])):
+        scale, codes, recon = golden_api.encode_head([int(b) for b in g[f"h{i}_in"]])
+        assert scale == int(g[f"h{i}_scale"]), i
+        assert codes == [int(c) for c in g[f"h{i}_codes"]], i
+        assert recon == [int(r) for r in g[f"h{i}_recon"]], i

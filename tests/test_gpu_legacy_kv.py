@@ -109,3 +109,18 @@ def test_decode_flags_forbidden_codes_padding_and_metadata(dev):
         ops.legacy_kv_decode(p, m, H, D, block, fmt)
         with pytest.raises(_lib.AnvilqError, match="legacy cache"):
             ops.raise_device_errors(dev)
+
+
+@pytest.mark.gpu
+def test_golden_api_cache_block_matches_reference(dev, golden_dir):
+    """golden_api.cache_block (the reference's signature, GPU codec) returns the
+    reference's own (metadata, codes, decoded) for every fixture block."""
+    from anvilq_b200 import golden_api
+    g = np.load(golden_dir / "legacy_kv.npz")
+    for i in range(int(g["count"])):
+        block = [int(v) for v in g[f"b{i}_in"]]
+        for fmt in (1, 2, 3):
+            meta, codes, decoded = golden_api.cache_block(block, fmt)
+            assert meta == int(g[f"b{i}_f{fmt}_meta"]), (i, fmt)
+            assert codes == [int(c) for c in g[f"b{i}_f{fmt}_codes"]], (i, fmt)
+            assert decoded == [int(d) for d in g[f"b{i}_f{fmt}_decoded"]], (i, fmt)
