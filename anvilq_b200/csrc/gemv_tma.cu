@@ -9,10 +9,10 @@
 // a tile is 16 rows of a band (4 KB), fetched by ONE cp.async.bulk.tensor.2d
 // from a tensor map over qweight [K][N/8], together with the tile's 16
 // activations (a 32-byte bulk copy) on the same mbarrier.  Every warp streams
-// its own range of tiles through a private 3-stage ring, so bytes in flight
-// cost no registers, and four 4-warp CTAs fit on an SM (16 warps, up to 192 KB
-// in flight).  Tiles past the last row or column are zero-filled by the TMA
-// unit and contribute nothing.
+// its own range of tiles through a private ring of 3 or 4 stages (chosen per
+// plan), so bytes in flight cost no registers: four 4-warp CTAs fit on an SM
+// with 3 stages, three with 4 (up to 192 KB in flight either way).  Tiles past
+// the last row or column are zero-filled by the TMA unit and contribute nothing.
 //
 // Split-K, two levels.  The c CTAs of a thread-block cluster and kc clusters
 // share one band; the band's tiles are split evenly over all their warps.
