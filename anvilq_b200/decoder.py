@@ -22,7 +22,6 @@ no checkpoint is available offline.
 """
 from __future__ import annotations
 
-import ctypes
 from dataclasses import dataclass, field
 
 import numpy as np

@@ -1,5 +1,4 @@
 """Shared pytest configuration: the `gpu` marker and import paths."""
-import os
 import sys
 from pathlib import Path
 

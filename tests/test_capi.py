@@ -3,7 +3,6 @@ import ctypes
 import re
 from pathlib import Path
 
-import pytest
 
 REPO = Path(__file__).resolve().parents[1]
 
