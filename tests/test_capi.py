@@ -37,3 +37,24 @@ def test_host_only_calls():
     assert lib.anvilq_w4a16_gemm(None, None, None, None, None, None, 1, 128, 64, 128, None, 0, None, None) == -1
     assert lib.anvilq_awq_pack(None, None, 1, 8, None) == -1
     assert lib.anvilq_awq_dequant(None, None, None, None, None, 128, 64, 128, None, None) == -1
+
+
+def test_every_entry_point_rejects_null_pointers_on_the_host():
+    """Every launching entry point checks its required pointers before touching
+    the device: all-null arguments return ANVILQ_EINVAL.  (Run only where no
+    GPU is visible, so that a missing check could never launch on null.)"""
+    import torch
+    if torch.cuda.is_available():
+        import pytest
+        pytest.skip("host-only check")
+    from anvilq_b200 import _lib
+    lib = _lib.load()
+    P, I, F, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+    checked = 0
+    for name, (res, args) in _lib.SIGNATURES.items():
+        if res is not I or P not in args:
+            continue
+        vals = [None if a is P else 128 if a is I else 1.0 if a is F else (1 << 20) if a is SZ else 0 for a in args]
+        assert getattr(lib, name)(*vals) == -1, name
+        checked += 1
+    assert checked >= 30
