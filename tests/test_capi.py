@@ -54,7 +54,9 @@ def test_every_entry_point_rejects_null_pointers_on_the_host():
     for name, (res, args) in _lib.SIGNATURES.items():
         if res is not I or P not in args:
             continue
-        vals = [None if a is P else 128 if a is I else 1.0 if a is F else (1 << 20) if a is SZ else 0 for a in args]
+        pointer = lambda a: a is P or (isinstance(a, type) and issubclass(a, ctypes._Pointer))
+        vals = [None if pointer(a) else 128 if a is I else 1.0 if a is F else (1 << 20) if a is SZ else 0
+                for a in args]
         assert getattr(lib, name)(*vals) == -1, name
         checked += 1
     assert checked >= 30
