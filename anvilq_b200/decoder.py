@@ -51,8 +51,8 @@ class DecoderWeights:
 
 
 def synthetic_weights(shape=QWEN05B_SHAPE, seed: int = 17) -> DecoderWeights:
-    """Random-init weights of the given shape.  W4 tensors use the BASELINE
-    distributions (u4 uniform, scales |N(0,1)|*0.01+1e-3); biases N(0,1);
+    """Random-init weights of the given shape.  W4 tensors use the benchmark
+    value distributions (u4 uniform, scales |N(0,1)|*0.01+1e-3); biases N(0,1);
     norm weights 1 + 0.1 N(0,1); embedding 0.5 N(0,1); all fp16."""
     L, H, I, QH, KVH, D, G, V, _ = shape
     rng = np.random.default_rng(seed)

@@ -289,8 +289,8 @@ int anvilq_rope_kv_append(const uint16_t* qkv, const int32_t* pos, uint16_t* q_o
 
 /* ---- tensor-parallel column split with the all-gather fused in ---------------
  *
- * Replaces the column-split projection followed by its all-gather (SURVEY
- * cfg4: rank r of W holds output columns [r N/W, (r+1) N/W); reference analog:
+ * Replaces the column-split projection followed by its all-gather (the
+ * 70B-class layer split: rank r of W holds output columns [r N/W, (r+1) N/W); reference analog:
  * the column interleave of anvil-q2/rtl/anvil_q2_gemv_lane.sv:117,187).
  *
  * Peer buffers: a rank exports any device pointer (e.g. a tensor's) as an IPC

@@ -181,7 +181,7 @@ def linear_fixture():
             xq = np.round(x.astype(np.float64) * 65536).astype(np.int64)
             out[key + "_xq16"] = xq.astype(np.int32)
             out[key + "_yq16"] = q16_linear(xq, qw, qz, sc, bias, G)
-    # (3) BASELINE value distributions at small sizes (x ~ N(0,1), u4 uniform, scales |N|*.01+1e-3)
+    # (3) the benchmark value distributions at small sizes (x ~ N(0,1), u4 uniform, scales |N|*.01+1e-3)
     for (M, K, N, seed, bias) in ((1, 256, 64, 17, False), (1, 256, 64, 43, True),
                                   (4, 384, 128, 89, False), (2, 128, 256, 17, True)):
         x, layer = synthetic.gemv_case(M, K, N, 128, seed, bias)
@@ -201,7 +201,7 @@ def linear_fixture():
     return out
 
 
-def cfg0_fixture():
+def qwen05b_gate_proj_fixture():
     """Qwen2.5-0.5B gate_proj shape, the reference's CPU-runnable case: K=896, N=4864, G=128,
     seed 17.  Inputs are regenerated from anvilq_b200.synthetic.gemv_case; their digests
     are stored to catch generator drift."""
@@ -339,7 +339,7 @@ def main():
     np.savez_compressed(HERE / "pack.npz", **pack_fixture())
     np.savez_compressed(HERE / "linear.npz", **linear_fixture())
     np.savez_compressed(HERE / "attention.npz", **attention_fixture())
-    np.savez_compressed(HERE / "cfg0_gate_proj.npz", **cfg0_fixture())
+    np.savez_compressed(HERE / "qwen05b_gate_proj_896x4864.npz", **qwen05b_gate_proj_fixture())
     np.savez_compressed(HERE / "decode_small.npz", **decode_fixture())
     np.savez_compressed(HERE / "kv_int8.npz", **kv_int8_fixture())
     np.savez_compressed(HERE / "legacy_kv.npz", **legacy_kv_fixture())

@@ -53,7 +53,7 @@ def test_reference_fixtures(dev, golden_dir):
 
 @pytest.mark.parametrize("B,Tmax", [(1, 512), (8, 512), (1, 4096), (8, 4096), (2, 32768)])
 def test_config_shapes(dev, B, Tmax):
-    """32 q heads / 8 kv heads, head_dim 128 (the BASELINE attention configuration)."""
+    """32 q heads / 8 kv heads, head_dim 128 (the decode-attention benchmark configuration)."""
     q, k, v = synthetic.kv_case(B, 32, 8, 128, Tmax, seed=17 + B)
     rng = np.random.default_rng(Tmax + B)
     seqlens = [Tmax] + list(rng.integers(1, Tmax + 1, size=B - 1))

@@ -99,10 +99,10 @@ def test_fast_kernel_golden_fixtures(dev, golden_dir):
         assert err <= TOL_ERR and (cos is None or cos >= TOL_COS), (key, err, cos)
 
 
-def test_cfg0_full_size(dev, golden_dir):
+def test_qwen05b_gate_proj_full_size(dev, golden_dir):
     """Qwen2.5-0.5B gate_proj (896 x 4864) against FP32Model.linear's own output."""
     from anvilq_b200 import ops
-    g = np.load(golden_dir / "cfg0_gate_proj.npz")
+    g = np.load(golden_dir / "qwen05b_gate_proj_896x4864.npz")
     x, layer = synthetic.gemv_case(1, 896, 4864, 128, 17, False)
     y = ops.gemm(T(x, dev), T(layer.qweight, dev), T(layer.qzeros, dev), T(layer.scales, dev), None, 128)
     ops.raise_device_errors(dev)

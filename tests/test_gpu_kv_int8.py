@@ -104,7 +104,7 @@ def _attention_case(dev, B, Hq, Hkv, D, Tmax, seqlens, seed, specials=False):
 
 
 @pytest.mark.parametrize("B,Hq,Hkv,D,Tmax,seqlens", [
-    (2, 32, 8, 128, 4096, [4096, 1000]),       # cfg2 heads, clusters of 2
+    (2, 32, 8, 128, 4096, [4096, 1000]),       # 32/8 heads of 128, clusters of 2
     (1, 14, 2, 64, 1088, [1050]),              # 0.5B heads, clusters of 8
     (1, 14, 2, 64, 8192, [8000]),              # several clusters per pair (global merge)
     (3, 8, 2, 128, 512, [1, 17, 512]),         # ragged, partial tiles

@@ -109,11 +109,11 @@ def test_q16_wide_cancellation():
     assert y[0].tolist() == expected
 
 
-def test_cfg0_full_size(golden_dir):
+def test_qwen05b_gate_proj_full_size(golden_dir):
     """Qwen2.5-0.5B gate_proj (K=896, N=4864): C restatement equals FP32Model.linear."""
     import hashlib
     from anvilq_b200 import synthetic
-    g = np.load(golden_dir / "cfg0_gate_proj.npz")
+    g = np.load(golden_dir / "qwen05b_gate_proj_896x4864.npz")
     x, layer = synthetic.gemv_case(1, 896, 4864, 128, 17, False)
     digest = hashlib.sha256()
     for a in (x, layer.qweight, layer.qzeros, layer.scales):
