@@ -24,6 +24,9 @@ SIGNATURES = {
     "anvilq_w4a16_gemm_workspace_size": (SZ, [I, I, I, I]),
     "anvilq_w4a16_gemm": (I, [P, P, P, P, P, P, I, I, I, I, P, SZ, P, P]),
     "anvilq_w4a16_gemm_ex": (I, [P, P, P, P, P, P, I, I, I, I, P, SZ, P, ctypes.c_uint, P]),
+    "anvilq_w4a16_gemv_plan": (I, [I, I, I, P]),
+    "anvilq_w4a16_gemv_plan_workspace_size": (SZ, [I, I, I, P]),
+    "anvilq_w4a16_gemv_planned": (I, [P, P, P, P, P, P, I, I, I, P, P, SZ, P, ctypes.c_uint, P]),
     "anvilq_w4a16_gemm_exact": (I, [P, P, P, P, P, P, I, I, I, I, P, P]),
     "anvilq_w4a16_verify_gemm": (I, [P, P, P, P, P, P, I, I, I, I, P, SZ, P, P]),
     "anvilq_w4a16_tc_pack_size": (SZ, [I, I, I]),
@@ -60,6 +63,19 @@ SIGNATURES = {
     "anvilq_legacy_kv_encode": (I, [P, P, P, I, I, I, I, I, P]),
     "anvilq_legacy_kv_decode": (I, [P, P, P, I, I, I, I, I, P, P]),
 }
+
+GEMV_KERNEL_CLUSTER = 0
+GEMV_KERNEL_STREAM = 1
+
+
+class GemvPlan(ctypes.Structure):
+    """anvilq_gemv_plan: the kernel and launch shape of one batch-1 GEMV."""
+    _fields_ = [("kernel", I), ("band_cols", I), ("cluster", I), ("kc", I), ("warps", I), ("stages", I),
+                ("ctas", I)]
+
+    def as_dict(self):
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
 
 _lib = None
 

@@ -555,6 +555,18 @@ static int launch_exact(const uint16_t* x, const int32_t* qweight, const int32_t
 
 using namespace anvilq;
 
+// The M = 1 plan: the stream-K kernel for layers of at least kStreamMinBytes
+// of int4 weights (where every SM streams several chunks), the cluster kernel
+// below that (decode-size layers, latency bound).
+static constexpr long long kStreamMinBytes = 8ll << 20;
+static bool default_gemv_plan(const void* x, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
+                              int K, int N, int G, GemvPlan* plan) {
+  if ((long long)K * N / 2 >= kStreamMinBytes && gemv_stream_supported(x, qweight, qzeros, scales, K, N, G) &&
+      gemv_stream_default_plan(K, N, plan) && gemv_stream_check_plan(K, N, *plan) == ANVILQ_OK)
+    return true;
+  return gemv_tma_supported(x, qweight, qzeros, scales, K, N, G) && gemv_cluster_default_plan(K, N, plan);
+}
+
 extern "C" {
 
 int anvilq_abi_version(void) { return ANVILQ_ABI_VERSION; }
@@ -577,7 +589,11 @@ size_t anvilq_w4a16_gemm_workspace_size(int M, int K, int N, int G) {
   const DeviceInfo* d = device_info();
   if (!d) return 0;
   size_t b = plan_for(*d, M, K, N).bytes;
-  if (M == 1) b = std::max(b, gemv_tma_workspace_bytes(K, N));
+  if (M == 1) {
+    b = std::max(b, gemv_tma_workspace_bytes(K, N));
+    GemvPlan sp;
+    if (gemv_stream_default_plan(K, N, &sp)) b = std::max(b, gemv_stream_workspace_bytes(sp));
+  }
   // the tensor-core path may serve any M (anvilq_w4a16_verify_gemm)
   if (G == 128 && K % 128 == 0 && N % 32 == 0) b = std::max(b, verify_tc_workspace_bytes(M, K, N));
   return b;
@@ -602,13 +618,19 @@ int anvilq_w4a16_gemm_ex(const uint16_t* x, const int32_t* qweight, const int32_
   if (!fast_path_ok(x, qweight, qzeros, scales, M, K, N, G))
     return launch_exact(x, qweight, qzeros, scales, bias, reinterpret_cast<__half*>(y), M, K, N, G,
                         dev_err, s);
-  if (M == 1 && gemv_tma_supported(x, qweight, qzeros, scales, K, N, G))
-  {
-    GemvIo io;
-    io.x = x;
-    io.y = y;
-    return launch_gemv_tma(io, qweight, qzeros, scales, bias, K, N, G, workspace, workspace_bytes, dev_err, s,
-                           (flags & ANVILQ_GEMM_OVERLAP_PRIOR) != 0);
+  if (M == 1) {
+    GemvPlan pl;
+    if (default_gemv_plan(x, qweight, qzeros, scales, K, N, G, &pl)) {
+      const bool overlap = (flags & ANVILQ_GEMM_OVERLAP_PRIOR) != 0;
+      if (pl.kernel == ANVILQ_GEMV_KERNEL_STREAM)
+        return launch_gemv_stream(pl, x, qweight, qzeros, scales, bias, y, K, N, G, workspace, workspace_bytes,
+                                  dev_err, s, overlap);
+      GemvIo io;
+      io.x = x;
+      io.y = y;
+      return launch_gemv_tma(io, qweight, qzeros, scales, bias, K, N, G, workspace, workspace_bytes, dev_err, s,
+                             overlap);
+    }
   }
   if (M >= ANVILQ_VERIFY_TC_MIN_M && verify_tc_supported(x, qweight, qzeros, scales, M, K, N, G))
     return launch_verify_tc(x, qweight, nullptr, qzeros, scales, bias, y, M, K, N, workspace, workspace_bytes,
@@ -620,6 +642,52 @@ int anvilq_w4a16_gemm_ex(const uint16_t* x, const int32_t* qweight, const int32_
   if (!workspace || workspace_bytes < pl.bytes) return ANVILQ_EWORKSPACE;
   if (!aligned16(workspace)) return ANVILQ_EALIGN;
   return launch_fast(pl, x, qweight, qzeros, scales, bias, y, M, K, N, G, workspace, dev_err, s);
+}
+
+int anvilq_w4a16_gemv_plan(int K, int N, int G, anvilq_gemv_plan* plan) {
+  if (!plan || !shape_ok(1, K, N, G)) return ANVILQ_EINVAL;
+  // any 16-byte aligned operands: the plan depends on the shape only
+  const void* a = reinterpret_cast<const void*>(uintptr_t(256));
+  if (!default_gemv_plan(a, static_cast<const int32_t*>(a), static_cast<const int32_t*>(a),
+                         static_cast<const uint16_t*>(a), K, N, G, plan))
+    return ANVILQ_ESHAPE;
+  return ANVILQ_OK;
+}
+
+size_t anvilq_w4a16_gemv_plan_workspace_size(int K, int N, int G, const anvilq_gemv_plan* plan) {
+  if (!plan || !shape_ok(1, K, N, G)) return 0;
+  GemvPlan pl = *plan;
+  if (pl.kernel == ANVILQ_GEMV_KERNEL_STREAM)
+    return gemv_stream_check_plan(K, N, pl) == ANVILQ_OK ? gemv_stream_workspace_bytes(pl) : 0;
+  if (pl.kernel == ANVILQ_GEMV_KERNEL_CLUSTER)
+    return gemv_cluster_check_plan(K, N, &pl) == ANVILQ_OK ? gemv_cluster_workspace_bytes(K, N, pl) : 0;
+  return 0;
+}
+
+int anvilq_w4a16_gemv_planned(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
+                              const uint16_t* scales, const uint16_t* bias, uint16_t* y, int K, int N, int G,
+                              const anvilq_gemv_plan* plan, void* workspace, size_t workspace_bytes,
+                              int* dev_err, unsigned flags, anvilq_stream_t stream) {
+  if (!x || !qweight || !qzeros || !scales || !y || !plan) return ANVILQ_EINVAL;
+  if (flags & ~(unsigned)ANVILQ_GEMM_OVERLAP_PRIOR) return ANVILQ_EINVAL;
+  if (!shape_ok(1, K, N, G)) return ANVILQ_EINVAL;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool overlap = (flags & ANVILQ_GEMM_OVERLAP_PRIOR) != 0;
+  GemvPlan pl = *plan;
+  if (pl.kernel == ANVILQ_GEMV_KERNEL_STREAM) {
+    if (!aligned16(y) || !gemv_stream_supported(x, qweight, qzeros, scales, K, N, G)) return ANVILQ_ESHAPE;
+    return launch_gemv_stream(pl, x, qweight, qzeros, scales, bias, y, K, N, G, workspace, workspace_bytes,
+                              dev_err, s, overlap);
+  }
+  if (pl.kernel != ANVILQ_GEMV_KERNEL_CLUSTER) return ANVILQ_EINVAL;
+  const int rc = gemv_cluster_check_plan(K, N, &pl);
+  if (rc != ANVILQ_OK) return rc;
+  if (!gemv_tma_supported(x, qweight, qzeros, scales, K, N, G)) return ANVILQ_ESHAPE;
+  GemvIo io;
+  io.x = x;
+  io.y = y;
+  return launch_gemv_tma(io, qweight, qzeros, scales, bias, K, N, G, workspace, workspace_bytes, dev_err, s,
+                         overlap, &pl);
 }
 
 int anvilq_w4a16_verify_gemm(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
@@ -730,7 +798,8 @@ int anvilq_w4a16_gemv_allgather(const uint16_t* x, const int32_t* qweight, const
   if (col_base < 0 || col_base % 8 || n_full < col_base + N) return ANVILQ_EINVAL;
   for (int r = 0; r < world; ++r)
     if (!peer_y[r] || !peer_flags[r]) return ANVILQ_EINVAL;
-  if (!aligned16(x) || !gemv_tma_supported(x, qweight, qzeros, scales, K, N, G)) return ANVILQ_ESHAPE;
+  GemvPlan pl;
+  if (!aligned16(x) || !default_gemv_plan(x, qweight, qzeros, scales, K, N, G, &pl)) return ANVILQ_ESHAPE;
   GemvIo io;
   io.xmode = 0;
   io.ymode = 3;
@@ -743,8 +812,14 @@ int anvilq_w4a16_gemv_allgather(const uint16_t* x, const int32_t* qweight, const
   io.world = world;
   io.tp_rank = rank;
   io.col_base = col_base;
+  // the kernel and plan of anvilq_w4a16_gemm for this slice, so the fused call's
+  // values are bit-identical to the GEMV followed by an all-gather
+  const bool overlap = (flags & ANVILQ_GEMM_OVERLAP_PRIOR) != 0;
+  if (pl.kernel == ANVILQ_GEMV_KERNEL_STREAM)
+    return launch_gemv_stream(pl, x, qweight, qzeros, scales, bias, nullptr, K, N, G, workspace, workspace_bytes,
+                              dev_err, reinterpret_cast<cudaStream_t>(stream), overlap, &io);
   return launch_gemv_tma(io, qweight, qzeros, scales, bias, K, N, G, workspace, workspace_bytes, dev_err,
-                         reinterpret_cast<cudaStream_t>(stream), (flags & ANVILQ_GEMM_OVERLAP_PRIOR) != 0);
+                         reinterpret_cast<cudaStream_t>(stream), overlap);
 }
 
 int anvilq_w4a16_gemm_exact(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,

@@ -44,8 +44,6 @@
 
 #include <algorithm>
 #include <cmath>
-#include <cstdio>
-#include <cstdlib>
 #include <mutex>
 
 #include "../../include/anvilq.h"
@@ -780,29 +778,6 @@ struct Plan {
   size_t bytes;   // workspace bytes (counters included)
 };
 
-// Tuning aid: ANVILQ_GEMV_PLAN="c,kc[,bw]" forces the cluster size, the number
-// of clusters per band and the band width in words (c a power of two <= 16,
-// 1 <= kc <= 8, bw 64, 32 or 16), for sweeps.
-static bool plan_override(int* c, int* kc, int* bw) {
-  static int oc = 0, okc = 0, obw = 0;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    const char* e = std::getenv("ANVILQ_GEMV_PLAN");
-    int a = 0, b = 0, w = 0;
-    const int n = e ? std::sscanf(e, "%d,%d,%d", &a, &b, &w) : 0;
-    if (n >= 2 && a >= 1 && a <= kMaxCluster && (a & (a - 1)) == 0 && b >= 1 && b <= 8) {
-      oc = a;
-      okc = b;
-      obw = n == 3 && (w == 64 || w == 32 || w == 16) ? w : 0;
-    }
-  });
-  if (!oc) return false;
-  *c = oc;
-  *kc = okc;
-  if (obw) *bw = obw;
-  return true;
-}
-
 // Grid of bands x kc clusters of c CTAs, in one of two regimes (measured on
 // B200 across the 0.5B, 7B and 70B projection shapes; each rule picks the
 // fastest plan or one within a few percent):
@@ -877,7 +852,6 @@ static Plan make_plan(const DeviceInfo& d, int K, int N, int stages) {
     }
   }
   pl.kc = kc;
-  if (plan_override(&pl.c, &pl.kc, &pl.bw)) pl.bands = (W8 + pl.bw - 1) / pl.bw;
   pl.bytes = ANVILQ_WORKSPACE_COUNTER_BYTES +
              (pl.kc > 1 ? (size_t)pl.bands * pl.kc * pl.bw * 8 * sizeof(float) : 0);
   return pl;
@@ -894,15 +868,63 @@ static Plan choose_plan(const DeviceInfo& d, int K, int N) {
   const Plan p3 = make_plan(d, K, N, kMinStages);
   const Plan p4 = make_plan(d, K, N, kMaxStages);
   const long long c3 = (long long)p3.bands * p3.kc * p3.c, c4 = (long long)p4.bands * p4.kc * p4.c;
-  const Plan& pl = c4 >= c3 ? p4 : p3;
-  static const bool log = std::getenv("ANVILQ_GEMV_PLAN_LOG") != nullptr;
-  if (log)
-    std::fprintf(stderr, "anvilq gemv plan K=%d N=%d: bw=%d bands=%d c=%d kc=%d stages=%d (CTAs %lld at 3 stages, "
-                 "%lld at 4)\n", K, N, pl.bw, pl.bands, pl.c, pl.kc, pl.stages, c3, c4);
+  return c4 >= c3 ? p4 : p3;
+}
+
+static Plan plan_from(const GemvPlan& g, int K, int N) {
+  Plan pl{};
+  pl.bw = g.band_cols / 8;
+  pl.bands = (N / 8 + pl.bw - 1) / pl.bw;
+  pl.tiles = (K + kTileRows - 1) / kTileRows;
+  pl.c = g.cluster;
+  pl.kc = g.kc;
+  pl.stages = g.stages;
+  pl.bytes = ANVILQ_WORKSPACE_COUNTER_BYTES +
+             (pl.kc > 1 ? (size_t)pl.bands * pl.kc * pl.bw * 8 * sizeof(float) : 0);
   return pl;
 }
 
 }  // namespace tma_gemv
+
+bool gemv_cluster_default_plan(int K, int N, GemvPlan* out) {
+  using namespace tma_gemv;
+  const DeviceInfo* d = device_info();
+  if (!d || d->sms <= 0) return false;
+  const Plan pl = choose_plan(*d, K, N);
+  out->kernel = ANVILQ_GEMV_KERNEL_CLUSTER;
+  out->band_cols = pl.bw * 8;
+  out->cluster = pl.c;
+  out->kc = pl.kc;
+  out->warps = kWarps;
+  out->stages = pl.stages;
+  out->ctas = pl.bands * pl.kc * pl.c;
+  return true;
+}
+
+int gemv_cluster_check_plan(int K, int N, GemvPlan* g) {
+  using namespace tma_gemv;
+  const DeviceInfo* d = device_info();
+  if (!d || d->sms <= 0) return ANVILQ_ECUDA;
+  const int bw = g->band_cols / 8;
+  if (g->kernel != ANVILQ_GEMV_KERNEL_CLUSTER || bw * 8 != g->band_cols || (bw != 64 && bw != 32 && bw != 16))
+    return ANVILQ_EINVAL;
+  const int c = g->cluster;
+  if (c < 1 || c > kMaxCluster || (c & (c - 1)) || g->kc < 1 || g->kc > 8 || g->warps != kWarps ||
+      g->stages < kMinStages || g->stages > kMaxStages)
+    return ANVILQ_EINVAL;
+  int li = 0;
+  while ((1 << li) < c) ++li;
+  if (d->max_clusters[g->stages - kMinStages][li] < 1) return ANVILQ_ESHAPE;   // a cluster does not fit
+  const long long bands = (N / 8 + bw - 1) / bw;
+  if (g->kc > 1 && bands * c * (long long)sizeof(int) > ANVILQ_WORKSPACE_COUNTER_BYTES) return ANVILQ_ESHAPE;
+  if (bands * g->kc * c > (1ll << 31) - 1) return ANVILQ_ESHAPE;
+  g->ctas = (int)(bands * g->kc * c);
+  return ANVILQ_OK;
+}
+
+size_t gemv_cluster_workspace_bytes(int K, int N, const GemvPlan& g) {
+  return tma_gemv::plan_from(g, K, N).bytes;
+}
 
 bool gemv_tma_supported(const void* x, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
                         int K, int N, int G) {
@@ -919,14 +941,15 @@ size_t gemv_tma_workspace_bytes(int K, int N) {
 
 int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
                     const uint16_t* bias, int K, int N, int G, void* workspace, size_t workspace_bytes, int* dev_err,
-                    cudaStream_t stream, bool overlap_prior) {
+                    cudaStream_t stream, bool overlap_prior, const GemvPlan* plan) {
   using namespace tma_gemv;
   const DeviceInfo* d = device_info();
   auto encode = encode_fn();
   if (!d || d->sms <= 0 || !encode) return ANVILQ_ECUDA;
   if (io.xmode < 0 || io.xmode > 2 || io.ymode < 0 || io.ymode > 3) return ANVILQ_EINVAL;
   if (io.ymode == kYPeer && io.xmode != kXHalf) return ANVILQ_EINVAL;
-  Plan pl = choose_plan(*d, K, N);
+  if (plan && (io.xmode != kXHalf || io.ymode != kYHalf)) return ANVILQ_EINVAL;
+  Plan pl = plan ? plan_from(*plan, K, N) : choose_plan(*d, K, N);
   const int* max_clusters = d->max_clusters[pl.stages - kMinStages];
   if (io.ymode == kYPeer) {
     if (io.world < 1 || io.world > kMaxPeers || io.tp_rank < 0 || io.tp_rank >= io.world || !io.epoch)

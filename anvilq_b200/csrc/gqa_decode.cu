@@ -714,13 +714,6 @@ static Plan plan_for(int B, int Hq, int Hkv, int D, int Tmax, const DeviceInfo& 
   const int per_sm = D == 64 ? 2 : 1;   // shared memory per CTA: ~83 KB / ~165 KB
   const long long slots = (long long)dev.sms * per_sm;
   long long ctas = std::max<long long>(1, std::min<long long>(slots / pairs, (tiles + kWarps - 1) / kWarps));
-  // Tuning aid: ANVILQ_ATTN_SPLITS=n (1..128) forces the CTAs per pair, for sweeps.
-  static const int forced = [] {
-    const char* e = std::getenv("ANVILQ_ATTN_SPLITS");
-    const int v = e ? std::atoi(e) : 0;
-    return v >= 1 && v <= kMaxCluster * kMaxClusters ? v : 0;
-  }();
-  if (forced) ctas = forced;
   const int max_clusters = dev.max_clusters[D == 64 ? 0 : 1];
   pl.cluster = 1;
   if (max_clusters >= 1)

@@ -5,12 +5,19 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/anvilq.h"
+
 namespace anvilq {
+
+using GemvPlan = anvilq_gemv_plan;
 
 // Batch-1 W4A16 GEMV on the TMA + cluster kernel (gemv_tma.cu).
 bool gemv_tma_supported(const void* x, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
                         int K, int N, int G);
 size_t gemv_tma_workspace_bytes(int K, int N);
+bool gemv_cluster_default_plan(int K, int N, GemvPlan* plan);
+int gemv_cluster_check_plan(int K, int N, GemvPlan* plan);   // validates, fills in ctas
+size_t gemv_cluster_workspace_bytes(int K, int N, const GemvPlan& plan);
 
 // Source of the activations and destination of the result of one GEMV launch
 // (modes as in ANVILQ_GEMV_X_* / ANVILQ_GEMV_Y_* of anvilq.h).
@@ -36,9 +43,24 @@ struct GemvIo {
   unsigned* epoch = nullptr;
   int world = 0, tp_rank = 0, col_base = 0;
 };
+// plan: null for the default plan of the shape; a given plan is only taken
+// for x_mode/y_mode 0 and must have passed gemv_cluster_check_plan.
 int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
                     const uint16_t* bias, int K, int N, int G, void* workspace, size_t workspace_bytes, int* dev_err,
-                    cudaStream_t stream, bool overlap_prior);
+                    cudaStream_t stream, bool overlap_prior, const GemvPlan* plan = nullptr);
+
+// Batch-1 W4A16 GEMV on the stream-K kernel (gemv_stream.cu).  peer: null, or
+// the tensor-parallel fields of a GemvIo (peer_y, peer_flags, epoch, world,
+// tp_rank, col_base) for the all-gather fused into the epilogue (y unused).
+bool gemv_stream_supported(const void* x, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
+                           int K, int N, int G);
+bool gemv_stream_default_plan(int K, int N, GemvPlan* plan);
+int gemv_stream_check_plan(int K, int N, const GemvPlan& plan);
+size_t gemv_stream_workspace_bytes(const GemvPlan& plan);
+int launch_gemv_stream(const GemvPlan& plan, const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
+                       const uint16_t* scales, const uint16_t* bias, uint16_t* y, int K, int N, int G,
+                       void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t stream,
+                       bool overlap_prior, const GemvIo* peer = nullptr);
 
 // Small-M (speculative verify) GEMM on tcgen05 tensor cores (verify_gemm_tc.cu):
 // G == 128, K % 128 == 0, N % 32 == 0, 16-byte aligned operands; M rows in

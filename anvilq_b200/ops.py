@@ -6,6 +6,7 @@ stream.
 """
 from __future__ import annotations
 
+import ctypes
 import threading
 
 import torch
@@ -142,6 +143,41 @@ def gemm(x, qweight, qzeros, scales, bias=None, group: int = 128, out=None, dev_
                                         _ptr(out), M, K, N, group, _ptr(ws), ws.numel(), _ptr(err), flags,
                                         _stream_ptr(x2.device)), "anvilq_w4a16_gemm_ex")
     return out.view(N) if squeeze else out
+
+
+def gemv_plan(K: int, N: int, group: int = 128) -> dict:
+    """The plan ``gemm`` uses for one row (anvilq_w4a16_gemv_plan): kernel
+    (``_lib.GEMV_KERNEL_CLUSTER`` / ``_lib.GEMV_KERNEL_STREAM``), band_cols,
+    cluster, kc, warps, stages, ctas."""
+    plan = _lib.GemvPlan()
+    lib = _lib.load()
+    _lib.check(lib.anvilq_w4a16_gemv_plan(K, N, group, ctypes.byref(plan)), "anvilq_w4a16_gemv_plan")
+    return plan.as_dict()
+
+
+def gemv_planned(x, qweight, qzeros, scales, bias=None, group: int = 128, plan=None, out=None, dev_err=None,
+                 overlap_prior: bool = False):
+    """y[N] = x[K] @ dequant(W) (+ bias) under an explicit plan (a dict with
+    the fields of ``gemv_plan``); the library checks the plan against the
+    kernel's rules and raises on one it does not accept."""
+    K, N = _check_awq(qweight, qzeros, scales, group)
+    x1 = x.reshape(-1)
+    if x1.dtype != torch.float16 or x1.numel() != K or not x1.is_contiguous():
+        raise ValueError(f"x must be contiguous float16 [{K}]")
+    if out is None:
+        out = torch.empty(N, dtype=torch.float16, device=x1.device)
+    p = _lib.GemvPlan(**plan)
+    lib = _lib.load()
+    need = lib.anvilq_w4a16_gemv_plan_workspace_size(K, N, group, ctypes.byref(p))
+    if need == 0:
+        raise _lib.AnvilqError(f"plan {plan} does not fit K={K}, N={N}, G={group}")
+    ws = workspace(x1.device, need)
+    err = device_error_word(x1.device) if dev_err is None else dev_err
+    _lib.check(lib.anvilq_w4a16_gemv_planned(_ptr(x1), _ptr(qweight), _ptr(qzeros), _ptr(scales), _ptr(bias),
+                                             _ptr(out), K, N, group, ctypes.byref(p), _ptr(ws), ws.numel(),
+                                             _ptr(err), GEMM_OVERLAP_PRIOR if overlap_prior else 0,
+                                             _stream_ptr(x1.device)), "anvilq_w4a16_gemv_planned")
+    return out
 
 
 def verify_gemm(x, qweight, qzeros, scales, bias=None, group: int = 128, out=None, dev_err=None):

@@ -108,6 +108,45 @@ int anvilq_w4a16_gemm_ex(const uint16_t* x, const int32_t* qweight, const int32_
                          void* workspace, size_t workspace_bytes,
                          int* dev_err, unsigned flags, anvilq_stream_t stream);
 
+/* ---- batch-1 GEMV plans ------------------------------------------------------
+ * The M = 1 GEMV runs on one of two kernels, chosen per shape:
+ *   ANVILQ_GEMV_KERNEL_CLUSTER  bands of band_cols columns; `cluster` CTAs of a
+ *     thread-block cluster and `kc` clusters split K per band (partials summed
+ *     over distributed shared memory, then, for kc > 1, by the cluster arriving
+ *     last at the band's workspace ticket); 4 warps per CTA.  Decode-size layers.
+ *   ANVILQ_GEMV_KERNEL_STREAM  256-column bands cut into 32-row chunks, the
+ *     chunks split evenly over `ctas` CTAs of `warps` warps (stream-K); a band
+ *     shared by several CTAs is summed by the CTA arriving last at its ticket.
+ *     7B / 70B-class layers.  Needs K % 32 == 0, G % 32 == 0, K % G == 0.
+ * `stages` is the depth of every warp's TMA ring.  Every sum has a fixed
+ * order: a plan's results are bit-reproducible.
+ * anvilq_w4a16_gemv_plan fills in the plan anvilq_w4a16_gemm(_ex) uses for
+ * M = 1 (ANVILQ_ESHAPE when no fast kernel serves the shape);
+ * anvilq_w4a16_gemv_planned runs y = x @ dequant(W) (+ bias) under a given
+ * plan, checked against the kernel's rules (ANVILQ_EINVAL for a plan the
+ * kernel does not have, ANVILQ_ESHAPE for one that does not fit the shape);
+ * its workspace is anvilq_w4a16_gemv_plan_workspace_size bytes (0: the plan
+ * does not fit).  Same meaning and tolerance as anvilq_w4a16_gemm with M = 1.
+ * Replaces FP32Model.linear (anvil-q1/tests/official_weights.py:418-437) like
+ * anvilq_w4a16_gemm; the plan is the launch shape a caller may pin. */
+#define ANVILQ_GEMV_KERNEL_CLUSTER 0
+#define ANVILQ_GEMV_KERNEL_STREAM 1
+typedef struct anvilq_gemv_plan {
+  int kernel;     /* ANVILQ_GEMV_KERNEL_* */
+  int band_cols;  /* output columns per band: 512, 256 or 128 (cluster), 256 (stream) */
+  int cluster;    /* CTAs per thread-block cluster (power of two <= 16); 1 for stream */
+  int kc;         /* clusters per band (1..8); 1 for stream */
+  int warps;      /* warps per CTA: 4 (cluster); 4, 8 or 16 (stream) */
+  int stages;     /* ring depth per warp: 3 or 4 (cluster); 2..4 (stream) */
+  int ctas;       /* CTAs launched (cluster: bands * kc * cluster, filled in) */
+} anvilq_gemv_plan;
+int anvilq_w4a16_gemv_plan(int K, int N, int G, anvilq_gemv_plan* plan);
+size_t anvilq_w4a16_gemv_plan_workspace_size(int K, int N, int G, const anvilq_gemv_plan* plan);
+int anvilq_w4a16_gemv_planned(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
+                              const uint16_t* scales, const uint16_t* bias, uint16_t* y, int K, int N, int G,
+                              const anvilq_gemv_plan* plan, void* workspace, size_t workspace_bytes,
+                              int* dev_err, unsigned flags, anvilq_stream_t stream);
+
 /* The speculative-verify GEMM on the tensor cores: M token rows against one
  * AWQ weight matrix with tcgen05.mma from shared memory into TMEM
  * accumulators (integer deltas q - z on the tensor cores, the group scale
