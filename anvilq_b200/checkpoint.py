@@ -81,13 +81,17 @@ class ArrayCheckpoint:
 
     def raw(self, name, coordinate):
         a = self._array(name)
-        try:
-            v = a[tuple(coordinate)]
-        except IndexError as exc:
-            raise CheckpointError("tensor coordinate out of bounds") from exc
+        coordinate = tuple(int(c) for c in coordinate)
+        # whole-element coordinates inside the tensor only (numpy would wrap negatives)
+        if len(coordinate) != a.ndim or any(not 0 <= c < n for c, n in zip(coordinate, a.shape)):
+            raise CheckpointError("tensor coordinate out of bounds")
+        v = a[coordinate]
         return int(v.view(np.uint32)) if a.dtype == np.int32 else int(v.view(np.uint16))
 
     def half(self, name, coordinate):
+        # official_weights.py half(): the tensor must be F16
+        if self._array(name).dtype != np.float16:
+            raise CheckpointError(f"{name} is not an F16 tensor")
         value = struct.unpack("<e", struct.pack("<H", self.raw(name, coordinate)))[0]
         if not np.isfinite(value):
             raise CheckpointError(f"nonfinite F16 {name}{tuple(coordinate)}")

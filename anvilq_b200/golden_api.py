@@ -18,13 +18,22 @@
 * ``cache_block(values, cache_format)`` mirrors legacy_reference.cache_block
   (anvil-q4/tests/legacy_reference.py:71-92): the legacy INT8/INT4 codecs of
   the Q16.16 datapath, encoded and decoded on the GPU.
+* ``attention(q, keys, values)`` mirrors fp64_reference.attention
+  (anvil-q1-fp/tests/fp64_reference.py:164-170): numpy in, numpy out, on the
+  decode-attention kernel.
+* ``pack_lanes(codes)`` / ``unpack_lanes(words, outputs)`` mirror
+  awq_prepare.pack_lanes / unpack_lanes (anvil-q1-fp/tests/awq_prepare.py:84-99)
+  on numpy arrays, packed and unpacked on the GPU.
+* ``GpuModel(checkpoint, shape).token(token, position, new_sequence)`` mirrors
+  FP32Model.token (anvil-q1/tests/official_weights.py:451-509): one decode step
+  of the device-resident decoder, the logits returned as a list.
 """
 from __future__ import annotations
 
 import numpy as np
 import torch
 
-from . import ops
+from . import ops, synthetic
 from ._lib import AnvilqError
 from .checkpoint import CheckpointError, output_width
 
@@ -199,3 +208,112 @@ def cache_block(values, cache_format, device="cuda"):
         raw = (int(words[i // per]) >> ((i % per) * bits)) & ((1 << bits) - 1)
         codes.append(raw - (1 << bits) if raw >= 1 << (bits - 1) else raw)
     return int(meta.cpu().numpy().view(np.uint32)[0, 0]), codes, [int(v) for v in decoded.cpu().numpy()[0]]
+
+
+def attention(q, keys, values, device="cuda"):
+    """fp64_reference.attention(q, keys, values): q [Hq, D], keys / values
+    [T, Hkv, D] -> [Hq, D] as a float64 numpy array, query head j attending
+    with kv head j // (Hq / Hkv).  Computed by the decode-attention kernel
+    (anvilq_gqa_decode) over the inputs rounded to binary16, the fp16 KV
+    cache of the W4A16 datapath; scores and softmax in fp32.  Head dims 64
+    and 128 are supported; others raise ValueError."""
+    q = np.asarray(q)
+    keys = np.asarray(keys)
+    values = np.asarray(values)
+    if q.ndim != 2 or keys.ndim != 3 or values.shape != keys.shape:
+        raise ValueError("q [Hq, D] and keys / values [T, Hkv, D] expected")
+    hq, d = q.shape
+    t, hkv, dk = keys.shape
+    if dk != d or t < 1 or hkv < 1 or hq % hkv:
+        raise ValueError("q, keys and values disagree on head dim, kv heads or length")
+    dev = torch.device(device)
+    f16 = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float16)).to(dev)
+    out = ops.gqa_decode(f16(q)[None], f16(keys)[None], f16(values)[None],
+                         torch.tensor([t], dtype=torch.int32, device=dev))
+    ops.raise_device_errors(dev)
+    return out[0].double().cpu().numpy()
+
+
+def pack_lanes(codes, device="cuda"):
+    """awq_prepare.pack_lanes(codes): output-major nibbles uint8 [N, K], N % 8 == 0,
+    -> little-endian uint32 [K, N / 8] with lane i of word w holding column 8 w + i
+    at bit shift (0, 16, 4, 20, 8, 24, 12, 28)[i]."""
+    codes = np.asarray(codes)
+    if codes.ndim != 2 or codes.shape[0] % 8 or codes.size == 0 or (codes < 0).any() or (codes > 15).any():
+        raise ValueError("invalid nibble array")
+    t = torch.from_numpy(np.ascontiguousarray(codes, np.uint8)).to(torch.device(device))
+    return ops.pack_lanes(t).cpu().numpy().view("<u4")
+
+
+def unpack_lanes(words, outputs, device="cuda"):
+    """awq_prepare.unpack_lanes(words, outputs): uint32 [K, N / 8] with N == outputs
+    -> uint8 [N, K]."""
+    words = np.asarray(words)
+    if words.ndim != 2 or words.shape[1] * 8 != outputs or words.size == 0:
+        raise ValueError("invalid packed output shape")
+    t = torch.from_numpy(np.ascontiguousarray(words).astype(np.uint32).view(np.int32)).to(torch.device(device))
+    return ops.unpack_lanes(t, int(outputs)).cpu().numpy()
+
+
+def _f16_tensor(checkpoint, kind, layer):
+    """A whole fp16 tensor (embedding, kind 0; norms, kinds 5-7) of a checkpoint."""
+    if hasattr(checkpoint, "embedding") and hasattr(checkpoint, "norms"):
+        if kind == 0:
+            return checkpoint.embedding
+        return checkpoint.norms[{5: ("input", layer), 6: ("post", layer), 7: ("final", 0)}[kind]]
+    name, _ = checkpoint.resolve(kind, layer if kind != 7 else 0, 0, 0, 0)
+    d = checkpoint.tensors[name]
+    count = (d["end"] - d["start"]) // d["width"]
+    return np.frombuffer(checkpoint.data, dtype=np.float16, count=count,
+                         offset=checkpoint.base + d["start"]).reshape(d["shape"])
+
+
+class GpuModel:
+    """``FP32Model(checkpoint, shape)`` for the decode step: ``token(token,
+    position, new_sequence)`` returns the logits after the token, as
+    FP32Model.token does, computed by one step of the device-resident decoder
+    (W4A16 projections with binary16 activations, fp16 KV cache, tied fp16
+    lm_head).  Positions must follow one another from 0 (a new sequence
+    restarts at 0); a violated bound or a device error raises CheckpointError,
+    as the reference's demand() does."""
+
+    def __init__(self, checkpoint, shape, device="cuda"):
+        from .decoder import Decoder, DecoderWeights
+        self.shape = tuple(int(v) for v in shape)
+        L, H, I, QH, KVH, D, G, V, SEQ = self.shape
+        layers = []
+        for l in range(L):
+            projs = {}
+            for p in range(7):
+                qweight, qzeros, scales, bias = _layer_arrays(checkpoint, l, p, self.shape)
+                projs[p] = synthetic.AwqLayer(np.asarray(qweight), np.asarray(qzeros), np.asarray(scales),
+                                              None if bias is None else np.asarray(bias), G)
+            layers.append(projs)
+        norms = {("input", l): _f16_tensor(checkpoint, 5, l) for l in range(L)}
+        norms.update({("post", l): _f16_tensor(checkpoint, 6, l) for l in range(L)})
+        norms["final", 0] = _f16_tensor(checkpoint, 7, 0)
+        weights = DecoderWeights(self.shape, layers, norms, _f16_tensor(checkpoint, 0, 0))
+        self.decoder = Decoder(weights, device, max_seq=SEQ, keep_logits=True)
+        self.next_position = 0
+
+    def token(self, token, position, new_sequence=False):
+        L, H, I, QH, KVH, D, G, V, SEQ = self.shape
+        token, position = int(token), int(position)
+        if not (0 <= token < V and 0 <= position < min(SEQ, self.decoder.max_seq)):
+            raise CheckpointError("token or position outside the model shape")
+        if new_sequence:
+            if position != 0:
+                raise CheckpointError("a new sequence starts at position 0")
+            self.next_position = 0
+        if position != self.next_position:
+            raise CheckpointError("positions must follow one another")
+        d = self.decoder
+        try:
+            d.set_position(token, position)
+            d.step()
+            d.stream.synchronize()
+            d.check_errors()
+        except AnvilqError as exc:
+            raise CheckpointError(str(exc)) from exc
+        self.next_position += 1
+        return [float(v) for v in d.logits.cpu().numpy()]

@@ -70,7 +70,12 @@ class BatchedDecoderTarget(DecoderTarget):
     token0 at pos and token1 at pos + 1 through M = 2 row GEMMs, so the weights
     stream once for the pair.  run_pair returns the greedy choice after each;
     the verifier uses the second only when the first equals token1, which is
-    exactly when the reference's controller would have run it."""
+    exactly when the reference's controller would have run it.
+
+    run_pair contract: it raises when the token0 half failed; a target that
+    can tell a failure of the token1 half alone returns None as the second
+    choice (the first stays valid).  This one cannot tell the halves apart
+    (device error bits cover the whole pass), so any error raises."""
 
     def run_pair(self, token0: int, token1: int, pos: int):
         a0, a1 = self.dec.verify_tokens([token0, token1], pos)
@@ -110,12 +115,14 @@ class SpeculativeVerifier:
         try:
             if hasattr(self.target, "run_pair"):   # both target runs in one batched pass
                 runs = 1
-                a0, a1 = self.target.run_pair(token0, token1, pos)
+                a0, a1 = self.target.run_pair(token0, token1, pos)   # a1 None: token1's half failed
                 if not 0 <= a0 < self.vocabulary:
                     return Verification(0, True, 0, 0, runs)
                 if a0 != token1:
+                    # the reference never runs token1 here (WAIT0 -> commit 1), so
+                    # whatever happened to the second half does not matter
                     return self._commit(pos, 1, a0, runs)
-                if not 0 <= a1 < self.vocabulary:
+                if a1 is None or not 0 <= a1 < self.vocabulary:
                     return Verification(0, True, 0, 0, runs)
                 return self._commit(pos, 2, a1, runs)
             runs += 1

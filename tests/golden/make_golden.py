@@ -2,7 +2,7 @@
 """Regenerate the golden fixtures in tests/golden/ by running the reference itself.
 
 This script imports the reference's own Python golden models read-only from a
-checkout of aHappend/anvil-q (default /root/reference, or $ANVILQ_REFERENCE):
+checkout of aHappend/anvil-q, named by --reference or $ANVILQ_REFERENCE:
 
 * anvil-q1/tests/verify.py         dequant_cases / dequant / pack / rounded / sat / half_fixed
 * anvil-q1/tests/official_weights.py  FP32Model.linear, FP32Model.token, f32
@@ -15,7 +15,7 @@ checkout of aHappend/anvil-q (default /root/reference, or $ANVILQ_REFERENCE):
 and writes their outputs on seeded inputs.  The tests only read the fixtures;
 nothing at test time needs the reference.  Run from the repository root:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --reference <checkout of aHappend/anvil-q>
 """
 from __future__ import annotations
 
@@ -30,7 +30,23 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("ANVILQ_REFERENCE", "/root/reference"))
+
+
+def _reference_root() -> Path:
+    import argparse
+    ap = argparse.ArgumentParser(description="regenerate tests/golden from the reference's own golden models")
+    ap.add_argument("--reference", default=os.environ.get("ANVILQ_REFERENCE"),
+                    help="checkout of aHappend/anvil-q (default: $ANVILQ_REFERENCE)")
+    args, _ = ap.parse_known_args()
+    if not args.reference:
+        raise SystemExit("name the reference checkout: --reference <path> or $ANVILQ_REFERENCE")
+    root = Path(args.reference)
+    if not (root / "anvil-q1" / "tests" / "official_weights.py").exists():
+        raise SystemExit(f"{root} does not hold anvil-q1/tests/official_weights.py")
+    return root
+
+
+REF = _reference_root()
 sys.path.insert(0, str(REPO))
 
 

@@ -63,6 +63,37 @@ def test_config_shapes(dev, B, Tmax):
         check(y[b], ref[b], (B, Tmax, b, seqlens[b]))
 
 
+@pytest.mark.parametrize("B", [32, 64])
+@pytest.mark.parametrize("Tmax", [512, 4096, 32768])
+def test_config_large_batches(dev, B, Tmax):
+    """Batches of 32 and 64 sequences (32 / 8 heads of 128) at every context of
+    the decode-attention configuration, with ragged lengths (the first sequence
+    full).  The caches are drawn on the device from a seeded generator; a sample
+    of sequences (first, middle, last, and the shortest) is checked against the
+    binary64 attention() restatement."""
+    from anvilq_b200 import ops
+    Hq, Hkv, D = 32, 8, 128
+    g = torch.Generator(device=dev)
+    g.manual_seed(B * 100003 + Tmax)
+    k = torch.randn((B, Tmax, Hkv, D), generator=g, device=dev, dtype=torch.float16)
+    v = torch.randn((B, Tmax, Hkv, D), generator=g, device=dev, dtype=torch.float16)
+    q = torch.randn((B, Hq, D), generator=g, device=dev, dtype=torch.float16)
+    rng = np.random.default_rng(B + Tmax)
+    seqlens = np.concatenate([[Tmax], rng.integers(1, Tmax + 1, size=B - 1)]).astype(np.int32)
+    sl = T(seqlens, dev)
+    y1 = ops.gqa_decode(q, k, v, sl).clone()
+    y2 = ops.gqa_decode(q, k, v, sl)
+    ops.raise_device_errors(dev)
+    assert torch.equal(y1, y2)
+    y = y1.float().cpu().numpy()
+    for b in sorted({0, B // 2, B - 1, int(np.argmin(seqlens))}):
+        L = int(seqlens[b])
+        ref = oracle.attention_f64(q[b].cpu().numpy(), k[b, :L].cpu().numpy(), v[b, :L].cpu().numpy())
+        check(y[b], ref, (B, Tmax, b, L))
+    del k, v
+    torch.cuda.empty_cache()
+
+
 def test_qwen05b_shape(dev):
     """14 q heads / 2 kv heads (group of 7), head_dim 64, context 1024."""
     q, k, v = synthetic.kv_case(3, 14, 2, 64, 1024, seed=43)

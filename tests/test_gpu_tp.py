@@ -109,3 +109,53 @@ def test_tp2_fused_allgather_matches_nccl(tmp_path):
     out = tmp_path / "same.npy"
     mp.spawn(_fused_rank_main, args=(2, _free_port(), 4096, 11008, str(out)), nprocs=2, join=True)
     assert np.load(out).all()
+
+
+def _timeout_rank_main(rank, world, port, K, N, out_path):
+    import datetime
+    import time
+    from anvilq_b200 import ops, tp
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        x, layer = synthetic.gemv_case(1, K, N, 128, 41)
+        to = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+        outs = tp.PeerOutputs(N, slots=2, device=dev)
+        fused = tp.FusedTPLinear(to(layer.qweight), to(layer.qzeros), to(layer.scales), None, 128, outs, 0)
+        err = ops.device_error_word(dev)
+        err.zero_()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        if rank == 0:   # rank 1 never enters the fused call
+            t0 = time.monotonic()
+            fused(to(x[0]))
+            torch.cuda.synchronize(dev)
+            dt = time.monotonic() - t0
+            bits = int(err.item())
+            err.zero_()
+            np.save(out_path, np.array([bits, dt]))
+        dist.barrier()   # both ranks, between steps, with no kernel of theirs in flight
+        torch.cuda.synchronize(dev)
+        outs.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("K,N", [(4096, 11008), (896, 1152)])
+def test_tp2_fused_allgather_wait_expires_when_a_rank_is_missing(tmp_path, K, N):
+    """The fused all-gather's flag wait is bounded: with rank 1 never entering
+    the call, rank 0's kernel gives up after about a second, sets
+    ANVILQ_DEV_ERR_TIMEOUT and returns, and the context stays usable (the
+    ranks then meet at a barrier and release their buffers).  Both the
+    stream-K kernel (7B-class slice) and the cluster kernel (decode-size
+    slice) are covered.  No multicast object; plain peer stores and flags."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = tmp_path / "timeout.npy"
+    mp.spawn(_timeout_rank_main, args=(2, _free_port(), K, N, str(out)), nprocs=2, join=True)
+    bits, dt = np.load(out)
+    assert int(bits) & 4, bits          # ANVILQ_DEV_ERR_TIMEOUT
+    assert 0.5 <= dt <= 10.0, dt

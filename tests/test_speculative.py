@@ -127,11 +127,15 @@ def test_target_failure_in_either_run_commits_nothing(kind, at):
 class FakePairTarget(FakeTarget):
     """A target that runs both draft tokens in one batched pass."""
 
+    def __init__(self, fail_second=False, **kw):
+        super().__init__(**kw)
+        self.fail_second = fail_second
+
     def run_pair(self, token0, token1, pos):
         self.runs.append(((token0, pos), (token1, pos + 1)))
         a0 = self.vocabulary if self.bad_argmax_at == pos else self.next(token0, pos)
         a1 = self.vocabulary if self.bad_argmax_at == pos + 1 else self.next(token1, pos + 1)
-        return a0, a1
+        return a0, None if self.fail_second else a1
 
 
 def test_batched_target_gives_the_same_commits_in_one_pass():
@@ -153,3 +157,19 @@ def test_batched_target_ignores_the_second_choice_when_the_first_misses():
     t = FakePairTarget(bad_argmax_at=1)
     r = SpeculativeVerifier(t).verify(3, t.next(3, 0), 0, new_sequence=True)
     assert (r.accepted, r.error) == (0, True)
+
+
+def test_batched_target_whose_second_half_failed():
+    """The token1 half failing only matters when token1 was accepted: with
+    a0 != token1 the reference controller (WAIT0) never runs token1 and
+    commits one token, so the batched pass must too."""
+    t = FakePairTarget(fail_second=True)
+    v = SpeculativeVerifier(t)
+    r = v.verify(3, (t.next(3, 0) + 1) % 50, 0, new_sequence=True)
+    assert (r.accepted, r.error, r.commit_length, r.prediction) == (1, False, 1, t.next(3, 0))
+    assert v.committed_tokens == 1 and v.sequence_valid
+    t = FakePairTarget(fail_second=True)
+    v = SpeculativeVerifier(t)
+    r = v.verify(3, t.next(3, 0), 0, new_sequence=True)
+    assert (r.accepted, r.error, r.commit_length) == (0, True, 0)
+    assert v.committed_tokens == 0 and not v.sequence_valid

@@ -68,3 +68,43 @@ def test_column_ranges():
     parts = [tp.shard_awq(qw, qz, sc, None, r, 4) for r in range(4)]
     assert torch.equal(torch.cat([p[0] for p in parts], 1), qw)
     assert all(p[2].shape == (2, 32) for p in parts)
+
+
+def _skip_rank_main(rank, world, port, skipper, out_dir):
+    """Every rank builds the split; rank `skipper` never enters the all-gather
+    (it stays alive past the others' process-group timeout)."""
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    x, layer = synthetic.gemv_case(1, 256, 768, 128, 23)   # 768 columns split over 2 or 3 ranks
+    lin = tp.TPLinear(torch.from_numpy(layer.qweight), torch.from_numpy(layer.qzeros),
+                      torch.from_numpy(layer.scales), None, 128, compute=_oracle_compute)
+    if rank == skipper:
+        time.sleep(9)
+        outcome = "skipped"
+    else:
+        t0 = time.monotonic()
+        try:
+            lin(torch.from_numpy(x))
+            outcome = "returned"
+        except RuntimeError:
+            outcome = f"raised {time.monotonic() - t0:.2f}"
+    with open(os.path.join(out_dir, f"rank{rank}.txt"), "w") as f:
+        f.write(outcome)
+    os._exit(0)   # the group is broken by design; leave without a collective teardown
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_rank_that_skips_the_gather_fails_the_others_on_timeout(tmp_path, world):
+    """Failure detection on the host: a rank that never joins the column
+    all-gather makes every other rank's call raise within the process-group
+    timeout -- no rank returns a partial row."""
+    mp.spawn(_skip_rank_main, args=(world, _free_port(), world - 1, str(tmp_path)), nprocs=world, join=True)
+    for r in range(world):
+        outcome = (tmp_path / f"rank{r}.txt").read_text()
+        if r == world - 1:
+            assert outcome == "skipped"
+        else:
+            assert outcome.startswith("raised"), outcome
+            assert float(outcome.split()[1]) < 8.0

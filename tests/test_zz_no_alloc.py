@@ -82,3 +82,31 @@ def test_noalloc_rejects_bad_arguments_before_launch(dev):
     assert lib.anvilq_gqa_decode_noalloc(None, _ptr(k), _ptr(v), _ptr(seqlens), _ptr(out), 1, 8, 2, 64, 64,
                                          0.0, _ptr(err), s) == -1
     assert b"fixed no-allocation" in lib.anvilq_strerror(-6)
+
+
+def test_noalloc_scratch_holds_every_plan_on_this_device(dev):
+    """ANVILQ_ENOSCRATCH guards the fixed 4 MiB array.  The split plan's scratch
+    is bounded by the resident CTA slots (pairs x splits <= 2 x SMs), so on a
+    148-SM B200 no valid shape reaches the limit: every extreme of the
+    supported range (largest batch x kv heads, largest group, both head dims,
+    long and short contexts) needs at most a few hundred KiB, and the
+    no-allocation entry point accepts it."""
+    lib = _lib.load()
+    limit = 4 << 20
+    worst = 0
+    for D in (64, 128):
+        for B, Hkv, group in ((1, 1, 8), (1, 8, 8), (2, 4, 8), (16, 8, 4), (2048, 8, 1), (4096, 4, 8)):
+            for Tmax in (16, 1024, 32768, 1 << 20):
+                need = lib.anvilq_gqa_decode_workspace_size(B, Hkv * group, Hkv, D, Tmax)
+                assert 0 < need <= limit, (B, Hkv, group, D, Tmax, need)
+                worst = max(worst, need)
+    assert worst <= limit // 4
+    # the largest-scratch case runs through the no-allocation entry point
+    q, k, v, seqlens = _case(dev, 1, 64, 8, 128, 32768, 7)
+    out = torch.full_like(q, float("nan"))
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    s = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    assert lib.anvilq_gqa_decode_noalloc(_ptr(q), _ptr(k), _ptr(v), _ptr(seqlens), _ptr(out), 1, 64, 8, 128,
+                                         32768, 0.0, _ptr(err), s) == 0
+    torch.cuda.synchronize(dev)
+    assert int(err.item()) == 0 and not torch.isnan(out).any()
