@@ -240,10 +240,20 @@ class Decoder:
         return graph
 
     def gemv_bytes_per_step(self) -> int:
+        """Algorithmic HBM bytes of the step's 4 L GEMV launches, with each fused
+        mode's own activation traffic: the weights of the projection (int4,
+        zeros, scales, bias) plus what the prologue reads and the epilogue
+        writes -- QKV: fp32 residual and fp16 gamma in, q and the new K / V rows
+        out (fp16); O: fp16 attention output in, fp32 residual read and written;
+        gate/up: fp32 residual and gamma in, fp16 [gate | up] out; down: fp16
+        gate and up in, fp32 residual read and written."""
         L, H, I, QH, KVH, D, G, V, _ = self.shape
-        b = 0
-        for K, N, bias in ((H, (QH + 2 * KVH) * D, True), (QH * D, H, False), (H, 2 * I, False), (I, H, False)):
-            b += synthetic.gemv_bytes(1, K, N, G, bias)
+        w = lambda K, N, bias: synthetic.gemv_bytes(1, K, N, G, bias) - 2 * K - 2 * N   # weights only
+        nqkv = (QH + 2 * KVH) * D
+        b = w(H, nqkv, True) + 4 * H + 2 * H + 2 * nqkv
+        b += w(QH * D, H, False) + 2 * QH * D + 8 * H
+        b += w(H, 2 * I, False) + 4 * H + 2 * H + 2 * 2 * I
+        b += w(I, H, False) + 2 * 2 * I + 8 * H
         return b * L
 
     def fill_context(self, length: int, seed: int = 0):
@@ -358,10 +368,7 @@ class Decoder:
     def bytes_per_step(self, context: int) -> int:
         """Algorithmic HBM bytes of one step at a given context length."""
         L, H, I, QH, KVH, D, G, V, _ = self.shape
-        b = 0
-        for K, N, bias in ((H, (QH + 2 * KVH) * D, True), (QH * D, H, False), (H, 2 * I, False), (I, H, False)):
-            b += synthetic.gemv_bytes(1, K, N, G, bias)
-        b *= L
+        b = self.gemv_bytes_per_step()
         b += L * (context * KVH * D * 2 * 2)    # K and V read once per layer
         b += V * H * 2                            # tied lm_head
         return b

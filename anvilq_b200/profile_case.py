@@ -1,6 +1,8 @@
 """Small, self-contained launch sequences of one kernel, for profiling with ncu.
 
     python -m anvilq_b200.profile_case gemv --K 4096 --N 11008 --M 1 --sets 8 --reps 2
+    python -m anvilq_b200.profile_case gemv --K 4096 --N 11008 --plan '{"kernel": 1, "band_cols": 256,
+        "cluster": 1, "kc": 1, "warps": 8, "stages": 3, "ctas": 296}'
     python -m anvilq_b200.profile_case attn --B 8 --T 32768 --reps 4
 
 Allocates `sets` independent weight sets of one shape (chosen so that together
@@ -17,26 +19,35 @@ from __future__ import annotations
 import argparse
 import json
 
-import numpy as np
 import torch
 
 from . import ops, synthetic
 
 
-def gemv_case(args):
-    dev = torch.device("cuda", 0)
+def gemv_sets(args, dev):
+    """`sets` independent (x, qweight, qzeros, scales, y) of one shape, drawn on the device."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(args.seed)
     sets = []
-    rng = np.random.default_rng(args.seed)
     for _ in range(args.sets):
-        lay = synthetic.awq_layer(args.K, args.N, args.G, rng=rng)
-        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
-        sets.append((t(synthetic.activations(args.M, args.K, rng=rng)), t(lay.qweight), t(lay.qzeros),
-                     t(lay.scales), torch.empty((args.M, args.N), dtype=torch.float16, device=dev)))
+        qw, qz, sc, _ = synthetic.device_awq_layer(args.K, args.N, args.G, gen, dev)
+        x = torch.randn((args.M, args.K), generator=gen, device=dev).half()
+        sets.append((x, qw, qz, sc, torch.empty((args.M, args.N), dtype=torch.float16, device=dev)))
+    return sets
+
+
+def gemv_case(args, sets=None):
+    dev = torch.device("cuda", 0)
+    sets = sets if sets is not None else gemv_sets(args, dev)
+    plan = json.loads(args.plan) if args.plan else None
     stream = torch.cuda.Stream(dev)
 
     def enqueue():
         for x, qw, qz, sc, y in sets:
-            ops.gemm(x, qw, qz, sc, None, args.G, out=y, overlap_prior=args.overlap)
+            if plan is not None:
+                ops.gemv_planned(x, qw, qz, sc, None, args.G, plan=plan, out=y, overlap_prior=args.overlap)
+            else:
+                ops.gemm(x, qw, qz, sc, None, args.G, out=y, overlap_prior=args.overlap)
 
     with torch.cuda.stream(stream):
         enqueue()                        # warm: workspaces, module load
@@ -59,9 +70,11 @@ def gemv_case(args):
     n = args.reps * args.sets
     us = start.elapsed_time(end) * 1e3 / n
     b = synthetic.gemv_bytes(args.M, args.K, args.N, args.G)
+    used = plan if plan is not None else (ops.gemv_plan(args.K, args.N, args.G) if args.M == 1 else None)
     print(json.dumps({"case": "gemv", "M": args.M, "K": args.K, "N": args.N, "launches": n,
-                      "graph": bool(args.graph), "overlap_prior": bool(args.overlap),
-                      "us_per_launch": round(us, 3), "bytes_per_launch": b, "GBps": round(b / us / 1e3, 1)}))
+                      "graph": bool(args.graph), "overlap_prior": bool(args.overlap), "plan": used,
+                      "us_per_launch": round(us, 3), "bytes_per_launch": b, "GBps": round(b / us / 1e3, 1)}),
+          flush=True)
 
 
 def attn_case(args):
@@ -107,6 +120,8 @@ def main(argv=None):
                     help="launch eagerly from Python instead of replaying a CUDA graph")
     ap.add_argument("--no-overlap", dest="overlap", action="store_false",
                     help="launch without programmatic dependent launch")
+    ap.add_argument("--plan", default=None,
+                    help="M = 1: a GEMV plan as JSON (the fields of anvilq_gemv_plan) instead of the default")
     args = ap.parse_args(argv)
     attn_case(args) if args.case == "attn" else gemv_case(args)
 

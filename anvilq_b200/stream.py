@@ -24,21 +24,34 @@ LLAMA7B_PROJECTIONS = ((4096, 4096, False),) * 4 + ((4096, 11008, False),) * 2 +
 
 class ProjectionStream:
     def __init__(self, projections, layers: int, M: int = 1, group: int = 128, seed: int = 17,
-                 device="cuda", host_io: bool = False):
+                 device="cuda", host_io: bool = False, device_init: bool = False):
+        """device_init: draw the weights and activations on the device (a seeded
+        torch generator, same value distributions) instead of on the host --
+        gigabytes of 7B-class layers in well under a second."""
         self.device = torch.device(device)
         self.M, self.group, self.host_io = M, group, host_io
         self.layers = []
         rng = np.random.default_rng(seed)
+        gen = None
+        if device_init:
+            gen = torch.Generator(device=self.device)
+            gen.manual_seed(seed)
         for _ in range(layers):
             for K, N, bias in projections:
-                lay = synthetic.awq_layer(K, N, group, rng=rng, bias=bias)
-                t = lambda a: None if a is None else torch.from_numpy(np.ascontiguousarray(a)).to(self.device)
-                x = synthetic.activations(M, K, rng=rng)
-                entry = dict(K=K, N=N, qweight=t(lay.qweight), qzeros=t(lay.qzeros), scales=t(lay.scales),
-                             bias=t(lay.bias), x=t(x), y=torch.empty((M, N), dtype=torch.float16,
-                                                                     device=self.device))
+                if gen is not None:
+                    qw, qz, sc, b = synthetic.device_awq_layer(K, N, group, gen, self.device, bias=bias)
+                    x = torch.randn((M, K), generator=gen, device=self.device).half()
+                    entry = dict(K=K, N=N, qweight=qw, qzeros=qz, scales=sc, bias=b, x=x)
+                    x_np = x.cpu().numpy() if host_io else None
+                else:
+                    lay = synthetic.awq_layer(K, N, group, rng=rng, bias=bias)
+                    t = lambda a: None if a is None else torch.from_numpy(np.ascontiguousarray(a)).to(self.device)
+                    x_np = synthetic.activations(M, K, rng=rng)
+                    entry = dict(K=K, N=N, qweight=t(lay.qweight), qzeros=t(lay.qzeros), scales=t(lay.scales),
+                                 bias=t(lay.bias), x=t(x_np))
+                entry["y"] = torch.empty((M, N), dtype=torch.float16, device=self.device)
                 if host_io:
-                    entry["x_host"] = torch.from_numpy(x).pin_memory()
+                    entry["x_host"] = torch.from_numpy(x_np).pin_memory()
                     entry["y_host"] = torch.empty((M, N), dtype=torch.float16).pin_memory()
                 self.layers.append(entry)
         self.graph = None

@@ -66,6 +66,21 @@ def awq_layer(K: int, N: int, G: int = 128, seed: int = 17, bias: bool = False,
     return AwqLayer(qweight, qzeros, scales, b, G)
 
 
+def device_awq_layer(K: int, N: int, G: int, generator, device, bias: bool = False):
+    """(qweight, qzeros, scales, bias or None) drawn on the device from a seeded
+    torch generator with the distributions of ``awq_layer`` (u4 uniform weights
+    and zeros, scales |N(0,1)| * 0.01 + 1e-3, bias N(0,1)); for benchmark-sized
+    layers that would take seconds to draw on the host."""
+    import torch
+    if K % G or N % 8:
+        raise ValueError("K must be a multiple of G and N a multiple of 8")
+    qw = torch.randint(-2**31, 2**31 - 1, (K, N // 8), dtype=torch.int32, device=device, generator=generator)
+    qz = torch.randint(-2**31, 2**31 - 1, (K // G, N // 8), dtype=torch.int32, device=device, generator=generator)
+    sc = (torch.randn((K // G, N), device=device, generator=generator).abs() * 0.01 + 1e-3).half()
+    b = torch.randn(N, device=device, generator=generator).half() if bias else None
+    return qw, qz, sc, b
+
+
 def activations(M: int, K: int, seed: int = 17, rng: np.random.Generator | None = None) -> np.ndarray:
     rng = rng if rng is not None else np.random.default_rng(seed)
     return rng.standard_normal((M, K), dtype=np.float32).astype(np.float16)
