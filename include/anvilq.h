@@ -354,7 +354,15 @@ int anvilq_peer_close(void* base);
  * peer_y[rank].  Every rank must make the same sequence of calls, and a
  * peer_y buffer must not be written again until every rank has passed a
  * later fused call (alternate two or more buffers).  The workspace is as for
- * anvilq_w4a16_gemm (its counter region holds the completion ticket).
+ * anvilq_w4a16_gemm (its counter region holds the completion tickets).
+ * The slice is computed with the kernel and plan anvilq_w4a16_gemm uses for
+ * these K, N (anvilq_w4a16_gemv_plan), so the gathered row is bit-identical
+ * to a GEMV on every rank followed by an all-gather; the stream-K kernel
+ * stores each finished 256-column band with 16-byte stores.
+ * After ANVILQ_DEV_ERR_TIMEOUT (a rank that never made the call) *epoch has
+ * still advanced and peer_y[rank] may lack other ranks' slices: the ranks'
+ * flags and epochs no longer agree, so every rank must zero its flag array
+ * and epoch (and rewrite the outputs) before the next fused call.
  * flags: ANVILQ_GEMM_OVERLAP_PRIOR. */
 int anvilq_w4a16_gemv_allgather(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
                                 const uint16_t* scales, const uint16_t* bias, int K, int N, int G, int rank,
