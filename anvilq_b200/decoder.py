@@ -9,8 +9,13 @@ and QwenFP64.step (anvil-q1-fp/tests/fp64_reference.py:210-246):
                 h = rmsnorm(x); g, u = h W_gate, h W_up; x += (silu(g) u) W_down
     logits = rmsnorm(x) E^T;  token = argmax (lowest index on ties)
 
-Kernels per token: 1 embedding + per layer 5 (QKV GEMV with RMSNorm prologue,
-bias and a RoPE + KV-append epilogue, attention, O GEMV with residual
+Kernels per token, fused step (the default where the shape allows): one
+persistent kernel runs every layer (anvilq_decode_layers: the five phases of a
+layer as roles of one CTA per SM, synchronised by producer counters, each CTA's
+next-layer weights streamed into shared memory ahead of use), then the
+lm_head/argmax and the token commit -- 3 launches.  Per-kernel step (larger
+models, or fused=False): 1 embedding + per layer 5 (QKV GEMV with RMSNorm
+prologue, bias and a RoPE + KV-append epilogue, attention, O GEMV with residual
 epilogue, gate/up GEMV with RMSNorm prologue, down GEMV with SiLU-product
 prologue and residual epilogue) + the lm_head/argmax + the token commit.  q/k/v and gate/up are each one GEMV
 over weights concatenated along N at load time (AWQ packs 8 columns per word,
@@ -82,7 +87,10 @@ class Decoder:
     """Device-resident greedy decoder; ``step`` enqueues one token, ``capture``
     records it as a CUDA graph that every later step replays."""
 
-    def __init__(self, weights: DecoderWeights, device="cuda", max_seq: int = 2048, keep_logits: bool = False):
+    def __init__(self, weights: DecoderWeights, device="cuda", max_seq: int = 2048, keep_logits: bool = False,
+                 fused: bool | None = None):
+        """fused: run the layers as one persistent kernel (None: when the shape
+        allows it; True: require it; False: one kernel per operation)."""
         self.shape = weights.shape
         L, H, I, QH, KVH, D, G, V, SEQ = self.shape
         self.max_seq = min(max_seq, SEQ)
@@ -120,6 +128,19 @@ class Decoder:
                        for K, N in ((H, (QH + 2 * KVH) * D), (QH * D, H), (H, 2 * I), (I, H)))
         ws_bytes = max(ws_bytes, lib.anvilq_gqa_decode_workspace_size(1, QH, KVH, D, self.max_seq))
         self.workspace = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+        fused_ws = lib.anvilq_decode_layers_workspace_size(L, H, I, QH, KVH, D, G, self.max_seq)
+        if fused and fused_ws == 0:
+            raise ValueError("the fused decode step does not support this model shape")
+        self.fused = fused is not False and fused_ws > 0
+        if self.fused:
+            self.fused_ws = torch.zeros(fused_ws, dtype=torch.uint8, device=dev)
+            p = lambda t: 0 if t is None else t.data_ptr()
+            rows = []
+            for l, w in enumerate(self.layers):   # anvilq_decode_layer, field by field
+                rows.append([p(a) for a in w["qkv"]] + [p(a) for a in w["o"][:3]] + [p(a) for a in w["gu"][:3]]
+                            + [p(a) for a in w["down"][:3]] + [p(self.gamma_in[l]), p(self.gamma_post[l]),
+                                                               p(self.k_cache[l]), p(self.v_cache[l])])
+            self.layer_table = torch.tensor(rows, dtype=torch.int64, device=dev)
         self.stream = torch.cuda.Stream(dev)
         self.graph = None
         # host staging for the end-to-end path
@@ -148,12 +169,32 @@ class Decoder:
             QH, KVH, D, self.max_seq, ROPE_THETA, self.workspace.data_ptr(), self.workspace.numel(),
             self.dev_err.data_ptr(), FLAG_OVERLAP, self.stream.cuda_stream), "anvilq_w4a16_gemv_qkv_rope")
 
+    def _layers_fused(self):
+        """Every layer of the step as one persistent kernel (anvilq_decode_layers)."""
+        L, H, I, QH, KVH, D, G, V, _ = self.shape
+        _lib.check(_lib.load().anvilq_decode_layers(
+            self.layer_table.data_ptr(), L, H, I, QH, KVH, D, G, self.max_seq, RMS_EPS, ROPE_THETA,
+            self.embedding.data_ptr(), V, self.token.data_ptr(), self.pos.data_ptr(), self.seqlen.data_ptr(),
+            self.x.data_ptr(), self.key.data_ptr(), self.fused_ws.data_ptr(), self.fused_ws.numel(),
+            self.dev_err.data_ptr(), self.stream.cuda_stream), "anvilq_decode_layers")
+
     def _enqueue(self, host_io: bool):
         L, H, I, QH, KVH, D, G, V, _ = self.shape
         lib = _lib.load()
         s = self.stream.cuda_stream
         if host_io:
             self.token.copy_(self.token_in, non_blocking=True)
+        if self.fused:
+            self._layers_fused()
+            _lib.check(lib.anvilq_lmhead_argmax(
+                self.x.data_ptr(), self.gamma_final.data_ptr(), RMS_EPS, self.embedding.data_ptr(),
+                None if self.logits is None else self.logits.data_ptr(), self.key.data_ptr(), H, V, FLAG_OVERLAP,
+                s), "anvilq_lmhead_argmax")
+            _lib.check(lib.anvilq_argmax_commit(self.key.data_ptr(), self.token.data_ptr(), self.pos.data_ptr(),
+                                                FLAG_OVERLAP, s), "anvilq_argmax_commit")
+            if host_io:
+                self.token_out.copy_(self.token, non_blocking=True)
+            return
         _lib.check(lib.anvilq_embed(self.embedding.data_ptr(), self.token.data_ptr(), self.x.data_ptr(), H, V,
                                     self.key.data_ptr(), self.dev_err.data_ptr(), FLAG_OVERLAP, s), "anvilq_embed")
         for l, w in enumerate(self.layers):
@@ -175,7 +216,26 @@ class Decoder:
             self.token_out.copy_(self.token, non_blocking=True)
 
     def kernels_per_step(self) -> int:
-        return 1 + 5 * self.shape[0] + 2
+        return 3 if self.fused else 1 + 5 * self.shape[0] + 2
+
+    def record_layers(self):
+        """A CUDA graph of the fused layers kernel alone (the step without the
+        lm_head), for timing it on its own; position and token stay as they are."""
+        if not self.fused:
+            raise ValueError("the decoder runs one kernel per operation")
+        with torch.cuda.stream(self.stream):
+            self._layers_fused()
+        self.stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=self.stream):
+            self._layers_fused()
+        return graph
+
+    def layer_bytes_per_step(self, context: int) -> int:
+        """Algorithmic HBM bytes of the layers of one step (no lm_head): the
+        projections with their activation traffic and K / V read once."""
+        L, H, I, QH, KVH, D, G, V, _ = self.shape
+        return self.gemv_bytes_per_step() + L * (context * KVH * D * 2 * 2)
 
     def reset(self, token: int):
         """Start a new sequence at position 0 with `token` as the first input."""

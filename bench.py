@@ -336,13 +336,14 @@ def decode_arm(args, world, rank, local):
     peak, peak_kind = load_peaks()
     w = decoder.synthetic_weights(decoder.QWEN05B_SHAPE, seed=17 + rank)
     total_steps = 2 * (args.warmup + args.steps) + 4
-    d = decoder.Decoder(w, dev, max_seq=ctx + total_steps + 8)
+    d = decoder.Decoder(w, dev, max_seq=ctx + total_steps + 8, fused=False if args.unfused else None)
     d.fill_context(ctx, seed=rank)
     d.token.fill_(1000)
     d.token_in.fill_(1000)
     g_dev = d.record(False)
     g_e2e = d.record(True)
-    g_gemv = d.record_gemvs()
+    # the dominant kernel timed on its own: the fused layers kernel, or the step's GEMVs
+    g_roof = d.record_layers() if d.fused else d.record_gemvs()
 
     def replay(graph):
         def run():
@@ -354,17 +355,24 @@ def decode_arm(args, world, rank, local):
         ms = timed(replay(g_dev), d.stream, args.steps, args.warmup, world, dev)
     d.pos.fill_(ctx)
     ms_e2e = timed(replay(g_e2e), d.stream, args.steps, args.warmup, world, dev, sync_each=True)
-    ms_gemv = timed(replay(g_gemv), d.stream, args.steps, args.warmup, world, dev)
+    pos_roof = int(d.pos.item())
+    ms_roof = timed(replay(g_roof), d.stream, args.steps, args.warmup, world, dev)
     d.check_errors()
 
     tok_s = world * args.steps / (ms / 1e3)
     step_bytes = d.bytes_per_step(ctx + args.warmup + args.steps // 2)
-    gemv_bytes = d.gemv_bytes_per_step()
-    gemv_launches = 4 * decoder.QWEN05B_SHAPE[0]
-    per_launch_s = ms_gemv / 1e3 / args.steps / gemv_launches
-    achieved = gemv_bytes / gemv_launches / per_launch_s / 1e9
-    entry = traffic_entry("gemv_tma_kernel/decode05b")
-    traffic = int(gemv_bytes / gemv_launches * entry["ratio_read_over_algorithmic"]) if entry else None
+    if d.fused:
+        roof_kernel, roof_launches = "decode_step_kernel", 1
+        roof_bytes = d.layer_bytes_per_step(pos_roof + 1)
+        roof_on = "the fused layers kernel (all 24 layers of a token, no lm_head) as its own CUDA graph, same run"
+    else:
+        roof_kernel, roof_launches = "gemv_tma_kernel", 4 * decoder.QWEN05B_SHAPE[0]
+        roof_bytes = d.gemv_bytes_per_step()
+        roof_on = "the step's 96 W4A16 GEMVs as their own CUDA graph, same run"
+    per_launch_s = ms_roof / 1e3 / args.steps / roof_launches
+    achieved = roof_bytes / roof_launches / per_launch_s / 1e9
+    entry = traffic_entry(f"{roof_kernel}/decode05b")
+    traffic = int(roof_bytes / roof_launches * entry["ratio_read_over_algorithmic"]) if entry else None
     line = {
         "metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
@@ -374,22 +382,21 @@ def decode_arm(args, world, rank, local):
         "config": {"workload": wl["name"], "batch": 1, "context": ctx, "layers": decoder.QWEN05B_SHAPE[0],
                    "step_bytes": step_bytes, "kernels_per_step": d.kernels_per_step(),
                    "l2": "inputs larger than L2 (no flush)", "parallelism": f"replicas x{world}",
-                   "graph": "one CUDA graph per token"},
+                   "graph": "one CUDA graph per token", "fused_layers_kernel": bool(d.fused)},
         "hbm_gbs": round(step_bytes * tok_s / world / 1e9, 2),
         "hbm_frac_of_measured_peak": round(step_bytes * tok_s / world / 1e9 / peak, 4),
-        "roofline": {"bound": "hbm", "kernel": "gemv_tma_kernel", "achieved": round(achieved, 2), "peak": peak,
+        "roofline": {"bound": "hbm", "kernel": roof_kernel, "achieved": round(achieved, 2), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "frac_of_8tbs_nominal": round(achieved / 8000.0, 4), "traffic": traffic,
-                     "algorithmic_bytes_per_launch": int(gemv_bytes / gemv_launches),
-                     "launch_avg_us": round(per_launch_s * 1e6, 4),
-                     "measured_on": "the step's 96 W4A16 GEMVs as their own CUDA graph, same run"},
+                     "algorithmic_bytes_per_launch": int(roof_bytes / roof_launches),
+                     "launch_avg_us": round(per_launch_s * 1e6, 4), "measured_on": roof_on},
         "e2e": {"value": round(world * args.steps / (ms_e2e / 1e3), 2), "unit": "tok/s",
                 "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
                 "ms_per_step": round(ms_e2e / args.steps, 5)},
         "gpu_launches": d.kernels_per_step() * args.steps,
         "clocks": clocks.summary(),
     }
-    del g_dev, g_e2e, g_gemv, d
+    del g_dev, g_e2e, g_roof, d
     torch.cuda.empty_cache()
     if not args.no_extras:
         line["proj7b"] = summary(proj_measure(args, world, rank, dev, "proj7b", e2e=False))
@@ -812,6 +819,8 @@ def main(argv=None):
     ap.add_argument("--no-extras", action="store_true",
                     help="decode05b: skip the proj7b / tp70b / attn measurements on the same line")
     ap.add_argument("--tokens", type=int, default=1, help="token rows per projection (tp70b)")
+    ap.add_argument("--unfused", action="store_true",
+                    help="decode05b: one kernel per operation instead of the fused layers kernel")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

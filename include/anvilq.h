@@ -370,6 +370,59 @@ int anvilq_w4a16_gemv_allgather(const uint16_t* x, const int32_t* qweight, const
                                 unsigned int* const* peer_flags, unsigned int* epoch, void* workspace,
                                 size_t workspace_bytes, int* dev_err, unsigned flags, anvilq_stream_t stream);
 
+/* ---- every decoder layer of one decode token in one persistent kernel ---------
+ *
+ * Replaces the per-layer body of FP32Model.token (anvil-q1/tests/official_weights.py:462-503)
+ * / QwenFP64.step (anvil-q1-fp/tests/fp64_reference.py:210-246) for all L layers
+ * of a Qwen2-architecture W4A16 AWQ model at batch 1: x = E[*token] (the
+ * embedding row), then per layer h = rmsnorm(x) gamma_in; q,k,v = h W_qkv + b
+ * with split-half RoPE at *pos (theta); k, v written to row *pos of the
+ * layer's caches [Tmax][KVH][D]; causal attention over rows [0, *pos];
+ * x += attn W_o; h = rmsnorm(x) gamma_post; x += (silu(h W_gate) (h W_up)) W_down.
+ * The final residual goes to x_out (fp32 [H]) for anvilq_lmhead_argmax;
+ * *seqlen = *pos + 1; *argmax_key = 0 when given.  Numerics as the per-kernel
+ * path (anvilq_w4a16_gemv_qkv_rope, anvilq_gqa_decode, anvilq_w4a16_gemv_fused):
+ * binary16 activations, fp32 residual and accumulation; attention scores,
+ * softmax and P.V in fp32.
+ *
+ * `layers` is a DEVICE array of L descriptors.  Per layer: qkv = the q, k, v
+ * projections concatenated along N ([H][(QH+2KVH) D / 8] AWQ, bias fp16
+ * [(QH+2KVH) D] or NULL); o [QH D][H / 8]; gu = gate and up concatenated
+ * along N ([H][2 I / 8]); down [I][H / 8]; gammas fp16 [H]; caches fp16.
+ * Requirements: G == 128, H % 128 == 0, I % 128 == 0, QH % KVH == 0,
+ * QH / KVH <= 8, D in {64, 128}, (QH D) % 128 == 0, 16-byte aligned tensors,
+ * and one SM's shared memory must hold a CTA's slices of a layer (ANVILQ_ESHAPE
+ * otherwise: larger models use the per-kernel path).  The grid is one CTA per
+ * SM, launched cooperatively: CTAs wait on one another's counters (bounded,
+ * ~1 s, then ANVILQ_DEV_ERR_TIMEOUT and the launch gives up).  An invalid
+ * *token or *pos sets ANVILQ_DEV_ERR_TOKEN / _SEQLEN and does nothing.
+ * workspace: anvilq_decode_layers_workspace_size bytes, 256-byte aligned,
+ * zero-filled once (every launch leaves its counters zero). */
+typedef struct anvilq_decode_layer {
+  const int32_t* qkv_qweight;
+  const int32_t* qkv_qzeros;
+  const uint16_t* qkv_scales;
+  const uint16_t* qkv_bias;
+  const int32_t* o_qweight;
+  const int32_t* o_qzeros;
+  const uint16_t* o_scales;
+  const int32_t* gu_qweight;
+  const int32_t* gu_qzeros;
+  const uint16_t* gu_scales;
+  const int32_t* down_qweight;
+  const int32_t* down_qzeros;
+  const uint16_t* down_scales;
+  const uint16_t* gamma_in;
+  const uint16_t* gamma_post;
+  uint16_t* k_cache;
+  uint16_t* v_cache;
+} anvilq_decode_layer;
+size_t anvilq_decode_layers_workspace_size(int L, int H, int I, int QH, int KVH, int D, int G, int Tmax);
+int anvilq_decode_layers(const anvilq_decode_layer* layers, int L, int H, int I, int QH, int KVH, int D, int G,
+                         int Tmax, float eps, float theta, const uint16_t* embedding, int V, const int32_t* token,
+                         const int32_t* pos, int32_t* seqlen, float* x_out, unsigned long long* argmax_key,
+                         void* workspace, size_t workspace_bytes, int* dev_err, anvilq_stream_t stream);
+
 /* Tied fp16 lm_head with the final RMSNorm and greedy argmax fused:
  * h = x * gamma / sqrt(mean(x^2) + eps) in fp32 (official_weights.py:504),
  * logits[v] = h . E[v] (:505-506; written when logits != NULL), and

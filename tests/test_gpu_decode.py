@@ -221,12 +221,15 @@ def test_lmhead_argmax(dev):
     assert ref[int(tok.item())] >= ref.max() - 1e-3 * max(1.0, abs(ref.max()))
 
 
-def test_decode_matches_reference_token(dev, golden_dir):
-    """Greedy decode against FP32Model.token itself (tests/golden/decode_small.npz)."""
+@pytest.mark.parametrize("fused", [True, False])
+def test_decode_matches_reference_token(dev, golden_dir, fused):
+    """Greedy decode against FP32Model.token itself (tests/golden/decode_small.npz),
+    through the fused layers kernel and through one kernel per operation."""
     g = np.load(golden_dir / "decode_small.npz")
     shape = tuple(int(v) for v in g["shape"])
     w = decoder.synthetic_weights(shape, seed=29)
-    d = decoder.Decoder(w, dev, max_seq=shape[-1], keep_logits=True)
+    d = decoder.Decoder(w, dev, max_seq=shape[-1], keep_logits=True, fused=fused)
+    assert d.fused == fused
     tokens = [int(t) for t in g["tokens"]]
     d.reset(tokens[0])
     for pos in range(len(g["logits"])):
@@ -237,11 +240,12 @@ def test_decode_matches_reference_token(dev, golden_dir):
         assert int(d.token.item()) == tokens[pos + 1]
 
 
-def test_decode_graph_replay_matches_eager(dev):
+@pytest.mark.parametrize("fused", [True, False])
+def test_decode_graph_replay_matches_eager(dev, fused):
     shape = (2, 128, 256, 2, 1, 64, 128, 64, 16)
     w = decoder.synthetic_weights(shape, seed=31)
-    eager = decoder.Decoder(w, dev, max_seq=16).generate(7, 8)
-    d = decoder.Decoder(w, dev, max_seq=16)
+    eager = decoder.Decoder(w, dev, max_seq=16, fused=fused).generate(7, 8)
+    d = decoder.Decoder(w, dev, max_seq=16, fused=fused)
     d.reset(7)
     d.capture()
     d.reset(7)
@@ -254,14 +258,16 @@ def test_decode_graph_replay_matches_eager(dev):
     assert out == eager
 
 
-def test_decode_qwen05b_shape(dev):
+@pytest.mark.parametrize("fused", [True, False])
+def test_decode_qwen05b_shape(dev, fused):
     """Full Qwen2.5-0.5B shape (24 layers, vocab 151936) against the binary64 oracle
     with binary16 rounding where the W4A16 datapath stores activations.  (Against
     the unrounded oracle the 24 random layers amplify the binary16 activation
     rounding to ~5e-2 normalized error; the small-shape test above checks the
     unrounded reference itself.)"""
     w = decoder.synthetic_weights(decoder.QWEN05B_SHAPE, seed=17)
-    d = decoder.Decoder(w, dev, max_seq=64, keep_logits=True)
+    d = decoder.Decoder(w, dev, max_seq=64, keep_logits=True, fused=fused)
+    assert d.fused == fused
     o = oracle.DecodeOracle(w, act16=True)
     token = 1000
     d.reset(token)
@@ -273,3 +279,72 @@ def test_decode_qwen05b_shape(dev):
         check(d.logits.cpu().numpy(), ref, TOL_DECODE, pos)
         token = int(d.token.item())
         assert ref[token] >= ref.max() - 1e-2 * max(1.0, abs(ref.max()))
+
+
+@pytest.fixture(scope="module")
+def qwen05b_weights():
+    return decoder.synthetic_weights(decoder.QWEN05B_SHAPE, seed=23)
+
+
+@pytest.mark.parametrize("context", [1000, 1087, 1600])
+def test_fused_layers_match_per_kernel_step(dev, qwen05b_weights, context):
+    """The fused layers kernel against the per-kernel step on the 0.5B shape over
+    a long synthetic context (many attention chunks, a partial last chunk):
+    the same greedy tokens and logits within the decode tolerance, step after
+    step, with the caches of both kept in step."""
+    a = decoder.Decoder(qwen05b_weights, dev, max_seq=2048, keep_logits=True, fused=True)
+    b = decoder.Decoder(qwen05b_weights, dev, max_seq=2048, keep_logits=True, fused=False)
+    for d in (a, b):
+        d.fill_context(context, seed=5)
+        d.set_position(321, context)
+    for step in range(3):
+        for d in (a, b):
+            d.step()
+            d.stream.synchronize()
+            d.check_errors()
+        check(a.logits.cpu().numpy(), b.logits.cpu().numpy(), TOL_DECODE, (context, step))
+        assert int(a.token.item()) == int(b.token.item())
+        assert int(a.pos.item()) == int(b.pos.item()) == context + step + 1
+
+
+def test_fused_layers_graph_replay_is_deterministic(dev, qwen05b_weights):
+    """Two decoders on the fused path, one replaying a CUDA graph: identical logits bit for bit."""
+    a = decoder.Decoder(qwen05b_weights, dev, max_seq=1100, keep_logits=True, fused=True)
+    b = decoder.Decoder(qwen05b_weights, dev, max_seq=1100, keep_logits=True, fused=True)
+    for d in (a, b):
+        d.fill_context(1024, seed=9)
+        d.set_position(77, 1024)
+    b.capture()
+    b.set_position(77, 1024)
+    for _ in range(3):
+        for d in (a, b):
+            d.step()
+            d.stream.synchronize()
+            d.check_errors()
+        assert torch.equal(a.logits, b.logits)
+
+
+def test_fused_layers_flag_invalid_scale(dev):
+    """An invalid AWQ scale in any layer fails the step (device error bit), as in the per-kernel path."""
+    shape = (2, 128, 256, 2, 1, 64, 128, 64, 16)
+    w = decoder.synthetic_weights(shape, seed=31)
+    bad = w.layers[1][6].scales.view(np.uint16).copy()
+    bad[1, 5] = 0xFC00
+    w.layers[1][6] = type(w.layers[1][6])(w.layers[1][6].qweight, w.layers[1][6].qzeros, bad.view(np.float16),
+                                          None, 128)
+    d = decoder.Decoder(w, dev, max_seq=16, fused=True)
+    d.reset(3)
+    d.step()
+    d.stream.synchronize()
+    with pytest.raises(Exception):
+        d.check_errors()
+
+
+def test_fused_layers_reject_bad_token(dev):
+    shape = (2, 128, 256, 2, 1, 64, 128, 64, 16)
+    d = decoder.Decoder(decoder.synthetic_weights(shape, seed=31), dev, max_seq=16, fused=True)
+    d.reset(shape[7])   # outside the vocabulary
+    d.step()
+    d.stream.synchronize()
+    with pytest.raises(Exception):
+        d.check_errors()
