@@ -663,8 +663,6 @@ static int sm_count() {
     int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     g_sms[dev] = n;
-    cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaGetLastError();
   });
   return g_sms[dev];
 }
@@ -783,6 +781,10 @@ extern "C" int anvilq_decode_layers(const anvilq_decode_layer* layers, int L, in
   p.offMisc = pl.offMisc; p.smem = pl.smem;
   for (int i = 0; i < D / 2; ++i) p.rope_inv[i] = std::pow((double)theta, -2.0 * i / D);
 
+  if (cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem) != cudaSuccess) {
+    cudaGetLastError();
+    return ANVILQ_ECUDA;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.P, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);

@@ -397,17 +397,37 @@ __global__ void __launch_bounds__(W * 32, W <= 8 ? 2 : 1)
       __syncthreads();
       if (!s_last) continue;
       __threadfence();
+      // the contributors' partials, loaded by all threads at once (not one
+      // dependent L2 round trip per contributor), staged through the ring
+      // (free again) in batches of kFixRows, then summed in CTA order
+      constexpr int kFixRows = L::kRingBytes / (kBandCols * 4) < 64 ? L::kRingBytes / (kBandCols * 4) : 64;
+      float* stage = reinterpret_cast<float*>(smem + L::kRingOff + L::kRedBytes);
+      constexpr int kStageRows = (L::kRingBytes - L::kRedBytes) / (kBandCols * 4) < kFixRows
+                                     ? (L::kRingBytes - L::kRedBytes) / (kBandCols * 4)
+                                     : kFixRows;
+      static_assert(kStageRows >= 4, "room to stage the fix-up");
+      float acc[kPer];
 #pragma unroll
-      for (int u = 0; u < kPer; ++u) {
-        const int t = threadIdx.x + u * W * 32;
-        if (t >= kBandCols) continue;
-        float acc = 0.0f;
-        for (int i = first; i <= last; ++i) {   // in CTA order
+      for (int u = 0; u < kPer; ++u) acc[u] = 0.0f;
+      for (int i0 = first; i0 <= last; i0 += kStageRows) {
+        const int rows = min(kStageRows, last - i0 + 1);
+        for (int e = threadIdx.x; e < rows * (kBandCols / 4); e += W * 32) {
+          const int r = e / (kBandCols / 4), c4 = e % (kBandCols / 4), i = i0 + r;
           const int slot = band - (int)((long long)i * T / P) / p.cpb;
-          acc += __ldcg(p.parts + ((size_t)i * 2 + slot) * kBandCols + t);
+          reinterpret_cast<float4*>(stage)[e] =
+              __ldcg(reinterpret_cast<const float4*>(p.parts + ((size_t)i * 2 + slot) * kBandCols) + c4);
         }
-        v[u] = acc;
+        __syncthreads();
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+          const int t = threadIdx.x + u * W * 32;
+          if (t < kBandCols)
+            for (int r = 0; r < rows; ++r) acc[u] += stage[r * kBandCols + t];   // in CTA order
+        }
+        __syncthreads();
       }
+#pragma unroll
+      for (int u = 0; u < kPer; ++u) v[u] = acc[u];
     }
     // the band's final values (uniform: every thread of the CTA is here)
 #pragma unroll
