@@ -92,6 +92,7 @@ struct Params {
   int n1, n2, n3, nsplit, maxch;
   // shared-memory carve-up (bytes)
   int offA, offB, offC, offX, offRed, offMisc, smem;
+  int regA_bytes;
   double rope_inv[kMaxD / 2];
 };
 
@@ -249,13 +250,19 @@ __device__ uint32_t tile_gemv(const uint32_t* wsm, const __half* xs, const uint3
 
 // x_norm[k] = fp16(x[k] * gamma[k] / sqrt(mean(x^2) + eps)) into shared memory.
 // x: the residual (fp32, L2-coherent loads) or, for layer 0, the embedding row.
+// One pass over x: every thread keeps its (at most kMaxPerThread) values.
+constexpr int kMaxPerThread = 8;   // H <= 4096
 __device__ void rmsnorm_to_smem(const Params& p, const float* x, const __half* xemb, const __half* gamma,
                                 __half* xs, float* misc) {
+  float v[kMaxPerThread];
   float ss = 0.0f;
-  for (int k = threadIdx.x; k < p.H; k += kThreads) {
-    const float v = x ? __ldcg(x + k) : __half2float(xemb[k]);
-    ss = fmaf(v, v, ss);
+#pragma unroll
+  for (int u = 0; u < kMaxPerThread; ++u) {
+    const int k = threadIdx.x + u * kThreads;
+    v[u] = k < p.H ? (x ? __ldcg(x + k) : __half2float(xemb[k])) : 0.0f;
   }
+#pragma unroll
+  for (int u = 0; u < kMaxPerThread; ++u) ss = fmaf(v[u], v[u], ss);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if ((threadIdx.x & 31) == 0) misc[threadIdx.x >> 5] = ss;
@@ -267,9 +274,10 @@ __device__ void rmsnorm_to_smem(const Params& p, const float* x, const __half* x
   }
   __syncthreads();
   const float inv = misc[kWarps];
-  for (int k = threadIdx.x; k < p.H; k += kThreads) {
-    const float v = x ? __ldcg(x + k) : __half2float(xemb[k]);
-    xs[k] = __float2half_rn(v * __half2float(gamma[k]) * inv);
+#pragma unroll
+  for (int u = 0; u < kMaxPerThread; ++u) {
+    const int k = threadIdx.x + u * kThreads;
+    if (k < p.H) xs[k] = __float2half_rn(v[u] * __half2float(gamma[k]) * inv);
   }
   __syncthreads();
 }
@@ -524,19 +532,37 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
         __syncthreads();
         if (s_last) {
           __threadfence();
-          for (int i = tid; i < grp * D; i += kThreads) {
-            const int j = i / D, d = i % D;
-            float M = -INFINITY;
-            for (int cc = 0; cc < nch; ++cc)
-              M = fmaxf(M, __ldcg(p.apart + ((size_t)(h * p.maxch + cc) * grp + j) * (D + 2)));
-            float Ls = 0.0f, O = 0.0f;
-            for (int cc = 0; cc < nch; ++cc) {
-              const float* pc = p.apart + ((size_t)(h * p.maxch + cc) * grp + j) * (D + 2);
-              const float w = exp2f(__ldcg(pc) - M);
-              Ls = fmaf(__ldcg(pc + 1), w, Ls);
-              O = fmaf(__ldcg(pc + 2 + d), w, O);
+          // every chunk's (m, l, o) of this head, loaded at once into shared
+          // memory (the K / V tiles are no longer needed), in batches that fit
+          float* st = reinterpret_cast<float*>(regA);
+          const int per_chunk = grp * (D + 2);
+          const int batch = max(1, (int)(p.regA_bytes / (per_chunk * 4)));
+          float M[2], Ls[2], O[2];
+          for (int k = 0; k < 2; ++k) M[k] = -INFINITY, Ls[k] = O[k] = 0.0f;
+          for (int c0 = 0; c0 < nch; c0 += batch) {
+            const int nb_ = min(batch, nch - c0);
+            const float* src = p.apart + (size_t)(h * p.maxch + c0) * per_chunk;
+            for (int i = tid; i < nb_ * per_chunk; i += kThreads) st[i] = __ldcg(src + i);
+            __syncthreads();
+            for (int k = 0; k < 2; ++k) {   // (head, dim) pairs tid and tid + 512 (grp * D <= 1024)
+              const int i = tid + k * kThreads;
+              if (i >= grp * D) continue;
+              const int j = i / D, d = i % D;
+              for (int cc = 0; cc < nb_; ++cc) {   // online merge in chunk order
+                const float* pc = st + cc * per_chunk + j * (D + 2);
+                const float m = pc[0];
+                const float mn = fmaxf(M[k], m);
+                const float a = exp2f(M[k] - mn), b = exp2f(m - mn);
+                Ls[k] = fmaf(Ls[k], a, pc[1] * b);
+                O[k] = fmaf(O[k], a, pc[2 + d] * b);
+                M[k] = mn;
+              }
             }
-            p.attn[(size_t)(h * grp + j) * D + d] = __float2half_rn(O / Ls);
+            __syncthreads();
+          }
+          for (int k = 0; k < 2; ++k) {
+            const int i = tid + k * kThreads;
+            if (i < grp * D) p.attn[(size_t)h * grp * D + i] = __float2half_rn(O[k] / Ls[k]);
           }
           publish(ctr + 1, 1);
         }
@@ -609,9 +635,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
       __syncthreads();
       if (s_lastd) {
         __threadfence();
+        float* st = misc + 32;   // [nsplit][32], every split loaded at once
+        for (int i = tid; i < p.nsplit * 32; i += kThreads) st[i] = __ldcg(p.dpart + (size_t)db * p.nsplit * 32 + i);
+        __syncthreads();
         if (tid < 32) {
           float acc = 0.0f;
-          for (int s2 = 0; s2 < p.nsplit; ++s2) acc += __ldcg(p.dpart + ((size_t)db * p.nsplit + s2) * 32 + tid);
+          for (int s2 = 0; s2 < p.nsplit; ++s2) acc += st[s2 * 32 + tid];   // in split order
           const int col = db * 32 + tid;
           x_next[col] = __ldcg(p.xa + col) + acc;
         }
@@ -673,7 +702,7 @@ static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 static int make_plan(int L, int H, int I, int QH, int KVH, int D, int G, int Tmax, Plan* pl) {
   if (L < 1 || H < 128 || I < 128 || QH < 1 || KVH < 1 || Tmax < 1) return ANVILQ_EINVAL;
   if (G != kG || H % kG || I % kG || QH % KVH || QH / KVH > kMaxGroup || (D != 64 && D != 128) ||
-      (QH * D) % kG)
+      (QH * D) % kG || H > kThreads * kMaxPerThread)
     return ANVILQ_ESHAPE;
   const int P = sm_count();
   if (P <= 0) return ANVILQ_ECUDA;
@@ -684,7 +713,7 @@ static int make_plan(int L, int H, int I, int QH, int KVH, int D, int G, int Tma
   pl->maxch = (Tmax + kChunk - 1) / kChunk;
   pl->n2 = std::min(KVH * pl->maxch, P - pl->n1 - pl->n3);
   if (pl->n2 < 1) return ANVILQ_ESHAPE;
-  pl->nsplit = std::min(P / nb, ngI);
+  pl->nsplit = std::min(std::min(P / nb, ngI), 48);   // the fix-up stages nsplit x 32 floats in `misc`
   if (pl->nsplit < 1 || (I / 32 + P - 1) / P > 2) return ANVILQ_ESHAPE;
   // shared memory
   const size_t qkvA = (size_t)H * (D / 8) * 4 + (H / kG) * (D / 8) * 4 + (H / kG) * D * 2;
@@ -779,6 +808,7 @@ extern "C" int anvilq_decode_layers(const anvilq_decode_layer* layers, int L, in
   p.n1 = pl.n1; p.n2 = pl.n2; p.n3 = pl.n3; p.nsplit = pl.nsplit; p.maxch = pl.maxch;
   p.offA = pl.offA; p.offB = pl.offB; p.offC = pl.offC; p.offX = pl.offX; p.offRed = pl.offRed;
   p.offMisc = pl.offMisc; p.smem = pl.smem;
+  p.regA_bytes = pl.offB - pl.offA;
   for (int i = 0; i < D / 2; ++i) p.rope_inv[i] = std::pow((double)theta, -2.0 * i / D);
 
   if (cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem) != cudaSuccess) {
