@@ -153,25 +153,26 @@ __device__ void publish(int* ctr, int n) {
   if (threadIdx.x == 0) atomicAdd(ctr, n);
 }
 
-// Copy rows [row0, row0 + rows) x words [w0, w0 + words) of a [*][W8] int32
-// matrix into shared memory [rows][words] (words % 4 == 0), plus the groups'
-// zeros [ng][words] and scales [ng][8 words] (as binary16 pairs).
-__device__ void prefetch_awq(uint32_t* wdst, uint32_t* zdst, uint32_t* sdst, const int32_t* qw, const int32_t* qz,
-                             const __half* sc, int W8, int N, int row0, int rows, int w0, int words) {
-  const int q4 = words / 4;
-  for (int i = threadIdx.x; i < rows * q4; i += kThreads) {
-    const int r = i / q4, c = i % q4;
-    cp16(wdst + r * words + 4 * c, qw + (size_t)(row0 + r) * W8 + w0 + 4 * c);
-  }
-  const int g0 = row0 / kG, ng = (rows + kG - 1) / kG;
-  for (int i = threadIdx.x; i < ng * q4; i += kThreads) {
-    const int g = i / q4, c = i % q4;
-    cp16(zdst + g * words + 4 * c, qz + (size_t)(g0 + g) * W8 + w0 + 4 * c);
-  }
-  const int s8 = words;   // 16-byte pieces of a group's 8 * words binary16 scales
-  for (int i = threadIdx.x; i < ng * s8; i += kThreads) {
-    const int g = i / s8, c = i % s8;
-    cp16(sdst + g * 4 * words + 4 * c, sc + (size_t)(g0 + g) * N + 8 * w0 + 8 * c);
+// Copy one column block of a projection (see anvilq_block_columns): `rows`
+// rows of `words` int4 words, then the zeros [ng][words] and the scales
+// [ng][8 words] (binary16) of its ng groups -- three contiguous ranges, so the
+// 16-byte copies of consecutive threads are consecutive in memory.
+__device__ void prefetch_block(uint32_t* wdst, uint32_t* zdst, uint32_t* sdst, const int32_t* wsrc,
+                               const int32_t* zsrc, const __half* ssrc, int rows, int words, int ng) {
+  const int nw = rows * words / 4, nz = ng * words / 4, ns = ng * words;
+  for (int i = threadIdx.x; i < nw; i += kThreads) cp16(wdst + 4 * i, wsrc + 4 * i);
+  for (int i = threadIdx.x; i < nz; i += kThreads) cp16(zdst + 4 * i, zsrc + 4 * i);
+  for (int i = threadIdx.x; i < ns; i += kThreads) cp16(sdst + 4 * i, ssrc + 8 * i);
+}
+
+// dst[b][r][e] = src[r][b * block + e]: the column blocks of a row-major matrix
+// laid out one after another (16-byte pieces; block * elem_bytes % 16 == 0).
+__global__ void block_columns_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, long long rows,
+                                     long long row_vecs, long long block_vecs) {
+  const long long n = rows * row_vecs;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / row_vecs, c = i % row_vecs, b = c / block_vecs, e = c % block_vecs;
+    dst[(b * rows + r) * block_vecs + e] = src[i];
   }
 }
 
@@ -298,7 +299,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
   const int nb = H / 32;                  // 32-column blocks of H
   const int n_gu = I / 32;                // gate/up units
   const int ngI = I / kG;                 // groups of K = I
-  const int qkv_w8 = (QH + 2 * KVH) * D / 8, h_w8 = H / 8, gu_w8 = 2 * I / 8;
   uint32_t bad = 0;
 
   int pos = *p.pos;
@@ -342,9 +342,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
 
   auto prefetchA = [&](int l) {
     const anvilq_decode_layer& Ly = p.layers[l];
-    if (roleA == 1) {
-      prefetch_awq(A_w, A_z, A_s, Ly.qkv_qweight, Ly.qkv_qzeros, reinterpret_cast<const __half*>(Ly.qkv_scales),
-                   qkv_w8, 8 * qkv_w8, 0, H, idxA * a_words(D), a_words(D));
+    if (roleA == 1) {   // column block idxA (one head) of the blocked QKV projection
+      const int wd = a_words(D), ng = H / kG;
+      prefetch_block(A_w, A_z, A_s, Ly.qkv_qweight + (size_t)idxA * H * wd, Ly.qkv_qzeros + (size_t)idxA * ng * wd,
+                     reinterpret_cast<const __half*>(Ly.qkv_scales) + (size_t)idxA * ng * 8 * wd, H, wd, ng);
     } else if (roleA == 2) {
       // the first chunk this CTA owns: rows before the current position only
       const int u = idxA;
@@ -361,9 +362,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
           cp16(Vc + r * D + 8 * c8, vc + off);
         }
       }
-    } else if (roleA == 3) {
-      prefetch_awq(A_w, A_z, A_s, Ly.o_qweight, Ly.o_qzeros, reinterpret_cast<const __half*>(Ly.o_scales), h_w8, H,
-                   0, QH * D, idxA * kBW, kBW);
+    } else if (roleA == 3) {   // column block idxA of the blocked O projection
+      const int K = QH * D, ng = K / kG;
+      prefetch_block(A_w, A_z, A_s, Ly.o_qweight + (size_t)idxA * K * kBW, Ly.o_qzeros + (size_t)idxA * ng * kBW,
+                     reinterpret_cast<const __half*>(Ly.o_scales) + (size_t)idxA * ng * 8 * kBW, K, kBW, ng);
     }
     cp_commit();
   };
@@ -373,11 +375,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     for (int sl = 0; sl < 2; ++sl) {
       const int u = units[sl];
       if (u < 0 || u >= n_gu) continue;
-      for (int which = 0; which < 2; ++which) {   // gate words [4u, 4u+4), up words I/8 + 4u ..
+      for (int which = 0; which < 2; ++which) {   // column blocks u (gate) and I / 32 + u (up)
         uint32_t* w = gu_w(sl, which);
-        prefetch_awq(w, w + H * kBW, w + H * kBW + (H / kG) * kBW, Ly.gu_qweight, Ly.gu_qzeros,
-                     reinterpret_cast<const __half*>(Ly.gu_scales), gu_w8, 2 * I, 0, H,
-                     (which ? I / 8 : 0) + u * kBW, kBW);
+        const size_t b = (size_t)(which ? n_gu : 0) + u;
+        const int ng = H / kG;
+        prefetch_block(w, w + H * kBW, w + H * kBW + ng * kBW, Ly.gu_qweight + b * H * kBW,
+                       Ly.gu_qzeros + b * ng * kBW, reinterpret_cast<const __half*>(Ly.gu_scales) + b * ng * 8 * kBW,
+                       H, kBW, ng);
       }
     }
     cp_commit();
@@ -385,8 +389,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
   auto prefetchC = [&](int l) {
     if (has_down) {
       const anvilq_decode_layer& Ly = p.layers[l];
-      prefetch_awq(C_w, C_z, C_s, Ly.down_qweight, Ly.down_qzeros, reinterpret_cast<const __half*>(Ly.down_scales),
-                   h_w8, H, drow0, drows, db * kBW, kBW);
+      // rows [drow0, drow0 + drows) of column block db of the blocked down projection
+      prefetch_block(C_w, C_z, C_s, Ly.down_qweight + ((size_t)db * I + drow0) * kBW,
+                     Ly.down_qzeros + ((size_t)db * ngI + dg0) * kBW,
+                     reinterpret_cast<const __half*>(Ly.down_scales) + ((size_t)db * ngI + dg0) * 8 * kBW, drows, kBW,
+                     dg1 - dg0);
     }
     cp_commit();
   };
@@ -830,4 +837,18 @@ extern "C" int anvilq_decode_layers(const anvilq_decode_layer* layers, int L, in
     return ANVILQ_ECUDA;
   }
   return ANVILQ_OK;
+}
+
+extern "C" int anvilq_block_columns(const void* src, void* dst, int rows, int cols, int block, int elem_bytes,
+                                    anvilq_stream_t stream) {
+  if (!src || !dst || rows < 1 || cols < 1 || block < 1 || (elem_bytes != 2 && elem_bytes != 4)) return ANVILQ_EINVAL;
+  if (cols % block || (block * elem_bytes) % 16) return ANVILQ_ESHAPE;
+  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15u) return ANVILQ_EALIGN;
+  const long long row_vecs = (long long)cols * elem_bytes / 16, block_vecs = (long long)block * elem_bytes / 16;
+  const long long n = (long long)rows * row_vecs;
+  const int threads = 256;
+  const long long blocks = std::min<long long>((n + threads - 1) / threads, 1 << 20);
+  block_columns_kernel<<<(unsigned)blocks, threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), rows, row_vecs, block_vecs);
+  return cudaGetLastError() == cudaSuccess ? ANVILQ_OK : ANVILQ_ECUDA;
 }

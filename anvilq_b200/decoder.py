@@ -134,13 +134,30 @@ class Decoder:
         self.fused = fused is not False and fused_ws > 0
         if self.fused:
             self.fused_ws = torch.zeros(fused_ws, dtype=torch.uint8, device=dev)
+            s = torch.cuda.current_stream(dev).cuda_stream
+
+            def blocked(t, block):
+                """The tensor's column blocks of `block` elements one after another (anvilq_block_columns)."""
+                out = torch.empty_like(t)
+                _lib.check(lib.anvilq_block_columns(t.data_ptr(), out.data_ptr(), t.shape[0], t.shape[1], block,
+                                                    t.element_size(), s), "anvilq_block_columns")
+                return out
+
+            def blocked_awq(w, words):   # qweight, qzeros in blocks of `words` words, scales of 8 words
+                return (blocked(w[0], words), blocked(w[1], words), blocked(w[2], 8 * words), w[3])
+
             p = lambda t: 0 if t is None else t.data_ptr()
             rows = []
+            self.blocked_layers = []
             for l, w in enumerate(self.layers):   # anvilq_decode_layer, field by field
-                rows.append([p(a) for a in w["qkv"]] + [p(a) for a in w["o"][:3]] + [p(a) for a in w["gu"][:3]]
-                            + [p(a) for a in w["down"][:3]] + [p(self.gamma_in[l]), p(self.gamma_post[l]),
+                b = {"qkv": blocked_awq(w["qkv"], D // 8), "o": blocked_awq(w["o"], 4),
+                     "gu": blocked_awq(w["gu"], 4), "down": blocked_awq(w["down"], 4)}
+                self.blocked_layers.append(b)
+                rows.append([p(a) for a in b["qkv"]] + [p(a) for a in b["o"][:3]] + [p(a) for a in b["gu"][:3]]
+                            + [p(a) for a in b["down"][:3]] + [p(self.gamma_in[l]), p(self.gamma_post[l]),
                                                                p(self.k_cache[l]), p(self.v_cache[l])])
             self.layer_table = torch.tensor(rows, dtype=torch.int64, device=dev)
+            torch.cuda.synchronize(dev)
         self.stream = torch.cuda.Stream(dev)
         self.graph = None
         # host staging for the end-to-end path

@@ -386,9 +386,13 @@ int anvilq_w4a16_gemv_allgather(const uint16_t* x, const int32_t* qweight, const
  * softmax and P.V in fp32.
  *
  * `layers` is a DEVICE array of L descriptors.  Per layer: qkv = the q, k, v
- * projections concatenated along N ([H][(QH+2KVH) D / 8] AWQ, bias fp16
+ * projections concatenated along N (AWQ [H][(QH+2KVH) D / 8], bias fp16
  * [(QH+2KVH) D] or NULL); o [QH D][H / 8]; gu = gate and up concatenated
  * along N ([H][2 I / 8]); down [I][H / 8]; gammas fp16 [H]; caches fp16.
+ * The AWQ tensors are given COLUMN-BLOCKED (anvilq_block_columns), so that the
+ * slice a CTA streams is one contiguous range: qkv in blocks of one head
+ * (qweight and qzeros D / 8 words, scales D halves), o, gu and down in blocks
+ * of 4 words (scales 32 halves): a block's rows follow one another.
  * Requirements: G == 128, H % 128 == 0, I % 128 == 0, QH % KVH == 0,
  * QH / KVH <= 8, D in {64, 128}, (QH D) % 128 == 0, 16-byte aligned tensors,
  * and one SM's shared memory must hold a CTA's slices of a layer (ANVILQ_ESHAPE
@@ -398,6 +402,13 @@ int anvilq_w4a16_gemv_allgather(const uint16_t* x, const int32_t* qweight, const
  * *token or *pos sets ANVILQ_DEV_ERR_TOKEN / _SEQLEN and does nothing.
  * workspace: anvilq_decode_layers_workspace_size bytes, 256-byte aligned,
  * zero-filled once (every launch leaves its counters zero). */
+/* dst[b][r][e] = src[r][b * block + e] for a row-major [rows][cols] matrix of
+ * elem_bytes-byte elements (2 or 4): its column blocks of `block` elements
+ * stored one after another.  block * elem_bytes % 16 == 0, cols % block == 0,
+ * 16-byte aligned pointers.  A layout step for anvilq_decode_layers; no
+ * counterpart computation in the reference (the AWQ words are moved, never changed). */
+int anvilq_block_columns(const void* src, void* dst, int rows, int cols, int block, int elem_bytes,
+                         anvilq_stream_t stream);
 typedef struct anvilq_decode_layer {
   const int32_t* qkv_qweight;
   const int32_t* qkv_qzeros;
