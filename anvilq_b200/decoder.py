@@ -37,6 +37,9 @@ from .checkpoint import ArrayCheckpoint
 
 # (L, H, I, QH, KVH, D, G, V, SEQ) as in official_weights.py:21 DEFAULT_SHAPE
 QWEN05B_SHAPE = (24, 896, 4864, 14, 2, 64, 128, 151936, 32768)
+# a Llama-7B-class decoder in the same tuple: 32 layers, hidden 4096, intermediate
+# 11008, 32 heads of 128 (no grouping), vocabulary 32000; no q/k/v bias
+LLAMA7B_SHAPE = (32, 4096, 11008, 32, 32, 128, 128, 32000, 4096)
 ROPE_THETA = 1_000_000.0
 RMS_EPS = 1e-6
 FLAG_OVERLAP = 1   # ANVILQ_GEMM_OVERLAP_PRIOR
@@ -55,13 +58,15 @@ class DecoderWeights:
         return ArrayCheckpoint(flat, embedding=self.embedding, norms=self.norms)
 
 
-def synthetic_weights(shape=QWEN05B_SHAPE, seed: int = 17) -> DecoderWeights:
+def synthetic_weights(shape=QWEN05B_SHAPE, seed: int = 17, qkv_bias: bool = True) -> DecoderWeights:
     """Random-init weights of the given shape.  W4 tensors use the benchmark
-    value distributions (u4 uniform, scales |N(0,1)|*0.01+1e-3); biases N(0,1);
-    norm weights 1 + 0.1 N(0,1); embedding 0.5 N(0,1); all fp16."""
+    value distributions (u4 uniform, scales |N(0,1)|*0.01+1e-3); biases N(0,1)
+    (q/k/v only, and only with qkv_bias); norm weights 1 + 0.1 N(0,1);
+    embedding 0.5 N(0,1); all fp16."""
     L, H, I, QH, KVH, D, G, V, _ = shape
     rng = np.random.default_rng(seed)
-    dims = ((H, QH * D, True), (H, KVH * D, True), (H, KVH * D, True), (QH * D, H, False),
+    b = qkv_bias
+    dims = ((H, QH * D, b), (H, KVH * D, b), (H, KVH * D, b), (QH * D, H, False),
             (H, I, False), (H, I, False), (I, H, False))
     layers = []
     norms = {}
@@ -74,8 +79,35 @@ def synthetic_weights(shape=QWEN05B_SHAPE, seed: int = 17) -> DecoderWeights:
     return DecoderWeights(shape, layers, norms, embedding)
 
 
+def device_synthetic_weights(shape, device, seed: int = 17, qkv_bias: bool = True) -> DecoderWeights:
+    """``synthetic_weights`` drawn on the device (a seeded torch generator, the
+    same value distributions): the tensors are torch tensors, for model sizes
+    whose host-side generation would take minutes (7B-class)."""
+    L, H, I, QH, KVH, D, G, V, _ = shape
+    dev = torch.device(device)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    dims = ((H, QH * D, qkv_bias), (H, KVH * D, qkv_bias), (H, KVH * D, qkv_bias), (QH * D, H, False),
+            (H, I, False), (H, I, False), (I, H, False))
+    layers = []
+    norms = {}
+    gamma = lambda: (1.0 + 0.1 * torch.randn(H, generator=gen, device=dev)).half()
+    for l in range(L):
+        layers.append({p: synthetic.AwqLayer(*synthetic.device_awq_layer(K, N, G, gen, dev, bias=b), G)
+                       for p, (K, N, b) in enumerate(dims)})
+        norms["input", l] = gamma()
+        norms["post", l] = gamma()
+    norms["final", 0] = gamma()
+    embedding = (0.5 * torch.randn((V, H), generator=gen, device=dev)).half()
+    return DecoderWeights(shape, layers, norms, embedding)
+
+
 def _concat(layers):
-    """AWQ layers with equal K and G concatenated along N."""
+    """AWQ layers with equal K and G concatenated along N (numpy arrays or torch tensors)."""
+    if isinstance(layers[0].qweight, torch.Tensor):
+        cat = lambda name: torch.cat([getattr(l, name) for l in layers], dim=1)
+        bias = None if layers[0].bias is None else torch.cat([l.bias for l in layers])
+        return synthetic.AwqLayer(cat("qweight"), cat("qzeros"), cat("scales"), bias, layers[0].group)
     cat = lambda name: np.concatenate([getattr(l, name) for l in layers], axis=1)
     bias = None
     if layers[0].bias is not None:
@@ -96,7 +128,8 @@ class Decoder:
         self.max_seq = min(max_seq, SEQ)
         self.device = torch.device(device)
         dev = self.device
-        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+        t = lambda a: (None if a is None else a.to(dev).contiguous() if isinstance(a, torch.Tensor)
+                       else torch.from_numpy(np.ascontiguousarray(a)).to(dev))
         self.layers = []
         for projs in weights.layers:
             qkv = _concat([projs[0], projs[1], projs[2]])

@@ -2,7 +2,7 @@
 """Benchmark of the W4A16 AWQ decode datapath on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl anvilq|reference]
-                    [--workload decode05b|proj05b|proj7b|attn|tp70b] [--no-extras]
+                    [--workload decode05b|decode7b|proj05b|proj7b|attn|tp70b] [--no-extras] [--unfused]
 
 decode05b (default): one step = one greedy decode token of a Qwen2.5-0.5B-shape
 W4A16 AWQ model (24 layers, hidden 896, 14/2 heads of 64, intermediate 4864,
@@ -14,8 +14,9 @@ times the step's 96 W4A16 GEMVs (same weights, buffers and fused modes) as a
 graph of their own in the same run.  e2e drives the public Decoder API with the
 input token copied from pinned host memory and the chosen token copied back
 inside every step, and the host waiting for it.  Unless --no-extras, the same
-line carries three more measurements taken in the same run, on every rank:
-"proj7b" (the W4A16 GEMVs of a Llama-7B-class decode step, GB/s, one replica
+line carries four more measurements taken in the same run, on every rank:
+"decode7b" (the same decode step for a Llama-7B-class model, tok/s, one replica
+per GPU), "proj7b" (the W4A16 GEMVs of a Llama-7B-class decode step, GB/s, one replica
 per GPU), "tp70b" (the 70B-class layer column-split over the N GPUs and
 all-gathered, GB/s, strong scaling) and "attn" (decode attention over a
 64-sequence batch at context 32768 sharded over the N GPUs, GB/s).
@@ -66,7 +67,11 @@ WORKLOADS = {
     "decode05b": dict(name="Qwen2.5-0.5B-shape greedy decode step, batch 1, context 1024: 24 layers, hidden 896, "
                            "14 q / 2 kv heads of 64, intermediate 4864, W4A16 AWQ G128 projections, RMSNorm eps 1e-6, "
                            "RoPE theta 1e6, fp16 KV cache, tied fp16 lm_head [151936, 896], greedy argmax",
-                      context=1024),
+                      context=1024, shape="QWEN05B_SHAPE"),
+    "decode7b": dict(name="Llama-7B-class greedy decode step, batch 1, context 1024: 32 layers, hidden 4096, 32 heads "
+                          "of 128 (no grouping), intermediate 11008, W4A16 AWQ G128 projections without bias, RMSNorm "
+                          "eps 1e-6, RoPE theta 1e6, fp16 KV cache, tied fp16 lm_head [32000, 4096], greedy argmax",
+                     context=1024, shape="LLAMA7B_SHAPE", device_init=True, qkv_bias=False),
     "proj05b": dict(name="Qwen2.5-0.5B decode-step W4A16 projections: 24 layers x (q 896x896+bias, "
                          "k,v 896x128+bias, o 896x896, gate,up 896x4864, down 4864x896), G128, M=1",
                     layers=24, projections="QWEN05B_PROJECTIONS"),
@@ -326,17 +331,22 @@ def decode_reference_arm(args, world, rank):
     return 0
 
 
-def decode_arm(args, world, rank, local):
+def decode_measure(args, world, rank, dev, name):
+    """One greedy decode token per step of the workload's model (decode05b or
+    decode7b), as one CUDA graph; the line without the CPU baseline."""
     import torch
     from anvilq_b200 import decoder
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    wl = WORKLOADS["decode05b"]
+    wl = WORKLOADS[name]
+    shape = getattr(decoder, wl["shape"])
     ctx = wl["context"]
     peak, peak_kind = load_peaks()
-    w = decoder.synthetic_weights(decoder.QWEN05B_SHAPE, seed=17 + rank)
+    if wl.get("device_init"):
+        w = decoder.device_synthetic_weights(shape, dev, seed=17 + rank, qkv_bias=wl["qkv_bias"])
+    else:
+        w = decoder.synthetic_weights(shape, seed=17 + rank)
     total_steps = 2 * (args.warmup + args.steps) + 4
     d = decoder.Decoder(w, dev, max_seq=ctx + total_steps + 8, fused=False if args.unfused else None)
+    del w
     d.fill_context(ctx, seed=rank)
     d.token.fill_(1000)
     d.token_in.fill_(1000)
@@ -359,19 +369,20 @@ def decode_arm(args, world, rank, local):
     ms_roof = timed(replay(g_roof), d.stream, args.steps, args.warmup, world, dev)
     d.check_errors()
 
+    L = shape[0]
     tok_s = world * args.steps / (ms / 1e3)
     step_bytes = d.bytes_per_step(ctx + args.warmup + args.steps // 2)
     if d.fused:
         roof_kernel, roof_launches = "decode_step_kernel", 1
         roof_bytes = d.layer_bytes_per_step(pos_roof + 1)
-        roof_on = "the fused layers kernel (all 24 layers of a token, no lm_head) as its own CUDA graph, same run"
+        roof_on = f"the fused layers kernel (all {L} layers of a token, no lm_head) as its own CUDA graph, same run"
     else:
-        roof_kernel, roof_launches = "gemv_tma_kernel", 4 * decoder.QWEN05B_SHAPE[0]
+        roof_kernel, roof_launches = "gemv_tma_kernel", 4 * L
         roof_bytes = d.gemv_bytes_per_step()
-        roof_on = "the step's 96 W4A16 GEMVs as their own CUDA graph, same run"
+        roof_on = f"the step's {4 * L} W4A16 GEMVs as their own CUDA graph, same run"
     per_launch_s = ms_roof / 1e3 / args.steps / roof_launches
     achieved = roof_bytes / roof_launches / per_launch_s / 1e9
-    entry = traffic_entry(f"{roof_kernel}/decode05b")
+    entry = traffic_entry(f"{roof_kernel}/{name}")
     traffic = int(roof_bytes / roof_launches * entry["ratio_read_over_algorithmic"]) if entry else None
     line = {
         "metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -379,7 +390,7 @@ def decode_arm(args, world, rank, local):
         "scaling": "weak", "vs_baseline": None,
         "dtype": "f16 activations x int4 weights, fp32 accumulate; fp16 KV and lm_head",
         "data": "synthetic (seeded random-init weights and context; u4 uniform, scales |N(0,1)|*0.01+1e-3)",
-        "config": {"workload": wl["name"], "batch": 1, "context": ctx, "layers": decoder.QWEN05B_SHAPE[0],
+        "config": {"workload": wl["name"], "batch": 1, "context": ctx, "layers": L,
                    "step_bytes": step_bytes, "kernels_per_step": d.kernels_per_step(),
                    "l2": "inputs larger than L2 (no flush)", "parallelism": f"replicas x{world}",
                    "graph": "one CUDA graph per token", "fused_layers_kernel": bool(d.fused)},
@@ -398,16 +409,25 @@ def decode_arm(args, world, rank, local):
     }
     del g_dev, g_e2e, g_roof, d
     torch.cuda.empty_cache()
-    if not args.no_extras:
-        line["proj7b"] = summary(proj_measure(args, world, rank, dev, "proj7b", e2e=False))
-        torch.cuda.empty_cache()
-        line["tp70b"] = summary(tp_measure(args, world, rank, dev, 1, e2e=False))
-        torch.cuda.empty_cache()
-        line["attn"] = summary(attn_measure(args, world, rank, dev, e2e=False))
-        torch.cuda.empty_cache()
-        line["gpu_launches"] += sum(line[k]["gpu_launches"] for k in ("proj7b", "tp70b", "attn"))
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = decode_cpu_baseline(ctx)
+    return line
+
+
+def decode_arm(args, world, rank, local):
+    import torch
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    name = args.workload
+    line = decode_measure(args, world, rank, dev, name)
+    if name == "decode05b" and not args.no_extras:
+        for key, fn in (("decode7b", lambda: decode_measure(args, world, rank, dev, "decode7b")),
+                        ("proj7b", lambda: proj_measure(args, world, rank, dev, "proj7b", e2e=False)),
+                        ("tp70b", lambda: tp_measure(args, world, rank, dev, 1, e2e=False)),
+                        ("attn", lambda: attn_measure(args, world, rank, dev, e2e=False))):
+            line[key] = summary(fn())
+            torch.cuda.empty_cache()
+            line["gpu_launches"] += line[key]["gpu_launches"]
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and name == "decode05b":
+        line["cpu_baseline"] = decode_cpu_baseline(WORKLOADS[name]["context"])
     if rank == 0:
         print(json.dumps(line), flush=True)
     return 0
@@ -487,6 +507,11 @@ def anvilq_arm(args, world, rank, local):
 
 
 def reference_arm(args, world, rank):
+    if args.workload == "decode7b":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the CPU restatement of FP32Model.token is timed "
+                              "on the 0.5B decode workload (decode05b); a 7B-class token takes hours in it"}))
+        return 0
     if args.workload == "decode05b":
         return decode_reference_arm(args, world, rank)
     if args.workload == "attn":
@@ -830,7 +855,7 @@ def main(argv=None):
         return reference_arm(args, world, rank)
     world, rank, local = dist_init()
     try:
-        if args.workload == "decode05b":
+        if args.workload in ("decode05b", "decode7b"):
             return decode_arm(args, world, rank, local)
         if args.workload == "tp70b":
             return tp_arm(args, world, rank, local)

@@ -348,3 +348,42 @@ def test_fused_layers_reject_bad_token(dev):
     d.stream.synchronize()
     with pytest.raises(Exception):
         d.check_errors()
+
+
+def test_decode_llama7b_width_per_kernel_path(dev):
+    """Two layers at the Llama-7B width (hidden 4096, 32 heads of 128, intermediate
+    11008, no q/k/v bias; vocabulary cut to 512) through the per-kernel step --
+    the fused layers kernel does not take this width -- against the binary64
+    oracle with the W4A16 datapath's binary16 activations."""
+    shape = (2, 4096, 11008, 32, 32, 128, 128, 512, 64)
+    w = decoder.synthetic_weights(shape, seed=41, qkv_bias=False)
+    d = decoder.Decoder(w, dev, max_seq=64, keep_logits=True)
+    assert not d.fused
+    o = oracle.DecodeOracle(w, act16=True)
+    token = 77
+    d.reset(token)
+    for pos in range(2):
+        ref = o.step(token, pos)
+        d.step()
+        d.stream.synchronize()
+        d.check_errors()
+        check(d.logits.cpu().numpy(), ref, TOL_DECODE, pos)
+        token = int(d.token.item())
+        assert ref[token] >= ref.max() - 1e-2 * max(1.0, abs(ref.max()))
+
+
+def test_device_synthetic_weights_decode(dev):
+    """Weights drawn on the device drive the same decoder (both paths agree)."""
+    shape = (2, 256, 512, 4, 2, 64, 128, 128, 64)
+    w = decoder.device_synthetic_weights(shape, dev, seed=3)
+    a = decoder.Decoder(w, dev, max_seq=64, keep_logits=True, fused=True)
+    b = decoder.Decoder(w, dev, max_seq=64, keep_logits=True, fused=False)
+    for d in (a, b):
+        d.reset(5)
+    for _ in range(3):
+        for d in (a, b):
+            d.step()
+            d.stream.synchronize()
+            d.check_errors()
+        check(a.logits.cpu().numpy(), b.logits.cpu().numpy(), TOL_DECODE, "device weights")
+        assert int(a.token.item()) == int(b.token.item())
