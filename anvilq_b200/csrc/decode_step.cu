@@ -146,11 +146,41 @@ __device__ bool wait_count(const Params& p, const int* ctr, int target) {
   __syncthreads();
   return s_ok != 0;
 }
-// every thread's stores of this phase are visible at GPU scope, then the counter moves
+// every thread's stores of this phase are visible at GPU scope, then the counter
+// moves: the barrier orders the CTA's stores before thread 0's fence (cumulative)
 __device__ void publish(int* ctr, int n) {
-  __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) atomicAdd(ctr, n);
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(ctr, n);
+  }
+}
+
+// this CTA's stores so far visible, then a ticket; true for the last arriver
+// (whose loads after the call see every other arriver's stores)
+__device__ bool last_arrival(int* ticket, int arrivals) {
+  __shared__ int s_last_arrival;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const bool last = atomicAdd(ticket, 1) == arrivals - 1;
+    if (last) __threadfence();
+    s_last_arrival = last;
+  }
+  __syncthreads();
+  return s_last_arrival != 0;
+}
+
+// dst[0:n] = src[0:n] (L2-coherent loads), 8 loads in flight per thread
+__device__ void stage_floats(float* dst, const float* src, int n) {
+  for (int i0 = threadIdx.x; i0 < n; i0 += 8 * kThreads) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = i0 + u * kThreads < n ? __ldcg(src + i0 + u * kThreads) : 0.0f;
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (i0 + u * kThreads < n) dst[i0 + u * kThreads] = v[u];
+  }
 }
 
 // Copy one column block of a projection (see anvilq_block_columns): `rows`
@@ -216,22 +246,28 @@ __device__ uint32_t tile_gemv(const uint32_t* wsm, const __half* xs, const uint3
     Xg = 0.0f;
   };
   const unsigned short* xh = reinterpret_cast<const unsigned short*>(xs);
-  for (int r = rb; r < re; ++r) {
-    if (r == bnd) {
-      flush(g - g0);
-      ++g;
-      bnd += kG;
+  auto rows = [&](int r0, int r1) {   // rows of one group
+#pragma unroll 4
+    for (int r = r0; r < r1; ++r) {
+      const uint32_t wd = wsm[r * W + word];
+      const unsigned short xv = xh[r];
+      Xg += __half2float(__ushort_as_half(xv));
+      const uint32_t w8 = wd >> 8;
+      fma_f32_f16x2(A[0], A[1], wd & 0x000F000Fu, xv);   // columns 0,1
+      fma_f32_f16x2(A[2], A[3], wd & 0x00F000F0u, xv);   // columns 2,3 (x16)
+      fma_f32_f16x2(A[4], A[5], w8 & 0x000F000Fu, xv);   // columns 4,5
+      fma_f32_f16x2(A[6], A[7], w8 & 0x00F000F0u, xv);   // columns 6,7 (x16)
     }
-    const uint32_t wd = wsm[r * W + word];
-    const unsigned short xv = xh[r];
-    Xg += __half2float(__ushort_as_half(xv));
-    const uint32_t w8 = wd >> 8;
-    fma_f32_f16x2(A[0], A[1], wd & 0x000F000Fu, xv);   // columns 0,1
-    fma_f32_f16x2(A[2], A[3], wd & 0x00F000F0u, xv);   // columns 2,3 (x16)
-    fma_f32_f16x2(A[4], A[5], w8 & 0x000F000Fu, xv);   // columns 4,5
-    fma_f32_f16x2(A[6], A[7], w8 & 0x00F000F0u, xv);   // columns 6,7 (x16)
+  };
+  // a thread's contiguous rows (fewer than 128) cross at most one group boundary
+  for (int r = rb; r < re;) {
+    const int e = min(re, bnd);
+    rows(r, e);
+    flush(g - g0);
+    r = e;
+    ++g;
+    bnd += kG;
   }
-  if (rb < re) flush(g - g0);
 #pragma unroll
   for (int o = W; o < 32; o <<= 1)
 #pragma unroll
@@ -472,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
         float* qs = misc + 32;                     // [grp][D]
         float* sc = qs + kMaxGroup * kMaxD;         // [grp][64] scores, then probabilities
         const float qscale = 1.4426950408889634f / sqrtf((float)D);
-        for (int i = tid; i < grp * D; i += kThreads)
+        for (int i = tid; i < grp * D; i += kThreads)   // grp * D <= 1024: two loads per thread at most
           qs[i] = __half2float(__ldcg(p.q + (size_t)h * grp * D + i)) * qscale;
         __syncthreads();
         // scores: warp w takes rows w, w + 16, ...; lanes split the head dim
@@ -529,16 +565,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
           __stcg(part_out + tid * (D + 2) + 1, ml[2 * tid + 1]);
         }
         // the last chunk of kv head h to arrive merges the chunks in chunk order
-        __threadfence();
-        __syncthreads();
-        __shared__ int s_last;
-        if (tid == 0) {
-          const int n = atomicAdd(p.aticket + l * KVH + h, 1);
-          s_last = n == nch - 1;
-        }
-        __syncthreads();
-        if (s_last) {
-          __threadfence();
+        if (last_arrival(p.aticket + l * KVH + h, nch)) {
           // every chunk's (m, l, o) of this head, loaded at once into shared
           // memory (the K / V tiles are no longer needed), in batches that fit
           float* st = reinterpret_cast<float*>(regA);
@@ -548,8 +575,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
           for (int k = 0; k < 2; ++k) M[k] = -INFINITY, Ls[k] = O[k] = 0.0f;
           for (int c0 = 0; c0 < nch; c0 += batch) {
             const int nb_ = min(batch, nch - c0);
-            const float* src = p.apart + (size_t)(h * p.maxch + c0) * per_chunk;
-            for (int i = tid; i < nb_ * per_chunk; i += kThreads) st[i] = __ldcg(src + i);
+            stage_floats(st, p.apart + (size_t)(h * p.maxch + c0) * per_chunk, nb_ * per_chunk);
             __syncthreads();
             for (int k = 0; k < 2; ++k) {   // (head, dim) pairs tid and tid + 512 (grp * D <= 1024)
               const int i = tid + k * kThreads;
@@ -632,18 +658,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
       float* y = misc + 32;
       bad |= tile_gemv<kBW>(C_w, xs, C_z, C_s, drows, drow0, red, y);
       if (tid < 32) __stcg(p.dpart + ((size_t)db * p.nsplit + ds) * 32 + tid, y[tid]);
-      __threadfence();
-      __syncthreads();
-      __shared__ int s_lastd;
-      if (tid == 0) {
-        const int n = atomicAdd(p.dticket + l * nb + db, 1);
-        s_lastd = n == p.nsplit - 1;
-      }
-      __syncthreads();
-      if (s_lastd) {
-        __threadfence();
+      if (last_arrival(p.dticket + l * nb + db, p.nsplit)) {
         float* st = misc + 32;   // [nsplit][32], every split loaded at once
-        for (int i = tid; i < p.nsplit * 32; i += kThreads) st[i] = __ldcg(p.dpart + (size_t)db * p.nsplit * 32 + i);
+        stage_floats(st, p.dpart + (size_t)db * p.nsplit * 32, p.nsplit * 32);
         __syncthreads();
         if (tid < 32) {
           float acc = 0.0f;

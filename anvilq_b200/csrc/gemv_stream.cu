@@ -387,16 +387,21 @@ __global__ void __launch_bounds__(W * 32, W <= 8 ? 2 : 1)
         const int t = threadIdx.x + u * W * 32;
         if (t < kBandCols) __stcg(p.parts + ((size_t)blockIdx.x * 2 + s) * kBandCols + t, v[u]);
       }
-      __threadfence();
+      // one thread fences for the CTA: the barrier orders every thread's stores
+      // before its fence (cumulative), and the last arriver's fence orders its
+      // CTA's loads after every contributor's stores
       __syncthreads();
       if (threadIdx.x == 0) {
+        __threadfence();
         const int arrived = atomicAdd(p.tickets + band, 1);
         s_last = arrived == last - first;
-        if (s_last) p.tickets[band] = 0;   // re-armed for the next launch
+        if (s_last) {
+          p.tickets[band] = 0;   // re-armed for the next launch
+          __threadfence();
+        }
       }
       __syncthreads();
       if (!s_last) continue;
-      __threadfence();
       // the contributors' partials, loaded by all threads at once (not one
       // dependent L2 round trip per contributor), staged through the ring
       // (free again) in batches of kFixRows, then summed in CTA order
@@ -411,11 +416,19 @@ __global__ void __launch_bounds__(W * 32, W <= 8 ? 2 : 1)
       for (int u = 0; u < kPer; ++u) acc[u] = 0.0f;
       for (int i0 = first; i0 <= last; i0 += kStageRows) {
         const int rows = min(kStageRows, last - i0 + 1);
-        for (int e = threadIdx.x; e < rows * (kBandCols / 4); e += W * 32) {
-          const int r = e / (kBandCols / 4), c4 = e % (kBandCols / 4), i = i0 + r;
-          const int slot = band - (int)((long long)i * T / P) / p.cpb;
-          reinterpret_cast<float4*>(stage)[e] =
-              __ldcg(reinterpret_cast<const float4*>(p.parts + ((size_t)i * 2 + slot) * kBandCols) + c4);
+        constexpr int kU = 4;   // loads in flight per thread
+        for (int e0 = threadIdx.x; e0 < rows * (kBandCols / 4); e0 += kU * W * 32) {
+          float4 vv[kU];
+#pragma unroll
+          for (int u = 0; u < kU; ++u) {
+            const int e = e0 + u * W * 32, r = e / (kBandCols / 4), c4 = e % (kBandCols / 4), i = i0 + r;
+            const int slot = band - (int)((long long)i * T / P) / p.cpb;
+            if (e < rows * (kBandCols / 4))
+              vv[u] = __ldcg(reinterpret_cast<const float4*>(p.parts + ((size_t)i * 2 + slot) * kBandCols) + c4);
+          }
+#pragma unroll
+          for (int u = 0; u < kU; ++u)
+            if (e0 + u * W * 32 < rows * (kBandCols / 4)) reinterpret_cast<float4*>(stage)[e0 + u * W * 32] = vv[u];
         }
         __syncthreads();
 #pragma unroll
@@ -453,10 +466,10 @@ __global__ void __launch_bounds__(W * 32, W <= 8 ? 2 : 1)
           for (int r = 0; r < p.world; ++r)
             *reinterpret_cast<uint4*>(p.peer_y[r] + p.col_base + col) = val;
         }
-        __threadfence_system();   // the stores reach every rank before this band is counted
       }
       __syncthreads();
       if (threadIdx.x == 0) {
+        __threadfence_system();   // the CTA's peer stores (ordered by the barrier) reach every rank first
         const int done = atomicAdd(p.tickets + kRankTicket, 1);
         if (done == p.bands - 1) {
           p.tickets[kRankTicket] = 0;   // re-armed for the next launch
