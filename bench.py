@@ -2,7 +2,7 @@
 """Benchmark of the W4A16 AWQ decode datapath on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl anvilq|reference]
-                    [--workload decode05b|decode7b|proj05b|proj7b|attn|tp70b] [--no-extras] [--unfused]
+                    [--workload decode05b|decode7b|proj05b|proj7b|attn|tp70b] [--no-extras] [--fused]
 
 decode05b (default): one step = one greedy decode token of a Qwen2.5-0.5B-shape
 W4A16 AWQ model (24 layers, hidden 896, 14/2 heads of 64, intermediate 4864,
@@ -345,7 +345,7 @@ def decode_measure(args, world, rank, dev, name):
     else:
         w = decoder.synthetic_weights(shape, seed=17 + rank)
     total_steps = 2 * (args.warmup + args.steps) + 4
-    d = decoder.Decoder(w, dev, max_seq=ctx + total_steps + 8, fused=False if args.unfused else None)
+    d = decoder.Decoder(w, dev, max_seq=ctx + total_steps + 8, fused=True if args.fused else False)
     del w
     d.fill_context(ctx, seed=rank)
     d.token.fill_(1000)
@@ -844,8 +844,8 @@ def main(argv=None):
     ap.add_argument("--no-extras", action="store_true",
                     help="decode05b: skip the proj7b / tp70b / attn measurements on the same line")
     ap.add_argument("--tokens", type=int, default=1, help="token rows per projection (tp70b)")
-    ap.add_argument("--unfused", action="store_true",
-                    help="decode05b: one kernel per operation instead of the fused layers kernel")
+    ap.add_argument("--fused", action="store_true",
+                    help="decode05b: the fused layers kernel instead of one kernel per operation")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
