@@ -25,6 +25,7 @@ SIGNATURES = {
     "anvilq_w4a16_gemm": (I, [P, P, P, P, P, P, I, I, I, I, P, SZ, P, P]),
     "anvilq_w4a16_gemm_ex": (I, [P, P, P, P, P, P, I, I, I, I, P, SZ, P, ctypes.c_uint, P]),
     "anvilq_w4a16_gemv_plan": (I, [I, I, I, P]),
+    "anvilq_w4a16_gemv_kernel_plan": (I, [I, I, I, I, P]),
     "anvilq_w4a16_gemv_plan_workspace_size": (SZ, [I, I, I, P]),
     "anvilq_w4a16_gemv_planned": (I, [P, P, P, P, P, P, I, I, I, P, P, SZ, P, ctypes.c_uint, P]),
     "anvilq_w4a16_gemm_exact": (I, [P, P, P, P, P, P, I, I, I, I, P, P]),

@@ -63,6 +63,16 @@ __device__ __forceinline__ void unpack_deltas(uint32_t w, const ZeroPoint& zp, h
   d[3] = __hfma2(u32_as_half2((w8 & kHiPairMask) | kMagic1024), sixteenth, zp.n67);
 }
 
+// a0 += x * d.lo and a1 += x * d.hi in binary32: the product of two binary16
+// operands is exact in binary32 (11 + 11 significant bits), so each step of a
+// sum of x (q - z) rounds once, in fp32, as FP32Model.linear's accumulation does.
+__device__ __forceinline__ void fma2_f32_f16(float& a0, float& a1, half2 d, __half x) {
+  asm("{\n .reg .f16 d0, d1;\n mov.b32 {d0, d1}, %2;\n"
+      " fma.rn.f32.f16 %0, %3, d0, %0;\n fma.rn.f32.f16 %1, %3, d1, %1;\n}"
+      : "+f"(a0), "+f"(a1)
+      : "r"(half2_as_u32(d)), "h"(__half_as_ushort(x)));
+}
+
 // Nonzero iff either binary16 half of `u` is an invalid AWQ scale: exponent 31
 // (Inf/NaN) or negative and nonzero (anvil-q1/design/SPEC.md:175-177).
 // Per half: (e & 0x7C00) + 0x0400 carries into bit 15 exactly when e == 31;

@@ -12,30 +12,40 @@
 //
 // Why one kernel.  A 0.5B-class layer moves ~8 MB of int4 weights, 1.3 us of
 // HBM time, but as five launches (QKV, attention, O, gate/up, down) it costs
-// ~22 us: every launch pays its ramp and tail.  Here the five phases of a layer
+// ~26 us: every launch pays its ramp and tail.  Here the five phases of a layer
 // are roles that CTAs take, and a phase starts when the counter its producers
 // increment reaches the number of producers (release / acquire at GPU scope,
 // bounded waits).  No CTA waits for CTAs that do not produce its input.
 //
+// One round trip per phase.  A decode layer is a chain of five dependent
+// phases, so what bounds it is latency: each phase costs the wait, ONE batch
+// of L2 loads of its inputs, its arithmetic and the publish.  Nothing is
+// merged or fixed up in a phase of its own:
+//   - attention units publish unnormalised partials (m, l, o); every O CTA
+//     merges all of them while it loads its inputs (the merge is redundant
+//     across O CTAs, a few KB of L2 reads each, instead of a serial phase);
+//   - down splits publish partial column sums; the residual after layer l is
+//     never stored: the next layer's QKV and O CTAs add x_a and the splits in
+//     split order as part of their input load.
+//
 // Weights stream ahead.  Each CTA's slice of a phase's weights (int4 words,
-// zeros, scales) and, for attention, its chunk of the KV cache up to the
-// previous position, are copied into shared memory with cp.async as soon as
-// the CTA has finished the same phase of the previous layer: a whole layer of
-// lead time, so the copies never sit on the critical path.  Three groups are
-// in flight per CTA (roles A = QKV or attention or O, B = gate/up, C = down).
+// zeros, scales, and the RMSNorm gamma) and, for attention, the first chunk of
+// its KV range up to the previous position, are copied into shared memory with
+// cp.async as soon as the CTA has finished the same phase of the previous
+// layer: a whole layer of lead time, so the copies never sit on the critical
+// path.  Three groups are in flight per CTA (roles A = QKV or attention or O,
+// B = gate/up, C = down).
 //
 // Work per layer (P = #CTAs, 512 threads each):
 //   QKV   one head (D columns, all H rows) per CTA: RoPE and the K / V cache
 //         append need both halves of a head, so the head is the unit.
-//   attn  (kv head, 64-token chunk) per CTA: fp32 scores and softmax over the
-//         chunk; the CTA arriving last at its kv head's ticket merges the
-//         chunks in chunk order.
+//   attn  (kv head, range of 64-token chunks) per CTA, online softmax over the
+//         range's chunks in fp32.
 //   O     32 output columns (4 qweight words) per CTA; residual added.
-//   g/u   32 intermediate columns of gate AND of up per CTA, so silu(g) u is
+//   g/u   32 intermediate columns of gate AND of up per CTA as ONE tile of 8
+//         words a row (gate and up interleaved at load time), so silu(g) u is
 //         formed locally; I / 32 units over P CTAs.
-//   down  32 output columns x a split of the groups of K = I per CTA; the last
-//         split to arrive at the block's ticket adds the splits in order and
-//         writes the layer's residual.
+//   down  32 output columns x a split of the groups of K = I per CTA.
 // The GEMV arithmetic is that of the batch-1 kernels: binary16-subnormal
 // nibbles, exact products by fma.rn.f32.f16 into fp32, zero points through
 // the group's sum of x, scales in fp32.  Every sum has a fixed order.
@@ -57,12 +67,26 @@ namespace dstep {
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kG = 128;            // AWQ group (rows)
-constexpr int kBW = 4;             // words of an O / gate-up / down unit (32 columns)
-constexpr int kChunk = 64;         // attention tokens per unit
+constexpr int kBW = 4;             // words of an O / down unit (32 columns)
+constexpr int kGU = 8;             // words of a gate/up unit (32 gate + 32 up columns)
+constexpr int kChunk = 64;         // attention tokens per chunk
 constexpr int kPhases = 5;
 constexpr int kMaxGroup = 8;       // q heads per kv head
 constexpr int kMaxD = 128;
+constexpr int kMaxUnits = 32;      // attention units per kv head (one merge lane each)
+constexpr int kMaxSplit = 16;      // down splits (each adds a load to the residual)
 constexpr unsigned long long kWaitNs = 1000000000ull;
+
+// shared-memory scratch `misc` (floats)
+constexpr int kMiscY = 32;         // GEMV outputs, up to 128
+constexpr int kMiscBig = 160;      // attention state or O merge weights
+constexpr int kAttQs = kMiscBig;                              // [grp][D] scaled q
+constexpr int kAttP = kAttQs + kMaxGroup * kMaxD;             // [grp][64] probabilities
+constexpr int kAttWmax = kAttP + kMaxGroup * kChunk;          // [grp][2]
+constexpr int kAttWsum = kAttWmax + 2 * kMaxGroup;            // [grp][2]
+constexpr int kAttM = kAttWsum + 2 * kMaxGroup;               // [2][grp] running max by chunk parity
+constexpr int kAttL = kAttM + 2 * kMaxGroup;                  // [grp] running sum
+constexpr int kAttEnd = kAttL + kMaxGroup;
 
 struct Params {
   const anvilq_decode_layer* layers;
@@ -76,23 +100,19 @@ struct Params {
   unsigned long long* key;
   int* dev_err;
   // workspace
-  float* xbuf;      // [2][H] residual after each layer (ping-pong)
   float* xa;        // [H] residual after attention
   __half* q;        // [QH * D] rotated q
-  float* apart;     // [KVH][maxch][group][D + 2] attention chunk partials (m, l, o)
-  __half* attn;     // [QH * D] attention output
+  float* apart;     // [KVH][nu_max][group][D + 2] attention partials (m, l, o)
   __half* act;      // [I] silu(g) u
   float* dpart;     // [H / 32][nsplit][32] down partials
   int* ctr;         // [L][kPhases] producer counters
-  int* aticket;     // [L][KVH]
-  int* dticket;     // [L][H / 32]
   int* exit_ctr;    // [1]
   int* abort_flag;  // [1]
   // roles: A = QKV heads [0, n1), attention [n1, n1 + n2), O blocks [n1 + n2, n1 + n2 + n3)
-  int n1, n2, n3, nsplit, maxch;
+  int n1, n2, n3, nsplit, nu_max;
   // shared-memory carve-up (bytes)
   int offA, offB, offC, offX, offRed, offMisc, smem;
-  int regA_bytes;
+  int offStage;     // within region A, after every role's tile: staged inputs, attention's P V sums
   double rope_inv[kMaxD / 2];
 };
 
@@ -122,6 +142,15 @@ __device__ __forceinline__ void fma_f32_f16x2(float& a0, float& a1, uint32_t q2,
       : "+f"(a0), "+f"(a1)
       : "r"(q2), "h"(x));
 }
+__device__ __forceinline__ bool misaligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; }
+
+// Give up the launch: the error bit, then the flag every bounded wait watches.
+__device__ void abort_launch(const Params& p, int bit) {
+  if (threadIdx.x == 0) {
+    if (p.dev_err) atomicOr(p.dev_err, bit);
+    atomicExch(p.abort_flag, 1);
+  }
+}
 
 // Block until *ctr >= target (thread 0 polls, the CTA follows); false when the
 // wait expired (~1 s) or another CTA already gave up: the launch then aborts.
@@ -133,11 +162,17 @@ __device__ bool wait_count(const Params& p, const int* ctr, int target) {
       const unsigned long long t0 = globaltimer();
       for (uint32_t i = 0;; ++i) {
         if (ld_acquire(ctr) >= target) break;
-        if ((i & 63u) == 63u && (globaltimer() - t0 > kWaitNs || ld_acquire(p.abort_flag))) {
-          ok = 0;
-          if (p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_TIMEOUT);
-          atomicExch(p.abort_flag, 1);
-          break;
+        if ((i & 63u) == 63u) {
+          if (ld_acquire(p.abort_flag)) {
+            ok = 0;
+            break;
+          }
+          if (globaltimer() - t0 > kWaitNs) {
+            ok = 0;
+            if (p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_TIMEOUT);
+            atomicExch(p.abort_flag, 1);
+            break;
+          }
         }
       }
     }
@@ -146,41 +181,13 @@ __device__ bool wait_count(const Params& p, const int* ctr, int target) {
   __syncthreads();
   return s_ok != 0;
 }
-// every thread's stores of this phase are visible at GPU scope, then the counter
-// moves: the barrier orders the CTA's stores before thread 0's fence (cumulative)
+// Every thread's stores of this phase reach GPU scope before the counter
+// moves: the barrier orders the CTA's stores before thread 0, whose
+// acquire-release fence is cumulative over them; the add itself is relaxed.
 __device__ void publish(int* ctr, int n) {
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(ctr, n);
-  }
-}
-
-// this CTA's stores so far visible, then a ticket; true for the last arriver
-// (whose loads after the call see every other arriver's stores)
-__device__ bool last_arrival(int* ticket, int arrivals) {
-  __shared__ int s_last_arrival;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const bool last = atomicAdd(ticket, 1) == arrivals - 1;
-    if (last) __threadfence();
-    s_last_arrival = last;
-  }
-  __syncthreads();
-  return s_last_arrival != 0;
-}
-
-// dst[0:n] = src[0:n] (L2-coherent loads), 8 loads in flight per thread
-__device__ void stage_floats(float* dst, const float* src, int n) {
-  for (int i0 = threadIdx.x; i0 < n; i0 += 8 * kThreads) {
-    float v[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) v[u] = i0 + u * kThreads < n ? __ldcg(src + i0 + u * kThreads) : 0.0f;
-#pragma unroll
-    for (int u = 0; u < 8; ++u)
-      if (i0 + u * kThreads < n) dst[i0 + u * kThreads] = v[u];
-  }
+  if (threadIdx.x == 0)
+    asm volatile("fence.acq_rel.gpu;\n\tred.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(ctr), "r"(n) : "memory");
 }
 
 // Copy one column block of a projection (see anvilq_block_columns): `rows`
@@ -193,6 +200,9 @@ __device__ void prefetch_block(uint32_t* wdst, uint32_t* zdst, uint32_t* sdst, c
   for (int i = threadIdx.x; i < nw; i += kThreads) cp16(wdst + 4 * i, wsrc + 4 * i);
   for (int i = threadIdx.x; i < nz; i += kThreads) cp16(zdst + 4 * i, zsrc + 4 * i);
   for (int i = threadIdx.x; i < ns; i += kThreads) cp16(sdst + 4 * i, ssrc + 8 * i);
+}
+__device__ void prefetch_halves(__half* dst, const __half* src, int n) {   // n % 8 == 0
+  for (int i = threadIdx.x; i < n / 8; i += kThreads) cp16(dst + 8 * i, src + 8 * i);
 }
 
 // dst[b][r][e] = src[r][b * block + e]: the column blocks of a row-major matrix
@@ -285,18 +295,41 @@ __device__ uint32_t tile_gemv(const uint32_t* wsm, const __half* xs, const uint3
   return bad;
 }
 
-// x_norm[k] = fp16(x[k] * gamma[k] / sqrt(mean(x^2) + eps)) into shared memory.
-// x: the residual (fp32, L2-coherent loads) or, for layer 0, the embedding row.
-// One pass over x: every thread keeps its (at most kMaxPerThread) values.
+// n floats gathered from a flat index space into shared memory with 8 L2
+// loads in flight per thread: dst[i] = *src(i).
+template <class Src>
+__device__ void stage_flat(float* dst, int n, Src src) {
+  for (int i0 = threadIdx.x; i0 < n; i0 += 8 * kThreads) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = i0 + u * kThreads < n ? __ldcg(src(i0 + u * kThreads)) : 0.0f;
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (i0 + u * kThreads < n) dst[i0 + u * kThreads] = v[u];
+  }
+}
+
+// The residual entering a layer after the first at column k of a 32-column
+// block: x_a of the previous layer plus its down splits added in split order,
+// from values staged as xa[k] and splits[s * 32 + k % 32] of the block.
+__device__ __forceinline__ float residual_sum(float xa, const float* splits, int nsplit, int k) {
+  float acc = 0.0f;
+  for (int s = 0; s < nsplit; ++s) acc += splits[s * 32 + (k & 31)];
+  return xa + acc;
+}
+
+// x_norm[k] = fp16(x[k] * gamma[k] / sqrt(mean(x^2) + eps)) into shared memory,
+// x[k] = val(k) (shared memory or one batch of loads), gamma in shared memory.
+// Every thread keeps its (at most kMaxPerThread) values: one pass over x.
 constexpr int kMaxPerThread = 8;   // H <= 4096
-__device__ void rmsnorm_to_smem(const Params& p, const float* x, const __half* xemb, const __half* gamma,
-                                __half* xs, float* misc) {
+template <class Val>
+__device__ void rmsnorm_to_smem(const Params& p, Val val, const __half* gamma, __half* xs, float* misc) {
   float v[kMaxPerThread];
   float ss = 0.0f;
 #pragma unroll
   for (int u = 0; u < kMaxPerThread; ++u) {
     const int k = threadIdx.x + u * kThreads;
-    v[u] = k < p.H ? (x ? __ldcg(x + k) : __half2float(xemb[k])) : 0.0f;
+    v[u] = k < p.H ? val(k) : 0.0f;
   }
 #pragma unroll
   for (int u = 0; u < kMaxPerThread; ++u) ss = fmaf(v[u], v[u], ss);
@@ -319,8 +352,8 @@ __device__ void rmsnorm_to_smem(const Params& p, const float* x, const __half* x
   __syncthreads();
 }
 
-// sizes of the role-A shared-memory tiles
 __device__ __host__ inline int a_words(int D) { return D / 8; }
+__device__ __host__ inline int kv_stride(int D) { return D + 8; }   // halves; 16-byte rows, no bank conflicts
 
 __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -335,6 +368,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
   const int nb = H / 32;                  // 32-column blocks of H
   const int n_gu = I / 32;                // gate/up units
   const int ngI = I / kG;                 // groups of K = I
+  const int ngH = H / kG;
+  const int KS = kv_stride(D);
   uint32_t bad = 0;
 
   int pos = *p.pos;
@@ -346,6 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
   }
   const int T = pos + 1;                  // attention length
   const int nch = (T + kChunk - 1) / kChunk;
+  const int nu = min(p.nu_max, nch);      // attention units per kv head this token
   const __half* xemb = p.emb + (size_t)token * H;
   if (cta == 0 && tid == 0) {
     if (p.seqlen) *p.seqlen = T;
@@ -355,81 +391,103 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
   // ---- roles of this CTA --------------------------------------------------
   const int roleA = cta < p.n1 ? 1 : cta < p.n1 + p.n2 ? 2 : cta < p.n1 + p.n2 + p.n3 ? 3 : 0;
   const int idxA = roleA == 1 ? cta : roleA == 2 ? cta - p.n1 : cta - p.n1 - p.n2;
+  const int ah = roleA == 2 ? idxA / p.nu_max : 0, au = roleA == 2 ? idxA % p.nu_max : 0;   // kv head, unit
+  const int ac0 = au * nch / nu, ac1 = (au + 1) * nch / nu;                                   // its chunks
+  const bool att_on = roleA == 2 && au < nu;
   const int gu0 = cta, gu1 = cta + P < n_gu ? cta + P : -1;        // gate/up units
   const bool has_down = cta < nb * p.nsplit;
   const int db = cta / p.nsplit, ds = cta % p.nsplit;              // down block and split
   const int dg0 = ds * ngI / p.nsplit, dg1 = (ds + 1) * ngI / p.nsplit;
   const int drow0 = dg0 * kG, drows = (dg1 - dg0) * kG;
 
-  // role-A tile layout (QKV head / attention chunk / O block)
+  // role-A tile layout (QKV head / O block): weights, zeros, scales[, gamma]
   const int wA = roleA == 1 ? a_words(D) : kBW;
   const int rowsA = roleA == 1 ? H : QH * D;
   uint32_t* A_w = reinterpret_cast<uint32_t*>(regA);
   uint32_t* A_z = A_w + rowsA * wA;
   uint32_t* A_s = A_z + ((rowsA + kG - 1) / kG) * wA;
-  __half* Kc = reinterpret_cast<__half*>(regA);                   // attention: [64][D]
-  __half* Vc = Kc + kChunk * D;
-  // gate/up: two units of (gate, up) tiles, each [H][4] + zeros + scales
-  const int guTile = H * kBW + (H / kG) * kBW + (H / kG) * 4 * kBW;   // uint32 per tile
-  auto gu_w = [&](int slot, int which) { return reinterpret_cast<uint32_t*>(regB) + (2 * slot + which) * guTile; };
+  __half* A_gamma = reinterpret_cast<__half*>(A_s + ((rowsA + kG - 1) / kG) * 4 * wA);
+  float* stage = reinterpret_cast<float*>(regA + p.offStage);   // O: partials; attention: PV sums
+  __half* Kc = reinterpret_cast<__half*>(regA);                  // attention: [64][KS]
+  __half* Vc = Kc + kChunk * KS;
+  // gate/up: up to two units, each [H][8 words] + zeros + scales, then gamma_post
+  const int guTile = H * kGU + ngH * kGU + ngH * 4 * kGU;        // uint32 per unit
+  auto gu_w = [&](int slot) { return reinterpret_cast<uint32_t*>(regB) + slot * guTile; };
+  __half* B_gamma = reinterpret_cast<__half*>(gu_w(2));
   uint32_t* C_w = reinterpret_cast<uint32_t*>(regC);
   uint32_t* C_z = C_w + drows * kBW;
   uint32_t* C_s = C_z + (drows / kG) * kBW;
 
+  bool ok = true, misal = false;   // misal: a tensor of the layer table is not 16-byte aligned
+  // a chunk of kv head h: rows t0 .. t0 + cnt - 1 except the current position
+  // (written by this token's QKV phase, read after it)
+  auto copy_chunk = [&](const anvilq_decode_layer& Ly, int h, int c) {
+    const int t0 = c * kChunk, cnt = min(kChunk, T - t0), d8 = D / 8;
+    const __half* kc = reinterpret_cast<const __half*>(Ly.k_cache);
+    const __half* vc = reinterpret_cast<const __half*>(Ly.v_cache);
+    for (int i = tid; i < cnt * d8; i += kThreads) {
+      const int r = i / d8, c8 = i % d8, tok = t0 + r;
+      if (tok == pos) continue;
+      const size_t off = ((size_t)tok * KVH + h) * D + 8 * c8;
+      cp16(Kc + r * KS + 8 * c8, kc + off);
+      cp16(Vc + r * KS + 8 * c8, vc + off);
+    }
+  };
   auto prefetchA = [&](int l) {
     const anvilq_decode_layer& Ly = p.layers[l];
-    if (roleA == 1) {   // column block idxA (one head) of the blocked QKV projection
-      const int wd = a_words(D), ng = H / kG;
-      prefetch_block(A_w, A_z, A_s, Ly.qkv_qweight + (size_t)idxA * H * wd, Ly.qkv_qzeros + (size_t)idxA * ng * wd,
-                     reinterpret_cast<const __half*>(Ly.qkv_scales) + (size_t)idxA * ng * 8 * wd, H, wd, ng);
-    } else if (roleA == 2) {
-      // the first chunk this CTA owns: rows before the current position only
-      const int u = idxA;
-      if (u < KVH * nch) {
-        const int h = u % KVH, c = u / KVH, t0 = c * kChunk, cnt = min(kChunk, T - t0);
-        const int d8 = D / 8;
-        const __half* kc = reinterpret_cast<const __half*>(Ly.k_cache);
-        const __half* vc = reinterpret_cast<const __half*>(Ly.v_cache);
-        for (int i = tid; i < cnt * d8; i += kThreads) {
-          const int r = i / d8, c8 = i % d8, tok = t0 + r;
-          if (tok == pos) continue;   // written by this token's QKV phase; read after it
-          const size_t off = ((size_t)tok * KVH + h) * D + 8 * c8;
-          cp16(Kc + r * D + 8 * c8, kc + off);
-          cp16(Vc + r * D + 8 * c8, vc + off);
-        }
+    if (roleA == 1) {   // column block idxA (one head) of the blocked QKV projection, and gamma_in
+      const int wd = a_words(D);
+      if (misaligned16(Ly.qkv_qweight) || misaligned16(Ly.qkv_qzeros) || misaligned16(Ly.qkv_scales) ||
+          misaligned16(Ly.gamma_in) || misaligned16(Ly.k_cache) || misaligned16(Ly.v_cache)) {
+        misal = true, ok = false;
+      } else {
+        prefetch_block(A_w, A_z, A_s, Ly.qkv_qweight + (size_t)idxA * H * wd, Ly.qkv_qzeros + (size_t)idxA * ngH * wd,
+                       reinterpret_cast<const __half*>(Ly.qkv_scales) + (size_t)idxA * ngH * 8 * wd, H, wd, ngH);
+        prefetch_halves(A_gamma, reinterpret_cast<const __half*>(Ly.gamma_in), H);
       }
+    } else if (att_on) {   // the unit's first chunk
+      if (misaligned16(Ly.k_cache) || misaligned16(Ly.v_cache)) misal = true, ok = false;
+      else copy_chunk(Ly, ah, ac0);
     } else if (roleA == 3) {   // column block idxA of the blocked O projection
       const int K = QH * D, ng = K / kG;
-      prefetch_block(A_w, A_z, A_s, Ly.o_qweight + (size_t)idxA * K * kBW, Ly.o_qzeros + (size_t)idxA * ng * kBW,
-                     reinterpret_cast<const __half*>(Ly.o_scales) + (size_t)idxA * ng * 8 * kBW, K, kBW, ng);
+      if (misaligned16(Ly.o_qweight) || misaligned16(Ly.o_qzeros) || misaligned16(Ly.o_scales)) misal = true, ok = false;
+      else
+        prefetch_block(A_w, A_z, A_s, Ly.o_qweight + (size_t)idxA * K * kBW, Ly.o_qzeros + (size_t)idxA * ng * kBW,
+                       reinterpret_cast<const __half*>(Ly.o_scales) + (size_t)idxA * ng * 8 * kBW, K, kBW, ng);
     }
     cp_commit();
   };
   auto prefetchB = [&](int l) {
     const anvilq_decode_layer& Ly = p.layers[l];
-    const int units[2] = {gu0, gu1};
-    for (int sl = 0; sl < 2; ++sl) {
-      const int u = units[sl];
-      if (u < 0 || u >= n_gu) continue;
-      for (int which = 0; which < 2; ++which) {   // column blocks u (gate) and I / 32 + u (up)
-        uint32_t* w = gu_w(sl, which);
-        const size_t b = (size_t)(which ? n_gu : 0) + u;
-        const int ng = H / kG;
-        prefetch_block(w, w + H * kBW, w + H * kBW + ng * kBW, Ly.gu_qweight + b * H * kBW,
-                       Ly.gu_qzeros + b * ng * kBW, reinterpret_cast<const __half*>(Ly.gu_scales) + b * ng * 8 * kBW,
-                       H, kBW, ng);
+    if (misaligned16(Ly.gu_qweight) || misaligned16(Ly.gu_qzeros) || misaligned16(Ly.gu_scales) ||
+        misaligned16(Ly.gamma_post)) {
+      misal = true, ok = false;
+    } else {
+      const int units[2] = {gu0, gu1};
+      for (int sl = 0; sl < 2; ++sl) {
+        const int u = units[sl];
+        if (u < 0 || u >= n_gu) continue;
+        uint32_t* w = gu_w(sl);
+        prefetch_block(w, w + H * kGU, w + H * kGU + ngH * kGU, Ly.gu_qweight + (size_t)u * H * kGU,
+                       Ly.gu_qzeros + (size_t)u * ngH * kGU,
+                       reinterpret_cast<const __half*>(Ly.gu_scales) + (size_t)u * ngH * 8 * kGU, H, kGU, ngH);
       }
+      prefetch_halves(B_gamma, reinterpret_cast<const __half*>(Ly.gamma_post), H);
     }
     cp_commit();
   };
   auto prefetchC = [&](int l) {
     if (has_down) {
       const anvilq_decode_layer& Ly = p.layers[l];
-      // rows [drow0, drow0 + drows) of column block db of the blocked down projection
-      prefetch_block(C_w, C_z, C_s, Ly.down_qweight + ((size_t)db * I + drow0) * kBW,
-                     Ly.down_qzeros + ((size_t)db * ngI + dg0) * kBW,
-                     reinterpret_cast<const __half*>(Ly.down_scales) + ((size_t)db * ngI + dg0) * 8 * kBW, drows, kBW,
-                     dg1 - dg0);
+      if (misaligned16(Ly.down_qweight) || misaligned16(Ly.down_qzeros) || misaligned16(Ly.down_scales)) {
+        misal = true, ok = false;
+      } else {
+        // rows [drow0, drow0 + drows) of column block db of the blocked down projection
+        prefetch_block(C_w, C_z, C_s, Ly.down_qweight + ((size_t)db * I + drow0) * kBW,
+                       Ly.down_qzeros + ((size_t)db * ngI + dg0) * kBW,
+                       reinterpret_cast<const __half*>(Ly.down_scales) + ((size_t)db * ngI + dg0) * 8 * kBW, drows,
+                       kBW, dg1 - dg0);
+      }
     }
     cp_commit();
   };
@@ -437,20 +495,25 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
   prefetchB(0);
   prefetchC(0);
 
-  bool ok = true;
   for (int l = 0; l < p.L && ok; ++l) {
     const anvilq_decode_layer& Ly = p.layers[l];
     int* ctr = p.ctr + l * kPhases;
-    const float* x_in = l == 0 ? nullptr : p.xbuf + (l & 1) * H;   // null: the embedding row
-    float* x_next = l == p.L - 1 ? p.x_out : p.xbuf + ((l + 1) & 1) * H;
 
     // ---- role A --------------------------------------------------------------
     cp_wait2();
     __syncthreads();
     if (roleA == 1) {   // QKV head idxA: rmsnorm -> GEMV -> bias -> RoPE -> q / cache
-      if (l > 0 && !(ok = wait_count(p, p.ctr + (l - 1) * kPhases + 4, nb))) break;
-      rmsnorm_to_smem(p, x_in, xemb, reinterpret_cast<const __half*>(Ly.gamma_in), xs, misc);
-      float* y = misc + 32;
+      if (l > 0) {   // x_a and every down split of the previous layer: one batch of loads
+        if (!(ok = wait_count(p, p.ctr + (l - 1) * kPhases + 4, nb * p.nsplit))) break;
+        stage_flat(stage, H * (p.nsplit + 1), [&](int i) { return i < H ? p.xa + i : p.dpart + (i - H); });
+        __syncthreads();
+        rmsnorm_to_smem(
+            p, [&](int k) { return residual_sum(stage[k], stage + H + (k >> 5) * p.nsplit * 32, p.nsplit, k); },
+            A_gamma, xs, misc);
+      } else {
+        rmsnorm_to_smem(p, [&](int k) { return __half2float(xemb[k]); }, A_gamma, xs, misc);
+      }
+      float* y = misc + kMiscY;
       bad |= D == 64 ? tile_gemv<8>(A_w, xs, A_z, A_s, H, 0, red, y) : tile_gemv<16>(A_w, xs, A_z, A_s, H, 0, red, y);
       const int head = idxA, hd = D / 2;
       const __half* bias = reinterpret_cast<const __half*>(Ly.qkv_bias);
@@ -479,139 +542,173 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
         }
       }
       publish(ctr + 0, 1);
-    } else if (roleA == 2) {   // attention chunks u = idxA, idxA + n2, ...
+    } else if (att_on) {   // kv head ah, chunks [ac0, ac1): online softmax, unnormalised partial out
       if (!(ok = wait_count(p, ctr + 0, QH + 2 * KVH))) break;
-      for (int u = idxA, first = 1; u < KVH * nch; u += p.n2, first = 0) {
-        const int h = u % KVH, c = u / KVH, t0 = c * kChunk, cnt = min(kChunk, T - t0);
-        const __half* kc = reinterpret_cast<const __half*>(Ly.k_cache);
-        const __half* vc = reinterpret_cast<const __half*>(Ly.v_cache);
-        const int d8 = D / 8;
-        if (!first) {   // later chunks of this CTA: copied now
-          for (int i = tid; i < cnt * d8; i += kThreads) {
-            const int r = i / d8, c8 = i % d8, tok = t0 + r;
-            if (tok == pos) continue;
-            const size_t off = ((size_t)tok * KVH + h) * D + 8 * c8;
-            cp16(Kc + r * D + 8 * c8, kc + off);
-            cp16(Vc + r * D + 8 * c8, vc + off);
-          }
+      const int h = ah;
+      const __half* kc = reinterpret_cast<const __half*>(Ly.k_cache);
+      const __half* vc = reinterpret_cast<const __half*>(Ly.v_cache);
+      float* qs = misc + kAttQs;
+      float* Pp = misc + kAttP;
+      float* wmax = misc + kAttWmax;
+      float* wsum = misc + kAttWsum;
+      float* mbuf = misc + kAttM;
+      float* lrun = misc + kAttL;
+      const float qscale = 1.4426950408889634f / sqrtf((float)D);   // log2(e) / sqrt(D)
+      const int lane = tid & 31, warp = tid >> 5;
+      const int sj = warp >> 1, srh = warp & 1;                      // scores: head, row half
+      const int pairs = D / 2, nrg = kThreads / pairs, rpg = kChunk / nrg;
+      const int dp = tid % pairs, rg = tid / pairs;                  // PV: dim pair, row group
+      float O[2] = {0.0f, 0.0f};
+      for (int c = ac0; c < ac1; ++c) {
+        const int t0 = c * kChunk, cnt = min(kChunk, T - t0), ci = c - ac0;
+        if (c != ac0) {   // later chunks of the range: copied now
+          __syncthreads();
+          copy_chunk(Ly, h, c);
           cp_commit();
           cp_wait0();
-        }
-        if (pos >= t0 && pos < t0 + cnt) {   // this token's row, written by the QKV phase
-          for (int i = tid; i < d8; i += kThreads) {
-            const size_t off = ((size_t)pos * KVH + h) * D + 8 * i;
-            *reinterpret_cast<uint4*>(Kc + (pos - t0) * D + 8 * i) = __ldcg(reinterpret_cast<const uint4*>(kc + off));
-            *reinterpret_cast<uint4*>(Vc + (pos - t0) * D + 8 * i) = __ldcg(reinterpret_cast<const uint4*>(vc + off));
+        } else {          // q of the group, scaled, as fp32 (one batch with the current row below)
+          for (int i = tid; i < grp * D; i += kThreads)   // grp * D <= 1024
+            qs[i] = __half2float(__ldcg(p.q + (size_t)h * grp * D + i)) * qscale;
+          if (tid < grp) {
+            mbuf[tid] = -INFINITY;
+            lrun[tid] = 0.0f;
           }
         }
-        // q of the group, scaled by log2(e) / sqrt(D), as fp32 in shared memory
-        float* qs = misc + 32;                     // [grp][D]
-        float* sc = qs + kMaxGroup * kMaxD;         // [grp][64] scores, then probabilities
-        const float qscale = 1.4426950408889634f / sqrtf((float)D);
-        for (int i = tid; i < grp * D; i += kThreads)   // grp * D <= 1024: two loads per thread at most
-          qs[i] = __half2float(__ldcg(p.q + (size_t)h * grp * D + i)) * qscale;
+        if (pos >= t0 && pos < t0 + cnt)   // this token's row, written by the QKV phase
+          for (int i = tid; i < 2 * (D / 8); i += kThreads) {
+            const int which = i / (D / 8), e = i % (D / 8);
+            const size_t off = ((size_t)pos * KVH + h) * D + 8 * e;
+            *reinterpret_cast<uint4*>((which ? Vc : Kc) + (pos - t0) * KS + 8 * e) =
+                __ldcg(reinterpret_cast<const uint4*>((which ? vc : kc) + off));
+          }
         __syncthreads();
-        // scores: warp w takes rows w, w + 16, ...; lanes split the head dim
-        const int lane = tid & 31, warp = tid >> 5;
-        for (int r = warp; r < kChunk; r += kWarps) {
-          float part[kMaxGroup];
-#pragma unroll
-          for (int j = 0; j < kMaxGroup; ++j) part[j] = 0.0f;
+        // scores: warp (head sj, rows srh*32 + lane); 16-byte K loads, q broadcast
+        const int r = srh * 32 + lane;
+        float sc = -INFINITY;
+        if (sj < grp) {
           if (r < cnt) {
-            for (int d = 2 * lane; d < D; d += 64) {
-              const float2 kv = __half22float2(*reinterpret_cast<const half2*>(Kc + r * D + d));
+            const __half* kr = Kc + r * KS;
+            const float* qj = qs + sj * D;
+            float acc = 0.0f;
+            for (int d = 0; d < D; d += 8) {
+              const uint4 kv = *reinterpret_cast<const uint4*>(kr + d);
+              const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
-              for (int j = 0; j < kMaxGroup; ++j)
-                if (j < grp) part[j] = fmaf(qs[j * D + d + 1], kv.y, fmaf(qs[j * D + d], kv.x, part[j]));
+              for (int e = 0; e < 4; ++e) {
+                const float2 k2 = __half22float2(h2(kw[e]));
+                acc = fmaf(qj[d + 2 * e], k2.x, acc);
+                acc = fmaf(qj[d + 2 * e + 1], k2.y, acc);
+              }
             }
+            sc = acc;
           }
-#pragma unroll
-          for (int j = 0; j < kMaxGroup; ++j) {
-            float v = part[j];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0 && j < grp) sc[j * kChunk + r] = r < cnt ? v : -INFINITY;
-          }
-        }
-        __syncthreads();
-        // per head: max, exp2, sum over the chunk (warp j)
-        float* ml = sc + kMaxGroup * kChunk;        // [grp][2]
-        if (warp < grp) {
-          const float a = sc[warp * kChunk + lane], b = sc[warp * kChunk + lane + 32];
-          float m = fmaxf(a, b);
+          float m = sc;
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-          const float pa = lane < cnt ? exp2f(a - m) : 0.0f, pb = lane + 32 < cnt ? exp2f(b - m) : 0.0f;
-          sc[warp * kChunk + lane] = pa;
-          sc[warp * kChunk + lane + 32] = pb;
-          float s = pa + pb;
+          if (lane == 0) wmax[2 * sj + srh] = m;
+        }
+        __syncthreads();
+        float* mold = mbuf + (ci & 1) * kMaxGroup;
+        float* mnew = mbuf + ((ci + 1) & 1) * kMaxGroup;
+        if (sj < grp) {
+          const float mn = fmaxf(mold[sj], fmaxf(wmax[2 * sj], wmax[2 * sj + 1]));
+          const float pr = r < cnt ? exp2f(sc - mn) : 0.0f;
+          Pp[sj * kChunk + r] = pr;
+          float s = pr;
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
           if (lane == 0) {
-            ml[2 * warp] = m;
-            ml[2 * warp + 1] = s;
+            wsum[2 * sj + srh] = s;
+            if (srh == 0) mnew[sj] = mn;
           }
         }
         __syncthreads();
-        float* part_out = p.apart + ((size_t)(h * p.maxch + c) * grp) * (D + 2);
-        for (int i = tid; i < grp * D; i += kThreads) {
-          const int j = i / D, d = i % D;
-          float o = 0.0f;
-          for (int r = 0; r < cnt; ++r) o = fmaf(sc[j * kChunk + r], __half2float(Vc[r * D + d]), o);
-          __stcg(part_out + j * (D + 2) + 2 + d, o);
-        }
-        if (tid < grp) {
-          __stcg(part_out + tid * (D + 2), ml[2 * tid]);
-          __stcg(part_out + tid * (D + 2) + 1, ml[2 * tid + 1]);
-        }
-        // the last chunk of kv head h to arrive merges the chunks in chunk order
-        if (last_arrival(p.aticket + l * KVH + h, nch)) {
-          // every chunk's (m, l, o) of this head, loaded at once into shared
-          // memory (the K / V tiles are no longer needed), in batches that fit
-          float* st = reinterpret_cast<float*>(regA);
-          const int per_chunk = grp * (D + 2);
-          const int batch = max(1, (int)(p.regA_bytes / (per_chunk * 4)));
-          float M[2], Ls[2], O[2];
-          for (int k = 0; k < 2; ++k) M[k] = -INFINITY, Ls[k] = O[k] = 0.0f;
-          for (int c0 = 0; c0 < nch; c0 += batch) {
-            const int nb_ = min(batch, nch - c0);
-            stage_floats(st, p.apart + (size_t)(h * p.maxch + c0) * per_chunk, nb_ * per_chunk);
-            __syncthreads();
-            for (int k = 0; k < 2; ++k) {   // (head, dim) pairs tid and tid + 512 (grp * D <= 1024)
-              const int i = tid + k * kThreads;
-              if (i >= grp * D) continue;
-              const int j = i / D, d = i % D;
-              for (int cc = 0; cc < nb_; ++cc) {   // online merge in chunk order
-                const float* pc = st + cc * per_chunk + j * (D + 2);
-                const float m = pc[0];
-                const float mn = fmaxf(M[k], m);
-                const float a = exp2f(M[k] - mn), b = exp2f(m - mn);
-                Ls[k] = fmaf(Ls[k], a, pc[1] * b);
-                O[k] = fmaf(O[k], a, pc[2 + d] * b);
-                M[k] = mn;
+        // P V: thread (row group rg, dims 2 dp, 2 dp + 1) over its rows, all heads
+        float acc[kMaxGroup][2];
+#pragma unroll
+        for (int j = 0; j < kMaxGroup; ++j) acc[j][0] = acc[j][1] = 0.0f;
+        for (int i = 0; i < rpg; ++i) {
+          const int rr = rg * rpg + i;
+          if (rr < cnt) {
+            const float2 v2 = __half22float2(*reinterpret_cast<const half2*>(Vc + rr * KS + 2 * dp));
+#pragma unroll
+            for (int j = 0; j < kMaxGroup; ++j)
+              if (j < grp) {
+                const float pj = Pp[j * kChunk + rr];
+                acc[j][0] = fmaf(pj, v2.x, acc[j][0]);
+                acc[j][1] = fmaf(pj, v2.y, acc[j][1]);
               }
-            }
-            __syncthreads();
           }
-          for (int k = 0; k < 2; ++k) {
-            const int i = tid + k * kThreads;
-            if (i < grp * D) p.attn[(size_t)h * grp * D + i] = __float2half_rn(O[k] / Ls[k]);
-          }
-          publish(ctr + 1, 1);
         }
+#pragma unroll
+        for (int j = 0; j < kMaxGroup; ++j)
+          if (j < grp)
+            *reinterpret_cast<float2*>(stage + (rg * grp + j) * D + 2 * dp) = make_float2(acc[j][0], acc[j][1]);
         __syncthreads();
+        for (int k = 0; k < 2; ++k) {   // (head, dim) pairs tid and tid + 512 (grp * D <= 1024)
+          const int i = tid + k * kThreads;
+          if (i >= grp * D) continue;
+          const int j = i / D, d = i % D;
+          float s = 0.0f;
+          for (int g2 = 0; g2 < nrg; ++g2) s += stage[(g2 * grp + j) * D + d];   // in row-group order
+          O[k] = fmaf(O[k], exp2f(mold[j] - mnew[j]), s);
+        }
+        if (tid < grp) lrun[tid] = fmaf(lrun[tid], exp2f(mold[tid] - mnew[tid]), wsum[2 * tid] + wsum[2 * tid + 1]);
       }
-    } else if (roleA == 3) {   // O block idxA: x_a = x + attn W_o
-      if (!(ok = wait_count(p, ctr + 1, KVH))) break;
-      for (int i = tid; i < QH * D / 8; i += kThreads)
-        reinterpret_cast<uint4*>(xs)[i] = __ldcg(reinterpret_cast<const uint4*>(p.attn) + i);
+      const float* mfin = mbuf + ((ac1 - ac0) & 1) * kMaxGroup;
+      float* part_out = p.apart + (size_t)(h * p.nu_max + au) * grp * (D + 2);
+      for (int k = 0; k < 2; ++k) {
+        const int i = tid + k * kThreads;
+        if (i < grp * D) __stcg(part_out + (i / D) * (D + 2) + 2 + i % D, O[k]);
+      }
+      if (tid < grp) {
+        __stcg(part_out + tid * (D + 2), mfin[tid]);
+        __stcg(part_out + tid * (D + 2) + 1, lrun[tid]);
+      }
+      publish(ctr + 1, 1);
+    } else if (roleA == 3) {   // O block idxA: merge the partials, x_a = x + attn W_o
+      if (!(ok = wait_count(p, ctr + 1, KVH * nu))) break;
+      const int per = grp * (D + 2), unit = nu * per, n = KVH * unit;
+      float* ew = misc + kMiscBig;      // [QH][nu] merge weights
+      float* Ls = ew + QH * nu;         // [QH]
+      // every unit's (m, l, o), then this block's x_a and down splits: one batch of loads
+      const int nres = l > 0 ? 32 * (p.nsplit + 1) : 0;
+      const float* dsrc = p.dpart + (size_t)idxA * p.nsplit * 32;
+      stage_flat(stage, n + nres, [&](int i) {
+        return i < n ? p.apart + (size_t)(i / unit) * p.nu_max * per + i % unit
+                     : i < n + 32 ? p.xa + idxA * 32 + (i - n) : dsrc + (i - n - 32);
+      });
       __syncthreads();
-      float* y = misc + 32;
+      // per q head: M = max m_u, e_u = 2^(m_u - M), L = sum l_u e_u (warp per head, lane per unit)
+      const int lane = tid & 31, warp = tid >> 5;
+      for (int jj = warp; jj < QH; jj += kWarps) {
+        const float* pc = stage + (size_t)(jj / grp) * unit + min(lane, nu - 1) * per + (jj % grp) * (D + 2);
+        const float m = lane < nu ? pc[0] : -INFINITY;
+        float M = m;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        const float e = lane < nu ? exp2f(m - M) : 0.0f;
+        float s = lane < nu ? pc[1] * e : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane < nu) ew[jj * nu + lane] = e;
+        if (lane == 0) Ls[jj] = s;
+      }
+      __syncthreads();
+      for (int i = tid; i < QH * D; i += kThreads) {
+        const int jj = i / D, d = i % D;
+        const float* pc = stage + (size_t)(jj / grp) * unit + (jj % grp) * (D + 2) + 2 + d;
+        float acc = 0.0f;
+        for (int u = 0; u < nu; ++u) acc = fmaf(ew[jj * nu + u], pc[u * per], acc);   // in unit order
+        xs[i] = __float2half_rn(acc / Ls[jj]);
+      }
+      __syncthreads();
+      float* y = misc + kMiscY;
       bad |= tile_gemv<kBW>(A_w, xs, A_z, A_s, QH * D, 0, red, y);
       if (tid < 32) {
-        const int col = idxA * 32 + tid;
-        const float xin = x_in ? __ldcg(x_in + col) : __half2float(xemb[col]);
-        p.xa[col] = xin + y[tid];
+        const int k = idxA * 32 + tid;
+        const float x = l > 0 ? residual_sum(stage[n + tid], stage + n + 32, p.nsplit, k) : __half2float(xemb[k]);
+        p.xa[k] = x + y[tid];
       }
       publish(ctr + 2, 1);
     }
@@ -622,20 +719,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     // ---- role B: gate/up -----------------------------------------------------
     cp_wait2();
     __syncthreads();
-    if (!(ok = wait_count(p, ctr + 2, nb))) break;
-    rmsnorm_to_smem(p, p.xa, nullptr, reinterpret_cast<const __half*>(Ly.gamma_post), xs, misc);
+    if (!(ok = ok && wait_count(p, ctr + 2, nb))) break;
+    rmsnorm_to_smem(p, [&](int k) { return __ldcg(p.xa + k); }, B_gamma, xs, misc);
     int produced = 0;
     for (int sl = 0; sl < 2; ++sl) {
       const int u = sl == 0 ? gu0 : gu1;
       if (u < 0 || u >= n_gu) continue;
-      float* g = misc + 32;
-      float* up = g + 32;
-      uint32_t* wg = gu_w(sl, 0);
-      uint32_t* wu = gu_w(sl, 1);
-      bad |= tile_gemv<kBW>(wg, xs, wg + H * kBW, wg + H * kBW + (H / kG) * kBW, H, 0, red, g);
-      bad |= tile_gemv<kBW>(wu, xs, wu + H * kBW, wu + H * kBW + (H / kG) * kBW, H, 0, red, up);
+      float* g = misc + kMiscY;   // g[0:32] gate, g[32:64] up
+      uint32_t* w = gu_w(sl);
+      bad |= tile_gemv<kGU>(w, xs, w + H * kGU, w + H * kGU + ngH * kGU, H, 0, red, g);
       if (tid < 32) {
-        const float gh = __half2float(__float2half_rn(g[tid])), uh = __half2float(__float2half_rn(up[tid]));
+        const float gh = __half2float(__float2half_rn(g[tid])), uh = __half2float(__float2half_rn(g[32 + tid]));
         const float e = expf(-fabsf(gh));   // stable silu (official_weights.py:494-499)
         const float sg = gh >= 0.0f ? gh / (1.0f + e) : (gh * e) / (1.0f + e);
         p.act[u * 32 + tid] = __float2half_rn(sg * uh);
@@ -647,48 +741,43 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     if (l + 1 < p.L) prefetchB(l + 1);
     else cp_commit();
 
-    // ---- role C: down + residual ----------------------------------------------
+    // ---- role C: down split --------------------------------------------------
     cp_wait2();
     __syncthreads();
     if (has_down) {
-      if (!(ok = wait_count(p, ctr + 3, n_gu))) break;
+      if (!(ok = ok && wait_count(p, ctr + 3, n_gu))) break;
       for (int i = tid; i < drows / 8; i += kThreads)
         reinterpret_cast<uint4*>(xs)[i] = __ldcg(reinterpret_cast<const uint4*>(p.act + drow0) + i);
       __syncthreads();
-      float* y = misc + 32;
+      float* y = misc + kMiscY;
       bad |= tile_gemv<kBW>(C_w, xs, C_z, C_s, drows, drow0, red, y);
       if (tid < 32) __stcg(p.dpart + ((size_t)db * p.nsplit + ds) * 32 + tid, y[tid]);
-      if (last_arrival(p.dticket + l * nb + db, p.nsplit)) {
-        float* st = misc + 32;   // [nsplit][32], every split loaded at once
-        stage_floats(st, p.dpart + (size_t)db * p.nsplit * 32, p.nsplit * 32);
-        __syncthreads();
-        if (tid < 32) {
-          float acc = 0.0f;
-          for (int s2 = 0; s2 < p.nsplit; ++s2) acc += st[s2 * 32 + tid];   // in split order
-          const int col = db * 32 + tid;
-          x_next[col] = __ldcg(p.xa + col) + acc;
-        }
-        publish(ctr + 4, 1);
-      }
+      publish(ctr + 4, 1);
     }
     __syncthreads();
     if (l + 1 < p.L) prefetchC(l + 1);
     else cp_commit();
   }
   cp_wait0();
+  if (!ok) abort_launch(p, misal ? ANVILQ_DEV_ERR_ALIGN : 0);   // a misaligned tensor or a wait that gave up
+  // ---- the residual after the last layer: column block cta ---------------------
+  if (ok && cta < nb && wait_count(p, p.ctr + (p.L - 1) * kPhases + 4, nb * p.nsplit) && tid < 32) {
+    const int k = cta * 32 + tid;
+    float acc = 0.0f;
+    for (int s = 0; s < p.nsplit; ++s) acc += __ldcg(p.dpart + ((size_t)cta * p.nsplit + s) * 32 + tid);
+    p.x_out[k] = __ldcg(p.xa + k) + acc;
+  }
   if (bad && p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_SCALE);
 
   // ---- exit: the last CTA out re-arms every counter for the next launch ------
-  __threadfence();
   __syncthreads();
   if (tid == 0) {
+    __threadfence();
     __shared__ int s_exit;
     s_exit = atomicAdd(p.exit_ctr, 1) == P - 1;
     if (s_exit) {
       __threadfence();
       for (int i = 0; i < p.L * kPhases; ++i) p.ctr[i] = 0;
-      for (int i = 0; i < p.L * KVH; ++i) p.aticket[i] = 0;
-      for (int i = 0; i < p.L * nb; ++i) p.dticket[i] = 0;
       *p.abort_flag = 0;
       __threadfence();
       *p.exit_ctr = 0;
@@ -698,11 +787,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
 
 // ---------------------------------------------------------------------------
 struct Plan {
-  int P, n1, n2, n3, nsplit, maxch;
-  int offA, offB, offC, offX, offRed, offMisc, smem;
+  int P, n1, n2, n3, nsplit, nu_max;
+  int offA, offB, offC, offX, offRed, offMisc, offStage, smem;
   size_t ws_bytes;
-  size_t off_xbuf, off_xa, off_q, off_apart, off_attn, off_act, off_dpart, off_ctr, off_at, off_dt, off_exit,
-      off_abort;
+  size_t off_xa, off_q, off_apart, off_act, off_dpart, off_ctr, off_exit, off_abort;
 };
 
 constexpr int kMaxDevices = 64;
@@ -721,6 +809,7 @@ static int sm_count() {
 }
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+constexpr size_t kSmemLimit = 220 * 1024;
 
 // ANVILQ_OK and the plan, or the status that rejects the shape.
 static int make_plan(int L, int H, int I, int QH, int KVH, int D, int G, int Tmax, Plan* pl) {
@@ -731,34 +820,49 @@ static int make_plan(int L, int H, int I, int QH, int KVH, int D, int G, int Tma
   const int P = sm_count();
   if (P <= 0) return ANVILQ_ECUDA;
   pl->P = P;
-  const int nb = H / 32, ngI = I / kG;
+  const int nb = H / 32, ngI = I / kG, ngH = H / kG, grp = QH / KVH;
   pl->n1 = QH + 2 * KVH;
   pl->n3 = nb;
-  pl->maxch = (Tmax + kChunk - 1) / kChunk;
-  pl->n2 = std::min(KVH * pl->maxch, P - pl->n1 - pl->n3);
-  if (pl->n2 < 1) return ANVILQ_ESHAPE;
-  pl->nsplit = std::min(std::min(P / nb, ngI), 48);   // the fix-up stages nsplit x 32 floats in `misc`
-  if (pl->nsplit < 1 || (I / 32 + P - 1) / P > 2) return ANVILQ_ESHAPE;
-  // shared memory
-  const size_t qkvA = (size_t)H * (D / 8) * 4 + (H / kG) * (D / 8) * 4 + (H / kG) * D * 2;
-  const size_t attA = (size_t)2 * kChunk * D * 2;
-  const size_t oA = (size_t)QH * D * kBW * 4 + (QH * D / kG) * kBW * 4 + (QH * D / kG) * 32 * 2;
-  const size_t regA = align_up(std::max(qkvA, std::max(attA, oA)), 128);
-  const size_t guTile = ((size_t)H * kBW + (H / kG) * kBW + (H / kG) * 4 * kBW) * 4;
-  const size_t regB = align_up(4 * guTile, 128);
+  pl->nsplit = std::min(std::min(P / nb, ngI), kMaxSplit);
+  if (pl->nsplit < 1 || (I / 32 + P - 1) / P > 2 || pl->n1 + pl->n3 + KVH > P) return ANVILQ_ESHAPE;
+  // shared memory other than region A
+  const size_t guTile = ((size_t)H * kGU + ngH * kGU + ngH * 4 * kGU) * 4;
+  const size_t regB = align_up(2 * guTile + (size_t)H * 2, 128);
   const int maxdg = (ngI + pl->nsplit - 1) / pl->nsplit;
   const size_t regC = align_up((size_t)maxdg * kG * kBW * 4 + maxdg * kBW * 4 + maxdg * 32 * 2, 128);
   const size_t xsB = align_up((size_t)std::max(std::max(H, QH * D), maxdg * kG) * 2, 128);
   const size_t redB = align_up((size_t)kWarps * 8 * 16 * 4, 128);
-  const size_t miscB = align_up((size_t)(32 + kMaxGroup * kMaxD + kMaxGroup * kChunk + 2 * kMaxGroup) * 4, 128);
+  // region A: the role's tile (QKV head + gamma, attention chunk, O block),
+  // then from offStage the role's staged inputs (QKV: x_a and the down splits;
+  // O: the partials of every unit, x_a and the splits of its block) or the
+  // attention's P V sums
+  const size_t qkvA = align_up((size_t)H * (D / 8) * 4 + ngH * (D / 8) * 4 + ngH * D * 2 + (size_t)H * 2, 128);
+  const size_t attKV = align_up((size_t)2 * kChunk * kv_stride(D) * 2, 128);
+  const size_t attPV = (size_t)kThreads * 2 * grp * 4;          // [512 / (D/2)][grp][D] floats
+  const size_t oW = align_up((size_t)QH * D * kBW * 4 + (QH * D / kG) * kBW * 4 + (QH * D / kG) * 32 * 2, 128);
+  const size_t unitB = (size_t)KVH * grp * (D + 2) * 4;         // staged bytes per unit index
+  const size_t offStage = std::max(qkvA, std::max(attKV, oW));
+  const size_t qkvStage = (size_t)H * (pl->nsplit + 1) * 4, oRes = (size_t)32 * (pl->nsplit + 1) * 4;
+  const size_t fixed = regB + regC + xsB + redB;
+  auto regA_bytes = [&](int u) {
+    return align_up(offStage + std::max(std::max(qkvStage, attPV), (size_t)u * unitB + oRes), 128);
+  };
+  auto misc_bytes = [&](int u) { return align_up((size_t)std::max(kAttEnd, kMiscBig + QH * (u + 1)) * 4, 128); };
+  // units per kv head: the spare CTAs, at most one per chunk, and what region A can stage
+  int nu = std::min((P - pl->n1 - pl->n3) / KVH, std::min(kMaxUnits, (Tmax + kChunk - 1) / kChunk));
+  while (nu > 1 && regA_bytes(nu) + fixed + misc_bytes(nu) > kSmemLimit) --nu;
+  if (nu < 1 || regA_bytes(nu) + fixed + misc_bytes(nu) > kSmemLimit) return ANVILQ_ESHAPE;   // must fit one SM
+  pl->nu_max = nu;
+  pl->n2 = KVH * nu;
+  const size_t regA = regA_bytes(nu);
   pl->offA = 0;
+  pl->offStage = (int)offStage;
   pl->offB = (int)regA;
   pl->offC = (int)(regA + regB);
   pl->offX = (int)(regA + regB + regC);
   pl->offRed = pl->offX + (int)xsB;
   pl->offMisc = pl->offRed + (int)redB;
-  pl->smem = pl->offMisc + (int)miscB;
-  if (pl->smem > 220 * 1024) return ANVILQ_ESHAPE;   // a layer's slices must fit one SM's shared memory
+  pl->smem = pl->offMisc + (int)misc_bytes(nu);
   // workspace
   size_t o = 0;
   auto take = [&](size_t bytes) {
@@ -767,15 +871,11 @@ static int make_plan(int L, int H, int I, int QH, int KVH, int D, int G, int Tma
     return at;
   };
   pl->off_ctr = take((size_t)L * kPhases * 4);
-  pl->off_at = take((size_t)L * KVH * 4);
-  pl->off_dt = take((size_t)L * nb * 4);
   pl->off_exit = take(4);
   pl->off_abort = take(4);
-  pl->off_xbuf = take((size_t)2 * H * 4);
   pl->off_xa = take((size_t)H * 4);
   pl->off_q = take((size_t)QH * D * 2);
-  pl->off_apart = take((size_t)KVH * pl->maxch * (QH / KVH) * (D + 2) * 4);
-  pl->off_attn = take((size_t)QH * D * 2);
+  pl->off_apart = take((size_t)KVH * nu * grp * (D + 2) * 4);
   pl->off_act = take((size_t)I * 2);
   pl->off_dpart = take((size_t)nb * pl->nsplit * 32 * 4);
   pl->ws_bytes = o;
@@ -818,21 +918,16 @@ extern "C" int anvilq_decode_layers(const anvilq_decode_layer* layers, int L, in
   p.dev_err = dev_err;
   char* w = static_cast<char*>(workspace);
   p.ctr = reinterpret_cast<int*>(w + pl.off_ctr);
-  p.aticket = reinterpret_cast<int*>(w + pl.off_at);
-  p.dticket = reinterpret_cast<int*>(w + pl.off_dt);
   p.exit_ctr = reinterpret_cast<int*>(w + pl.off_exit);
   p.abort_flag = reinterpret_cast<int*>(w + pl.off_abort);
-  p.xbuf = reinterpret_cast<float*>(w + pl.off_xbuf);
   p.xa = reinterpret_cast<float*>(w + pl.off_xa);
   p.q = reinterpret_cast<__half*>(w + pl.off_q);
   p.apart = reinterpret_cast<float*>(w + pl.off_apart);
-  p.attn = reinterpret_cast<__half*>(w + pl.off_attn);
   p.act = reinterpret_cast<__half*>(w + pl.off_act);
   p.dpart = reinterpret_cast<float*>(w + pl.off_dpart);
-  p.n1 = pl.n1; p.n2 = pl.n2; p.n3 = pl.n3; p.nsplit = pl.nsplit; p.maxch = pl.maxch;
+  p.n1 = pl.n1; p.n2 = pl.n2; p.n3 = pl.n3; p.nsplit = pl.nsplit; p.nu_max = pl.nu_max;
   p.offA = pl.offA; p.offB = pl.offB; p.offC = pl.offC; p.offX = pl.offX; p.offRed = pl.offRed;
-  p.offMisc = pl.offMisc; p.smem = pl.smem;
-  p.regA_bytes = pl.offB - pl.offA;
+  p.offMisc = pl.offMisc; p.offStage = pl.offStage; p.smem = pl.smem;
   for (int i = 0; i < D / 2; ++i) p.rope_inv[i] = std::pow((double)theta, -2.0 * i / D);
 
   if (cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem) != cudaSuccess) {

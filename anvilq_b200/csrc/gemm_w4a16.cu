@@ -181,18 +181,18 @@ __global__ void __launch_bounds__(kThreads, 3) gemv_m1_kernel(const GemmParams p
         ZeroPoint zp[WPT];
 #pragma unroll
         for (int i = 0; i < WPT; ++i) zp[i] = make_zero_point(z.w[i]);
-        half2 part[WPT * 4];
+        float part[WPT * 8];   // the slot's sums of x (q - z), fp32
 #pragma unroll
-        for (int j = 0; j < WPT * 4; ++j) part[j] = __float2half2_rn(0.0f);
+        for (int j = 0; j < WPT * 8; ++j) part[j] = 0.0f;
 #pragma unroll
         for (int r = 0; r < kSlotRows; ++r) {
-          const half2 xx = bcast_half(r < 8 ? xa : xb, r & 7);
+          const __half xx = __low2half(bcast_half(r < 8 ? xa : xb, r & 7));
 #pragma unroll
           for (int i = 0; i < WPT; ++i) {
             half2 d[4];
             unpack_deltas(q[r].w[i], zp[i], d);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) part[i * 4 + e] = __hfma2(xx, d[e], part[i * 4 + e]);
+            for (int e = 0; e < 4; ++e) fma2_f32_f16(part[i * 8 + 2 * e], part[i * 8 + 2 * e + 1], d[e], xx);
           }
         }
         if (k0 % p.G == 0) {   // each (group, column) scale is checked exactly once
@@ -206,10 +206,9 @@ __global__ void __launch_bounds__(kThreads, 3) gemv_m1_kernel(const GemmParams p
           const uint32_t sw[4] = {sc[i].x, sc[i].y, sc[i].z, sc[i].w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(part[i * 4 + e]);
             const float2 s2 = __half22float2(u32_as_half2(sw[e]));
-            acc[i * 8 + 2 * e] = fmaf(f.x, s2.x, acc[i * 8 + 2 * e]);
-            acc[i * 8 + 2 * e + 1] = fmaf(f.y, s2.y, acc[i * 8 + 2 * e + 1]);
+            acc[i * 8 + 2 * e] = fmaf(part[i * 8 + 2 * e], s2.x, acc[i * 8 + 2 * e]);
+            acc[i * 8 + 2 * e + 1] = fmaf(part[i * 8 + 2 * e + 1], s2.y, acc[i * 8 + 2 * e + 1]);
           }
         }
       }
@@ -286,11 +285,11 @@ __global__ void __launch_bounds__(kThreads) gemm_smallm_kernel(const GemmParams 
         const uint32_t zw = __ldg(reinterpret_cast<const unsigned int*>(p.qzeros + (size_t)g * p.W8 + w0));
         const uint4 sc = ld_ro_v4(p.scales + (size_t)g * p.N + 8 * w0);
         const ZeroPoint zp = make_zero_point(zw);
-        half2 part[M][4];
+        float part[M][8];   // the slot's sums of x (q - z), fp32
 #pragma unroll
         for (int m = 0; m < M; ++m)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) part[m][e] = __float2half2_rn(0.0f);
+          for (int j = 0; j < 8; ++j) part[m][j] = 0.0f;
 #pragma unroll
         for (int r = 0; r < kSlotRows; ++r) {
           half2 d[4];
@@ -298,9 +297,9 @@ __global__ void __launch_bounds__(kThreads) gemm_smallm_kernel(const GemmParams 
           const uint4 xr = *reinterpret_cast<const uint4*>(&xs[lg][r][0]);
 #pragma unroll
           for (int m = 0; m < M; ++m) {
-            const half2 xx = bcast_half(xr, m);
+            const __half xx = __low2half(bcast_half(xr, m));
 #pragma unroll
-            for (int e = 0; e < 4; ++e) part[m][e] = __hfma2(xx, d[e], part[m][e]);
+            for (int e = 0; e < 4; ++e) fma2_f32_f16(part[m][2 * e], part[m][2 * e + 1], d[e], xx);
           }
         }
         if (k0 % p.G == 0)
@@ -312,9 +311,8 @@ __global__ void __launch_bounds__(kThreads) gemm_smallm_kernel(const GemmParams 
           const float2 s2 = __half22float2(u32_as_half2(sw[e]));
 #pragma unroll
           for (int m = 0; m < M; ++m) {
-            const float2 f = __half22float2(part[m][e]);
-            acc[m][2 * e] = fmaf(f.x, s2.x, acc[m][2 * e]);
-            acc[m][2 * e + 1] = fmaf(f.y, s2.y, acc[m][2 * e + 1]);
+            acc[m][2 * e] = fmaf(part[m][2 * e], s2.x, acc[m][2 * e]);
+            acc[m][2 * e + 1] = fmaf(part[m][2 * e + 1], s2.y, acc[m][2 * e + 1]);
           }
         }
       }
@@ -652,6 +650,22 @@ int anvilq_w4a16_gemv_plan(int K, int N, int G, anvilq_gemv_plan* plan) {
                          static_cast<const uint16_t*>(a), K, N, G, plan))
     return ANVILQ_ESHAPE;
   return ANVILQ_OK;
+}
+
+int anvilq_w4a16_gemv_kernel_plan(int kernel, int K, int N, int G, anvilq_gemv_plan* plan) {
+  if (!plan || !shape_ok(1, K, N, G)) return ANVILQ_EINVAL;
+  const void* a = reinterpret_cast<const void*>(uintptr_t(256));
+  const int32_t* w = static_cast<const int32_t*>(a);
+  const uint16_t* h = static_cast<const uint16_t*>(a);
+  if (kernel == ANVILQ_GEMV_KERNEL_STREAM)
+    return gemv_stream_supported(a, w, w, h, K, N, G) && gemv_stream_default_plan(K, N, plan) &&
+                   gemv_stream_check_plan(K, N, *plan) == ANVILQ_OK
+               ? ANVILQ_OK
+               : ANVILQ_ESHAPE;
+  if (kernel == ANVILQ_GEMV_KERNEL_CLUSTER)
+    return gemv_tma_supported(a, w, w, h, K, N, G) && gemv_cluster_default_plan(K, N, plan) ? ANVILQ_OK
+                                                                                           : ANVILQ_ESHAPE;
+  return ANVILQ_EINVAL;
 }
 
 size_t anvilq_w4a16_gemv_plan_workspace_size(int K, int N, int G, const anvilq_gemv_plan* plan) {

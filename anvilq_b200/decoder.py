@@ -180,12 +180,19 @@ class Decoder:
             def blocked_awq(w, words):   # qweight, qzeros in blocks of `words` words, scales of 8 words
                 return (blocked(w[0], words), blocked(w[1], words), blocked(w[2], 8 * words), w[3])
 
+            def interleaved_gu(w):
+                """gate|up ([.., 2 I / 8] words, [.., 2 I] scales) as 32-column units u, each
+                row holding the gate's 4 words then the up's 4 (whole AWQ words move)."""
+                qw, qz, sc = w[0], w[1], w[2]
+                unit = lambda t, per: t.view(t.shape[0], 2, I // 32, per).permute(2, 0, 1, 3).contiguous()
+                return (unit(qw, 4), unit(qz, 4), unit(sc, 32), None)
+
             p = lambda t: 0 if t is None else t.data_ptr()
             rows = []
             self.blocked_layers = []
             for l, w in enumerate(self.layers):   # anvilq_decode_layer, field by field
                 b = {"qkv": blocked_awq(w["qkv"], D // 8), "o": blocked_awq(w["o"], 4),
-                     "gu": blocked_awq(w["gu"], 4), "down": blocked_awq(w["down"], 4)}
+                     "gu": interleaved_gu(w["gu"]), "down": blocked_awq(w["down"], 4)}
                 self.blocked_layers.append(b)
                 rows.append([p(a) for a in b["qkv"]] + [p(a) for a in b["o"][:3]] + [p(a) for a in b["gu"][:3]]
                             + [p(a) for a in b["down"][:3]] + [p(self.gamma_in[l]), p(self.gamma_post[l]),

@@ -145,13 +145,18 @@ def gemm(x, qweight, qzeros, scales, bias=None, group: int = 128, out=None, dev_
     return out.view(N) if squeeze else out
 
 
-def gemv_plan(K: int, N: int, group: int = 128) -> dict:
-    """The plan ``gemm`` uses for one row (anvilq_w4a16_gemv_plan): kernel
-    (``_lib.GEMV_KERNEL_CLUSTER`` / ``_lib.GEMV_KERNEL_STREAM``), band_cols,
-    cluster, kc, warps, stages, ctas."""
+def gemv_plan(K: int, N: int, group: int = 128, kernel: int | None = None) -> dict:
+    """The plan ``gemm`` uses for one row (anvilq_w4a16_gemv_plan), or with
+    ``kernel`` the best plan of that kernel (anvilq_w4a16_gemv_kernel_plan):
+    kernel (``_lib.GEMV_KERNEL_CLUSTER`` / ``_lib.GEMV_KERNEL_STREAM``),
+    band_cols, cluster, kc, warps, stages, ctas."""
     plan = _lib.GemvPlan()
     lib = _lib.load()
-    _lib.check(lib.anvilq_w4a16_gemv_plan(K, N, group, ctypes.byref(plan)), "anvilq_w4a16_gemv_plan")
+    if kernel is None:
+        _lib.check(lib.anvilq_w4a16_gemv_plan(K, N, group, ctypes.byref(plan)), "anvilq_w4a16_gemv_plan")
+    else:
+        _lib.check(lib.anvilq_w4a16_gemv_kernel_plan(int(kernel), K, N, group, ctypes.byref(plan)),
+                   "anvilq_w4a16_gemv_kernel_plan")
     return plan.as_dict()
 
 

@@ -55,6 +55,7 @@ typedef struct CUstream_st* anvilq_stream_t; /* same type as cudaStream_t */
 #define ANVILQ_DEV_ERR_PAGE 32     /* a page-table entry of a live page was absent or out of range */
 #define ANVILQ_DEV_ERR_TREE 64     /* a draft node's ancestor mask broke the tree contract */
 #define ANVILQ_DEV_ERR_CODEC 128   /* a legacy cache block held a forbidden code, padding or metadata */
+#define ANVILQ_DEV_ERR_ALIGN 256   /* a tensor named by a device-side table was not 16-byte aligned */
 
 /* Workspace layout shared by every entry point that takes one: the first
  * ANVILQ_WORKSPACE_COUNTER_BYTES hold arrival counters that must be zero
@@ -76,8 +77,8 @@ const char* anvilq_strerror(int status);
  * batch of anvil-q4/rtl/anvil_q4_speculative.sv:57-92 computed in one pass).
  *
  * x fp16 [M][K], y fp16 [M][N], bias fp16 [N] or NULL.  Products are
- * accumulated in fp32 (partial sums of at most 16 products in fp16 for
- * M<=8), then rounded once to fp16: results differ from the reference's
+ * accumulated in fp32 (each x (q - z) product exact, every partial sum fp32),
+ * then rounded once to fp16: results differ from the reference's
  * strictly sequential binary32 sum only by accumulation order and the final
  * fp16 rounding.
  * Requirements: M >= 1, K >= 1, N >= 8, N % 8 == 0, G >= 1.
@@ -122,6 +123,9 @@ int anvilq_w4a16_gemm_ex(const uint16_t* x, const int32_t* qweight, const int32_
  * order: a plan's results are bit-reproducible.
  * anvilq_w4a16_gemv_plan fills in the plan anvilq_w4a16_gemm(_ex) uses for
  * M = 1 (ANVILQ_ESHAPE when no fast kernel serves the shape);
+ * anvilq_w4a16_gemv_kernel_plan the best plan of one named kernel for the
+ * shape (ANVILQ_EINVAL for an unknown kernel, ANVILQ_ESHAPE when that kernel
+ * cannot serve it);
  * anvilq_w4a16_gemv_planned runs y = x @ dequant(W) (+ bias) under a given
  * plan, checked against the kernel's rules (ANVILQ_EINVAL for a plan the
  * kernel does not have, ANVILQ_ESHAPE for one that does not fit the shape);
@@ -141,6 +145,7 @@ typedef struct anvilq_gemv_plan {
   int ctas;       /* CTAs launched (cluster: bands * kc * cluster, filled in) */
 } anvilq_gemv_plan;
 int anvilq_w4a16_gemv_plan(int K, int N, int G, anvilq_gemv_plan* plan);
+int anvilq_w4a16_gemv_kernel_plan(int kernel, int K, int N, int G, anvilq_gemv_plan* plan);
 size_t anvilq_w4a16_gemv_plan_workspace_size(int K, int N, int G, const anvilq_gemv_plan* plan);
 int anvilq_w4a16_gemv_planned(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
                               const uint16_t* scales, const uint16_t* bias, uint16_t* y, int K, int N, int G,
@@ -391,15 +396,22 @@ int anvilq_w4a16_gemv_allgather(const uint16_t* x, const int32_t* qweight, const
  * along N ([H][2 I / 8]); down [I][H / 8]; gammas fp16 [H]; caches fp16.
  * The AWQ tensors are given COLUMN-BLOCKED (anvilq_block_columns), so that the
  * slice a CTA streams is one contiguous range: qkv in blocks of one head
- * (qweight and qzeros D / 8 words, scales D halves), o, gu and down in blocks
- * of 4 words (scales 32 halves): a block's rows follow one another.
+ * (qweight and qzeros D / 8 words, scales D halves), o and down in blocks of
+ * 4 words (scales 32 halves): a block's rows follow one another.  gate and up
+ * are interleaved by 32-column unit u: gu_qweight [I/32][H][8] holds in words
+ * 0-3 of a row the gate's columns 32u..32u+31 and in words 4-7 the up's,
+ * gu_qzeros [I/32][H/G][8] likewise, gu_scales [I/32][H/G][64] the gate's 32
+ * scales then the up's (a column permutation of whole AWQ words: the packing
+ * is unchanged).
  * Requirements: G == 128, H % 128 == 0, I % 128 == 0, QH % KVH == 0,
  * QH / KVH <= 8, D in {64, 128}, (QH D) % 128 == 0, 16-byte aligned tensors,
  * and one SM's shared memory must hold a CTA's slices of a layer (ANVILQ_ESHAPE
  * otherwise: larger models use the per-kernel path).  The grid is one CTA per
  * SM, launched cooperatively: CTAs wait on one another's counters (bounded,
  * ~1 s, then ANVILQ_DEV_ERR_TIMEOUT and the launch gives up).  An invalid
- * *token or *pos sets ANVILQ_DEV_ERR_TOKEN / _SEQLEN and does nothing.
+ * *token or *pos sets ANVILQ_DEV_ERR_TOKEN / _SEQLEN and does nothing; a
+ * tensor of the table that is not 16-byte aligned sets ANVILQ_DEV_ERR_ALIGN
+ * and the launch gives up before copying from it (x_out is then not written).
  * workspace: anvilq_decode_layers_workspace_size bytes, 256-byte aligned,
  * zero-filled once (every launch leaves its counters zero). */
 /* dst[b][r][e] = src[r][b * block + e] for a row-major [rows][cols] matrix of

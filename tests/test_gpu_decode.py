@@ -286,10 +286,11 @@ def qwen05b_weights():
     return decoder.synthetic_weights(decoder.QWEN05B_SHAPE, seed=23)
 
 
-@pytest.mark.parametrize("context", [1000, 1087, 1600])
+@pytest.mark.parametrize("context", [1000, 1087, 1700, 2040])
 def test_fused_layers_match_per_kernel_step(dev, qwen05b_weights, context):
     """The fused layers kernel against the per-kernel step on the 0.5B shape over
-    a long synthetic context (many attention chunks, a partial last chunk):
+    a long synthetic context (many attention units, a partial last chunk; past
+    ~1660 tokens some units take two or more chunks with the online softmax):
     the same greedy tokens and logits within the decode tolerance, step after
     step, with the caches of both kept in step."""
     a = decoder.Decoder(qwen05b_weights, dev, max_seq=2048, keep_logits=True, fused=True)
@@ -370,6 +371,52 @@ def test_decode_llama7b_width_per_kernel_path(dev):
         check(d.logits.cpu().numpy(), ref, TOL_DECODE, pos)
         token = int(d.token.item())
         assert ref[token] >= ref.max() - 1e-2 * max(1.0, abs(ref.max()))
+
+
+def test_fused_layers_head_dim_128(dev):
+    """Heads of 128 through the fused layers kernel (16-word QKV head tiles,
+    64 dim pairs in the P V step) against the per-kernel step."""
+    shape = (2, 256, 512, 4, 2, 128, 128, 128, 200)
+    w = decoder.synthetic_weights(shape, seed=43)
+    a = decoder.Decoder(w, dev, max_seq=200, keep_logits=True, fused=True)
+    b = decoder.Decoder(w, dev, max_seq=200, keep_logits=True, fused=False)
+    for d in (a, b):
+        d.fill_context(150, seed=2)
+        d.set_position(9, 150)
+    for _ in range(3):
+        for d in (a, b):
+            d.step()
+            d.stream.synchronize()
+            d.check_errors()
+        check(a.logits.cpu().numpy(), b.logits.cpu().numpy(), TOL_DECODE, "D=128")
+        assert int(a.token.item()) == int(b.token.item())
+
+
+def test_fused_layers_reject_misaligned_table_entry(dev):
+    """A layer-table tensor that is not 16-byte aligned (here gamma_post of layer
+    1, offset by 8 bytes) is found before anything is copied from it: the launch
+    gives up with ANVILQ_DEV_ERR_ALIGN, and the next aligned launch runs."""
+    shape = (2, 128, 256, 2, 1, 64, 128, 64, 16)
+    w = decoder.synthetic_weights(shape, seed=31)
+    d = decoder.Decoder(w, dev, max_seq=16, keep_logits=True, fused=True)
+    good = d.layer_table.clone()
+    col = 14   # gamma_post in anvilq_decode_layer
+    d.layer_table[1, col] += 8
+    torch.cuda.synchronize(dev)
+    d.reset(3)
+    d.step()
+    d.stream.synchronize()
+    assert int(d.dev_err.item()) & 256
+    d.dev_err.zero_()
+    d.layer_table.copy_(good)
+    torch.cuda.synchronize(dev)
+    ref = decoder.Decoder(w, dev, max_seq=16, keep_logits=True, fused=False)
+    for x in (d, ref):
+        x.reset(3)
+        x.step()
+        x.stream.synchronize()
+        x.check_errors()
+    check(d.logits.cpu().numpy(), ref.logits.cpu().numpy(), TOL_DECODE, "after the misaligned launch")
 
 
 def test_device_synthetic_weights_decode(dev):

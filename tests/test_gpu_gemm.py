@@ -13,7 +13,7 @@ pytestmark = pytest.mark.gpu
 # Per-operator tolerance of the reference's FP datapath: cosine >= 0.9999 and
 # max|y - ref| / max(1, max|ref|) <= 0.002 (anvil-q1-fp/design/SPEC.md:311-317).
 # The fast kernels differ from FP32Model.linear by accumulation order (split-K,
-# 16-product binary16 partial sums folded into fp32) and one fp16 output rounding.
+# per-slot fp32 partial sums) and one fp16 output rounding.
 TOL_ERR, TOL_COS = 2e-3, 0.9999
 
 
@@ -129,6 +129,27 @@ def test_fast_kernel_shapes(dev, M, K, N):
     assert torch.equal(y1, y2)
     err, cos = oracle.normalized_error(y1.float().cpu().numpy(), ref)
     assert err <= TOL_ERR and cos >= TOL_COS, (M, K, N, err, cos)
+
+
+@pytest.mark.parametrize("M", [2, 4, 8, 12])
+def test_small_m_large_activations(dev, M):
+    """Activations up to |x| = 1000 (past where 16-product binary16 partial sums
+    overflow: 16 * 15 * 1000 > 65504) stay finite and within the tolerance: the
+    small-M kernels sum x (q - z) in fp32."""
+    from anvilq_b200 import ops
+    x, layer = synthetic.gemv_case(M, 4096, 4096, 128, 61)
+    rng = np.random.default_rng(61)
+    x = np.clip(rng.standard_normal((M, 4096)) * 300.0, -1000.0, 1000.0).astype(np.float16)
+    x[:, 0] = 1000.0
+    ref = oracle.gemv_fp32(x.astype(np.float32), layer.qweight, layer.qzeros, layer.scales_bits,
+                           None, 128, threads=oracle.max_threads())
+    assert np.isfinite(ref).all() and np.abs(ref).max() < 6e4
+    y = ops.gemm(T(x, dev), T(layer.qweight, dev), T(layer.qzeros, dev), T(layer.scales, dev), None, 128)
+    ops.raise_device_errors(dev)
+    got = y.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    err, cos = oracle.normalized_error(got, ref)
+    assert err <= TOL_ERR and cos >= TOL_COS, (M, err, cos)
 
 
 @pytest.mark.parametrize("M", [16, 64])
