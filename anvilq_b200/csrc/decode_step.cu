@@ -102,7 +102,7 @@ struct Params {
   // workspace
   float* xa;        // [H] residual after attention
   __half* q;        // [QH * D] rotated q
-  float* apart;     // [KVH][nu_max][group][D + 2] attention partials (m, l, o)
+  float* apart;     // [KVH][nu_max][perP] attention partials: [group][D + 2] (m, l, o), padded
   __half* act;      // [I] silu(g) u
   float* dpart;     // [H / 32][nsplit][32] down partials
   int* ctr;         // [L][kPhases] producer counters
@@ -110,6 +110,7 @@ struct Params {
   int* abort_flag;  // [1]
   // roles: A = QKV heads [0, n1), attention [n1, n1 + n2), O blocks [n1 + n2, n1 + n2 + n3)
   int n1, n2, n3, nsplit, nu_max;
+  int perP;         // floats of one unit's partials, group * (D + 2) rounded up to 16 bytes
   // shared-memory carve-up (bytes)
   int offA, offB, offC, offX, offRed, offMisc, smem;
   int offStage;     // within region A, after every role's tile: staged inputs, attention's P V sums
@@ -219,8 +220,10 @@ __global__ void block_columns_kernel(const uint4* __restrict__ src, uint4* __res
 // out[8 W] = x[0:R] . dequant(W[0:R][0:W]) for a tile in shared memory whose
 // row 0 is row `row0` of the matrix (groups of 128 rows).  Thread t takes word
 // t % W and the contiguous rows of row set t / W; row sets are summed within
-// the warp by shuffles and across warps in warp order.  `red` holds
-// kWarps x 8 W floats.  Returns nonzero if a scale of the tile was invalid.
+// the warp by shuffles, then the warps' sums by every thread: the 512 / (8 W)
+// lanes of an output add 16 W / 32 warps' values each and a shuffle tree adds
+// the lanes (a fixed order).  `red` holds kWarps x 8 W floats.  Returns
+// nonzero if a scale of the tile was invalid.
 template <int W>
 __device__ uint32_t tile_gemv(const uint32_t* wsm, const __half* xs, const uint32_t* zsm, const uint32_t* ssm,
                               int R, int row0, float* red, float* out) {
@@ -286,23 +289,30 @@ __device__ uint32_t tile_gemv(const uint32_t* wsm, const __half* xs, const uint3
 #pragma unroll
     for (int i = 0; i < 8; ++i) red[warp * 8 * W + 8 * lane + i] = Y[i];
   __syncthreads();
-  if (t < 8 * W) {
+  constexpr int G = kThreads / (8 * W);   // lanes per output (W >= 2: within a warp)
+  static_assert(G <= 32 && kWarps % G == 0, "tile width");
+  {
+    const int o = t / G, k = t % G;
     float v = 0.0f;
-    for (int w = 0; w < kWarps; ++w) v += red[w * 8 * W + t];   // in warp order
-    out[t] = v;
+#pragma unroll
+    for (int j = 0; j < kWarps / G; ++j) v += red[(k + j * G) * 8 * W + o];
+#pragma unroll
+    for (int m = G / 2; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+    if (k == 0) out[o] = v;
   }
   __syncthreads();
   return bad;
 }
 
-// n floats gathered from a flat index space into shared memory with 8 L2
-// loads in flight per thread: dst[i] = *src(i).
+// n float4 gathered from a flat index space into shared memory with 8 L2
+// loads of 16 bytes in flight per thread: dst[i] = *src(i).
 template <class Src>
-__device__ void stage_flat(float* dst, int n, Src src) {
+__device__ void stage_flat4(float4* dst, int n, Src src) {
   for (int i0 = threadIdx.x; i0 < n; i0 += 8 * kThreads) {
-    float v[8];
+    float4 v[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) v[u] = i0 + u * kThreads < n ? __ldcg(src(i0 + u * kThreads)) : 0.0f;
+    for (int u = 0; u < 8; ++u)
+      if (i0 + u * kThreads < n) v[u] = __ldcg(src(i0 + u * kThreads));
 #pragma unroll
     for (int u = 0; u < 8; ++u)
       if (i0 + u * kThreads < n) dst[i0 + u * kThreads] = v[u];
@@ -337,13 +347,11 @@ __device__ void rmsnorm_to_smem(const Params& p, Val val, const __half* gamma, _
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if ((threadIdx.x & 31) == 0) misc[threadIdx.x >> 5] = ss;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float t = 0.0f;
-    for (int w = 0; w < kWarps; ++w) t += misc[w];
-    misc[kWarps] = 1.0f / sqrtf(t / (float)p.H + p.eps);
-  }
-  __syncthreads();
-  const float inv = misc[kWarps];
+  // every warp adds the 16 warp sums by the same shuffle tree (no second barrier)
+  float tsum = misc[threadIdx.x & (kWarps - 1)];
+#pragma unroll
+  for (int o = kWarps / 2; o > 0; o >>= 1) tsum += __shfl_xor_sync(0xffffffffu, tsum, o);
+  const float inv = 1.0f / sqrtf(tsum / (float)p.H + p.eps);
 #pragma unroll
   for (int u = 0; u < kMaxPerThread; ++u) {
     const int k = threadIdx.x + u * kThreads;
@@ -418,6 +426,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
   uint32_t* C_z = C_w + drows * kBW;
   uint32_t* C_s = C_z + (drows / kG) * kBW;
 
+  // QKV role: sin / cos of this launch's position for each rotated pair (every layer alike)
+  float* rope_sc = misc + kMiscBig;   // [sin: D / 2][cos: D / 2], the QKV role's part of misc
+  if (roleA == 1)
+    for (int i = tid; i < D / 2; i += kThreads) {
+      const float angle = (float)((double)pos * p.rope_inv[i]);
+      sincosf(angle, &rope_sc[i], &rope_sc[kMaxD / 2 + i]);
+    }
   bool ok = true, misal = false;   // misal: a tensor of the layer table is not 16-byte aligned
   // a chunk of kv head h: rows t0 .. t0 + cnt - 1 except the current position
   // (written by this token's QKV phase, read after it)
@@ -505,7 +520,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     if (roleA == 1) {   // QKV head idxA: rmsnorm -> GEMV -> bias -> RoPE -> q / cache
       if (l > 0) {   // x_a and every down split of the previous layer: one batch of loads
         if (!(ok = wait_count(p, p.ctr + (l - 1) * kPhases + 4, nb * p.nsplit))) break;
-        stage_flat(stage, H * (p.nsplit + 1), [&](int i) { return i < H ? p.xa + i : p.dpart + (i - H); });
+        const int h4 = H / 4;
+        stage_flat4(reinterpret_cast<float4*>(stage), h4 * (p.nsplit + 1), [&](int i) {
+          return i < h4 ? reinterpret_cast<const float4*>(p.xa) + i : reinterpret_cast<const float4*>(p.dpart) + (i - h4);
+        });
         __syncthreads();
         rmsnorm_to_smem(
             p, [&](int k) { return residual_sum(stage[k], stage + H + (k >> 5) * p.nsplit * 32, p.nsplit, k); },
@@ -525,9 +543,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
         }
         const __half ha = __float2half_rn(va), hb = __float2half_rn(vb);
         if (head < QH + KVH) {
-          const float angle = (float)((double)pos * p.rope_inv[i]);
-          float si, co;
-          sincosf(angle, &si, &co);
+          const float si = rope_sc[i], co = rope_sc[kMaxD / 2 + i];
           const float xa = __half2float(ha), xb = __half2float(hb);
           const float ra = __fsub_rn(__fmul_rn(xa, co), __fmul_rn(xb, si));
           const float rb = __fadd_rn(__fmul_rn(xb, co), __fmul_rn(xa, si));
@@ -645,18 +661,23 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
           if (j < grp)
             *reinterpret_cast<float2*>(stage + (rg * grp + j) * D + 2 * dp) = make_float2(acc[j][0], acc[j][1]);
         __syncthreads();
-        for (int k = 0; k < 2; ++k) {   // (head, dim) pairs tid and tid + 512 (grp * D <= 1024)
-          const int i = tid + k * kThreads;
-          if (i >= grp * D) continue;
-          const int j = i / D, d = i % D;
-          float s = 0.0f;
-          for (int g2 = 0; g2 < nrg; ++g2) s += stage[(g2 * grp + j) * D + d];   // in row-group order
-          O[k] = fmaf(O[k], exp2f(mold[j] - mnew[j]), s);
+        {   // (head, dim) pairs tid and tid + 512 (grp * D <= 1024), two chains
+          const int i0 = tid, i1 = min(tid + kThreads, grp * D - 1);
+          const int j0 = i0 / D, j1 = i1 / D;
+          const float* s0 = stage + j0 * D + i0 % D;
+          const float* s1 = stage + j1 * D + i1 % D;
+          float a0 = 0.0f, a1 = 0.0f;
+          for (int g2 = 0; g2 < nrg; ++g2) {   // in row-group order
+            a0 += s0[g2 * grp * D];
+            a1 += s1[g2 * grp * D];
+          }
+          if (i0 < grp * D) O[0] = fmaf(O[0], exp2f(mold[j0] - mnew[j0]), a0);
+          if (tid + kThreads < grp * D) O[1] = fmaf(O[1], exp2f(mold[j1] - mnew[j1]), a1);
         }
         if (tid < grp) lrun[tid] = fmaf(lrun[tid], exp2f(mold[tid] - mnew[tid]), wsum[2 * tid] + wsum[2 * tid + 1]);
       }
       const float* mfin = mbuf + ((ac1 - ac0) & 1) * kMaxGroup;
-      float* part_out = p.apart + (size_t)(h * p.nu_max + au) * grp * (D + 2);
+      float* part_out = p.apart + (size_t)(h * p.nu_max + au) * p.perP;
       for (int k = 0; k < 2; ++k) {
         const int i = tid + k * kThreads;
         if (i < grp * D) __stcg(part_out + (i / D) * (D + 2) + 2 + i % D, O[k]);
@@ -668,15 +689,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
       publish(ctr + 1, 1);
     } else if (roleA == 3) {   // O block idxA: merge the partials, x_a = x + attn W_o
       if (!(ok = wait_count(p, ctr + 1, KVH * nu))) break;
-      const int per = grp * (D + 2), unit = nu * per, n = KVH * unit;
+      const int per = p.perP, unit = nu * per, n = KVH * unit;   // per % 4 == 0
       float* ew = misc + kMiscBig;      // [QH][nu] merge weights
       float* Ls = ew + QH * nu;         // [QH]
       // every unit's (m, l, o), then this block's x_a and down splits: one batch of loads
-      const int nres = l > 0 ? 32 * (p.nsplit + 1) : 0;
-      const float* dsrc = p.dpart + (size_t)idxA * p.nsplit * 32;
-      stage_flat(stage, n + nres, [&](int i) {
-        return i < n ? p.apart + (size_t)(i / unit) * p.nu_max * per + i % unit
-                     : i < n + 32 ? p.xa + idxA * 32 + (i - n) : dsrc + (i - n - 32);
+      const int n4 = n / 4, u4 = unit / 4, r4 = l > 0 ? 8 * (p.nsplit + 1) : 0;
+      const float4* asrc = reinterpret_cast<const float4*>(p.apart);
+      const float4* xsrc = reinterpret_cast<const float4*>(p.xa + idxA * 32);
+      const float4* dsrc = reinterpret_cast<const float4*>(p.dpart + (size_t)idxA * p.nsplit * 32);
+      stage_flat4(reinterpret_cast<float4*>(stage), n4 + r4, [&](int i) {
+        return i < n4 ? asrc + (size_t)(i / u4) * (p.nu_max * per / 4) + i % u4 : i < n4 + 8 ? xsrc + (i - n4) : dsrc + (i - n4 - 8);
       });
       __syncthreads();
       // per q head: M = max m_u, e_u = 2^(m_u - M), L = sum l_u e_u (warp per head, lane per unit)
@@ -695,12 +717,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
         if (lane == 0) Ls[jj] = s;
       }
       __syncthreads();
-      for (int i = tid; i < QH * D; i += kThreads) {
-        const int jj = i / D, d = i % D;
-        const float* pc = stage + (size_t)(jj / grp) * unit + (jj % grp) * (D + 2) + 2 + d;
-        float acc = 0.0f;
-        for (int u = 0; u < nu; ++u) acc = fmaf(ew[jj * nu + u], pc[u * per], acc);   // in unit order
-        xs[i] = __float2half_rn(acc / Ls[jj]);
+      for (int i0 = tid; i0 < QH * D; i0 += 2 * kThreads) {   // two independent chains a thread
+        const int i1 = min(i0 + kThreads, QH * D - 1), j0 = i0 / D, j1 = i1 / D;
+        const float* pc0 = stage + (size_t)(j0 / grp) * unit + (j0 % grp) * (D + 2) + 2 + i0 % D;
+        const float* pc1 = stage + (size_t)(j1 / grp) * unit + (j1 % grp) * (D + 2) + 2 + i1 % D;
+        float a0 = 0.0f, a1 = 0.0f;
+        for (int u = 0; u < nu; ++u) {   // in unit order
+          a0 = fmaf(ew[j0 * nu + u], pc0[u * per], a0);
+          a1 = fmaf(ew[j1 * nu + u], pc1[u * per], a1);
+        }
+        xs[i0] = __float2half_rn(a0 / Ls[j0]);
+        if (i0 + kThreads < QH * D) xs[i1] = __float2half_rn(a1 / Ls[j1]);
       }
       __syncthreads();
       float* y = misc + kMiscY;
@@ -787,7 +814,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
 
 // ---------------------------------------------------------------------------
 struct Plan {
-  int P, n1, n2, n3, nsplit, nu_max;
+  int P, n1, n2, n3, nsplit, nu_max, perP;
   int offA, offB, offC, offX, offRed, offMisc, offStage, smem;
   size_t ws_bytes;
   size_t off_xa, off_q, off_apart, off_act, off_dpart, off_ctr, off_exit, off_abort;
@@ -840,7 +867,8 @@ static int make_plan(int L, int H, int I, int QH, int KVH, int D, int G, int Tma
   const size_t attKV = align_up((size_t)2 * kChunk * kv_stride(D) * 2, 128);
   const size_t attPV = (size_t)kThreads * 2 * grp * 4;          // [512 / (D/2)][grp][D] floats
   const size_t oW = align_up((size_t)QH * D * kBW * 4 + (QH * D / kG) * kBW * 4 + (QH * D / kG) * 32 * 2, 128);
-  const size_t unitB = (size_t)KVH * grp * (D + 2) * 4;         // staged bytes per unit index
+  const int perP = (grp * (D + 2) + 3) / 4 * 4;
+  const size_t unitB = (size_t)KVH * perP * 4;                   // staged bytes per unit index
   const size_t offStage = std::max(qkvA, std::max(attKV, oW));
   const size_t qkvStage = (size_t)H * (pl->nsplit + 1) * 4, oRes = (size_t)32 * (pl->nsplit + 1) * 4;
   const size_t fixed = regB + regC + xsB + redB;
@@ -853,6 +881,7 @@ static int make_plan(int L, int H, int I, int QH, int KVH, int D, int G, int Tma
   while (nu > 1 && regA_bytes(nu) + fixed + misc_bytes(nu) > kSmemLimit) --nu;
   if (nu < 1 || regA_bytes(nu) + fixed + misc_bytes(nu) > kSmemLimit) return ANVILQ_ESHAPE;   // must fit one SM
   pl->nu_max = nu;
+  pl->perP = perP;
   pl->n2 = KVH * nu;
   const size_t regA = regA_bytes(nu);
   pl->offA = 0;
@@ -875,7 +904,7 @@ static int make_plan(int L, int H, int I, int QH, int KVH, int D, int G, int Tma
   pl->off_abort = take(4);
   pl->off_xa = take((size_t)H * 4);
   pl->off_q = take((size_t)QH * D * 2);
-  pl->off_apart = take((size_t)KVH * nu * grp * (D + 2) * 4);
+  pl->off_apart = take((size_t)KVH * nu * perP * 4);
   pl->off_act = take((size_t)I * 2);
   pl->off_dpart = take((size_t)nb * pl->nsplit * 32 * 4);
   pl->ws_bytes = o;
@@ -925,7 +954,7 @@ extern "C" int anvilq_decode_layers(const anvilq_decode_layer* layers, int L, in
   p.apart = reinterpret_cast<float*>(w + pl.off_apart);
   p.act = reinterpret_cast<__half*>(w + pl.off_act);
   p.dpart = reinterpret_cast<float*>(w + pl.off_dpart);
-  p.n1 = pl.n1; p.n2 = pl.n2; p.n3 = pl.n3; p.nsplit = pl.nsplit; p.nu_max = pl.nu_max;
+  p.n1 = pl.n1; p.n2 = pl.n2; p.n3 = pl.n3; p.nsplit = pl.nsplit; p.nu_max = pl.nu_max; p.perP = pl.perP;
   p.offA = pl.offA; p.offB = pl.offB; p.offC = pl.offC; p.offX = pl.offX; p.offRed = pl.offRed;
   p.offMisc = pl.offMisc; p.offStage = pl.offStage; p.smem = pl.smem;
   for (int i = 0; i < D / 2; ++i) p.rope_inv[i] = std::pow((double)theta, -2.0 * i / D);

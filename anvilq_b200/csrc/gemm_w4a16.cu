@@ -553,13 +553,18 @@ static int launch_exact(const uint16_t* x, const int32_t* qweight, const int32_t
 
 using namespace anvilq;
 
-// The M = 1 plan: the stream-K kernel for layers of at least kStreamMinBytes
-// of int4 weights (where every SM streams several chunks), the cluster kernel
-// below that (decode-size layers, latency bound).
-static constexpr long long kStreamMinBytes = 8ll << 20;
+// The M = 1 plan: the stream-K kernel for deep layers (K >= 8192) of at least
+// kStreamMinBytes of int4 weights, the cluster kernel otherwise.  Measured on
+// B200 (CUDA graph, L2-cold): stream-K wins 3-52 % on 8192x3584 .. 28672x8192
+// and 28672x1024 (the cluster kernel's deep-K split costs a fix-up per band),
+// the cluster kernel wins 4-20 % on the K = 4096 layers of 7B-class models and
+// on every decode-size (0.5B) layer.
+static constexpr long long kStreamMinBytes = 12ll << 20;
+static constexpr int kStreamMinK = 8192;
 static bool default_gemv_plan(const void* x, const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
                               int K, int N, int G, GemvPlan* plan) {
-  if ((long long)K * N / 2 >= kStreamMinBytes && gemv_stream_supported(x, qweight, qzeros, scales, K, N, G) &&
+  if (K >= kStreamMinK && (long long)K * N / 2 >= kStreamMinBytes &&
+      gemv_stream_supported(x, qweight, qzeros, scales, K, N, G) &&
       gemv_stream_default_plan(K, N, plan) && gemv_stream_check_plan(K, N, *plan) == ANVILQ_OK)
     return true;
   return gemv_tma_supported(x, qweight, qzeros, scales, K, N, G) && gemv_cluster_default_plan(K, N, plan);

@@ -539,7 +539,6 @@ static const Variant* variant(int warps, int stages) {
 constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   int sms = 0;
-  int per_sm[sizeof(kVariants) / sizeof(kVariants[0])] = {};   // resident CTAs per SM
 };
 static DeviceInfo g_dev[kMaxDevices];
 static std::once_flag g_dev_once[kMaxDevices];
@@ -554,17 +553,10 @@ static const DeviceInfo* device_info() {
       const Variant& v = kVariants[i];
       cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem);
       cudaFuncSetAttribute(v.peer_fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem);
-      int n = 0;
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, v.fn, v.warps * 32, v.smem) != cudaSuccess) n = 0;
-      d.per_sm[i] = n;
     }
     cudaGetLastError();
   });
   return &g_dev[dev];
-}
-
-static int resident(const DeviceInfo& d, const Variant* v) {
-  return d.per_sm[v - kVariants] * d.sms;
 }
 
 }  // namespace stream_gemv
@@ -579,16 +571,19 @@ bool gemv_stream_supported(const void* x, const int32_t* qweight, const int32_t*
          stream_gemv::encode_fn() != nullptr;
 }
 
-// Default plan: 8 warps and 3 stages per CTA (two CTAs per SM), every resident
-// CTA slot filled, and never more CTAs than chunks.
+// Default plan, from sweeps on B200 over the 7B / 70B-class projection shapes
+// (the 16 KB and 8 KB ring variants x 1 or 2 CTAs per SM): one CTA per SM
+// (two per SM lost 5-60 %: the per-CTA fix-up and tail cost more than the
+// extra warps hide), two ring stages, 16 warps for layers of >= 8192 columns
+// and 8 below; never fewer CTAs than bands, never more than chunks.
 bool gemv_stream_default_plan(int K, int N, GemvPlan* plan) {
   using namespace stream_gemv;
   const DeviceInfo* d = device_info();
   if (!d || d->sms <= 0) return false;
-  const Variant* v = variant(8, 3);
+  const Variant* v = variant(N >= 8192 ? 16 : 8, 2);
   const int bands = (N / 8 + kBandWords - 1) / kBandWords;
   const long long T = (long long)bands * (K / kChunkRows);
-  long long ctas = std::max<long long>(resident(*d, v), bands);
+  long long ctas = std::max<long long>(d->sms, bands);
   ctas = std::min<long long>(ctas, T);
   plan->kernel = ANVILQ_GEMV_KERNEL_STREAM;
   plan->band_cols = kBandCols;

@@ -68,12 +68,15 @@ def slice_layer(layer, rank, world):
 
 def test_default_plans(dev):
     from anvilq_b200 import ops
-    assert ops.gemv_plan(896, 4864)["kernel"] == _lib.GEMV_KERNEL_CLUSTER
-    assert ops.gemv_plan(4864, 896)["kernel"] == _lib.GEMV_KERNEL_CLUSTER
-    for K, N in [(4096, 4096), (4096, 11008), (11008, 4096)] + SHAPES_70B:
+    for K, N in [(896, 4864), (4864, 896), (4096, 4096), (4096, 11008), (4096, 22016)]:
+        assert ops.gemv_plan(K, N)["kernel"] == _lib.GEMV_KERNEL_CLUSTER, (K, N)
+    nsm = torch.cuda.get_device_properties(dev).multi_processor_count
+    for K, N in [(11008, 4096), (8192, 3584), (28672, 1024)] + SHAPES_70B:
         plan = ops.gemv_plan(K, N)
         assert plan["kernel"] == _lib.GEMV_KERNEL_STREAM, (K, N, plan)
-        assert plan["ctas"] >= 1
+        assert plan["ctas"] == max(nsm, -(-N // 256)) and plan["stages"] == 2, plan
+    for kernel in (_lib.GEMV_KERNEL_CLUSTER, _lib.GEMV_KERNEL_STREAM):   # either kernel on demand
+        assert ops.gemv_plan(4096, 11008, kernel=kernel)["kernel"] == kernel
 
 
 @pytest.mark.parametrize("K,N", SHAPES_70B)
