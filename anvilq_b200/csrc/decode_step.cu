@@ -12,19 +12,27 @@
 //
 // Why one kernel.  A 0.5B-class layer moves ~8 MB of int4 weights, 1.3 us of
 // HBM time, but as five launches (QKV, attention, O, gate/up, down) it costs
-// ~26 us: every launch pays its ramp and tail.  Here the five phases of a layer
-// are roles that CTAs take, and a phase starts when the counter its producers
-// increment reaches the number of producers (release / acquire at GPU scope,
-// bounded waits).  No CTA waits for CTAs that do not produce its input.
+// ~24 us: every launch pays its ramp and tail.  Here the five phases of a layer
+// are roles that CTAs take (one CTA per SM for the whole launch).
 //
-// One round trip per phase.  A decode layer is a chain of five dependent
-// phases, so what bounds it is latency: each phase costs the wait, ONE batch
-// of L2 loads of its inputs, its arithmetic and the publish.  Nothing is
-// merged or fixed up in a phase of its own:
-//   - attention units publish unnormalised partials (m, l, o); every O CTA
-//     merges all of them while it loads its inputs (the merge is redundant
-//     across O CTAs, a few KB of L2 reads each, instead of a serial phase);
-//   - down splits publish partial column sums; the residual after layer l is
+// Tagged words instead of counters.  A decode layer is a chain of five
+// dependent phases, so latency bounds it, and a counter handoff costs three
+// serial trips through L2: the producer's fence, the consumer's poll of the
+// counter, then its loads of the data.  Here every value a phase hands on is
+// stored as one 8-byte word (value bits | tag << 32; 8-byte relaxed stores and
+// loads are single-copy atomic), the tag naming launch and layer.  A consumer
+// loads exactly the words it needs and re-loads those whose tag is not yet
+// this layer's: one trip, no fence, and no CTA waits for data it does not use
+// (a down split waits only for the gate/up units of its rows).  Every poll is
+// bounded (~1 s, or another CTA gave up), then ANVILQ_DEV_ERR_TIMEOUT.  A
+// buffer is rewritten only by a later layer, whose producers depend, through
+// the data they consume, on every read of the earlier layer's words.
+//
+// Nothing is merged or fixed up in a phase of its own:
+//   - attention units hand on unnormalised partials (m, l, o); every O CTA
+//     merges all of them as it stages its inputs (redundant across O CTAs, a
+//     few tens of KB of L2 reads each, instead of a serial phase);
+//   - down splits hand on partial column sums; the residual after layer l is
 //     never stored: the next layer's QKV and O CTAs add x_a and the splits in
 //     split order as part of their input load.
 //
@@ -44,7 +52,8 @@
 //   O     32 output columns (4 qweight words) per CTA; residual added.
 //   g/u   32 intermediate columns of gate AND of up per CTA as ONE tile of 8
 //         words a row (gate and up interleaved at load time), so silu(g) u is
-//         formed locally; I / 32 units over P CTAs.
+//         formed locally; units beyond P go to the last CTAs, which have no
+//         down split, and the rows of those units form the last split alone.
 //   down  32 output columns x a split of the groups of K = I per CTA.
 // The GEMV arithmetic is that of the batch-1 kernels: binary16-subnormal
 // nibbles, exact products by fma.rn.f32.f16 into fp32, zero points through
@@ -64,13 +73,14 @@
 namespace anvilq {
 namespace dstep {
 
+using u64 = unsigned long long;
+
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kG = 128;            // AWQ group (rows)
 constexpr int kBW = 4;             // words of an O / down unit (32 columns)
 constexpr int kGU = 8;             // words of a gate/up unit (32 gate + 32 up columns)
 constexpr int kChunk = 64;         // attention tokens per chunk
-constexpr int kPhases = 5;
 constexpr int kMaxGroup = 8;       // q heads per kv head
 constexpr int kMaxD = 128;
 constexpr int kMaxUnits = 32;      // attention units per kv head (one merge lane each)
@@ -79,14 +89,17 @@ constexpr unsigned long long kWaitNs = 1000000000ull;
 
 // shared-memory scratch `misc` (floats)
 constexpr int kMiscY = 32;         // GEMV outputs, up to 128
-constexpr int kMiscBig = 160;      // attention state or O merge weights
+constexpr int kMiscAct = 96;       // gate/up: the unit's 32 silu(g) u (binary16)
+constexpr int kMiscBig = 160;      // per role: RoPE table and QKV output, attention state, O merge weights
+constexpr int kQkvOut = kMiscBig + kMaxD;                     // QKV: the head's D binary16 outputs
 constexpr int kAttQs = kMiscBig;                              // [grp][D] scaled q
 constexpr int kAttP = kAttQs + kMaxGroup * kMaxD;             // [grp][64] probabilities
 constexpr int kAttWmax = kAttP + kMaxGroup * kChunk;          // [grp][2]
 constexpr int kAttWsum = kAttWmax + 2 * kMaxGroup;            // [grp][2]
 constexpr int kAttM = kAttWsum + 2 * kMaxGroup;               // [2][grp] running max by chunk parity
 constexpr int kAttL = kAttM + 2 * kMaxGroup;                  // [grp] running sum
-constexpr int kAttEnd = kAttL + kMaxGroup;
+constexpr int kAttRaw = kAttL + kMaxGroup;                    // staged q (grp D halves), k and v rows (2 D halves)
+constexpr int kAttEnd = kAttRaw + (kMaxGroup * kMaxD + 2 * kMaxD) / 2;
 
 struct Params {
   const anvilq_decode_layer* layers;
@@ -97,22 +110,25 @@ struct Params {
   const int* pos;
   int* seqlen;
   float* x_out;
-  unsigned long long* key;
+  u64* key;
   int* dev_err;
-  // workspace
-  float* xa;        // [H] residual after attention
-  __half* q;        // [QH * D] rotated q
-  float* apart;     // [KVH][nu_max][perP] attention partials: [group][D + 2] (m, l, o), padded
-  __half* act;      // [I] silu(g) u
-  float* dpart;     // [H / 32][nsplit][32] down partials
-  int* ctr;         // [L][kPhases] producer counters
-  int* exit_ctr;    // [1]
-  int* abort_flag;  // [1]
+  // workspace: launch bookkeeping
+  int* exit_ctr;    // CTAs out of this launch
+  int* abort_flag;  // a CTA gave up
+  unsigned* seq;    // launches completed (the tags' launch part)
+  // workspace: tagged words (value bits | tag << 32), one buffer per handoff
+  u64* ll_xa;       // [H] residual after attention
+  u64* ll_dpart;    // [H / 32][nsplit][32] down partial sums
+  u64* ll_q;        // [QH * D / 2] rotated q, two binary16 a word
+  u64* ll_kv;       // [2][KVH][D / 2] this token's k rows, then its v rows
+  u64* ll_apart;    // [KVH][nu_max][perP] attention partials: [group][D + 2] (m, l, o), padded
+  u64* ll_act;      // [I / 2] silu(g) u, two binary16 a word
   // roles: A = QKV heads [0, n1), attention [n1, n1 + n2), O blocks [n1 + n2, n1 + n2 + n3)
   int n1, n2, n3, nsplit, nu_max;
-  int perP;         // floats of one unit's partials, group * (D + 2) rounded up to 16 bytes
+  int perP;         // words of one unit's partials, group * (D + 2) rounded up to a multiple of 4
+  int gx;           // > 0: the last down split is groups [gx, I / 128) (the extra gate/up units' rows)
   // shared-memory carve-up (bytes)
-  int offA, offB, offC, offX, offRed, offMisc, smem;
+  int offA, offB, offC, offX, offRed, offMisc, offBst, smem;
   int offStage;     // within region A, after every role's tile: staged inputs, attention's P V sums
   double rope_inv[kMaxD / 2];
 };
@@ -131,12 +147,15 @@ __device__ __forceinline__ void cp16(void* dst, const void* src) {
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_wait2() { asm volatile("cp.async.wait_group 2;" ::: "memory"); }
 __device__ __forceinline__ void cp_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-__device__ __forceinline__ int ld_acquire(const int* p) {
+__device__ __forceinline__ int ld_relaxed(const int* p) {
   int v;
-  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 __device__ __forceinline__ half2 h2(uint32_t u) { return *reinterpret_cast<half2*>(&u); }
+__device__ __forceinline__ uint32_t h2u(__half lo, __half hi) {
+  return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+}
 __device__ __forceinline__ void fma_f32_f16x2(float& a0, float& a1, uint32_t q2, unsigned short x) {
   asm("{\n .reg .f16 q0, q1;\n mov.b32 {q0, q1}, %2;\n"
       " fma.rn.f32.f16 %0, %3, q0, %0;\n fma.rn.f32.f16 %1, %3, q1, %1;\n}"
@@ -145,50 +164,101 @@ __device__ __forceinline__ void fma_f32_f16x2(float& a0, float& a1, uint32_t q2,
 }
 __device__ __forceinline__ bool misaligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; }
 
-// Give up the launch: the error bit, then the flag every bounded wait watches.
-__device__ void abort_launch(const Params& p, int bit) {
-  if (threadIdx.x == 0) {
-    if (p.dev_err) atomicOr(p.dev_err, bit);
-    atomicExch(p.abort_flag, 1);
-  }
+// ---- tagged words ------------------------------------------------------------
+__device__ __forceinline__ void ll_put(u64* dst, uint32_t bits, uint32_t tag) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(dst), "l"(((u64)tag << 32) | bits) : "memory");
+}
+__device__ __forceinline__ ulonglong2 ll_get2(const u64* src) {
+  ulonglong2 v;
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(src));
+  return v;
 }
 
-// Block until *ctr >= target (thread 0 polls, the CTA follows); false when the
-// wait expired (~1 s) or another CTA already gave up: the launch then aborts.
-__device__ bool wait_count(const Params& p, const int* ctr, int target) {
-  __shared__ int s_ok;
-  if (threadIdx.x == 0) {
-    int ok = 1;
-    if (ld_acquire(ctr) < target) {
-      const unsigned long long t0 = globaltimer();
-      for (uint32_t i = 0;; ++i) {
-        if (ld_acquire(ctr) >= target) break;
-        if ((i & 63u) == 63u) {
-          if (ld_acquire(p.abort_flag)) {
-            ok = 0;
-            break;
-          }
-          if (globaltimer() - t0 > kWaitNs) {
-            ok = 0;
-            if (p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_TIMEOUT);
-            atomicExch(p.abort_flag, 1);
-            break;
-          }
+// Where a gather reads: up to three segments, each `rows` runs of
+// `row_chunks` 16-byte chunks (two tagged words) `stride` words apart, all
+// expected to carry `tag`.
+struct LLSeg {
+  const u64* base;
+  int rows, row_chunks, stride;
+  unsigned tag;
+};
+struct LLSrc {
+  LLSeg s[3];
+  int nseg;
+};
+__device__ __forceinline__ LLSrc ll_src(LLSeg a) { return LLSrc{{a, a, a}, 1}; }
+__device__ __forceinline__ LLSrc ll_src(LLSeg a, LLSeg b) { return LLSrc{{a, b, b}, 2}; }
+__device__ __forceinline__ LLSrc ll_src(LLSeg a, LLSeg b, LLSeg c) { return LLSrc{{a, b, c}, 3}; }
+__device__ __forceinline__ LLSeg ll_run(const u64* base, int words, unsigned tag) {   // one contiguous run
+  return LLSeg{base, 1, words / 2, 0, tag};
+}
+
+// Gather the chunks of `src` into shared memory as their value bits, chunk i
+// (counted across the segments in order) to dst[2i], dst[2i + 1], once both
+// its words carry the segment's tag.  Each thread re-loads only its chunks
+// not yet complete, four loads in flight.  Bounded: after ~1 s, or when
+// another CTA gave up, the CTA gives up.  Ends with a barrier; returns the
+// CTA's verdict.
+__device__ __noinline__ bool ll_gather(const Params& p, uint32_t* dst, const LLSrc src) {
+  constexpr int kFly = 4;
+  int n = 0;
+  for (int k = 0; k < src.nseg; ++k) n += src.s[k].rows * src.s[k].row_chunks;
+  auto where = [&](int i, unsigned* tag) {
+    int k = 0;
+    for (; k + 1 < src.nseg; ++k) {
+      const int c = src.s[k].rows * src.s[k].row_chunks;
+      if (i < c) break;
+      i -= c;
+    }
+    const LLSeg& g = src.s[k];
+    *tag = g.tag;
+    const int r = g.rows > 1 ? i / g.row_chunks : 0;
+    return g.base + (size_t)r * g.stride + 2 * (i - r * g.row_chunks);
+  };
+  bool ok = true;
+  for (int base = 0; base < n; base += 32 * kThreads) {
+    uint32_t pending = 0;
+    for (int k = 0; k < 32; ++k)
+      if (base + (int)threadIdx.x + k * kThreads < n) pending |= 1u << k;
+    unsigned long long t0 = 0;
+    uint32_t rounds = 0;
+    while (pending && ok) {
+      uint32_t rest = pending;
+      while (rest) {
+        int ks[kFly];
+        unsigned tg[kFly];
+        ulonglong2 v[kFly];
+#pragma unroll
+        for (int j = 0; j < kFly; ++j) {
+          ks[j] = rest ? __ffs(rest) - 1 : -1;
+          rest &= rest - 1;
         }
+#pragma unroll
+        for (int j = 0; j < kFly; ++j)
+          if (ks[j] >= 0) v[j] = ll_get2(where(base + (int)threadIdx.x + ks[j] * kThreads, &tg[j]));
+#pragma unroll
+        for (int j = 0; j < kFly; ++j)
+          if (ks[j] >= 0 && (uint32_t)(v[j].x >> 32) == tg[j] && (uint32_t)(v[j].y >> 32) == tg[j]) {
+            const int i = base + (int)threadIdx.x + ks[j] * kThreads;
+            dst[2 * i] = (uint32_t)v[j].x;
+            dst[2 * i + 1] = (uint32_t)v[j].y;
+            pending &= ~(1u << ks[j]);
+          }
+      }
+      if (pending && (++rounds & 15u) == 0) {
+        const unsigned long long now = globaltimer();
+        if (t0 == 0) {
+          t0 = now;
+        } else if (now - t0 > kWaitNs) {
+          ok = false;
+          if (p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_TIMEOUT);
+          atomicExch(p.abort_flag, 1);
+        }
+        if (ok && ld_relaxed(p.abort_flag)) ok = false;
       }
     }
-    s_ok = ok;
   }
-  __syncthreads();
-  return s_ok != 0;
-}
-// Every thread's stores of this phase reach GPU scope before the counter
-// moves: the barrier orders the CTA's stores before thread 0, whose
-// acquire-release fence is cumulative over them; the add itself is relaxed.
-__device__ void publish(int* ctr, int n) {
-  __syncthreads();
-  if (threadIdx.x == 0)
-    asm volatile("fence.acq_rel.gpu;\n\tred.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(ctr), "r"(n) : "memory");
+  return __syncthreads_and(ok) != 0;
 }
 
 // Copy one column block of a projection (see anvilq_block_columns): `rows`
@@ -304,21 +374,6 @@ __device__ uint32_t tile_gemv(const uint32_t* wsm, const __half* xs, const uint3
   return bad;
 }
 
-// n float4 gathered from a flat index space into shared memory with 8 L2
-// loads of 16 bytes in flight per thread: dst[i] = *src(i).
-template <class Src>
-__device__ void stage_flat4(float4* dst, int n, Src src) {
-  for (int i0 = threadIdx.x; i0 < n; i0 += 8 * kThreads) {
-    float4 v[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u)
-      if (i0 + u * kThreads < n) v[u] = __ldcg(src(i0 + u * kThreads));
-#pragma unroll
-    for (int u = 0; u < 8; ++u)
-      if (i0 + u * kThreads < n) dst[i0 + u * kThreads] = v[u];
-  }
-}
-
 // The residual entering a layer after the first at column k of a 32-column
 // block: x_a of the previous layer plus its down splits added in split order,
 // from values staged as xa[k] and splits[s * 32 + k % 32] of the block.
@@ -329,8 +384,8 @@ __device__ __forceinline__ float residual_sum(float xa, const float* splits, int
 }
 
 // x_norm[k] = fp16(x[k] * gamma[k] / sqrt(mean(x^2) + eps)) into shared memory,
-// x[k] = val(k) (shared memory or one batch of loads), gamma in shared memory.
-// Every thread keeps its (at most kMaxPerThread) values: one pass over x.
+// x[k] = val(k) (from shared memory), gamma in shared memory.  Every thread
+// keeps its (at most kMaxPerThread) values: one pass over x.
 constexpr int kMaxPerThread = 8;   // H <= 4096
 template <class Val>
 __device__ void rmsnorm_to_smem(const Params& p, Val val, const __half* gamma, __half* xs, float* misc) {
@@ -362,6 +417,16 @@ __device__ void rmsnorm_to_smem(const Params& p, Val val, const __half* gamma, _
 
 __device__ __host__ inline int a_words(int D) { return D / 8; }
 __device__ __host__ inline int kv_stride(int D) { return D + 8; }   // halves; 16-byte rows, no bank conflicts
+// groups [*g0, *g1) of K = I in down split ds
+__device__ __host__ inline void down_split(int ds, int nsplit, int ngI, int gx, int* g0, int* g1) {
+  if (gx > 0) {
+    *g0 = ds < nsplit - 1 ? ds * gx / (nsplit - 1) : gx;
+    *g1 = ds < nsplit - 1 ? (ds + 1) * gx / (nsplit - 1) : ngI;
+  } else {
+    *g0 = ds * ngI / nsplit;
+    *g1 = (ds + 1) * ngI / nsplit;
+  }
+}
 
 __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -372,6 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
   __half* xs = reinterpret_cast<__half*>(smem + p.offX);
   float* red = reinterpret_cast<float*>(smem + p.offRed);
   float* misc = reinterpret_cast<float*>(smem + p.offMisc);
+  float* bst = reinterpret_cast<float*>(smem + p.offBst);   // gate/up: x_a staged
   const int H = p.H, I = p.I, QH = p.QH, KVH = p.KVH, D = p.D, grp = QH / KVH;
   const int nb = H / 32;                  // 32-column blocks of H
   const int n_gu = I / 32;                // gate/up units
@@ -385,8 +451,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
   if (pos < 0 || pos >= p.Tmax || token < 0 || token >= p.V) {
     if (cta == 0 && tid == 0 && p.dev_err)
       atomicOr(p.dev_err, pos < 0 || pos >= p.Tmax ? ANVILQ_DEV_ERR_SEQLEN : ANVILQ_DEV_ERR_TOKEN);
-    return;   // every CTA returns here alike: nothing was counted
+    return;   // every CTA returns here alike: nothing was written
   }
+  const unsigned seq = *p.seq;            // the tag of layer l: seq * L + l + 1 (never 0 before it wraps)
+  auto tag_of = [&](int l) { return seq * (unsigned)p.L + (unsigned)l + 1u; };
   const int T = pos + 1;                  // attention length
   const int nch = (T + kChunk - 1) / kChunk;
   const int nu = min(p.nu_max, nch);      // attention units per kv head this token
@@ -402,10 +470,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
   const int ah = roleA == 2 ? idxA / p.nu_max : 0, au = roleA == 2 ? idxA % p.nu_max : 0;   // kv head, unit
   const int ac0 = au * nch / nu, ac1 = (au + 1) * nch / nu;                                   // its chunks
   const bool att_on = roleA == 2 && au < nu;
-  const int gu0 = cta, gu1 = cta + P < n_gu ? cta + P : -1;        // gate/up units
+  const int extra = max(0, n_gu - P);                              // units beyond one a CTA
+  const int gu0 = cta < n_gu ? cta : -1;
+  const int gu1 = cta >= P - extra ? P + (P - 1 - cta) : -1;       // the extra units, from the last CTA down
   const bool has_down = cta < nb * p.nsplit;
   const int db = cta / p.nsplit, ds = cta % p.nsplit;              // down block and split
-  const int dg0 = ds * ngI / p.nsplit, dg1 = (ds + 1) * ngI / p.nsplit;
+  int dg0 = 0, dg1 = 0;
+  down_split(ds, p.nsplit, ngI, p.gx, &dg0, &dg1);
   const int drow0 = dg0 * kG, drows = (dg1 - dg0) * kG;
 
   // role-A tile layout (QKV head / O block): weights, zeros, scales[, gamma]
@@ -415,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
   uint32_t* A_z = A_w + rowsA * wA;
   uint32_t* A_s = A_z + ((rowsA + kG - 1) / kG) * wA;
   __half* A_gamma = reinterpret_cast<__half*>(A_s + ((rowsA + kG - 1) / kG) * 4 * wA);
-  float* stage = reinterpret_cast<float*>(regA + p.offStage);   // O: partials; attention: PV sums
+  float* stage = reinterpret_cast<float*>(regA + p.offStage);   // staged inputs; attention: P V sums
   __half* Kc = reinterpret_cast<__half*>(regA);                  // attention: [64][KS]
   __half* Vc = Kc + kChunk * KS;
   // gate/up: up to two units, each [H][8 words] + zeros + scales, then gamma_post
@@ -435,7 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     }
   bool ok = true, misal = false;   // misal: a tensor of the layer table is not 16-byte aligned
   // a chunk of kv head h: rows t0 .. t0 + cnt - 1 except the current position
-  // (written by this token's QKV phase, read after it)
+  // (this token's row comes from the QKV phase's tagged words)
   auto copy_chunk = [&](const anvilq_decode_layer& Ly, int h, int c) {
     const int t0 = c * kChunk, cnt = min(kChunk, T - t0), d8 = D / 8;
     const __half* kc = reinterpret_cast<const __half*>(Ly.k_cache);
@@ -473,21 +544,23 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     cp_commit();
   };
   auto prefetchB = [&](int l) {
-    const anvilq_decode_layer& Ly = p.layers[l];
-    if (misaligned16(Ly.gu_qweight) || misaligned16(Ly.gu_qzeros) || misaligned16(Ly.gu_scales) ||
-        misaligned16(Ly.gamma_post)) {
-      misal = true, ok = false;
-    } else {
-      const int units[2] = {gu0, gu1};
-      for (int sl = 0; sl < 2; ++sl) {
-        const int u = units[sl];
-        if (u < 0 || u >= n_gu) continue;
-        uint32_t* w = gu_w(sl);
-        prefetch_block(w, w + H * kGU, w + H * kGU + ngH * kGU, Ly.gu_qweight + (size_t)u * H * kGU,
-                       Ly.gu_qzeros + (size_t)u * ngH * kGU,
-                       reinterpret_cast<const __half*>(Ly.gu_scales) + (size_t)u * ngH * 8 * kGU, H, kGU, ngH);
+    if (gu0 >= 0) {
+      const anvilq_decode_layer& Ly = p.layers[l];
+      if (misaligned16(Ly.gu_qweight) || misaligned16(Ly.gu_qzeros) || misaligned16(Ly.gu_scales) ||
+          misaligned16(Ly.gamma_post)) {
+        misal = true, ok = false;
+      } else {
+        const int units[2] = {gu0, gu1};
+        for (int sl = 0; sl < 2; ++sl) {
+          const int u = units[sl];
+          if (u < 0) continue;
+          uint32_t* w = gu_w(sl);
+          prefetch_block(w, w + H * kGU, w + H * kGU + ngH * kGU, Ly.gu_qweight + (size_t)u * H * kGU,
+                         Ly.gu_qzeros + (size_t)u * ngH * kGU,
+                         reinterpret_cast<const __half*>(Ly.gu_scales) + (size_t)u * ngH * 8 * kGU, H, kGU, ngH);
+        }
+        prefetch_halves(B_gamma, reinterpret_cast<const __half*>(Ly.gamma_post), H);
       }
-      prefetch_halves(B_gamma, reinterpret_cast<const __half*>(Ly.gamma_post), H);
     }
     cp_commit();
   };
@@ -512,19 +585,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
 
   for (int l = 0; l < p.L && ok; ++l) {
     const anvilq_decode_layer& Ly = p.layers[l];
-    int* ctr = p.ctr + l * kPhases;
+    const unsigned tag = tag_of(l), tag_prev = tag_of(l - 1);
 
     // ---- role A --------------------------------------------------------------
     cp_wait2();
     __syncthreads();
     if (roleA == 1) {   // QKV head idxA: rmsnorm -> GEMV -> bias -> RoPE -> q / cache
-      if (l > 0) {   // x_a and every down split of the previous layer: one batch of loads
-        if (!(ok = wait_count(p, p.ctr + (l - 1) * kPhases + 4, nb * p.nsplit))) break;
-        const int h4 = H / 4;
-        stage_flat4(reinterpret_cast<float4*>(stage), h4 * (p.nsplit + 1), [&](int i) {
-          return i < h4 ? reinterpret_cast<const float4*>(p.xa) + i : reinterpret_cast<const float4*>(p.dpart) + (i - h4);
-        });
-        __syncthreads();
+      if (l > 0) {   // x_a and every down split of the previous layer: one trip
+        if (!(ok = ll_gather(p, reinterpret_cast<uint32_t*>(stage),
+                             ll_src(ll_run(p.ll_xa, H, tag_prev), ll_run(p.ll_dpart, H * p.nsplit, tag_prev)))))
+          break;
         rmsnorm_to_smem(
             p, [&](int k) { return residual_sum(stage[k], stage + H + (k >> 5) * p.nsplit * 32, p.nsplit, k); },
             A_gamma, xs, misc);
@@ -535,6 +605,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
       bad |= D == 64 ? tile_gemv<8>(A_w, xs, A_z, A_s, H, 0, red, y) : tile_gemv<16>(A_w, xs, A_z, A_s, H, 0, red, y);
       const int head = idxA, hd = D / 2;
       const __half* bias = reinterpret_cast<const __half*>(Ly.qkv_bias);
+      __half* hout = reinterpret_cast<__half*>(misc + kQkvOut);   // the head's D outputs
       for (int i = tid; i < hd; i += kThreads) {
         float va = y[i], vb = y[i + hd];
         if (bias) {
@@ -547,29 +618,49 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
           const float xa = __half2float(ha), xb = __half2float(hb);
           const float ra = __fsub_rn(__fmul_rn(xa, co), __fmul_rn(xb, si));
           const float rb = __fadd_rn(__fmul_rn(xb, co), __fmul_rn(xa, si));
-          __half* dst = head < QH ? p.q + (size_t)head * D
-                                  : reinterpret_cast<__half*>(Ly.k_cache) + ((size_t)pos * KVH + (head - QH)) * D;
-          dst[i] = __float2half_rn(ra);
-          dst[i + hd] = __float2half_rn(rb);
+          hout[i] = __float2half_rn(ra);
+          hout[i + hd] = __float2half_rn(rb);
         } else {
-          __half* dst = reinterpret_cast<__half*>(Ly.v_cache) + ((size_t)pos * KVH + (head - QH - KVH)) * D;
-          dst[i] = ha;
-          dst[i + hd] = hb;
+          hout[i] = ha;
+          hout[i + hd] = hb;
         }
       }
-      publish(ctr + 0, 1);
+      __syncthreads();
+      // hand on as tagged pairs; k and v also into the cache (plain stores, read by later launches)
+      u64* dst = head < QH ? p.ll_q + (size_t)head * hd : p.ll_kv + (size_t)(head - QH) * hd;
+      for (int w = tid; w < hd; w += kThreads) {
+        const uint32_t pair = h2u(hout[2 * w], hout[2 * w + 1]);
+        ll_put(dst + w, pair, tag);
+        if (head >= QH) {
+          const bool isv = head >= QH + KVH;
+          __half* c = reinterpret_cast<__half*>(isv ? Ly.v_cache : Ly.k_cache) +
+                      ((size_t)pos * KVH + (head - QH - (isv ? KVH : 0))) * D;
+          reinterpret_cast<uint32_t*>(c)[w] = pair;
+        }
+      }
     } else if (att_on) {   // kv head ah, chunks [ac0, ac1): online softmax, unnormalised partial out
-      if (!(ok = wait_count(p, ctr + 0, QH + 2 * KVH))) break;
       const int h = ah;
-      const __half* kc = reinterpret_cast<const __half*>(Ly.k_cache);
-      const __half* vc = reinterpret_cast<const __half*>(Ly.v_cache);
       float* qs = misc + kAttQs;
       float* Pp = misc + kAttP;
       float* wmax = misc + kAttWmax;
       float* wsum = misc + kAttWsum;
       float* mbuf = misc + kAttM;
       float* lrun = misc + kAttL;
+      uint32_t* raw = reinterpret_cast<uint32_t*>(misc + kAttRaw);   // q pairs, then k and v row pairs
+      {   // q of the group and, for the unit holding this token's row, its k and v: one trip
+        const int qw = grp * D / 2;                            // q words of the group
+        const LLSeg q = ll_run(p.ll_q + (size_t)h * qw, qw, tag);
+        // k row of head h, then its v row (the v rows follow the KVH k rows)
+        const LLSeg kv{p.ll_kv + (size_t)h * (D / 2), 2, D / 4, KVH * (D / 2), tag};
+        if (!(ok = ll_gather(p, raw, ac1 == nch ? ll_src(q, kv) : ll_src(q)))) break;
+      }
       const float qscale = 1.4426950408889634f / sqrtf((float)D);   // log2(e) / sqrt(D)
+      for (int i = tid; i < grp * D; i += kThreads)   // grp * D <= 1024
+        qs[i] = __half2float(reinterpret_cast<const __half*>(raw)[i]) * qscale;
+      if (tid < grp) {
+        mbuf[tid] = -INFINITY;
+        lrun[tid] = 0.0f;
+      }
       const int lane = tid & 31, warp = tid >> 5;
       const int sj = warp >> 1, srh = warp & 1;                      // scores: head, row half
       const int pairs = D / 2, nrg = kThreads / pairs, rpg = kChunk / nrg;
@@ -582,21 +673,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
           copy_chunk(Ly, h, c);
           cp_commit();
           cp_wait0();
-        } else {          // q of the group, scaled, as fp32 (one batch with the current row below)
-          for (int i = tid; i < grp * D; i += kThreads)   // grp * D <= 1024
-            qs[i] = __half2float(__ldcg(p.q + (size_t)h * grp * D + i)) * qscale;
-          if (tid < grp) {
-            mbuf[tid] = -INFINITY;
-            lrun[tid] = 0.0f;
+        }
+        if (pos >= t0 && pos < t0 + cnt) {   // this token's row, from the staged k and v pairs
+          const uint4* kr = reinterpret_cast<const uint4*>(raw + grp * D / 2);
+          for (int i = tid; i < D / 8; i += kThreads) {
+            *reinterpret_cast<uint4*>(Kc + (pos - t0) * KS + 8 * i) = kr[i];
+            *reinterpret_cast<uint4*>(Vc + (pos - t0) * KS + 8 * i) = kr[D / 8 + i];
           }
         }
-        if (pos >= t0 && pos < t0 + cnt)   // this token's row, written by the QKV phase
-          for (int i = tid; i < 2 * (D / 8); i += kThreads) {
-            const int which = i / (D / 8), e = i % (D / 8);
-            const size_t off = ((size_t)pos * KVH + h) * D + 8 * e;
-            *reinterpret_cast<uint4*>((which ? Vc : Kc) + (pos - t0) * KS + 8 * e) =
-                __ldcg(reinterpret_cast<const uint4*>((which ? vc : kc) + off));
-          }
         __syncthreads();
         // scores: warp (head sj, rows srh*32 + lane); 16-byte K loads, q broadcast
         const int r = srh * 32 + lane;
@@ -677,30 +761,26 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
         if (tid < grp) lrun[tid] = fmaf(lrun[tid], exp2f(mold[tid] - mnew[tid]), wsum[2 * tid] + wsum[2 * tid + 1]);
       }
       const float* mfin = mbuf + ((ac1 - ac0) & 1) * kMaxGroup;
-      float* part_out = p.apart + (size_t)(h * p.nu_max + au) * p.perP;
+      u64* part_out = p.ll_apart + (size_t)(h * p.nu_max + au) * p.perP;
       for (int k = 0; k < 2; ++k) {
         const int i = tid + k * kThreads;
-        if (i < grp * D) __stcg(part_out + (i / D) * (D + 2) + 2 + i % D, O[k]);
+        if (i < grp * D) ll_put(part_out + (i / D) * (D + 2) + 2 + i % D, __float_as_uint(O[k]), tag);
       }
       if (tid < grp) {
-        __stcg(part_out + tid * (D + 2), mfin[tid]);
-        __stcg(part_out + tid * (D + 2) + 1, lrun[tid]);
+        ll_put(part_out + tid * (D + 2), __float_as_uint(mfin[tid]), tag);
+        ll_put(part_out + tid * (D + 2) + 1, __float_as_uint(lrun[tid]), tag);
       }
-      publish(ctr + 1, 1);
+      for (int i = grp * (D + 2) + tid; i < p.perP; i += kThreads) ll_put(part_out + i, 0u, tag);   // padding words
     } else if (roleA == 3) {   // O block idxA: merge the partials, x_a = x + attn W_o
-      if (!(ok = wait_count(p, ctr + 1, KVH * nu))) break;
-      const int per = p.perP, unit = nu * per, n = KVH * unit;   // per % 4 == 0
+      const int per = p.perP, unit = nu * per, n = KVH * unit;   // words; per % 4 == 0
       float* ew = misc + kMiscBig;      // [QH][nu] merge weights
       float* Ls = ew + QH * nu;         // [QH]
-      // every unit's (m, l, o), then this block's x_a and down splits: one batch of loads
-      const int n4 = n / 4, u4 = unit / 4, r4 = l > 0 ? 8 * (p.nsplit + 1) : 0;
-      const float4* asrc = reinterpret_cast<const float4*>(p.apart);
-      const float4* xsrc = reinterpret_cast<const float4*>(p.xa + idxA * 32);
-      const float4* dsrc = reinterpret_cast<const float4*>(p.dpart + (size_t)idxA * p.nsplit * 32);
-      stage_flat4(reinterpret_cast<float4*>(stage), n4 + r4, [&](int i) {
-        return i < n4 ? asrc + (size_t)(i / u4) * (p.nu_max * per / 4) + i % u4 : i < n4 + 8 ? xsrc + (i - n4) : dsrc + (i - n4 - 8);
-      });
-      __syncthreads();
+      // every unit's (m, l, o), then this block's x_a and down splits: one trip
+      const LLSeg parts{p.ll_apart, KVH, unit / 2, p.nu_max * per, tag};
+      const LLSeg xblk = ll_run(p.ll_xa + idxA * 32, 32, tag_prev);
+      const LLSeg dblk = ll_run(p.ll_dpart + (size_t)idxA * p.nsplit * 32, 32 * p.nsplit, tag_prev);
+      if (!(ok = ll_gather(p, reinterpret_cast<uint32_t*>(stage), l > 0 ? ll_src(parts, xblk, dblk) : ll_src(parts))))
+        break;
       // per q head: M = max m_u, e_u = 2^(m_u - M), L = sum l_u e_u (warp per head, lane per unit)
       const int lane = tid & 31, warp = tid >> 5;
       for (int jj = warp; jj < QH; jj += kWarps) {
@@ -735,9 +815,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
       if (tid < 32) {
         const int k = idxA * 32 + tid;
         const float x = l > 0 ? residual_sum(stage[n + tid], stage + n + 32, p.nsplit, k) : __half2float(xemb[k]);
-        p.xa[k] = x + y[tid];
+        ll_put(p.ll_xa + k, __float_as_uint(x + y[tid]), tag);
       }
-      publish(ctr + 2, 1);
     }
     __syncthreads();
     if (l + 1 < p.L) prefetchA(l + 1);
@@ -746,24 +825,26 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     // ---- role B: gate/up -----------------------------------------------------
     cp_wait2();
     __syncthreads();
-    if (!(ok = ok && wait_count(p, ctr + 2, nb))) break;
-    rmsnorm_to_smem(p, [&](int k) { return __ldcg(p.xa + k); }, B_gamma, xs, misc);
-    int produced = 0;
-    for (int sl = 0; sl < 2; ++sl) {
-      const int u = sl == 0 ? gu0 : gu1;
-      if (u < 0 || u >= n_gu) continue;
-      float* g = misc + kMiscY;   // g[0:32] gate, g[32:64] up
-      uint32_t* w = gu_w(sl);
-      bad |= tile_gemv<kGU>(w, xs, w + H * kGU, w + H * kGU + ngH * kGU, H, 0, red, g);
-      if (tid < 32) {
-        const float gh = __half2float(__float2half_rn(g[tid])), uh = __half2float(__float2half_rn(g[32 + tid]));
-        const float e = expf(-fabsf(gh));   // stable silu (official_weights.py:494-499)
-        const float sg = gh >= 0.0f ? gh / (1.0f + e) : (gh * e) / (1.0f + e);
-        p.act[u * 32 + tid] = __float2half_rn(sg * uh);
+    if (gu0 >= 0) {
+      if (!(ok = ok && ll_gather(p, reinterpret_cast<uint32_t*>(bst), ll_src(ll_run(p.ll_xa, H, tag))))) break;
+      rmsnorm_to_smem(p, [&](int k) { return bst[k]; }, B_gamma, xs, misc);
+      for (int sl = 0; sl < 2; ++sl) {
+        const int u = sl == 0 ? gu0 : gu1;
+        if (u < 0) continue;
+        float* g = misc + kMiscY;   // g[0:32] gate, g[32:64] up
+        __half* act = reinterpret_cast<__half*>(misc + kMiscAct);
+        uint32_t* w = gu_w(sl);
+        bad |= tile_gemv<kGU>(w, xs, w + H * kGU, w + H * kGU + ngH * kGU, H, 0, red, g);
+        if (tid < 32) {
+          const float gh = __half2float(__float2half_rn(g[tid])), uh = __half2float(__float2half_rn(g[32 + tid]));
+          const float e = expf(-fabsf(gh));   // stable silu (official_weights.py:494-499)
+          const float sg = gh >= 0.0f ? gh / (1.0f + e) : (gh * e) / (1.0f + e);
+          act[tid] = __float2half_rn(sg * uh);
+        }
+        __syncthreads();
+        if (tid < 16) ll_put(p.ll_act + u * 16 + tid, h2u(act[2 * tid], act[2 * tid + 1]), tag);
       }
-      ++produced;
     }
-    if (produced) publish(ctr + 3, produced);
     __syncthreads();
     if (l + 1 < p.L) prefetchB(l + 1);
     else cp_commit();
@@ -771,32 +852,35 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     // ---- role C: down split --------------------------------------------------
     cp_wait2();
     __syncthreads();
-    if (has_down) {
-      if (!(ok = ok && wait_count(p, ctr + 3, n_gu))) break;
-      for (int i = tid; i < drows / 8; i += kThreads)
-        reinterpret_cast<uint4*>(xs)[i] = __ldcg(reinterpret_cast<const uint4*>(p.act + drow0) + i);
-      __syncthreads();
+    if (has_down) {   // the act rows of this split, staged as the GEMV's binary16 x
+      if (!(ok = ok && ll_gather(p, reinterpret_cast<uint32_t*>(xs), ll_src(ll_run(p.ll_act + drow0 / 2, drows / 2, tag)))))
+        break;
       float* y = misc + kMiscY;
       bad |= tile_gemv<kBW>(C_w, xs, C_z, C_s, drows, drow0, red, y);
-      if (tid < 32) __stcg(p.dpart + ((size_t)db * p.nsplit + ds) * 32 + tid, y[tid]);
-      publish(ctr + 4, 1);
+      if (tid < 32) ll_put(p.ll_dpart + ((size_t)db * p.nsplit + ds) * 32 + tid, __float_as_uint(y[tid]), tag);
     }
     __syncthreads();
     if (l + 1 < p.L) prefetchC(l + 1);
     else cp_commit();
   }
   cp_wait0();
-  if (!ok) abort_launch(p, misal ? ANVILQ_DEV_ERR_ALIGN : 0);   // a misaligned tensor or a wait that gave up
+  if (!ok && tid == 0) {   // a misaligned tensor, a wait that expired, or another CTA gave up
+    if (misal && p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_ALIGN);
+    atomicExch(p.abort_flag, 1);
+  }
   // ---- the residual after the last layer: column block cta ---------------------
-  if (ok && cta < nb && wait_count(p, p.ctr + (p.L - 1) * kPhases + 4, nb * p.nsplit) && tid < 32) {
-    const int k = cta * 32 + tid;
-    float acc = 0.0f;
-    for (int s = 0; s < p.nsplit; ++s) acc += __ldcg(p.dpart + ((size_t)cta * p.nsplit + s) * 32 + tid);
-    p.x_out[k] = __ldcg(p.xa + k) + acc;
+  if (ok && cta < nb) {
+    float* st = misc + kMiscBig;
+    const unsigned tl = tag_of(p.L - 1);
+    if (ll_gather(p, reinterpret_cast<uint32_t*>(st),
+                  ll_src(ll_run(p.ll_xa + cta * 32, 32, tl), ll_run(p.ll_dpart + (size_t)cta * p.nsplit * 32,
+                                                                     32 * p.nsplit, tl))) &&
+        tid < 32)
+      p.x_out[cta * 32 + tid] = residual_sum(st[tid], st + 32, p.nsplit, tid);
   }
   if (bad && p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_SCALE);
 
-  // ---- exit: the last CTA out re-arms every counter for the next launch ------
+  // ---- exit: the last CTA out advances the launch count and re-arms the flags --
   __syncthreads();
   if (tid == 0) {
     __threadfence();
@@ -804,7 +888,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     s_exit = atomicAdd(p.exit_ctr, 1) == P - 1;
     if (s_exit) {
       __threadfence();
-      for (int i = 0; i < p.L * kPhases; ++i) p.ctr[i] = 0;
+      *p.seq = seq + 1u;
       *p.abort_flag = 0;
       __threadfence();
       *p.exit_ctr = 0;
@@ -814,10 +898,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
 
 // ---------------------------------------------------------------------------
 struct Plan {
-  int P, n1, n2, n3, nsplit, nu_max, perP;
-  int offA, offB, offC, offX, offRed, offMisc, offStage, smem;
+  int P, n1, n2, n3, nsplit, nu_max, perP, gx;
+  int offA, offB, offC, offX, offRed, offMisc, offBst, offStage, smem;
   size_t ws_bytes;
-  size_t off_xa, off_q, off_apart, off_act, off_dpart, off_ctr, off_exit, off_abort;
+  size_t off_exit, off_abort, off_seq, off_xa, off_dpart, off_q, off_kv, off_apart, off_act;
 };
 
 constexpr int kMaxDevices = 64;
@@ -847,18 +931,28 @@ static int make_plan(int L, int H, int I, int QH, int KVH, int D, int G, int Tma
   const int P = sm_count();
   if (P <= 0) return ANVILQ_ECUDA;
   pl->P = P;
-  const int nb = H / 32, ngI = I / kG, ngH = H / kG, grp = QH / KVH;
+  const int nb = H / 32, ngI = I / kG, ngH = H / kG, grp = QH / KVH, n_gu = I / 32;
   pl->n1 = QH + 2 * KVH;
   pl->n3 = nb;
   pl->nsplit = std::min(std::min(P / nb, ngI), kMaxSplit);
-  if (pl->nsplit < 1 || (I / 32 + P - 1) / P > 2 || pl->n1 + pl->n3 + KVH > P) return ANVILQ_ESHAPE;
+  if (pl->nsplit < 1 || n_gu > 2 * P || pl->n1 + pl->n3 + KVH > P) return ANVILQ_ESHAPE;
+  // the rows of the units beyond P form the last down split alone, when every
+  // other split keeps at least one group
+  const int gx = (P * 32) / kG;
+  pl->gx = n_gu > P && pl->nsplit >= 2 && gx >= pl->nsplit - 1 && gx < ngI ? gx : 0;
+  int maxdg = 0;
+  for (int s = 0; s < pl->nsplit; ++s) {
+    int g0 = 0, g1 = 0;
+    down_split(s, pl->nsplit, ngI, pl->gx, &g0, &g1);
+    maxdg = std::max(maxdg, g1 - g0);
+  }
   // shared memory other than region A
   const size_t guTile = ((size_t)H * kGU + ngH * kGU + ngH * 4 * kGU) * 4;
   const size_t regB = align_up(2 * guTile + (size_t)H * 2, 128);
-  const int maxdg = (ngI + pl->nsplit - 1) / pl->nsplit;
   const size_t regC = align_up((size_t)maxdg * kG * kBW * 4 + maxdg * kBW * 4 + maxdg * 32 * 2, 128);
   const size_t xsB = align_up((size_t)std::max(std::max(H, QH * D), maxdg * kG) * 2, 128);
   const size_t redB = align_up((size_t)kWarps * 8 * 16 * 4, 128);
+  const size_t bstB = align_up((size_t)H * 4, 128);
   // region A: the role's tile (QKV head + gamma, attention chunk, O block),
   // then from offStage the role's staged inputs (QKV: x_a and the down splits;
   // O: the partials of every unit, x_a and the splits of its block) or the
@@ -871,11 +965,15 @@ static int make_plan(int L, int H, int I, int QH, int KVH, int D, int G, int Tma
   const size_t unitB = (size_t)KVH * perP * 4;                   // staged bytes per unit index
   const size_t offStage = std::max(qkvA, std::max(attKV, oW));
   const size_t qkvStage = (size_t)H * (pl->nsplit + 1) * 4, oRes = (size_t)32 * (pl->nsplit + 1) * 4;
-  const size_t fixed = regB + regC + xsB + redB;
+  const size_t fixed = regB + regC + xsB + redB + bstB;
   auto regA_bytes = [&](int u) {
     return align_up(offStage + std::max(std::max(qkvStage, attPV), (size_t)u * unitB + oRes), 128);
   };
-  auto misc_bytes = [&](int u) { return align_up((size_t)std::max(kAttEnd, kMiscBig + QH * (u + 1)) * 4, 128); };
+  auto misc_bytes = [&](int u) {   // the largest role's part, and the final residual's staging
+    const int big = std::max(std::max(kAttEnd, kQkvOut + kMaxD / 2),
+                             std::max(kMiscBig + QH * (u + 1), kMiscBig + 32 * (kMaxSplit + 1)));
+    return align_up((size_t)big * 4, 128);
+  };
   // units per kv head: the spare CTAs, at most one per chunk, and what region A can stage
   int nu = std::min((P - pl->n1 - pl->n3) / KVH, std::min(kMaxUnits, (Tmax + kChunk - 1) / kChunk));
   while (nu > 1 && regA_bytes(nu) + fixed + misc_bytes(nu) > kSmemLimit) --nu;
@@ -890,7 +988,8 @@ static int make_plan(int L, int H, int I, int QH, int KVH, int D, int G, int Tma
   pl->offC = (int)(regA + regB);
   pl->offX = (int)(regA + regB + regC);
   pl->offRed = pl->offX + (int)xsB;
-  pl->offMisc = pl->offRed + (int)redB;
+  pl->offBst = pl->offRed + (int)redB;
+  pl->offMisc = pl->offBst + (int)bstB;
   pl->smem = pl->offMisc + (int)misc_bytes(nu);
   // workspace
   size_t o = 0;
@@ -899,14 +998,15 @@ static int make_plan(int L, int H, int I, int QH, int KVH, int D, int G, int Tma
     o = align_up(o + bytes, 256);
     return at;
   };
-  pl->off_ctr = take((size_t)L * kPhases * 4);
   pl->off_exit = take(4);
   pl->off_abort = take(4);
-  pl->off_xa = take((size_t)H * 4);
-  pl->off_q = take((size_t)QH * D * 2);
-  pl->off_apart = take((size_t)KVH * nu * perP * 4);
-  pl->off_act = take((size_t)I * 2);
-  pl->off_dpart = take((size_t)nb * pl->nsplit * 32 * 4);
+  pl->off_seq = take(4);
+  pl->off_xa = take((size_t)H * 8);
+  pl->off_dpart = take((size_t)nb * pl->nsplit * 32 * 8);
+  pl->off_q = take((size_t)QH * D / 2 * 8);
+  pl->off_kv = take((size_t)KVH * D * 8);
+  pl->off_apart = take((size_t)KVH * nu * perP * 8);
+  pl->off_act = take((size_t)I / 2 * 8);
   pl->ws_bytes = o;
   return ANVILQ_OK;
 }
@@ -946,17 +1046,19 @@ extern "C" int anvilq_decode_layers(const anvilq_decode_layer* layers, int L, in
   p.key = argmax_key;
   p.dev_err = dev_err;
   char* w = static_cast<char*>(workspace);
-  p.ctr = reinterpret_cast<int*>(w + pl.off_ctr);
   p.exit_ctr = reinterpret_cast<int*>(w + pl.off_exit);
   p.abort_flag = reinterpret_cast<int*>(w + pl.off_abort);
-  p.xa = reinterpret_cast<float*>(w + pl.off_xa);
-  p.q = reinterpret_cast<__half*>(w + pl.off_q);
-  p.apart = reinterpret_cast<float*>(w + pl.off_apart);
-  p.act = reinterpret_cast<__half*>(w + pl.off_act);
-  p.dpart = reinterpret_cast<float*>(w + pl.off_dpart);
+  p.seq = reinterpret_cast<unsigned*>(w + pl.off_seq);
+  p.ll_xa = reinterpret_cast<u64*>(w + pl.off_xa);
+  p.ll_dpart = reinterpret_cast<u64*>(w + pl.off_dpart);
+  p.ll_q = reinterpret_cast<u64*>(w + pl.off_q);
+  p.ll_kv = reinterpret_cast<u64*>(w + pl.off_kv);
+  p.ll_apart = reinterpret_cast<u64*>(w + pl.off_apart);
+  p.ll_act = reinterpret_cast<u64*>(w + pl.off_act);
   p.n1 = pl.n1; p.n2 = pl.n2; p.n3 = pl.n3; p.nsplit = pl.nsplit; p.nu_max = pl.nu_max; p.perP = pl.perP;
+  p.gx = pl.gx;
   p.offA = pl.offA; p.offB = pl.offB; p.offC = pl.offC; p.offX = pl.offX; p.offRed = pl.offRed;
-  p.offMisc = pl.offMisc; p.offStage = pl.offStage; p.smem = pl.smem;
+  p.offMisc = pl.offMisc; p.offBst = pl.offBst; p.offStage = pl.offStage; p.smem = pl.smem;
   for (int i = 0; i < D / 2; ++i) p.rope_inv[i] = std::pow((double)theta, -2.0 * i / D);
 
   if (cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem) != cudaSuccess) {
