@@ -141,12 +141,34 @@ __device__ __forceinline__ unsigned long long globaltimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-__device__ __forceinline__ void cp16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+// ---- bulk copies into shared memory, completion counted on an mbarrier -------
+__device__ __forceinline__ void mbar_init(u64* bar) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(bar)) : "memory");
 }
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_wait2() { asm volatile("cp.async.wait_group 2;" ::: "memory"); }
-__device__ __forceinline__ void cp_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+// The one arrival of a phase, by the thread that then issues its copies; the
+// proxy fence orders the CTA's earlier shared-memory reads (made visible to it
+// by the barrier before the prefetch) before the bulk copies' writes.
+__device__ __forceinline__ void mbar_expect(u64* bar, uint32_t bytes) {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(u64* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// `bytes` (a multiple of 16, both addresses 16-byte aligned) from global memory,
+// counted on `bar` (no multicast)
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, u64* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
 __device__ __forceinline__ int ld_relaxed(const int* p) {
   int v;
   asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -196,11 +218,11 @@ __device__ __forceinline__ LLSeg ll_run(const u64* base, int words, unsigned tag
 // Gather the chunks of `src` into shared memory as their value bits, chunk i
 // (counted across the segments in order) to dst[2i], dst[2i + 1], once both
 // its words carry the segment's tag.  Each thread re-loads only its chunks
-// not yet complete, four loads in flight.  Bounded: after ~1 s, or when
+// not yet complete, eight loads in flight.  Bounded: after ~1 s, or when
 // another CTA gave up, the CTA gives up.  Ends with a barrier; returns the
 // CTA's verdict.
 __device__ __noinline__ bool ll_gather(const Params& p, uint32_t* dst, const LLSrc src) {
-  constexpr int kFly = 4;
+  constexpr int kFly = 8;
   int n = 0;
   for (int k = 0; k < src.nseg; ++k) n += src.s[k].rows * src.s[k].row_chunks;
   auto where = [&](int i, unsigned* tag) {
@@ -261,19 +283,18 @@ __device__ __noinline__ bool ll_gather(const Params& p, uint32_t* dst, const LLS
   return __syncthreads_and(ok) != 0;
 }
 
-// Copy one column block of a projection (see anvilq_block_columns): `rows`
-// rows of `words` int4 words, then the zeros [ng][words] and the scales
-// [ng][8 words] (binary16) of its ng groups -- three contiguous ranges, so the
-// 16-byte copies of consecutive threads are consecutive in memory.
-__device__ void prefetch_block(uint32_t* wdst, uint32_t* zdst, uint32_t* sdst, const int32_t* wsrc,
-                               const int32_t* zsrc, const __half* ssrc, int rows, int words, int ng) {
-  const int nw = rows * words / 4, nz = ng * words / 4, ns = ng * words;
-  for (int i = threadIdx.x; i < nw; i += kThreads) cp16(wdst + 4 * i, wsrc + 4 * i);
-  for (int i = threadIdx.x; i < nz; i += kThreads) cp16(zdst + 4 * i, zsrc + 4 * i);
-  for (int i = threadIdx.x; i < ns; i += kThreads) cp16(sdst + 4 * i, ssrc + 8 * i);
+// Bytes of one column block of a projection (see anvilq_block_columns):
+// `rows` rows of `words` int4 words, the zeros [ng][words] and the scales
+// [ng][8 words] (binary16) of its ng groups -- three contiguous ranges.
+__host__ __device__ inline uint32_t block_bytes(int rows, int words, int ng) {
+  return (uint32_t)(rows * words * 4 + ng * words * 4 + ng * words * 16);
 }
-__device__ void prefetch_halves(__half* dst, const __half* src, int n) {   // n % 8 == 0
-  for (int i = threadIdx.x; i < n / 8; i += kThreads) cp16(dst + 8 * i, src + 8 * i);
+// The three ranges of a column block as three bulk copies (one thread).
+__device__ void load_block(uint32_t* wdst, uint32_t* zdst, uint32_t* sdst, const int32_t* wsrc, const int32_t* zsrc,
+                           const __half* ssrc, int rows, int words, int ng, u64* bar) {
+  bulk_load(wdst, wsrc, rows * words * 4, bar);
+  bulk_load(zdst, zsrc, ng * words * 4, bar);
+  bulk_load(sdst, ssrc, ng * words * 16, bar);
 }
 
 // dst[b][r][e] = src[r][b * block + e]: the column blocks of a row-major matrix
@@ -505,20 +526,58 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
       sincosf(angle, &rope_sc[i], &rope_sc[kMaxD / 2 + i]);
     }
   bool ok = true, misal = false;   // misal: a tensor of the layer table is not 16-byte aligned
-  // a chunk of kv head h: rows t0 .. t0 + cnt - 1 except the current position
-  // (this token's row comes from the QKV phase's tagged words)
-  auto copy_chunk = [&](const anvilq_decode_layer& Ly, int h, int c) {
-    const int t0 = c * kChunk, cnt = min(kChunk, T - t0), d8 = D / 8;
-    const __half* kc = reinterpret_cast<const __half*>(Ly.k_cache);
-    const __half* vc = reinterpret_cast<const __half*>(Ly.v_cache);
-    for (int i = tid; i < cnt * d8; i += kThreads) {
-      const int r = i / d8, c8 = i % d8, tok = t0 + r;
-      if (tok == pos) continue;
-      const size_t off = ((size_t)tok * KVH + h) * D + 8 * c8;
-      cp16(Kc + r * KS + 8 * c8, kc + off);
-      cp16(Vc + r * KS + 8 * c8, vc + off);
+  // Prefetches: bulk copies counted on one mbarrier per region (A, B, C, and
+  // K for the attention's later chunks), one phase per layer; `armed` marks a
+  // phase issued and not yet waited for.
+  __shared__ __align__(8) u64 s_bar[4];
+  uint32_t parity[4] = {0u, 0u, 0u, 0u};
+  bool armed[4] = {false, false, false, false};
+  if (tid == 0) {
+    for (int i = 0; i < 4; ++i) mbar_init(&s_bar[i]);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  // every thread waits for region r's phase, bounded; false when it expired
+  auto wait_region = [&](int r) {
+    if (!armed[r]) return true;
+    armed[r] = false;
+    const uint32_t ph = parity[r];
+    parity[r] ^= 1u;
+    if (mbar_test(&s_bar[r], ph)) return true;
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t i = 0;; ++i) {
+      if (mbar_test(&s_bar[r], ph)) return true;
+      if ((i & 255u) == 255u && globaltimer() - t0 > kWaitNs) {
+        if (p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_TIMEOUT);
+        atomicExch(p.abort_flag, 1);
+        return false;
+      }
     }
   };
+  // a chunk of kv head h: rows t0 .. t0 + cnt - 1 except the current position
+  // (this token's row comes from the QKV phase's tagged words), one bulk copy a
+  // row of K and of V, issued by warp 0
+  auto load_chunk = [&](const anvilq_decode_layer& Ly, int h, int c, int r) {
+    const int t0 = c * kChunk, cnt = min(kChunk, T - t0);
+    if (tid < 32) {
+      const uint32_t rowb = D * 2;
+      const int rows = cnt - (pos >= t0 && pos < t0 + cnt ? 1 : 0);
+      if (tid == 0) mbar_expect(&s_bar[r], 2u * rowb * rows);
+      __syncwarp();
+      const __half* kc = reinterpret_cast<const __half*>(Ly.k_cache);
+      const __half* vc = reinterpret_cast<const __half*>(Ly.v_cache);
+      for (int i = tid; i < cnt; i += 32) {
+        const int tok = t0 + i;
+        if (tok == pos) continue;
+        const size_t off = ((size_t)tok * KVH + h) * D;
+        bulk_load(Kc + i * KS, kc + off, rowb, &s_bar[r]);
+        bulk_load(Vc + i * KS, vc + off, rowb, &s_bar[r]);
+      }
+    }
+    armed[r] = true;
+  };
+  // Each prefetch first checks the alignment the bulk copies need, and runs
+  // after a barrier: nothing still reads the region it overwrites.
   auto prefetchA = [&](int l) {
     const anvilq_decode_layer& Ly = p.layers[l];
     if (roleA == 1) {   // column block idxA (one head) of the blocked QKV projection, and gamma_in
@@ -527,57 +586,71 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
           misaligned16(Ly.gamma_in) || misaligned16(Ly.k_cache) || misaligned16(Ly.v_cache)) {
         misal = true, ok = false;
       } else {
-        prefetch_block(A_w, A_z, A_s, Ly.qkv_qweight + (size_t)idxA * H * wd, Ly.qkv_qzeros + (size_t)idxA * ngH * wd,
-                       reinterpret_cast<const __half*>(Ly.qkv_scales) + (size_t)idxA * ngH * 8 * wd, H, wd, ngH);
-        prefetch_halves(A_gamma, reinterpret_cast<const __half*>(Ly.gamma_in), H);
+        if (tid == 0) {
+          mbar_expect(&s_bar[0], block_bytes(H, wd, ngH) + H * 2);
+          load_block(A_w, A_z, A_s, Ly.qkv_qweight + (size_t)idxA * H * wd, Ly.qkv_qzeros + (size_t)idxA * ngH * wd,
+                     reinterpret_cast<const __half*>(Ly.qkv_scales) + (size_t)idxA * ngH * 8 * wd, H, wd, ngH,
+                     &s_bar[0]);
+          bulk_load(A_gamma, Ly.gamma_in, H * 2, &s_bar[0]);
+        }
+        armed[0] = true;
       }
     } else if (att_on) {   // the unit's first chunk
       if (misaligned16(Ly.k_cache) || misaligned16(Ly.v_cache)) misal = true, ok = false;
-      else copy_chunk(Ly, ah, ac0);
+      else load_chunk(Ly, ah, ac0, 0);
     } else if (roleA == 3) {   // column block idxA of the blocked O projection
       const int K = QH * D, ng = K / kG;
-      if (misaligned16(Ly.o_qweight) || misaligned16(Ly.o_qzeros) || misaligned16(Ly.o_scales)) misal = true, ok = false;
-      else
-        prefetch_block(A_w, A_z, A_s, Ly.o_qweight + (size_t)idxA * K * kBW, Ly.o_qzeros + (size_t)idxA * ng * kBW,
-                       reinterpret_cast<const __half*>(Ly.o_scales) + (size_t)idxA * ng * 8 * kBW, K, kBW, ng);
+      if (misaligned16(Ly.o_qweight) || misaligned16(Ly.o_qzeros) || misaligned16(Ly.o_scales)) {
+        misal = true, ok = false;
+      } else {
+        if (tid == 0) {
+          mbar_expect(&s_bar[0], block_bytes(K, kBW, ng));
+          load_block(A_w, A_z, A_s, Ly.o_qweight + (size_t)idxA * K * kBW, Ly.o_qzeros + (size_t)idxA * ng * kBW,
+                     reinterpret_cast<const __half*>(Ly.o_scales) + (size_t)idxA * ng * 8 * kBW, K, kBW, ng,
+                     &s_bar[0]);
+        }
+        armed[0] = true;
+      }
     }
-    cp_commit();
   };
   auto prefetchB = [&](int l) {
-    if (gu0 >= 0) {
-      const anvilq_decode_layer& Ly = p.layers[l];
-      if (misaligned16(Ly.gu_qweight) || misaligned16(Ly.gu_qzeros) || misaligned16(Ly.gu_scales) ||
-          misaligned16(Ly.gamma_post)) {
-        misal = true, ok = false;
-      } else {
-        const int units[2] = {gu0, gu1};
-        for (int sl = 0; sl < 2; ++sl) {
-          const int u = units[sl];
-          if (u < 0) continue;
-          uint32_t* w = gu_w(sl);
-          prefetch_block(w, w + H * kGU, w + H * kGU + ngH * kGU, Ly.gu_qweight + (size_t)u * H * kGU,
-                         Ly.gu_qzeros + (size_t)u * ngH * kGU,
-                         reinterpret_cast<const __half*>(Ly.gu_scales) + (size_t)u * ngH * 8 * kGU, H, kGU, ngH);
-        }
-        prefetch_halves(B_gamma, reinterpret_cast<const __half*>(Ly.gamma_post), H);
-      }
+    if (gu0 < 0) return;
+    const anvilq_decode_layer& Ly = p.layers[l];
+    if (misaligned16(Ly.gu_qweight) || misaligned16(Ly.gu_qzeros) || misaligned16(Ly.gu_scales) ||
+        misaligned16(Ly.gamma_post)) {
+      misal = true, ok = false;
+      return;
     }
-    cp_commit();
+    if (tid == 0) {
+      mbar_expect(&s_bar[1], (gu1 >= 0 ? 2u : 1u) * block_bytes(H, kGU, ngH) + H * 2);
+      const int units[2] = {gu0, gu1};
+      for (int sl = 0; sl < 2; ++sl) {
+        const int u = units[sl];
+        if (u < 0) continue;
+        uint32_t* w = gu_w(sl);
+        load_block(w, w + H * kGU, w + H * kGU + ngH * kGU, Ly.gu_qweight + (size_t)u * H * kGU,
+                   Ly.gu_qzeros + (size_t)u * ngH * kGU,
+                   reinterpret_cast<const __half*>(Ly.gu_scales) + (size_t)u * ngH * 8 * kGU, H, kGU, ngH, &s_bar[1]);
+      }
+      bulk_load(B_gamma, Ly.gamma_post, H * 2, &s_bar[1]);
+    }
+    armed[1] = true;
   };
   auto prefetchC = [&](int l) {
-    if (has_down) {
-      const anvilq_decode_layer& Ly = p.layers[l];
-      if (misaligned16(Ly.down_qweight) || misaligned16(Ly.down_qzeros) || misaligned16(Ly.down_scales)) {
-        misal = true, ok = false;
-      } else {
-        // rows [drow0, drow0 + drows) of column block db of the blocked down projection
-        prefetch_block(C_w, C_z, C_s, Ly.down_qweight + ((size_t)db * I + drow0) * kBW,
-                       Ly.down_qzeros + ((size_t)db * ngI + dg0) * kBW,
-                       reinterpret_cast<const __half*>(Ly.down_scales) + ((size_t)db * ngI + dg0) * 8 * kBW, drows,
-                       kBW, dg1 - dg0);
-      }
+    if (!has_down) return;
+    const anvilq_decode_layer& Ly = p.layers[l];
+    if (misaligned16(Ly.down_qweight) || misaligned16(Ly.down_qzeros) || misaligned16(Ly.down_scales)) {
+      misal = true, ok = false;
+      return;
     }
-    cp_commit();
+    if (tid == 0) {   // rows [drow0, drow0 + drows) of column block db of the blocked down projection
+      mbar_expect(&s_bar[2], block_bytes(drows, kBW, dg1 - dg0));
+      load_block(C_w, C_z, C_s, Ly.down_qweight + ((size_t)db * I + drow0) * kBW,
+                 Ly.down_qzeros + ((size_t)db * ngI + dg0) * kBW,
+                 reinterpret_cast<const __half*>(Ly.down_scales) + ((size_t)db * ngI + dg0) * 8 * kBW, drows, kBW,
+                 dg1 - dg0, &s_bar[2]);
+    }
+    armed[2] = true;
   };
   prefetchA(0);
   prefetchB(0);
@@ -588,8 +661,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     const unsigned tag = tag_of(l), tag_prev = tag_of(l - 1);
 
     // ---- role A --------------------------------------------------------------
-    cp_wait2();
-    __syncthreads();
+    if (!(ok = __syncthreads_and(wait_region(0)) != 0)) break;
     if (roleA == 1) {   // QKV head idxA: rmsnorm -> GEMV -> bias -> RoPE -> q / cache
       if (l > 0) {   // x_a and every down split of the previous layer: one trip
         if (!(ok = ll_gather(p, reinterpret_cast<uint32_t*>(stage),
@@ -670,9 +742,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
         const int t0 = c * kChunk, cnt = min(kChunk, T - t0), ci = c - ac0;
         if (c != ac0) {   // later chunks of the range: copied now
           __syncthreads();
-          copy_chunk(Ly, h, c);
-          cp_commit();
-          cp_wait0();
+          load_chunk(Ly, h, c, 3);
+          if (!(ok = __syncthreads_and(wait_region(3)) != 0)) break;
         }
         if (pos >= t0 && pos < t0 + cnt) {   // this token's row, from the staged k and v pairs
           const uint4* kr = reinterpret_cast<const uint4*>(raw + grp * D / 2);
@@ -760,6 +831,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
         }
         if (tid < grp) lrun[tid] = fmaf(lrun[tid], exp2f(mold[tid] - mnew[tid]), wsum[2 * tid] + wsum[2 * tid + 1]);
       }
+      if (!ok) break;
       const float* mfin = mbuf + ((ac1 - ac0) & 1) * kMaxGroup;
       u64* part_out = p.ll_apart + (size_t)(h * p.nu_max + au) * p.perP;
       for (int k = 0; k < 2; ++k) {
@@ -820,11 +892,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     }
     __syncthreads();
     if (l + 1 < p.L) prefetchA(l + 1);
-    else cp_commit();
 
     // ---- role B: gate/up -----------------------------------------------------
-    cp_wait2();
-    __syncthreads();
+    if (!(ok = ok && __syncthreads_and(wait_region(1)) != 0)) break;
     if (gu0 >= 0) {
       if (!(ok = ok && ll_gather(p, reinterpret_cast<uint32_t*>(bst), ll_src(ll_run(p.ll_xa, H, tag))))) break;
       rmsnorm_to_smem(p, [&](int k) { return bst[k]; }, B_gamma, xs, misc);
@@ -847,11 +917,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     }
     __syncthreads();
     if (l + 1 < p.L) prefetchB(l + 1);
-    else cp_commit();
 
     // ---- role C: down split --------------------------------------------------
-    cp_wait2();
-    __syncthreads();
+    if (!(ok = ok && __syncthreads_and(wait_region(2)) != 0)) break;
     if (has_down) {   // the act rows of this split, staged as the GEMV's binary16 x
       if (!(ok = ok && ll_gather(p, reinterpret_cast<uint32_t*>(xs), ll_src(ll_run(p.ll_act + drow0 / 2, drows / 2, tag)))))
         break;
@@ -861,9 +929,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     }
     __syncthreads();
     if (l + 1 < p.L) prefetchC(l + 1);
-    else cp_commit();
   }
-  cp_wait0();
+  for (int r = 0; r < 4; ++r) wait_region(r);   // copies still in flight land before the CTA exits (bounded)
   if (!ok && tid == 0) {   // a misaligned tensor, a wait that expired, or another CTA gave up
     if (misal && p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_ALIGN);
     atomicExch(p.abort_flag, 1);
