@@ -218,11 +218,11 @@ __device__ __forceinline__ LLSeg ll_run(const u64* base, int words, unsigned tag
 // Gather the chunks of `src` into shared memory as their value bits, chunk i
 // (counted across the segments in order) to dst[2i], dst[2i + 1], once both
 // its words carry the segment's tag.  Each thread re-loads only its chunks
-// not yet complete, eight loads in flight.  Bounded: after ~1 s, or when
+// not yet complete, four loads in flight.  Bounded: after ~1 s, or when
 // another CTA gave up, the CTA gives up.  Ends with a barrier; returns the
 // CTA's verdict.
 __device__ __noinline__ bool ll_gather(const Params& p, uint32_t* dst, const LLSrc src) {
-  constexpr int kFly = 8;
+  constexpr int kFly = 4;
   int n = 0;
   for (int k = 0; k < src.nseg; ++k) n += src.s[k].rows * src.s[k].row_chunks;
   auto where = [&](int i, unsigned* tag) {
