@@ -53,6 +53,7 @@ SIGNATURES = {
     "anvilq_w4a16_gemv_allgather": (I, [P, P, P, P, P, I, I, I, I, I, I, I, P, P, P, P, SZ, P, ctypes.c_uint, P]),
     "anvilq_embed": (I, [P, P, P, I, I, P, P, ctypes.c_uint, P]),
     "anvilq_rope_kv_append": (I, [P, P, P, P, P, P, I, I, I, I, F, P, ctypes.c_uint, P]),
+    "anvilq_rope_kv_append_at": (I, [P, P, P, P, P, P, I, I, I, I, F, P, ctypes.c_uint, P]),
     "anvilq_block_columns": (I, [P, P, I, I, I, I, P]),
     "anvilq_decode_layers_workspace_size": (SZ, [I, I, I, I, I, I, I, I]),
     "anvilq_decode_layers": (I, [P, I, I, I, I, I, I, I, I, F, F, P, I, P, P, P, P, P, P, SZ, P, P]),

@@ -56,12 +56,14 @@ struct RopeFreq {
 };
 
 __global__ void rope_append_kernel(const __half* __restrict__ qkv, const int* __restrict__ pos_p,
-                                   __half* __restrict__ q_out, __half* __restrict__ k_cache,
-                                   __half* __restrict__ v_cache, int* __restrict__ seqlen, int Hq, int Hkv, int D,
-                                   int Tmax, const __grid_constant__ RopeFreq freq, int* dev_err) {
+                                   const int* __restrict__ row_p, __half* __restrict__ q_out,
+                                   __half* __restrict__ k_cache, __half* __restrict__ v_cache,
+                                   int* __restrict__ seqlen, int Hq, int Hkv, int D, int Tmax,
+                                   const __grid_constant__ RopeFreq freq, int* dev_err) {
   pdl_enter();
-  const int pos = *pos_p;
-  if (pos < 0 || pos >= Tmax) {
+  const int pos = *pos_p;                     // the rotation's position
+  const int crow = row_p ? *row_p : pos;      // the cache row written
+  if (pos < 0 || pos >= Tmax || crow < 0 || crow >= Tmax) {
     if (threadIdx.x == 0 && blockIdx.x == 0 && dev_err) atomicOr(dev_err, ANVILQ_DEV_ERR_SEQLEN);
     return;
   }
@@ -83,16 +85,16 @@ __global__ void rope_append_kernel(const __half* __restrict__ qkv, const int* __
         q_out[b] = __float2half_rn(rb);
       } else {
         const int kh = head - Hq;
-        __half* row = k_cache + ((size_t)pos * Hkv + kh) * D;
+        __half* row = k_cache + ((size_t)crow * Hkv + kh) * D;
         row[pair] = __float2half_rn(ra);
         row[pair + half_d] = __float2half_rn(rb);
       }
     } else {
       const int e = i - rot, kh = e / D, d = e % D;
-      v_cache[((size_t)pos * Hkv + kh) * D + d] = qkv[(Hq + Hkv) * D + e];
+      v_cache[((size_t)crow * Hkv + kh) * D + d] = qkv[(Hq + Hkv) * D + e];
     }
   }
-  if (seqlen && blockIdx.x == 0 && threadIdx.x == 0) *seqlen = pos + 1;
+  if (seqlen && blockIdx.x == 0 && threadIdx.x == 0) *seqlen = crow + 1;
 }
 
 // Orderable key of (logit, row): larger logit wins, then the lower row index.
@@ -305,9 +307,9 @@ int anvilq_embed(const uint16_t* table, const int32_t* token, float* x, int H, i
                 reinterpret_cast<const __half*>(table), (const int*)token, x, H, V, argmax_key, dev_err);
 }
 
-int anvilq_rope_kv_append(const uint16_t* qkv, const int32_t* pos, uint16_t* q_out, uint16_t* k_cache,
-                          uint16_t* v_cache, int32_t* seqlen, int Hq, int Hkv, int D, int Tmax, float theta,
-                          int* dev_err, unsigned flags, anvilq_stream_t stream) {
+static int rope_kv_append(const uint16_t* qkv, const int32_t* pos, const int32_t* row, uint16_t* q_out,
+                          uint16_t* k_cache, uint16_t* v_cache, int32_t* seqlen, int Hq, int Hkv, int D, int Tmax,
+                          float theta, int* dev_err, unsigned flags, anvilq_stream_t stream) {
   if (!qkv || !pos || !q_out || !k_cache || !v_cache) return ANVILQ_EINVAL;
   if (Hq < 1 || Hkv < 1 || Hq % Hkv || D < 2 || D % 2 || Tmax < 1 || !(theta > 0.0f)) return ANVILQ_EINVAL;
   if (D / 2 > kMaxRopePairs) return ANVILQ_ESHAPE;
@@ -317,9 +319,24 @@ int anvilq_rope_kv_append(const uint16_t* qkv, const int32_t* pos, uint16_t* q_o
   const int work = (Hq + Hkv) * (D / 2) + Hkv * D;
   const int threads = 256, blocks = std::min(32, (work + threads - 1) / threads);
   return launch(rope_append_kernel, dim3(blocks), dim3(threads), 0, reinterpret_cast<cudaStream_t>(stream), flags,
-                reinterpret_cast<const __half*>(qkv), (const int*)pos, reinterpret_cast<__half*>(q_out),
-                reinterpret_cast<__half*>(k_cache), reinterpret_cast<__half*>(v_cache), (int*)seqlen, Hq, Hkv, D,
-                Tmax, freq, dev_err);
+                reinterpret_cast<const __half*>(qkv), (const int*)pos, (const int*)row,
+                reinterpret_cast<__half*>(q_out), reinterpret_cast<__half*>(k_cache),
+                reinterpret_cast<__half*>(v_cache), (int*)seqlen, Hq, Hkv, D, Tmax, freq, dev_err);
+}
+
+int anvilq_rope_kv_append(const uint16_t* qkv, const int32_t* pos, uint16_t* q_out, uint16_t* k_cache,
+                          uint16_t* v_cache, int32_t* seqlen, int Hq, int Hkv, int D, int Tmax, float theta,
+                          int* dev_err, unsigned flags, anvilq_stream_t stream) {
+  return rope_kv_append(qkv, pos, nullptr, q_out, k_cache, v_cache, seqlen, Hq, Hkv, D, Tmax, theta, dev_err, flags,
+                        stream);
+}
+
+int anvilq_rope_kv_append_at(const uint16_t* qkv, const int32_t* pos, const int32_t* row, uint16_t* q_out,
+                             uint16_t* k_cache, uint16_t* v_cache, int Hq, int Hkv, int D, int Tmax, float theta,
+                             int* dev_err, unsigned flags, anvilq_stream_t stream) {
+  if (!row) return ANVILQ_EINVAL;
+  return rope_kv_append(qkv, pos, row, q_out, k_cache, v_cache, nullptr, Hq, Hkv, D, Tmax, theta, dev_err, flags,
+                        stream);
 }
 
 int anvilq_lmhead_argmax(const float* x, const uint16_t* gamma, float eps, const uint16_t* table, float* logits,

@@ -422,7 +422,7 @@ class Decoder:
                 x=z((M, H), torch.float32), h=z((M, H), torch.float16), y=z((M, H), torch.float16),
                 qkv=z((M, (QH + 2 * KVH) * D), torch.float16), q=z((M, QH, D), torch.float16),
                 attn=z((M, QH, D), torch.float16), gu=z((M, 2 * I), torch.float16), act=z((M, I), torch.float16),
-                anc=torch.tensor([(1 << (m + 1)) - 1 for m in range(M)], dtype=torch.int32, device=dev))
+                row=z(M, torch.int32), anc=z(M, torch.int32))
             self._vbufs = bufs
         return bufs[M]
 
@@ -437,17 +437,41 @@ class Decoder:
         and the draft tokens 0..m (tree attention with a chain of ancestors).
         Rows pos + m of the caches are overwritten.  The decoder's own token and
         position are left unchanged."""
+        return self.verify_tree(tokens, list(range(-1, len(tokens) - 1)), pos)
+
+    def verify_tree(self, tokens, parents, pos: int):
+        """Run a tree of M draft tokens through the model in one pass and return
+        the greedy choice after each node.
+
+        Node m holds token ``tokens[m]`` and continues node ``parents[m]``
+        (-1: the committed prefix [0, pos); parents come first, parents[m] < m).
+        Its depth d (0 for a child of the prefix) makes it the token at position
+        pos + d: it is rotated to that position, staged in cache row pos + m, and
+        attends to the prefix and its own ancestors (itself included) only --
+        per-node positions, RoPE and ancestor visibility of the draft-tree
+        decoder (anvil-q3-ht2/design/SPEC.md:71-86; ancestor contract
+        anvil-q1-ht3/design/SPEC.md:528-533).  A chain is verify_tokens.  Rows
+        pos .. pos + M - 1 of the caches are overwritten."""
         L, H, I, QH, KVH, D, G, V, _ = self.shape
         M = len(tokens)
-        if M < 1 or M > 32 or pos < 0 or pos + M > self.max_seq:
-            raise ValueError(f"{M} draft tokens at position {pos} do not fit the cache of {self.max_seq}")
+        if M < 1 or M > 32 or len(parents) != M or pos < 0 or pos + M > self.max_seq:
+            raise ValueError(f"{M} draft nodes at position {pos} do not fit the cache of {self.max_seq}")
+        depth, anc = [], []
+        for m, par in enumerate(parents):
+            par = int(par)
+            if not -1 <= par < m:
+                raise ValueError(f"node {m}: parent {par} must be -1 or an earlier node")
+            depth.append(0 if par < 0 else depth[par] + 1)
+            anc.append((1 << m) | (0 if par < 0 else anc[par]))
         lib = _lib.load()
         b = self._verify_buffers(M)
         s = self.stream.cuda_stream
         chk = _lib.check
         with torch.cuda.stream(self.stream):
             b["tok"].copy_(torch.tensor([int(t) for t in tokens], dtype=torch.int32), non_blocking=False)
-            b["pos"].copy_(torch.arange(pos, pos + M, dtype=torch.int32), non_blocking=False)
+            b["pos"].copy_(torch.tensor([pos + d for d in depth], dtype=torch.int32), non_blocking=False)
+            b["row"].copy_(torch.arange(pos, pos + M, dtype=torch.int32), non_blocking=False)
+            b["anc"].copy_(torch.tensor(anc, dtype=torch.int64).to(torch.int32), non_blocking=False)
             for m in range(M):
                 chk(lib.anvilq_embed(self.embedding.data_ptr(), b["tok"][m:].data_ptr(), b["x"][m].data_ptr(), H, V,
                                      b["key"][m:].data_ptr(), self.dev_err.data_ptr(), 0, s), "anvilq_embed")
@@ -456,10 +480,11 @@ class Decoder:
                                             b["h"].data_ptr(), M, H, 0, s), "anvilq_rmsnorm_rows")
                 ops.gemm(b["h"], *w["qkv"], G, out=b["qkv"], dev_err=self.dev_err)
                 for m in range(M):
-                    chk(lib.anvilq_rope_kv_append(b["qkv"][m].data_ptr(), b["pos"][m:].data_ptr(), b["q"][m].data_ptr(),
-                                                  self.k_cache[l].data_ptr(), self.v_cache[l].data_ptr(), None, QH,
-                                                  KVH, D, self.max_seq, ROPE_THETA, self.dev_err.data_ptr(), 0, s),
-                        "anvilq_rope_kv_append")
+                    chk(lib.anvilq_rope_kv_append_at(b["qkv"][m].data_ptr(), b["pos"][m:].data_ptr(),
+                                                     b["row"][m:].data_ptr(), b["q"][m].data_ptr(),
+                                                     self.k_cache[l].data_ptr(), self.v_cache[l].data_ptr(), QH, KVH,
+                                                     D, self.max_seq, ROPE_THETA, self.dev_err.data_ptr(), 0, s),
+                        "anvilq_rope_kv_append_at")
                 ops.tree_attention(b["q"], self.k_cache[l], self.v_cache[l], b["anc"], pos, out=b["attn"],
                                    dev_err=self.dev_err)
                 ops.gemm(b["attn"].view(M, QH * D), *w["o"][:3], None, G, out=b["y"], dev_err=self.dev_err)
@@ -482,6 +507,21 @@ class Decoder:
         self.stream.synchronize()
         self.check_errors()
         return [int(t) for t in b["out"].cpu()]
+
+    def commit_tree_path(self, path, pos: int):
+        """After verify_tree at `pos`, move the staged K/V rows of the accepted
+        nodes ``path`` (node indices, root first) to rows pos, pos + 1, ... --
+        where sequential decoding would have written them (each was rotated to
+        exactly that position).  Path nodes have increasing indices, so no row
+        is read after it was overwritten."""
+        with torch.cuda.stream(self.stream):
+            for d, m in enumerate(path):
+                if m < d:
+                    raise ValueError("a path node cannot come before its depth")
+                if m != d:
+                    self.k_cache[:, pos + d].copy_(self.k_cache[:, pos + m])
+                    self.v_cache[:, pos + d].copy_(self.v_cache[:, pos + m])
+        self.stream.synchronize()
 
     def bytes_per_step(self, context: int) -> int:
         """Algorithmic HBM bytes of one step at a given context length."""

@@ -150,3 +150,46 @@ class SpeculativeVerifier:
 
 
 __all__ = ["Verification", "DecoderTarget", "BatchedDecoderTarget", "SpeculativeVerifier"]
+
+
+# ---- draft trees --------------------------------------------------------------
+def accept_tree(tokens, parents, predictions, first: int):
+    """The longest greedy-accepted path of a draft tree.
+
+    ``tokens[m]`` continues node ``parents[m]`` (-1: the committed prefix);
+    ``predictions[m]`` is the target's greedy choice after node m (as returned
+    by ``Decoder.verify_tree``) and ``first`` its choice after the prefix.  From
+    the prefix, a child is accepted when its token is the standing prediction
+    (among several, the lowest node index), which then becomes that child's
+    prediction; the walk stops at the first node with no accepted child.
+    Returns (path, tokens committed, next prediction): the path as node
+    indices, the accepted tokens, and the prediction after the last one --
+    exactly what sequential greedy decoding from the prefix would produce for
+    those positions (the tree's batched evaluation of anvil-q3-ht2/design/SPEC.md:71-86,
+    with the accept rule of the two-token verifier, anvil-q4/rtl/anvil_q4_speculative.sv:64-84)."""
+    if len(tokens) != len(parents) or len(predictions) != len(tokens):
+        raise ValueError("tokens, parents and predictions must have one entry per node")
+    children = {}
+    for m, par in enumerate(parents):
+        if not -1 <= int(par) < m:
+            raise ValueError(f"node {m}: parent {par} must be -1 or an earlier node")
+        children.setdefault(int(par), []).append(m)
+    path, cur, pred = [], -1, int(first)
+    while True:
+        nxt = next((m for m in children.get(cur, []) if int(tokens[m]) == pred), None)
+        if nxt is None:
+            break
+        path.append(nxt)
+        cur, pred = nxt, int(predictions[nxt])
+    return path, [int(tokens[m]) for m in path], pred
+
+
+def speculate_tree(decoder, tokens, parents, pos: int, first: int):
+    """Verify a draft tree at `pos` on ``decoder`` (one batched pass), keep the
+    accepted path's K/V rows where sequential decoding would have put them and
+    return (accepted tokens, next prediction).  ``first`` is the decoder's
+    greedy choice after the committed prefix [0, pos)."""
+    preds = decoder.verify_tree(tokens, parents, pos)
+    path, accepted, pred = accept_tree(tokens, parents, preds, first)
+    decoder.commit_tree_path(path, pos)
+    return accepted, pred

@@ -330,6 +330,15 @@ int anvilq_embed(const uint16_t* table, const int32_t* token, float* x, int H, i
 int anvilq_rope_kv_append(const uint16_t* qkv, const int32_t* pos, uint16_t* q_out, uint16_t* k_cache,
                           uint16_t* v_cache, int32_t* seqlen, int Hq, int Hkv, int D, int Tmax, float theta,
                           int* dev_err, unsigned flags, anvilq_stream_t stream);
+/* The same with the cache row given apart from the rotation's position: k and
+ * v are written to row *row, rotated by angle *pos * theta^(-2i/D).  The
+ * draft-tree verifier stages node m of a tree at row prefix + m while rotating
+ * it to its own position, prefix + depth(m) (per-node positions and RoPE of
+ * anvil-q3-ht2/design/SPEC.md:71-86).  Both in [0, Tmax), else
+ * ANVILQ_DEV_ERR_SEQLEN and nothing is written. */
+int anvilq_rope_kv_append_at(const uint16_t* qkv, const int32_t* pos, const int32_t* row, uint16_t* q_out,
+                             uint16_t* k_cache, uint16_t* v_cache, int Hq, int Hkv, int D, int Tmax, float theta,
+                             int* dev_err, unsigned flags, anvilq_stream_t stream);
 
 /* ---- tensor-parallel column split with the all-gather fused in ---------------
  *

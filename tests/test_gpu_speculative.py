@@ -77,3 +77,43 @@ def test_verify_tokens_equal_sequential_decode_steps(dev, M):
     d.step()
     d.stream.synchronize()
     assert int(d.token.item()) == seq[P + M + 1]
+
+
+@pytest.mark.parametrize("shape_id", [0, 1])
+def test_tree_draft_commits_the_greedy_path(dev, shape_id):
+    """A draft tree (branching at several depths, wrong siblings before and
+    after the right ones) verified in one batched pass: the accepted path is the
+    plain greedy decode, the next prediction is its next token, and after the
+    accepted K/V rows are moved into place plain decode steps continue exactly
+    as the sequential decode does."""
+    from anvilq_b200.speculative import speculate_tree
+    w = decoder.synthetic_weights(SHAPE, seed=47 + shape_id)
+    seq = _greedy(w, dev, 3, 24)
+    V = SHAPE[7]
+    wrong = lambda t, k=1: (t + k) % V
+    P = 5
+    d = decoder.Decoder(w, dev, max_seq=32)
+    d.reset(seq[0])
+    for _ in range(P):                 # commit tokens 0 .. P-1 by plain steps
+        d.step()
+    d.stream.synchronize()
+    first = int(d.token.item())        # the decoder's greedy choice for position P
+    assert first == seq[P]
+    if shape_id == 0:   # wrong root first; the right chain 1 -> 3 -> 5 with wrong siblings 2, 4, 6
+        tokens = [wrong(seq[P]), seq[P], wrong(seq[P + 1]), seq[P + 1], wrong(seq[P + 2], 2), seq[P + 2],
+                  wrong(seq[P + 3])]
+        parents = [-1, -1, 1, 1, 3, 3, 5]
+        want = 3
+    else:               # a bushy tree: two right levels, then only wrong children
+        tokens = [seq[P], wrong(seq[P + 1]), seq[P + 1], wrong(seq[P + 1], 2), wrong(seq[P + 2]), wrong(seq[P + 2], 3)]
+        parents = [-1, 0, 0, 0, 2, 2]
+        want = 2
+    accepted, nxt = speculate_tree(d, tokens, parents, P, first)
+    assert accepted == seq[P:P + want]
+    assert nxt == seq[P + want]
+    # continue with plain steps after the accepted tokens
+    d.set_position(nxt, P + want)
+    for k in range(3):
+        d.step()
+        d.stream.synchronize()
+        assert int(d.token.item()) == seq[P + want + 1 + k], k

@@ -173,3 +173,33 @@ def test_batched_target_whose_second_half_failed():
     r = v.verify(3, t.next(3, 0), 0, new_sequence=True)
     assert (r.accepted, r.error, r.commit_length) == (0, True, 0)
     assert v.committed_tokens == 0 and not v.sequence_valid
+
+
+def test_accept_tree_walks_the_greedy_path():
+    """accept_tree: from the prefix's prediction, each accepted child's own
+    prediction selects the next; siblings that differ are skipped, the lowest
+    matching index wins, and the walk stops at the first miss."""
+    from anvilq_b200.speculative import accept_tree
+    #        prefix -> 0:(5)  1:(7)
+    #        0 -> 2:(6)  3:(9);  3 -> 4:(1);  1 -> 5:(2)
+    tokens = [5, 7, 6, 9, 1, 2]
+    parents = [-1, -1, 0, 0, 3, 1]
+    preds = [9, 2, 0, 1, 4, 3]
+    path, acc, nxt = accept_tree(tokens, parents, preds, first=5)
+    assert path == [0, 3, 4] and acc == [5, 9, 1] and nxt == 4
+    path, acc, nxt = accept_tree(tokens, parents, preds, first=7)
+    assert path == [1, 5] and acc == [7, 2] and nxt == 3
+    path, acc, nxt = accept_tree(tokens, parents, preds, first=8)   # no root matches
+    assert path == [] and acc == [] and nxt == 8
+    # two equal siblings: the lower index is taken
+    path, _, _ = accept_tree([5, 5], [-1, -1], [1, 2], first=5)
+    assert path == [0]
+
+
+def test_accept_tree_rejects_bad_parents():
+    from anvilq_b200.speculative import accept_tree
+    with pytest.raises(ValueError):
+        accept_tree([1, 2], [-1, 1], [0, 0], first=1)   # a node is its own parent
+    with pytest.raises(ValueError):
+        accept_tree([1, 2], [-1, -2], [0, 0], first=1)
+
