@@ -267,6 +267,18 @@ def traffic_entry(key):
     return json.loads(prof.read_text()).get(key)
 
 
+def weighted_traffic(name, launches):
+    """DRAM bytes per launch for a set of launches [(algorithmic bytes, kernel)], each scaled
+    by its kernel's captured ratio for workload `name`; None if a kernel has no capture."""
+    total = 0.0
+    for nbytes, kernel in launches:
+        entry = traffic_entry(f"{kernel}/{name}")
+        if entry is None:
+            return None
+        total += nbytes * entry["ratio_read_over_algorithmic"]
+    return int(total / len(launches)) if launches else None
+
+
 # ------------------------------------------------------------ decode05b
 def _decode_oracle_sample(context, seed=17):
     """One layer of the decode step plus 1/24 of the lm_head rows, in the binary64
@@ -444,7 +456,7 @@ def summary(m):
 
 # ------------------------------------------------------------ projection sets
 def proj_measure(args, world, rank, dev, name, e2e=True):
-    from anvilq_b200 import ops
+    from anvilq_b200 import ops, synthetic
     from anvilq_b200 import stream as st
     wl = WORKLOADS[name]
     projections = getattr(st, wl["projections"])
@@ -466,8 +478,10 @@ def proj_measure(args, world, rank, dev, name, e2e=True):
     achieved = step_bytes / s.launches() / (per_launch_ms / 1e3) / 1e9
     kernels = sorted({"gemv_stream_kernel" if k == 1 else "gemv_tma_kernel" for _, k in plans})
     kernel = " + ".join(kernels)
-    entry = traffic_entry(f"{kernels[0]}/{name}") if len(kernels) == 1 else None
-    traffic = int(step_bytes / s.launches() * entry["ratio_read_over_algorithmic"]) if entry else None
+    kind = dict(plans)
+    traffic = weighted_traffic(name, [(synthetic.gemv_bytes(1, K, N, 128, bias),
+                                       "gemv_stream_kernel" if kind[(K, N)] == 1 else "gemv_tma_kernel")
+                                      for K, N, bias in projections])
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
@@ -793,6 +807,9 @@ def tp_measure(args, world, rank, dev, M, e2e=True):
     K0, N0 = wl["shapes"][0]
     stream_plan = ops.gemv_plan(K0, N0 // world)["kernel"] == 1
     kernel = ("gemv_stream_kernel" if stream_plan else "gemv_tma_kernel") if M == 1 else "verify_tc_kernel"
+    traffic = weighted_traffic("tp70b", [(synthetic.gemv_bytes(M, K, N // world),
+                                          "gemv_stream_kernel" if ops.gemv_plan(K, N // world)["kernel"] == 1
+                                          else "gemv_tma_kernel") for K, N in wl["shapes"]]) if M == 1 else None
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
@@ -809,7 +826,7 @@ def tp_measure(args, world, rank, dev, M, e2e=True):
                    "exchange_ms_per_step": round(max(0.0, ms - ms_comp) / args.steps, 5),
                    "l2": "weights larger than L2 (no flush)"},
         "roofline": {"bound": "hbm", "kernel": kernel, "achieved": round(achieved, 2), "peak": peak,
-                     "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": traffic,
                      "algorithmic_bytes_per_launch": int(shard_bytes / launches),
                      "launch_avg_us": round(per_launch * 1e3, 4),
                      "measured_on": "the rank's three GEMVs without the exchange, same run"},
