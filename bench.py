@@ -770,9 +770,12 @@ def tp_measure(args, world, rank, dev, M, e2e=True):
 
     with ClockSampler(dev.index) as clocks:
         ms = ms_nccl = timed(replay(g_full), stream, args.steps, args.warmup, world, dev)
-        if fused:
-            ms = timed(replay(g_fused), stream, args.steps, args.warmup, world, dev)
+        ms_fused = timed(replay(g_fused), stream, args.steps, args.warmup, world, dev) if fused else None
     ms_comp = timed(replay(g_comp), stream, args.steps, args.warmup, world, dev)
+    # the step runs whichever exchange was faster here (max over ranks, so every rank agrees)
+    fused = fused and ms_fused < ms_nccl
+    if fused:
+        ms = ms_fused
     ms_e2e = h2d = d2h = None
     if e2e:
         # activations from pinned host memory in, gathered outputs back to the host, every step
@@ -822,6 +825,7 @@ def tp_measure(args, world, rank, dev, M, e2e=True):
                              else "one CUDA graph per step: 3 GEMMs + 3 NCCL all-gathers" if world > 1
                              else "one CUDA graph per step: 3 GEMMs (one GPU holds every column)"),
                    "nccl_allgather_path_ms_per_step": round(ms_nccl / args.steps, 5),
+                   "fused_allgather_path_ms_per_step": None if ms_fused is None else round(ms_fused / args.steps, 5),
                    "compute_only_ms_per_step": round(ms_comp / args.steps, 5),
                    "exchange_ms_per_step": round(max(0.0, ms - ms_comp) / args.steps, 5),
                    "l2": "weights larger than L2 (no flush)"},
