@@ -637,7 +637,7 @@ int anvilq_w4a16_gemm_ex(const uint16_t* x, const int32_t* qweight, const int32_
   }
   if (M >= ANVILQ_VERIFY_TC_MIN_M && verify_tc_supported(x, qweight, qzeros, scales, M, K, N, G))
     return launch_verify_tc(x, qweight, nullptr, qzeros, scales, bias, y, M, K, N, workspace, workspace_bytes,
-                            dev_err, s);
+                            dev_err, s, (flags & ANVILQ_GEMM_OVERLAP_PRIOR) != 0);
   const DeviceInfo* d = device_info();
   if (!d) return ANVILQ_ECUDA;
   const Plan pl = plan_for(*d, M, K, N);

@@ -71,7 +71,8 @@ size_t verify_tc_workspace_bytes(int M, int K, int N);
 // qweight: AWQ layout, or null when `packed` (anvilq_w4a16_tc_pack layout) is given.
 int launch_verify_tc(const uint16_t* x, const int32_t* qweight, const int32_t* packed, const int32_t* qzeros,
                      const uint16_t* scales, const uint16_t* bias, uint16_t* y, int M, int K, int N,
-                     void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t stream);
+                     void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t stream,
+                     bool overlap_prior = false);
 size_t tc_pack_bytes(int K, int N);
 int launch_tc_pack(const int32_t* qweight, int32_t* packed, int K, int N, cudaStream_t stream);
 

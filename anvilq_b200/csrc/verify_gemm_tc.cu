@@ -46,19 +46,23 @@
 // rows); units are ordered tile-major and split into equal contiguous ranges,
 // one per CTA of a persistent grid (one CTA per SM).  A tile covered by one CTA
 // is written directly; a tile split between CTAs leaves one fp32 partial per
-// CTA in the workspace and the warp that arrives last at the (tile, warp)
-// ticket sums them in CTA order -- deterministic, no spin-wait on other CTAs.
+// CTA in the workspace ([cta][slot][column][row]: a column's rows contiguous,
+// moved as 16-byte vectors) and the warp that arrives last at the (tile, warp)
+// ticket sums them in CTA order, two contributors' loads in flight at a time
+// -- deterministic, no spin-wait on other CTAs.
 //
 // Warp roles (14 warps, one CTA per SM):
 //   0-3   epilogue: warp q reads TMEM lanes 32q..32q+31 (one output column each)
-//   4-11  dequantisers: warp 4 + 4h + q writes lane quarter q, rows 64h..64h+63
+//   4-11  dequantisers: warp 4 + 4e + q writes lane quarter q (all 128 rows) of
+//         the units e, e + 2, e + 4, ...: two teams, two units in flight
 //   12    TMA producer (the whole warp loops, one elected lane issues)
 //   13    MMA issuer (likewise) and TMEM owner
 // Pipelines (mbarriers): a TMA ring of kSR stages carrying a unit's int4 tile,
 // activation tile, zero points and scales (full: tx bytes; empty: MMA commit
-// and the 4 epilogue warps, which read the scales), two TMEM A buffers (full:
-// 8 dequant warps; empty: MMA commit), 4 TMEM accumulators (full: MMA commit;
-// empty: 4 epilogue warps).  Every wait is bounded (1 s); on expiry the CTA
+// and the 4 epilogue warps, which read the scales), four TMEM A buffers (full:
+// the 4 warps of a dequant team; empty: MMA commit), 4 TMEM accumulators (full:
+// MMA commit; empty: 4 epilogue warps).  Waits spin on try_wait (no suspend-time
+// hint) and every wait is bounded (1 s); on expiry the CTA
 // raises ANVILQ_DEV_ERR_TIMEOUT, all roles leave their loops, copies and MMAs
 // in flight are drained (bounded) and TMEM is released.
 //
@@ -92,7 +96,7 @@ constexpr int kTileWords = kTileCols / 8;              // 16 qweight words per r
 constexpr int kGroupRows = 128;                        // AWQ group = one accumulation
 constexpr int kKSteps = kGroupRows / 16;               // 8 MMAs per unit
 constexpr int kNAcc = 4;                               // TMEM accumulators
-constexpr int kSA = 2;                                 // TMEM A buffers
+constexpr int kSA = 4;                                 // TMEM A buffers (columns 256 .. 511)
 constexpr int kQBytes = kGroupRows * kTileWords * 4;   // 8 KB: [128 rows][64 B], 64-byte swizzle
 constexpr int kZBytes = kTileWords * 4;                // qzeros of one unit: 64 B
 constexpr int kSBytes = kTileCols * 2;                 // scales of one unit: 256 B
@@ -124,7 +128,7 @@ struct Params {
   const __half* scales;    // [K/128][N]
   const __half* bias;      // [N] or null
   __half* y;               // [M][N]
-  float* partials;         // [P][2][MPAD][128]
+  float* partials;         // [P][2][128][MPAD]
   int* tickets;            // [tiles][4]: one per epilogue warp
   int* dev_err;
   int M, K, N, W8;
@@ -141,15 +145,12 @@ __device__ __forceinline__ unsigned long long globaltimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// try_wait with a suspend-time hint: a waiting warp sleeps in the barrier unit
-// until the phase completes (or 0.1 ms pass) instead of re-polling.
-constexpr uint32_t kSuspendNs = 100000;
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
       : "=r"(done)
-      : "r"(bar), "r"(parity), "r"(kSuspendNs)
+      : "r"(bar), "r"(parity)
       : "memory");
   return done != 0;
 }
@@ -228,6 +229,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
+// the same load without the wait (the caller waits once for several loads)
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 // thread t writes 32 consecutive 32-bit columns of lane (base lane + t)
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
   asm volatile(
@@ -239,6 +248,17 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32
       "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+// the same store without the wait (the caller waits once for several stores)
+__device__ __forceinline__ void tmem_st32_nowait(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+      "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+      "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
 }
 
 // Shared-memory matrix descriptor (tcgen05): start, leading and stride byte
@@ -314,24 +334,74 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 4);
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < C::kSR; ++s) {
-      mbar_init(full_r(s), 1);
-      mbar_init(empty_r(s), 1);
-      mbar_init(empty_m(s), kEpiWarps);
+  // programmatic dependent launch (a no-op without the launch attribute): the
+  // next kernel on the stream may launch now; the activations (TMA) and every
+  // global write (epilogue) wait for this kernel's predecessor below
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // unit u0 + li = (column tile t, group g), advanced without divisions
+  const int first_t = (int)(u0 / p.groups), first_g = (int)(u0 % p.groups);
+  auto next_unit = [&](int& t, int& g) {
+    if (++g == p.groups) {
+      g = 0;
+      ++t;
     }
-    for (int a = 0; a < kSA; ++a) {
-      mbar_init(full_a(a), kDeqWarps);
-      mbar_init(empty_a(a), 1);
+  };
+  // one unit's copies into stage li % kSR: weights, zero points and scales
+  // (never written by a preceding kernel), then, separately, the activations
+  auto issue_weights = [&](int li, int t, int g) {
+    const int s = li % C::kSR;
+    // the last column tile copies only its columns below N
+    const uint32_t zb = (uint32_t)min(kTileWords, p.W8 - t * kTileWords) * 4;
+    const uint32_t sb = (uint32_t)min(kTileCols, p.N - t * kTileCols) * 2;
+    const uint32_t dst = base + s * C::kStageR;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(full_r(s)),
+                 "r"(C::kStageR + zb + sb)
+                 : "memory");
+    if (PACKED)
+      bulk_copy(dst + C::kXBytes, p.packed + (size_t)(u0 + li) * (kQBytes / 4), kQBytes, full_r(s));
+    else
+      tma_2d(dst + C::kXBytes, &tmq, t * kTileWords, g * kGroupRows, full_r(s));
+    bulk_copy(meta0 + s * kMetaBytes, p.qzeros + (size_t)g * p.W8 + t * kTileWords, zb, full_r(s));
+    bulk_copy(meta0 + s * kMetaBytes + kZBytes, p.scales + (size_t)g * p.N + t * kTileCols, sb, full_r(s));
+  };
+  auto issue_acts = [&](int li, int g) {
+    const int s = li % C::kSR;
+    const uint32_t dst = base + s * C::kStageR;
+    tma_2d(dst, &tmx, g * kGroupRows, 0, full_r(s));
+    tma_2d(dst + MPAD * 128, &tmx, g * kGroupRows + 64, 0, full_r(s));
+  };
+  // the producer warp initialises the barriers and sends the first few units'
+  // copies before the CTA barrier, while the MMA warp allocates TMEM (a few: every
+  // copy issued here delays the other roles' start by ~70 cycles)
+  const int pro = min(min(C::kSR, 4), nunits);
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      for (int s = 0; s < C::kSR; ++s) {
+        mbar_init(full_r(s), 1);
+        mbar_init(empty_r(s), 1);
+        mbar_init(empty_m(s), kEpiWarps);
+      }
+      for (int a = 0; a < kSA; ++a) {
+        mbar_init(full_a(a), kDeqWarps / 2);
+        mbar_init(empty_a(a), 1);
+      }
+      for (int b = 0; b < kNAcc; ++b) {
+        mbar_init(acc_full(b), 1);
+        mbar_init(acc_empty(b), kEpiWarps);
+      }
+      *s_abort = 0;
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      if (!PACKED) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmq) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmx) : "memory");
+      int t = first_t, g = first_g;
+      for (int li = 0; li < pro; ++li, next_unit(t, g)) issue_weights(li, t, g);
     }
-    for (int b = 0; b < kNAcc; ++b) {
-      mbar_init(acc_full(b), 1);
-      mbar_init(acc_empty(b), kEpiWarps);
+    asm volatile("griddepcontrol.wait;" ::: "memory");   // x may come from the previous kernel
+    if (lane == 0) {
+      int t = first_t, g = first_g;
+      for (int li = 0; li < pro; ++li, next_unit(t, g)) issue_acts(li, g);
     }
-    *s_abort = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    if (!PACKED) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmq) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmx) : "memory");
+    __syncwarp();
   }
   if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(s_tmem)),
@@ -343,14 +413,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
-  // unit u0 + li = (column tile t, group g), advanced without divisions
-  const int first_t = (int)(u0 / p.groups), first_g = (int)(u0 % p.groups);
-  auto next_unit = [&](int& t, int& g) {
-    if (++g == p.groups) {
-      g = 0;
-      ++t;
-    }
-  };
   auto fail = [&]() {
     *s_abort = 1;
     if (p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_TIMEOUT);
@@ -358,9 +420,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kProducerWarp) {
     // ---------------------------------------------------------------- TMA
-    int issued = 0;
+    int issued = pro;
     int t = first_t, g = first_g;
-    for (int li = 0; li < nunits; ++li, next_unit(t, g)) {
+    for (int li = 0; li < pro; ++li) next_unit(t, g);
+    for (int li = pro; li < nunits; ++li, next_unit(t, g)) {
       const int s = li % C::kSR;
       const uint32_t par = ((li / C::kSR) & 1) ^ 1;
       const bool ok = mbar_wait(empty_r(s), par, s_abort) && mbar_wait(empty_m(s), par, s_abort);
@@ -369,22 +432,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       if (elect_one()) {
-        // the unit's zero points and scales ride on the same barrier; the last
-        // column tile copies only its columns below N
-        const uint32_t zb = (uint32_t)min(kTileWords, p.W8 - t * kTileWords) * 4;
-        const uint32_t sb = (uint32_t)min(kTileCols, p.N - t * kTileCols) * 2;
-        const uint32_t dst = base + s * C::kStageR;
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(full_r(s)),
-                     "r"(C::kStageR + zb + sb)
-                     : "memory");
-        tma_2d(dst, &tmx, g * kGroupRows, 0, full_r(s));
-        tma_2d(dst + MPAD * 128, &tmx, g * kGroupRows + 64, 0, full_r(s));
-        if (PACKED)
-          bulk_copy(dst + C::kXBytes, p.packed + (size_t)(u0 + li) * (kQBytes / 4), kQBytes, full_r(s));
-        else
-          tma_2d(dst + C::kXBytes, &tmq, t * kTileWords, g * kGroupRows, full_r(s));
-        bulk_copy(meta0 + s * kMetaBytes, p.qzeros + (size_t)g * p.W8 + t * kTileWords, zb, full_r(s));
-        bulk_copy(meta0 + s * kMetaBytes + kZBytes, p.scales + (size_t)g * p.N + t * kTileCols, sb, full_r(s));
+        issue_weights(li, t, g);
+        issue_acts(li, g);
       }
       __syncwarp();
       issued = li + 1;
@@ -430,11 +479,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= kEpiWarps) {
     // ---------------------------------------------------------------- dequantisers
     const int q = warp % 4;                    // lane quarter: tile columns 32q .. 32q + 31
-    const int h = (warp - kEpiWarps) / 4;      // rows 64h .. 64h + 63 of the unit
+    const int team = (warp - kEpiWarps) / 4;   // units team, team + 2, ...: two units in flight
     const int r = lane / 4, l = lane % 4;
     const uint32_t tlane = (uint32_t)(q * 32) << 16;
     const half2 sixteenth = __float2half2_rn(0.0625f);
-    for (int li = 0; li < nunits; ++li) {
+    for (int li = team; li < nunits; li += 2) {
       const int s = li % C::kSR, a = li % kSA;
       bool ok = mbar_wait(full_r(s), (li / C::kSR) & 1, s_abort);
       ok = ok && mbar_wait(empty_a(a), ((li / kSA) & 1) ^ 1, s_abort);
@@ -453,6 +502,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const half2 zz = u32_as_half2((z | (z << 16)) | kMagic1024);   // (1024 + z) in both halves
       // (1024 + 16 z) / 16 = 64 + z, exact
       const half2 nzz16 = __hneg2(__hmul2(u32_as_half2(((z << 4) | (z << 20)) | kMagic1024), sixteenth));
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {   // rows 64h .. 64h + 63 of the unit
       uint32_t w[8];
       if (PACKED) {
         // [h][q][blk / 4][lane][blk % 4]: two conflict-free 16-byte loads per lane
@@ -492,7 +543,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         cells[4 * blk + 2] = half2_as_u32(__hsub2(u32_as_half2((v8 & kLoPairMask) | kMagic1024), zz));
         cells[4 * blk + 3] = half2_as_u32(__hfma2(u32_as_half2((v8 & kHiPairMask) | kMagic1024), sixteenth, nzz16));
       }
-      tmem_st32(tmem + kTmemA + a * kACols + tlane + 32 * h, cells);
+      tmem_st32_nowait(tmem + kTmemA + a * kACols + tlane + 32 * h, cells);
+      }
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(full_a(a));
@@ -502,6 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp;                      // TMEM lanes 32q .. 32q + 31
     const int ct = q * 32 + 8 * (lane % 4) + awq_lane(lane / 4);   // column within the tile
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+    asm volatile("griddepcontrol.wait;" ::: "memory");   // y and the workspace are shared with the predecessor
     float acc[MPAD];
 #pragma unroll
     for (int m = 0; m < MPAD; ++m) acc[m] = 0.0f;
@@ -529,12 +583,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(empty_m(s));
       tc_fence_after();
+      // two 16-column loads in flight per wait
 #pragma unroll
-      for (int c = 0; c < MPAD / 16; ++c) {
-        float v[16];
-        tmem_ld16(lane_addr + b * MPAD + c * 16, v);
+      for (int c = 0; c < MPAD / 16; c += 2) {
+        uint32_t v0[16], v1[16];
+        tmem_ld16_nowait(lane_addr + b * MPAD + c * 16, v0);
+        if (c + 1 < MPAD / 16) tmem_ld16_nowait(lane_addr + b * MPAD + (c + 1) * 16, v1);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-        for (int i = 0; i < 16; ++i) acc[c * 16 + i] = fmaf(sc, v[i], acc[c * 16 + i]);
+        for (int i = 0; i < 16; ++i) acc[c * 16 + i] = fmaf(sc, __uint_as_float(v0[i]), acc[c * 16 + i]);
+        if (c + 1 < MPAD / 16) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            acc[(c + 1) * 16 + i] = fmaf(sc, __uint_as_float(v1[i]), acc[(c + 1) * 16 + i]);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -555,10 +617,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Each epilogue warp owns 32 columns of the tile and settles them on its
         // own ticket (tile, warp): no barrier between the epilogue warps.
         const int slot_j = seg_u0 == u0 ? 0 : 1;
-        float* mine = p.partials + ((size_t)blockIdx.x * 2 + slot_j) * (MPAD * kTileCols);
+        // partials [cta][slot][column][MPAD]: a column's rows are contiguous, so
+        // both sides move them as 16-byte vectors (rows past M hold zeros)
+        float* mine = p.partials + ((size_t)blockIdx.x * 2 + slot_j) * (MPAD * kTileCols) + (size_t)ct * MPAD;
 #pragma unroll
-        for (int m = 0; m < MPAD; ++m)
-          if (m < p.M) __stcg(mine + m * kTileCols + ct, acc[m]);
+        for (int m = 0; m < MPAD; m += 4)
+          __stcg(reinterpret_cast<float4*>(mine + m), make_float4(acc[m], acc[m + 1], acc[m + 2], acc[m + 3]));
         __threadfence();
         __syncwarp();
         const int c_lo = owner_of(tile_u0, p.units, P);
@@ -576,28 +640,42 @@ __global__ void __launch_bounds__(kThreads, 1)
           // its range starts at the tile start; every later contributor starts
           // inside the tile (slot 0)
           const int j_lo = range_begin(c_lo, p.units, P) < tile_u0 ? 1 : 0;
-          const float* first = p.partials + ((size_t)c_lo * 2 + j_lo) * (MPAD * kTileCols) + ct;
-          const float* rest = p.partials + ((size_t)(c_lo + 1) * 2) * (MPAD * kTileCols) + ct;
+          const float* first = p.partials + ((size_t)c_lo * 2 + j_lo) * (MPAD * kTileCols) + (size_t)ct * MPAD;
+          const float* rest = p.partials + ((size_t)(c_lo + 1) * 2) * (MPAD * kTileCols) + (size_t)ct * MPAD;
           const size_t stride = (size_t)2 * MPAD * kTileCols;
           const int n_rest = c_hi - c_lo;
           if (col < p.N) {
-            // 16 rows at a time: all loads of a chunk are issued before its
-            // stores, one L2 round trip per contributor and chunk
-            for (int m0 = 0; m0 < p.M; m0 += 16) {
-              float v[16];
+            // up to 32 rows at a time; the loads of two contributors are in
+            // flight together, and the sum still runs in CTA order
+            constexpr int kCh = MPAD < 32 ? MPAD : 32;
 #pragma unroll
-              for (int i = 0; i < 16; ++i) v[i] = m0 + i < p.M ? __ldcg(first + (m0 + i) * kTileCols) : 0.0f;
-              for (int rr = 0; rr < n_rest; ++rr) {
-                float w[16];
+            for (int m0 = 0; m0 < MPAD; m0 += kCh) {
+              if (m0 >= p.M) break;
+              float4 v[kCh / 4];
 #pragma unroll
-                for (int i = 0; i < 16; ++i)
-                  w[i] = m0 + i < p.M ? __ldcg(rest + rr * stride + (m0 + i) * kTileCols) : 0.0f;
+              for (int i = 0; i < kCh / 4; ++i) v[i] = __ldcg(reinterpret_cast<const float4*>(first + m0) + i);
+              for (int rr = 0; rr < n_rest; rr += 2) {
+                const bool two = rr + 1 < n_rest;
+                float4 w0[kCh / 4], w1[kCh / 4];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) v[i] += w[i];
+                for (int i = 0; i < kCh / 4; ++i) {
+                  w0[i] = __ldcg(reinterpret_cast<const float4*>(rest + rr * stride + m0) + i);
+                  w1[i] = two ? __ldcg(reinterpret_cast<const float4*>(rest + (rr + 1) * stride + m0) + i)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int i = 0; i < kCh / 4; ++i) {
+                  v[i].x += w0[i].x; v[i].y += w0[i].y; v[i].z += w0[i].z; v[i].w += w0[i].w;
+                  if (two) { v[i].x += w1[i].x; v[i].y += w1[i].y; v[i].z += w1[i].z; v[i].w += w1[i].w; }
+                }
               }
 #pragma unroll
-              for (int i = 0; i < 16; ++i)
-                if (m0 + i < p.M) p.y[(size_t)(m0 + i) * p.N + col] = __float2half_rn(v[i] + bv);
+              for (int i = 0; i < kCh / 4; ++i) {
+                const float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                  if (m0 + 4 * i + k < p.M) p.y[(size_t)(m0 + 4 * i + k) * p.N + col] = __float2half_rn(e[k] + bv);
+              }
             }
           }
         }
@@ -737,7 +815,8 @@ int launch_tc_pack(const int32_t* qweight, int32_t* packed, int K, int N, cudaSt
 
 int launch_verify_tc(const uint16_t* x, const int32_t* qweight, const int32_t* packed, const int32_t* qzeros,
                      const uint16_t* scales, const uint16_t* bias, uint16_t* y, int M, int K, int N,
-                     void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t stream) {
+                     void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t stream,
+                     bool overlap_prior) {
   using namespace tc_verify;
   const int sms = device_sms();
   auto encode = encode_fn();
@@ -792,7 +871,19 @@ int launch_verify_tc(const uint16_t* x, const int32_t* qweight, const int32_t* p
     p.M = mc;
     p.y = reinterpret_cast<__half*>(y) + (size_t)m0 * N;
     if (packed) mq = mx;   // not read by the packed kernel
-    auto launch = [&](auto kernel, int smem) { kernel<<<pl.grid, kThreads, smem, stream>>>(mq, mx, p); };
+    auto launch = [&](auto kernel, int smem) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(pl.grid, 1, 1);
+      cfg.blockDim = dim3(kThreads, 1, 1);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = stream;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = overlap_prior ? 1 : 0;
+      cudaLaunchKernelEx(&cfg, kernel, mq, mx, p);
+    };
     switch (mpad) {
       case 16:
         packed ? launch(verify_tc_kernel<16, true>, Cfg<16>::kSmem) : launch(verify_tc_kernel<16, false>, Cfg<16>::kSmem);
