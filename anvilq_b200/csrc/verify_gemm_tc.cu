@@ -448,8 +448,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     int issued = 0;
     for (int li = 0; li < nunits; ++li) {
       const int s = li % C::kSR, a = li % kSA, b = li % kNAcc;
-      const bool ok = mbar_wait(full_r(s), (li / C::kSR) & 1, s_abort) &&
-                      mbar_wait(full_a(a), (li / kSA) & 1, s_abort) &&
+      // full_a implies full_r: the dequant team waited for the stage's copies
+      // (activations included) before it dequantised and arrived
+      const bool ok = mbar_wait(full_a(a), (li / kSA) & 1, s_abort) &&
                       mbar_wait(acc_empty(b), ((li / kNAcc) & 1) ^ 1, s_abort);
       if (!__all_sync(0xffffffffu, ok)) {
         if (lane == 0) fail();
@@ -567,8 +568,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int col = t * kTileCols + ct;
       if (g == 0) seg_u0 = u;
       const int b = li % kNAcc, s = li % C::kSR;
-      const bool ok = mbar_wait(full_r(s), (li / C::kSR) & 1, s_abort) &&
-                      mbar_wait(acc_full(b), (li / kNAcc) & 1, s_abort);
+      // acc_full implies full_r (through the MMA's full_a): the scales have landed
+      const bool ok = mbar_wait(acc_full(b), (li / kNAcc) & 1, s_abort);
       if (!__all_sync(0xffffffffu, ok)) {
         if (lane == 0) fail();
         break;
