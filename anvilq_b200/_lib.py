@@ -46,6 +46,8 @@ SIGNATURES = {
     "anvilq_w4a16_gemv_fused": (I, [P, I, P, F, P, P, P, P, P, I, I, I, I, P, SZ, P, ctypes.c_uint, P]),
     "anvilq_w4a16_gemv_qkv_rope": (I, [P, I, P, F, P, P, P, P, I, I, P, P, P, P, P, I, I, I, I, F, P, SZ, P,
                                        ctypes.c_uint, P]),
+    "anvilq_w4a16_mlp_workspace_size": (SZ, [I, I, I]),
+    "anvilq_w4a16_mlp": (I, [P, P, F, P, P, P, P, P, P, I, I, I, P, SZ, P, ctypes.c_uint, P]),
     "anvilq_peer_handle_size": (SZ, []),
     "anvilq_peer_export": (I, [P, P, ctypes.POINTER(ctypes.c_size_t)]),
     "anvilq_peer_import": (I, [P, SZ, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)]),

@@ -767,6 +767,37 @@ int anvilq_w4a16_gemv_fused(const void* x, int x_mode, const uint16_t* gamma, fl
                          reinterpret_cast<cudaStream_t>(stream), (flags & ANVILQ_GEMM_OVERLAP_PRIOR) != 0);
 }
 
+size_t anvilq_w4a16_mlp_workspace_size(int H, int I, int G) {
+  if (H <= 0 || I <= 0 || G <= 0) return 0;
+  // the partial outputs of every band of at least 16 words (128 gate/up columns)
+  return ANVILQ_WORKSPACE_COUNTER_BYTES + (size_t)((2 * (size_t)I / 8 + 15) / 16) * H * sizeof(float);
+}
+
+int anvilq_w4a16_mlp(float* r, const uint16_t* gamma, float eps, const int32_t* gu_qweight,
+                     const int32_t* gu_qzeros, const uint16_t* gu_scales, const int32_t* dn_qweight,
+                     const int32_t* dn_qzeros, const uint16_t* dn_scales, int H, int I, int G, void* workspace,
+                     size_t workspace_bytes, int* dev_err, unsigned flags, anvilq_stream_t stream) {
+  if (!r || !gamma || !gu_qweight || !gu_qzeros || !gu_scales || !dn_qweight || !dn_qzeros || !dn_scales)
+    return ANVILQ_EINVAL;
+  if (flags & ~(unsigned)ANVILQ_GEMM_OVERLAP_PRIOR) return ANVILQ_EINVAL;
+  if (!(eps >= 0.0f) || I <= 0 || I % 32 || !shape_ok(1, H, 2 * I, G) || !shape_ok(1, I, H, G)) return ANVILQ_EINVAL;
+  if (!aligned16(r) || !aligned16(gamma) || !gemv_tma_supported(r, gu_qweight, gu_qzeros, gu_scales, H, 2 * I, G))
+    return ANVILQ_ESHAPE;
+  GemvIo io;
+  io.xmode = 1;   // RMSNorm of the residual
+  io.ymode = 4;   // the MLP epilogue
+  io.xr = r;
+  io.gamma = gamma;
+  io.eps = eps;
+  io.yr = r;
+  io.dn_qweight = dn_qweight;
+  io.dn_qzeros = dn_qzeros;
+  io.dn_scales = dn_scales;
+  io.dn_H = H;
+  return launch_gemv_tma(io, gu_qweight, gu_qzeros, gu_scales, nullptr, H, 2 * I, G, workspace, workspace_bytes,
+                         dev_err, reinterpret_cast<cudaStream_t>(stream), (flags & ANVILQ_GEMM_OVERLAP_PRIOR) != 0);
+}
+
 int anvilq_w4a16_gemv_qkv_rope(const void* x, int x_mode, const uint16_t* gamma, float eps,
                                const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
                                const uint16_t* bias, int K, int G, const int32_t* pos, uint16_t* q_out,

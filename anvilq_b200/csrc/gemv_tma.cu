@@ -100,9 +100,18 @@ constexpr int smem_bytes(int stages) { return stages == 3 ? Smem<3>::kBytes : Sm
 //              full-width output (peer memory over NVLink), then the ranks'
 //              completion flags exchanged, so that when the kernel completes
 //              the full row is present on every rank (the all-gather fused in).
+//   kYMlp      the decode step's MLP: this GEMV is gate/up in unit-interleaved
+//              columns (per 32 intermediate rows: 32 gate then 32 up columns);
+//              each slice owner forms fp16(silu(fp16 g) * fp16 u) for its rows
+//              (as kXSiluMul would from the stored gate/up output), multiplies
+//              them with its rows of the down matrix (prefetched at the start),
+//              and the partials are summed over the cluster (distributed shared
+//              memory, rank order) and then over the bands (workspace, band
+//              order, by the last band to arrive) into the fp32 residual.
 enum XMode { kXHalf = 0, kXRmsNorm = 1, kXSiluMul = 2 };
-enum YMode { kYHalf = 0, kYResidual = 1, kYRope = 2, kYPeer = 3 };
+enum YMode { kYHalf = 0, kYResidual = 1, kYRope = 2, kYPeer = 3, kYMlp = 4 };
 constexpr int kMaxRopePairs = 64;   // head_dim <= 128 in the fused RoPE epilogue
+constexpr int kMlpMaxBytes = 64 * 1024;   // kYMlp: down rows, meta and slots per CTA
 constexpr int kMaxPeers = 8;        // ranks of a fused all-gather
 
 struct Params {
@@ -135,6 +144,31 @@ struct Params {
   unsigned* peer_flags[kMaxPeers];   // every rank's flag array [kMaxPeers]
   unsigned* epoch;                   // this rank's count of fused calls (device)
   int world, tp_rank, col_base;      // col_base: first column of this rank's slice
+  // kYMlp only (yr: the residual the down projection is added to)
+  const int32_t* dn_qweight;   // down [I][H / 8]
+  const int32_t* dn_qzeros;    // [I / G][H / 8]
+  const __half* dn_scales;     // [I / G][H]
+  int dn_H;                    // H: the down projection's output width
+  int dn_rows;                 // intermediate rows per slice owner (per / 2)
+  int dn_groups;               // down groups a slice owner's rows can touch (1 or 2)
+  int bands;                   // clusters of the launch (kc == 1)
+  int mlp_off;                 // dynamic shared memory offset of the down region
+};
+// kYMlp shared memory after the GEMV's own layout: the owner's down rows
+// [rows][H/8] words, its groups' zero points [groups][H/8] words and scales
+// [groups][H] fp16, its rows' activations (fp16), the cluster's partial slices
+// [c][H/c] fp32 and one mbarrier for the prefetch.
+struct MlpSmem {
+  int w, z, s, act, dslots, bar, bytes;
+  __host__ __device__ MlpSmem(int H, int rows, int groups, int c) {
+    w = 0;
+    z = w + rows * H / 2;
+    s = z + groups * H / 2;
+    act = s + groups * H * 2;
+    dslots = act + ((rows * 2 + 15) / 16) * 16;
+    bar = dslots + c * (H / c) * 4;
+    bytes = bar + 16;
+  }
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -240,7 +274,34 @@ __global__ void __launch_bounds__(kThreads, 4)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8 * s) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap) : "memory");
   }
+  // kYMlp: this CTA's rows of the down matrix and their groups' zero points and
+  // scales do not depend on any earlier kernel: request them now
+  const MlpSmem ml(YMODE == kYMlp ? p.dn_H : 32, YMODE == kYMlp ? p.dn_rows : 16, YMODE == kYMlp ? p.dn_groups : 1,
+                   YMODE == kYMlp ? c : 1);
+  const uint32_t mlp0 = smem_u32(smem + (YMODE == kYMlp ? p.mlp_off : 0));
+  const int mlp_i0 = band * (kCols / 2) + rank * p.dn_rows;                      // first intermediate row
+  const int mlp_nr = YMODE == kYMlp ? max(0, min(p.dn_rows, p.N / 2 - mlp_i0)) : 0;   // rows below I
+  if (YMODE == kYMlp && threadIdx.x == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(mlp0 + ml.bar) : "memory");
+  }
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  if (YMODE == kYMlp && threadIdx.x == 0) {
+    const int H = p.dn_H, g0 = mlp_i0 / p.G;
+    const int ng = mlp_nr > 0 ? (mlp_i0 + mlp_nr - 1) / p.G - g0 + 1 : 0;   // <= dn_groups (host)
+    const uint32_t bytes = (uint32_t)mlp_nr * H / 2 + (uint32_t)ng * (H / 2 + 2 * H);
+    const uint32_t bar = mlp0 + ml.bar;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+    auto bulk = [&](uint32_t d, const void* src, uint32_t n) {
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(d),
+                   "l"(src), "r"(n), "r"(bar)
+                   : "memory");
+    };
+    if (mlp_nr > 0) bulk(mlp0 + ml.w, p.dn_qweight + (size_t)mlp_i0 * (H / 8), (uint32_t)mlp_nr * H / 2);
+    for (int k = 0; k < ng; ++k) {
+      bulk(mlp0 + ml.z + k * (H / 2), p.dn_qzeros + (size_t)(g0 + k) * (H / 8), H / 2);
+      bulk(mlp0 + ml.s + k * (2 * H), p.dn_scales + (size_t)(g0 + k) * H, 2 * H);
+    }
+  }
   // let the next kernel on the stream start its own weight prefetch (programmatic
   // dependent launch); it still waits for this grid before touching our output
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -523,6 +584,9 @@ __global__ void __launch_bounds__(kThreads, 4)
   // pair order (head, i, half) that gives every owner both columns i and
   // i + D/2 of the heads' dims it owns (bands hold whole heads)
   auto slot_of = [&](int col) {
+    // kYMlp: band column (unit u, gate/up half, i) -> 2 (32 u + i) + half, so an
+    // owner's slice holds (gate, up) pairs of per / 2 intermediate rows
+    if (YMODE == kYMlp) return 2 * ((col / 64) * 32 + col % 32) + (col % 64) / 32;
     if (YMODE != kYRope) return col;
     const int hd = p.D / 2, head = col / p.D, j = col % p.D;
     return 2 * (head * hd + j % hd) + (j >= hd ? 1 : 0);
@@ -627,6 +691,128 @@ __global__ void __launch_bounds__(kThreads, 4)
     if (p.seqlen && band == 0 && rank == 0 && threadIdx.x == 0) *p.seqlen = pos + 1;
     return;
   }
+  if (YMODE == kYMlp) {   // kc == 1 (the host plan guarantees it)
+    const int H = p.dn_H, W8d = H / 8, cs = H / c;   // cs: output columns owned per rank
+    __half* act = reinterpret_cast<__half*>(smem + p.mlp_off + ml.act);
+    const uint32_t* dnw = reinterpret_cast<const uint32_t*>(smem + p.mlp_off + ml.w);
+    const uint32_t* dnz = reinterpret_cast<const uint32_t*>(smem + p.mlp_off + ml.z);
+    const __half* dns = reinterpret_cast<const __half*>(smem + p.mlp_off + ml.s);
+    float* dslots = reinterpret_cast<float*>(smem + p.mlp_off + ml.dslots);   // [c][cs]
+    const uint32_t dslots_u32 = mlp0 + ml.dslots;
+    // this owner's rows: g and u summed in rank order (as for the stored
+    // projection), rounded to fp16, then silu(g) u rounded to fp16
+    for (int j = threadIdx.x; j < p.dn_rows; j += kThreads) {
+      float g = slots[2 * j], u = slots[2 * j + 1];
+      for (int k = 1; k < c; ++k) {
+        g += slots[k * per + 2 * j];
+        u += slots[k * per + 2 * j + 1];
+      }
+      const float gh = __half2float(__float2half_rn(g)), uh = __half2float(__float2half_rn(u));
+      const float e = expf(-fabsf(gh));   // stable silu (official_weights.py:494-499)
+      const float sg = gh >= 0.0f ? gh / (1.0f + e) : (gh * e) / (1.0f + e);
+      act[j] = j < mlp_nr ? __float2half_rn(sg * uh) : __float2half_rn(0.0f);
+    }
+    const bool landed = mbar_wait_bounded(mlp0 + ml.bar, 0);
+    if (!landed && p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_TIMEOUT);
+    __syncthreads();
+    // down partial of this owner's rows: thread t takes words t, t + 128, ...
+    // (8 output columns each), one group at a time, flushed as in the tile loop
+    const int g0 = mlp_i0 / p.G;
+    uint32_t mbad = 0;   // an invalid down scale fails the operation, as in the down GEMV
+    for (int w = threadIdx.x; w < W8d; w += kThreads) {
+      float Ad[8], Yd[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) Ad[i] = Yd[i] = 0.0f;
+      float Xs = 0.0f;
+      auto flush_down = [&](int gl) {   // gl: the group's index among this owner's groups
+        const uint32_t zw = dnz[gl * W8d + w];
+        const uint4 s4 = reinterpret_cast<const uint4*>(dns + (size_t)gl * H)[w];
+        const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w};
+        mbad |= invalid_scale_pair(s4.x) | invalid_scale_pair(s4.y) | invalid_scale_pair(s4.z) |
+                invalid_scale_pair(s4.w);
+        const uint32_t zp[4] = {(zw & 0x000F000Fu) | 0x64006400u, ((zw >> 4) & 0x000F000Fu) | 0x64006400u,
+                                ((zw >> 8) & 0x000F000Fu) | 0x64006400u, ((zw >> 12) & 0x000F000Fu) | 0x64006400u};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 s2 = __half22float2(h2(sw[e]));
+          const float2 z2 = __half22float2(h2(zp[e]));
+          const float pw = (e & 1) ? 1048576.0f : 16777216.0f;   // 2^20 (shifted pairs) or 2^24
+          const float a0 = fmaf(-(z2.x - 1024.0f), Xs, Ad[2 * e] * pw);
+          const float a1 = fmaf(-(z2.y - 1024.0f), Xs, Ad[2 * e + 1] * pw);
+          Yd[2 * e] = fmaf(s2.x, a0, Yd[2 * e]);
+          Yd[2 * e + 1] = fmaf(s2.y, a1, Yd[2 * e + 1]);
+          Ad[2 * e] = 0.0f;
+          Ad[2 * e + 1] = 0.0f;
+        }
+        Xs = 0.0f;
+      };
+      if (landed) {
+        for (int j = 0; j < mlp_nr; ++j) {
+          if (j > 0 && (mlp_i0 + j) % p.G == 0) flush_down((mlp_i0 + j - 1) / p.G - g0);
+          const unsigned short xh = __half_as_ushort(act[j]);
+          const uint32_t wd = dnw[j * W8d + w], w8 = wd >> 8;
+          fma_f32_f16x2(Ad[0], Ad[1], wd & 0x000F000Fu, xh);   // columns 0,1
+          fma_f32_f16x2(Ad[2], Ad[3], wd & 0x00F000F0u, xh);   // columns 2,3 (x16)
+          fma_f32_f16x2(Ad[4], Ad[5], w8 & 0x000F000Fu, xh);   // columns 4,5
+          fma_f32_f16x2(Ad[6], Ad[7], w8 & 0x00F000F0u, xh);   // columns 6,7 (x16)
+          Xs += __half2float(act[j]);
+        }
+        if (mlp_nr > 0) flush_down((mlp_i0 + mlp_nr - 1) / p.G - g0);
+      }
+      // columns 8w .. 8w + 7 belong to owner 8w / cs (cs % 8 == 0)
+      const int owner = (8 * w) / cs, lc = 8 * w - owner * cs;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (c > 1) {
+          st_dsmem_f32(dsmem_addr_u32(dslots_u32 + (rank * cs + lc + i) * 4, owner), Yd[i]);
+        } else {
+          dslots[lc + i] = Yd[i];
+        }
+      }
+    }
+    if (mbad && p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_SCALE);
+    if (!landed) mbar_wait_bounded(mlp0 + ml.bar, 0);   // copies in flight land before the CTA can exit
+    if (c > 1) {
+      cluster_arrive_release();
+      cluster_wait_acquire();
+    } else {
+      __syncthreads();
+    }
+    // the cluster's (the band's) partial of this rank's columns, summed in rank
+    // order, into the workspace; the band arriving last adds every band's
+    // partial in band order to the residual
+    float* part = p.partials + (size_t)band * H + rank * cs;
+    for (int t = threadIdx.x; t < cs; t += kThreads) {
+      float v = dslots[t];
+      for (int k = 1; k < c; ++k) v += dslots[k * cs + t];
+      __stcg(part + t, v);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      const int n = atomicAdd(p.tickets + rank, 1);
+      s_last = n == p.bands - 1;
+      if (s_last) p.tickets[rank] = 0;   // re-armed for the next launch
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int t = threadIdx.x; t < cs; t += kThreads) {
+      const float* col = p.partials + rank * cs + t;
+      float acc = 0.0f;
+      int b = 0;
+      for (; b + 8 <= p.bands; b += 8) {   // eight loads in flight, then the ordered sum
+        float r8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) r8[k] = __ldcg(col + (size_t)(b + k) * H);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc += r8[k];
+      }
+      for (; b < p.bands; ++b) acc += __ldcg(col + (size_t)b * H);
+      p.yr[rank * cs + t] += acc;
+    }
+    return;
+  }
   constexpr int kMaxPer = kCols / kThreads;   // up to 4 columns per thread (c == 1)
   float v[kMaxPer];
 #pragma unroll
@@ -724,6 +910,10 @@ static KernelFn kernel_y(int ymode, int bw) {
     if constexpr (XM == kXHalf) return kernel_bw<kXHalf, kYPeer, S>(bw);
     return nullptr;
   }
+  if (ymode == kYMlp) {   // the MLP reads the residual stream through RMSNorm
+    if constexpr (XM == kXRmsNorm) return kernel_bw<kXRmsNorm, kYMlp, S>(bw);
+    return nullptr;
+  }
   return ymode == kYHalf ? kernel_bw<XM, kYHalf, S>(bw) : ymode == kYResidual ? kernel_bw<XM, kYResidual, S>(bw)
                                                                             : kernel_bw<XM, kYRope, S>(bw);
 }
@@ -744,11 +934,12 @@ static const DeviceInfo* device_info() {
     cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
     for (int st = kMinStages; st <= kMaxStages; ++st)
       for (int xm = 0; xm < 3; ++xm)
-        for (int ym = 0; ym < 4; ++ym)
+        for (int ym = 0; ym < 5; ++ym)
           for (int bw : kBandWidths) {
             KernelFn k = kernel_for(xm, ym, bw, st);
             if (!k) continue;
-            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(st));
+            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 smem_bytes(st) + (ym == kYMlp ? kMlpMaxBytes + 128 : 0));
             cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
           }
     for (int st = kMinStages; st <= kMaxStages; ++st)
@@ -946,8 +1137,9 @@ int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qze
   const DeviceInfo* d = device_info();
   auto encode = encode_fn();
   if (!d || d->sms <= 0 || !encode) return ANVILQ_ECUDA;
-  if (io.xmode < 0 || io.xmode > 2 || io.ymode < 0 || io.ymode > 3) return ANVILQ_EINVAL;
+  if (io.xmode < 0 || io.xmode > 2 || io.ymode < 0 || io.ymode > 4) return ANVILQ_EINVAL;
   if (io.ymode == kYPeer && io.xmode != kXHalf) return ANVILQ_EINVAL;
+  if (io.ymode == kYMlp && (io.xmode != kXRmsNorm || bias || !io.yr)) return ANVILQ_EINVAL;
   if (plan && (io.xmode != kXHalf || io.ymode != kYHalf)) return ANVILQ_EINVAL;
   Plan pl = plan ? plan_from(*plan, K, N) : choose_plan(*d, K, N);
   const int* max_clusters = d->max_clusters[pl.stages - kMinStages];
@@ -973,6 +1165,29 @@ int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qze
       pl.kc = 1;
     }
   }
+  int dn_rows = 0, dn_groups = 0, mlp_off = 0, mlp_bytes = 0;
+  if (io.ymode == kYMlp) {
+    // one cluster per band (the owners' rows are final after the cluster sum),
+    // and every owner's share of the H outputs a whole number of 8-column words
+    const int H = io.dn_H;
+    if (H < 8 || H % 32 || N % 64 || !io.dn_qweight || !io.dn_qzeros || !io.dn_scales) return ANVILQ_ESHAPE;
+    auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    if (!a16(io.dn_qweight) || !a16(io.dn_qzeros) || !a16(io.dn_scales) || !a16(io.yr)) return ANVILQ_EALIGN;
+    pl.kc = 1;
+    while (pl.c > 1 && H % (8 * pl.c)) pl.c /= 2;
+    // the 3-stage ring: with the down region a CTA stays within a third of an
+    // SM's shared memory, so the plan's clusters remain co-resident in one wave
+    pl.stages = kMinStages;
+    dn_rows = pl.bw * 8 / pl.c / 2;
+    // groups an owner's rows can touch: owners start at multiples of dn_rows
+    dn_groups = G % dn_rows == 0 ? 1 : (dn_rows + G - 1) / G + 1;
+    mlp_bytes = MlpSmem(H, dn_rows, dn_groups, pl.c).bytes;
+    if (mlp_bytes > kMlpMaxBytes) return ANVILQ_ESHAPE;
+    mlp_off = (smem_bytes(pl.stages) + 127) / 128 * 128;
+    if (!workspace || workspace_bytes < ANVILQ_WORKSPACE_COUNTER_BYTES + (size_t)pl.bands * H * sizeof(float))
+      return ANVILQ_EWORKSPACE;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 15u) != 0) return ANVILQ_EALIGN;
+  }
   if (pl.kc > 1) {
     if (!workspace || workspace_bytes < pl.bytes) return ANVILQ_EWORKSPACE;
     if ((reinterpret_cast<uintptr_t>(workspace) & 15u) != 0) return ANVILQ_EALIGN;
@@ -992,7 +1207,7 @@ int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qze
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return ANVILQ_EALIGN;
-  Params p;
+  Params p = {};
   p.x = reinterpret_cast<const __half*>(io.x);
   p.xr = io.xr;
   p.gamma = reinterpret_cast<const __half*>(io.gamma);
@@ -1027,11 +1242,19 @@ int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qze
   p.cluster = pl.c;
   p.kc = pl.kc;
   p.tiles = pl.tiles;
+  p.dn_qweight = io.dn_qweight;
+  p.dn_qzeros = io.dn_qzeros;
+  p.dn_scales = reinterpret_cast<const __half*>(io.dn_scales);
+  p.dn_H = io.dn_H;
+  p.dn_rows = dn_rows;
+  p.dn_groups = dn_groups;
+  p.bands = pl.bands;
+  p.mlp_off = mlp_off;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.bands * pl.kc * pl.c, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem_bytes(pl.stages);
+  cfg.dynamicSmemBytes = io.ymode == kYMlp ? mlp_off + mlp_bytes : smem_bytes(pl.stages);
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;

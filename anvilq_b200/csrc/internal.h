@@ -42,6 +42,12 @@ struct GemvIo {
   unsigned* peer_flags[8] = {};
   unsigned* epoch = nullptr;
   int world = 0, tp_rank = 0, col_base = 0;
+  // ymode 4 (the MLP: gate/up in unit-interleaved columns, down in the
+  // epilogue, added into yr)
+  const int32_t* dn_qweight = nullptr;
+  const int32_t* dn_qzeros = nullptr;
+  const uint16_t* dn_scales = nullptr;
+  int dn_H = 0;
 };
 // plan: null for the default plan of the shape; a given plan is only taken
 // for x_mode/y_mode 0 and must have passed gemv_cluster_check_plan.

@@ -120,10 +120,12 @@ class Decoder:
     records it as a CUDA graph that every later step replays."""
 
     def __init__(self, weights: DecoderWeights, device="cuda", max_seq: int = 2048, keep_logits: bool = False,
-                 fused: bool | None = False):
+                 fused: bool | None = False, mlp: bool = False):
         """fused: run the layers as one persistent kernel (True: require it;
         None: when the shape allows it; False, the default: one kernel per
-        operation, the faster path on B200 at the 0.5B shape)."""
+        operation, the faster path on B200 at the 0.5B shape).
+        mlp: on the per-operation path, run each layer's MLP (gate/up and down)
+        as one launch (anvilq_w4a16_mlp) instead of two fused GEMVs."""
         self.shape = weights.shape
         L, H, I, QH, KVH, D, G, V, SEQ = self.shape
         self.max_seq = min(max_seq, SEQ)
@@ -199,6 +201,10 @@ class Decoder:
                                                                p(self.k_cache[l]), p(self.v_cache[l])])
             self.layer_table = torch.tensor(rows, dtype=torch.int64, device=dev)
             torch.cuda.synchronize(dev)
+        self.mlp = bool(mlp) and not self.fused
+        if self.mlp:
+            self.mlp_gu = [ops.mlp_interleave(*w["gu"][:3]) for w in self.layers]
+            self.mlp_ws = torch.zeros(lib.anvilq_w4a16_mlp_workspace_size(H, I, G), dtype=torch.uint8, device=dev)
         self.stream = torch.cuda.Stream(dev)
         self.graph = None
         # host staging for the end-to-end path
@@ -226,6 +232,16 @@ class Decoder:
             self.q.data_ptr(), self.k_cache[l].data_ptr(), self.v_cache[l].data_ptr(), self.seqlen.data_ptr(),
             QH, KVH, D, self.max_seq, ROPE_THETA, self.workspace.data_ptr(), self.workspace.numel(),
             self.dev_err.data_ptr(), FLAG_OVERLAP, self.stream.cuda_stream), "anvilq_w4a16_gemv_qkv_rope")
+
+    def _mlp(self, l, w):
+        """Layer l's MLP in one launch: x += down(silu(gate) up) of RMSNorm(x)."""
+        L, H, I, QH, KVH, D, G, V, _ = self.shape
+        gq, gz, gs = self.mlp_gu[l]
+        dq, dz, ds = w["down"][:3]
+        _lib.check(_lib.load().anvilq_w4a16_mlp(
+            self.x.data_ptr(), self.gamma_post[l].data_ptr(), RMS_EPS, gq.data_ptr(), gz.data_ptr(), gs.data_ptr(),
+            dq.data_ptr(), dz.data_ptr(), ds.data_ptr(), H, I, G, self.mlp_ws.data_ptr(), self.mlp_ws.numel(),
+            self.dev_err.data_ptr(), FLAG_OVERLAP, self.stream.cuda_stream), "anvilq_w4a16_mlp")
 
     def _layers_fused(self):
         """Every layer of the step as one persistent kernel (anvilq_decode_layers)."""
@@ -262,8 +278,11 @@ class Decoder:
                 self.attn.data_ptr(), 1, QH, KVH, D, self.max_seq, 0.0, self.workspace.data_ptr(),
                 self.workspace.numel(), self.dev_err.data_ptr(), s), "anvilq_gqa_decode")
             self._gemv(w["o"], self.attn, 0, None, self.x, 1, QH * D, H)
-            self._gemv(w["gu"], self.x, 1, self.gamma_post[l], self.gu, 0, H, 2 * I)
-            self._gemv(w["down"], self.gu, 2, None, self.x, 1, I, H)
+            if self.mlp:
+                self._mlp(l, w)
+            else:
+                self._gemv(w["gu"], self.x, 1, self.gamma_post[l], self.gu, 0, H, 2 * I)
+                self._gemv(w["down"], self.gu, 2, None, self.x, 1, I, H)
         _lib.check(lib.anvilq_lmhead_argmax(
             self.x.data_ptr(), self.gamma_final.data_ptr(), RMS_EPS, self.embedding.data_ptr(),
             None if self.logits is None else self.logits.data_ptr(), self.key.data_ptr(), H, V, FLAG_OVERLAP, s),
@@ -274,7 +293,7 @@ class Decoder:
             self.token_out.copy_(self.token, non_blocking=True)
 
     def kernels_per_step(self) -> int:
-        return 3 if self.fused else 1 + 5 * self.shape[0] + 2
+        return 3 if self.fused else 1 + (4 if self.mlp else 5) * self.shape[0] + 2
 
     def record_layers(self):
         """A CUDA graph of the fused layers kernel alone (the step without the

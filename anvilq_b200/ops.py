@@ -185,6 +185,40 @@ def gemv_planned(x, qweight, qzeros, scales, bias=None, group: int = 128, plan=N
     return out
 
 
+def mlp_interleave(qweight, qzeros, scales):
+    """gate|up AWQ tensors (gate columns first: qweight and qzeros [rows, 2I/8],
+    scales [groups, 2I]) in the unit-interleaved column order ``mlp`` takes: for
+    every 32 intermediate rows, the gate's 4 words (32 columns) then the up's 4."""
+    def perm(t, per):
+        r, n = t.shape
+        return t.view(r, 2, n // (2 * per), per).permute(0, 2, 1, 3).reshape(r, n).contiguous()
+    return perm(qweight, 4), perm(qzeros, 4), perm(scales, 32)
+
+
+def mlp(r, gamma, gu, down, group: int = 128, eps: float = 1e-6, dev_err=None, overlap_prior: bool = False):
+    """The decode step's MLP in one launch (anvilq_w4a16_mlp), in place on the fp32
+    residual r [H]: r += fp16(silu(g) u) @ W_down with g, u = fp16(RMSNorm(r) gamma @
+    W_gate / W_up).  gu: (qweight, qzeros, scales) in the order of ``mlp_interleave``;
+    down: AWQ (qweight, qzeros, scales) [I, H/8]."""
+    if r.dtype != torch.float32 or r.dim() != 1 or not r.is_contiguous():
+        raise ValueError("r must be a contiguous float32 vector")
+    H = r.numel()
+    gq, gz, gs = gu
+    dq, dz, ds = down[:3]
+    I = dq.shape[0]
+    if gq.shape != (H, 2 * I // 8) or dq.shape != (I, H // 8):
+        raise ValueError(f"gate/up must be [{H}, {2 * I // 8}] and down [{I}, {H // 8}] words")
+    lib = _lib.load()
+    need = lib.anvilq_w4a16_mlp_workspace_size(H, I, group)
+    ws = workspace(r.device, need)
+    err = device_error_word(r.device) if dev_err is None else dev_err
+    _lib.check(lib.anvilq_w4a16_mlp(_ptr(r), _ptr(gamma), eps, _ptr(gq), _ptr(gz), _ptr(gs), _ptr(dq), _ptr(dz),
+                                    _ptr(ds), H, I, group, _ptr(ws), ws.numel(), _ptr(err),
+                                    GEMM_OVERLAP_PRIOR if overlap_prior else 0, _stream_ptr(r.device)),
+               "anvilq_w4a16_mlp")
+    return r
+
+
 def verify_gemm(x, qweight, qzeros, scales, bias=None, group: int = 128, out=None, dev_err=None):
     """The speculative-verify GEMM forced onto the tcgen05 tensor-core kernel for any M.
 

@@ -216,6 +216,30 @@ int anvilq_w4a16_gemv_fused(const void* x, int x_mode, const uint16_t* gamma, fl
                             void* workspace, size_t workspace_bytes, int* dev_err, unsigned flags,
                             anvilq_stream_t stream);
 
+/* The decode step's MLP in one launch (FP32Model.token's feed-forward block,
+ * official_weights.py:491-503):
+ *   h = fp16(RMSNorm(r) * gamma);  g, u = fp16(h @ W_gate), fp16(h @ W_up)
+ *   r += fp16(silu(g) * u) @ W_down                      (r: fp32 [H], in place)
+ * with the same operations and precisions as anvilq_w4a16_gemv_fused
+ * (RMSNORM in, HALF out) on [gate | up] followed by anvilq_w4a16_gemv_fused
+ * (SILU_MUL in, RESIDUAL out) on down; only the order of the down projection's
+ * fp32 sums differs (per-row-slice partials summed over the cluster, then over
+ * the bands in band order: bit-reproducible).
+ * gate/up weights in unit-interleaved columns: for every 32 intermediate rows
+ * u, 32 gate columns then 32 up columns, i.e. qweight [H][2I/8] with word
+ * 8u + w = gate word 4u + w and word 8u + 4 + w = up word 4u + w (w < 4),
+ * qzeros [H/G][2I/8] the same, scales [H/G][2I] with column 64u + i = gate
+ * 32u + i and 64u + 32 + i = up 32u + i.  down: AWQ [I][H/8].  Needs
+ * I % 32 == 0, H % 32 == 0, G % 16 == 0, 16-byte aligned pointers
+ * (ANVILQ_ESHAPE / ANVILQ_EALIGN otherwise); workspace of
+ * anvilq_w4a16_mlp_workspace_size bytes, counters zeroed before the first call
+ * (the kernel re-arms them).  flags: ANVILQ_GEMM_OVERLAP_PRIOR. */
+size_t anvilq_w4a16_mlp_workspace_size(int H, int I, int G);
+int anvilq_w4a16_mlp(float* r, const uint16_t* gamma, float eps, const int32_t* gu_qweight,
+                     const int32_t* gu_qzeros, const uint16_t* gu_scales, const int32_t* dn_qweight,
+                     const int32_t* dn_qzeros, const uint16_t* dn_scales, int H, int I, int G, void* workspace,
+                     size_t workspace_bytes, int* dev_err, unsigned flags, anvilq_stream_t stream);
+
 /* The decode step's QKV projection with RoPE and the KV-cache append fused
  * into its epilogue: y = the GEMV of anvilq_w4a16_gemv_fused (same x_mode
  * inputs; N = (Hq + 2 Hkv) * D) rounded to fp16 (y_mode ANVILQ_GEMV_Y_HALF),
