@@ -749,14 +749,16 @@ int anvilq_w4a16_gemv_fused(const void* x, int x_mode, const uint16_t* gamma, fl
   if (!x || !qweight || !qzeros || !scales || !y) return ANVILQ_EINVAL;
   if (flags & ~(unsigned)ANVILQ_GEMM_OVERLAP_PRIOR) return ANVILQ_EINVAL;
   if (x_mode < ANVILQ_GEMV_X_HALF || x_mode > ANVILQ_GEMV_X_SILU_MUL) return ANVILQ_EINVAL;
-  if (y_mode < ANVILQ_GEMV_Y_HALF || y_mode > ANVILQ_GEMV_Y_RESIDUAL) return ANVILQ_EINVAL;
+  if (y_mode < ANVILQ_GEMV_Y_HALF || y_mode > ANVILQ_GEMV_Y_SILU_MUL) return ANVILQ_EINVAL;
   if (x_mode == ANVILQ_GEMV_X_RMSNORM && (!gamma || !(eps >= 0.0f))) return ANVILQ_EINVAL;
+  if (y_mode == ANVILQ_GEMV_Y_SILU_MUL && (x_mode == ANVILQ_GEMV_X_SILU_MUL || bias || N % 64))
+    return ANVILQ_EINVAL;
   if (!shape_ok(1, K, N, G)) return ANVILQ_EINVAL;
   const bool a16 = aligned16(x) && aligned16(y) && (!gamma || aligned16(gamma));
   if (!a16 || !gemv_tma_supported(x, qweight, qzeros, scales, K, N, G)) return ANVILQ_ESHAPE;
   GemvIo io;
   io.xmode = x_mode;
-  io.ymode = y_mode;
+  io.ymode = y_mode == ANVILQ_GEMV_Y_SILU_MUL ? 5 : y_mode;   // the kernel's activation epilogue
   io.x = static_cast<const uint16_t*>(x);
   io.xr = static_cast<const float*>(x);
   io.gamma = gamma;

@@ -109,7 +109,11 @@ constexpr int smem_bytes(int stages) { return stages == 3 ? Smem<3>::kBytes : Sm
 //              memory, rank order) and then over the bands (workspace, band
 //              order, by the last band to arrive) into the fp32 residual.
 enum XMode { kXHalf = 0, kXRmsNorm = 1, kXSiluMul = 2 };
-enum YMode { kYHalf = 0, kYResidual = 1, kYRope = 2, kYPeer = 3, kYMlp = 4 };
+//   kYAct      gate/up in the same unit-interleaved columns; y = the activations
+//              fp16(silu(fp16 g) * fp16 u) [N / 2] -- what the SiLU prologue of
+//              the down projection would compute from the stored gate/up output,
+//              so the down projection reads them as fp16 x (kXHalf), bit-identical.
+enum YMode { kYHalf = 0, kYResidual = 1, kYRope = 2, kYPeer = 3, kYMlp = 4, kYAct = 5 };
 constexpr int kMaxRopePairs = 64;   // head_dim <= 128 in the fused RoPE epilogue
 constexpr int kMlpMaxBytes = 64 * 1024;   // kYMlp: down rows, meta and slots per CTA
 constexpr int kMaxPeers = 8;        // ranks of a fused all-gather
@@ -586,7 +590,7 @@ __global__ void __launch_bounds__(kThreads, 4)
   auto slot_of = [&](int col) {
     // kYMlp: band column (unit u, gate/up half, i) -> 2 (32 u + i) + half, so an
     // owner's slice holds (gate, up) pairs of per / 2 intermediate rows
-    if (YMODE == kYMlp) return 2 * ((col / 64) * 32 + col % 32) + (col % 64) / 32;
+    if (YMODE == kYMlp || YMODE == kYAct) return 2 * ((col / 64) * 32 + col % 32) + (col % 64) / 32;
     if (YMODE != kYRope) return col;
     const int hd = p.D / 2, head = col / p.D, j = col % p.D;
     return 2 * (head * hd + j % hd) + (j >= hd ? 1 : 0);
@@ -689,6 +693,24 @@ __global__ void __launch_bounds__(kThreads, 4)
       }
     }
     if (p.seqlen && band == 0 && rank == 0 && threadIdx.x == 0) *p.seqlen = pos + 1;
+    return;
+  }
+  if (YMODE == kYAct) {   // kc == 1 (the host plan guarantees it)
+    // this owner's per / 2 intermediate rows: g and u summed in rank order (as
+    // for the stored projection), rounded to fp16, then silu(g) u rounded to fp16
+    const int i0 = band * (kCols / 2) + rank * (per / 2);
+    for (int j = threadIdx.x; j < per / 2; j += kThreads) {
+      if (i0 + j >= p.N / 2) continue;
+      float g = slots[2 * j], u = slots[2 * j + 1];
+      for (int k = 1; k < c; ++k) {
+        g += slots[k * per + 2 * j];
+        u += slots[k * per + 2 * j + 1];
+      }
+      const float gh = __half2float(__float2half_rn(g)), uh = __half2float(__float2half_rn(u));
+      const float e = expf(-fabsf(gh));   // stable silu (official_weights.py:494-499)
+      const float sg = gh >= 0.0f ? gh / (1.0f + e) : (gh * e) / (1.0f + e);
+      p.y[i0 + j] = __float2half_rn(sg * uh);
+    }
     return;
   }
   if (YMODE == kYMlp) {   // kc == 1 (the host plan guarantees it)
@@ -914,6 +936,10 @@ static KernelFn kernel_y(int ymode, int bw) {
     if constexpr (XM == kXRmsNorm) return kernel_bw<kXRmsNorm, kYMlp, S>(bw);
     return nullptr;
   }
+  if (ymode == kYAct) {   // gate/up: the residual through RMSNorm, or fp16 x
+    if constexpr (XM == kXRmsNorm || XM == kXHalf) return kernel_bw<XM, kYAct, S>(bw);
+    return nullptr;
+  }
   return ymode == kYHalf ? kernel_bw<XM, kYHalf, S>(bw) : ymode == kYResidual ? kernel_bw<XM, kYResidual, S>(bw)
                                                                             : kernel_bw<XM, kYRope, S>(bw);
 }
@@ -934,7 +960,7 @@ static const DeviceInfo* device_info() {
     cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
     for (int st = kMinStages; st <= kMaxStages; ++st)
       for (int xm = 0; xm < 3; ++xm)
-        for (int ym = 0; ym < 5; ++ym)
+        for (int ym = 0; ym < 6; ++ym)
           for (int bw : kBandWidths) {
             KernelFn k = kernel_for(xm, ym, bw, st);
             if (!k) continue;
@@ -1137,7 +1163,8 @@ int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qze
   const DeviceInfo* d = device_info();
   auto encode = encode_fn();
   if (!d || d->sms <= 0 || !encode) return ANVILQ_ECUDA;
-  if (io.xmode < 0 || io.xmode > 2 || io.ymode < 0 || io.ymode > 4) return ANVILQ_EINVAL;
+  if (io.xmode < 0 || io.xmode > 2 || io.ymode < 0 || io.ymode > 5) return ANVILQ_EINVAL;
+  if (io.ymode == kYAct && (io.xmode == kXSiluMul || bias || N % 64)) return ANVILQ_EINVAL;
   if (io.ymode == kYPeer && io.xmode != kXHalf) return ANVILQ_EINVAL;
   if (io.ymode == kYMlp && (io.xmode != kXRmsNorm || bias || !io.yr)) return ANVILQ_EINVAL;
   if (plan && (io.xmode != kXHalf || io.ymode != kYHalf)) return ANVILQ_EINVAL;
@@ -1165,6 +1192,7 @@ int launch_gemv_tma(const GemvIo& io, const int32_t* qweight, const int32_t* qze
       pl.kc = 1;
     }
   }
+  if (io.ymode == kYAct) pl.kc = 1;   // the owners' (gate, up) sums are final after the cluster sum
   int dn_rows = 0, dn_groups = 0, mlp_off = 0, mlp_bytes = 0;
   if (io.ymode == kYMlp) {
     // one cluster per band (the owners' rows are final after the cluster sum),

@@ -120,12 +120,16 @@ class Decoder:
     records it as a CUDA graph that every later step replays."""
 
     def __init__(self, weights: DecoderWeights, device="cuda", max_seq: int = 2048, keep_logits: bool = False,
-                 fused: bool | None = False, mlp: bool = False):
+                 fused: bool | None = False, mlp: bool = False, gu_act: bool = True):
         """fused: run the layers as one persistent kernel (True: require it;
         None: when the shape allows it; False, the default: one kernel per
         operation, the faster path on B200 at the 0.5B shape).
         mlp: on the per-operation path, run each layer's MLP (gate/up and down)
-        as one launch (anvilq_w4a16_mlp) instead of two fused GEMVs."""
+        as one launch (anvilq_w4a16_mlp) instead of two fused GEMVs.
+        gu_act: the gate/up GEMV stores fp16(silu(g) u) itself (its columns
+        interleaved at load time) and the down GEMV reads it as fp16 input --
+        bit-identical to the gate/up output followed by the SiLU prologue, and
+        faster (the prologue's per-row exp left the down GEMV's tile loop)."""
         self.shape = weights.shape
         L, H, I, QH, KVH, D, G, V, SEQ = self.shape
         self.max_seq = min(max_seq, SEQ)
@@ -202,9 +206,13 @@ class Decoder:
             self.layer_table = torch.tensor(rows, dtype=torch.int64, device=dev)
             torch.cuda.synchronize(dev)
         self.mlp = bool(mlp) and not self.fused
-        if self.mlp:
+        self.gu_act = bool(gu_act) and not self.fused and not self.mlp
+        if self.mlp or self.gu_act:   # gate/up columns unit-interleaved (anvilq_w4a16_mlp's order)
             self.mlp_gu = [ops.mlp_interleave(*w["gu"][:3]) for w in self.layers]
+        if self.mlp:
             self.mlp_ws = torch.zeros(lib.anvilq_w4a16_mlp_workspace_size(H, I, G), dtype=torch.uint8, device=dev)
+        if self.gu_act:
+            self.act = torch.empty(I, dtype=torch.float16, device=dev)
         self.stream = torch.cuda.Stream(dev)
         self.graph = None
         # host staging for the end-to-end path
@@ -280,6 +288,9 @@ class Decoder:
             self._gemv(w["o"], self.attn, 0, None, self.x, 1, QH * D, H)
             if self.mlp:
                 self._mlp(l, w)
+            elif self.gu_act:
+                self._gemv((*self.mlp_gu[l], None), self.x, 1, self.gamma_post[l], self.act, 2, H, 2 * I)
+                self._gemv(w["down"], self.act, 0, None, self.x, 1, I, H)
             else:
                 self._gemv(w["gu"], self.x, 1, self.gamma_post[l], self.gu, 0, H, 2 * I)
                 self._gemv(w["down"], self.gu, 2, None, self.x, 1, I, H)
@@ -382,15 +393,17 @@ class Decoder:
         zeros, scales, bias) plus what the prologue reads and the epilogue
         writes -- QKV: fp32 residual and fp16 gamma in, q and the new K / V rows
         out (fp16); O: fp16 attention output in, fp32 residual read and written;
-        gate/up: fp32 residual and gamma in, fp16 [gate | up] out; down: fp16
-        gate and up in, fp32 residual read and written."""
+        gate/up: fp32 residual and gamma in, fp16 [gate | up] out (fp16 silu(g) u
+        with gu_act); down: fp16 gate and up in (the fp16 products with gu_act),
+        fp32 residual read and written."""
         L, H, I, QH, KVH, D, G, V, _ = self.shape
         w = lambda K, N, bias: synthetic.gemv_bytes(1, K, N, G, bias) - 2 * K - 2 * N   # weights only
         nqkv = (QH + 2 * KVH) * D
+        act = I if getattr(self, "gu_act", False) else 2 * I   # fp16 elements between gate/up and down
         b = w(H, nqkv, True) + 4 * H + 2 * H + 2 * nqkv
         b += w(QH * D, H, False) + 2 * QH * D + 8 * H
-        b += w(H, 2 * I, False) + 4 * H + 2 * H + 2 * 2 * I
-        b += w(I, H, False) + 2 * 2 * I + 8 * H
+        b += w(H, 2 * I, False) + 4 * H + 2 * H + 2 * act
+        b += w(I, H, False) + 2 * act + 8 * H
         return b * L
 
     def fill_context(self, length: int, seed: int = 0):

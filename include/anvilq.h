@@ -202,6 +202,15 @@ int anvilq_w4a16_verify_gemm_packed(const uint16_t* x, const int32_t* packed, co
  *                                 (x: fp16 [2K] = [g | u], a fused gate/up output; :493-501)
  *   y_mode ANVILQ_GEMV_Y_HALF     y fp16 [N] = result (+ bias)
  *          ANVILQ_GEMV_Y_RESIDUAL y fp32 [N] += result (+ bias), the residual add (:489, :503)
+ *          ANVILQ_GEMV_Y_SILU_MUL the fused gate/up projection with the SiLU product
+ *                                 in its epilogue: the weights' N = 2I columns are
+ *                                 unit-interleaved (per 32 intermediate rows, 32 gate
+ *                                 columns then 32 up columns, as for anvilq_w4a16_mlp),
+ *                                 y fp16 [N/2] = fp16( silu(g) * u ) with g, u the
+ *                                 fp16-rounded projections (:492-501) -- exactly what
+ *                                 ANVILQ_GEMV_X_SILU_MUL computes from a stored [g | u],
+ *                                 so the down projection then takes y as HALF input.
+ *                                 No bias, N % 64 == 0, x_mode HALF or RMSNORM.
  * Same weights, workspace and requirements as anvilq_w4a16_gemm with M = 1
  * (fast-kernel shapes only: K % 16 == 0, G % 16 == 0, N % 32 == 0, 16-byte
  * aligned pointers; ANVILQ_ESHAPE otherwise).  flags: ANVILQ_GEMM_OVERLAP_PRIOR. */
@@ -210,6 +219,7 @@ int anvilq_w4a16_verify_gemm_packed(const uint16_t* x, const int32_t* packed, co
 #define ANVILQ_GEMV_X_SILU_MUL 2
 #define ANVILQ_GEMV_Y_HALF 0
 #define ANVILQ_GEMV_Y_RESIDUAL 1
+#define ANVILQ_GEMV_Y_SILU_MUL 2
 int anvilq_w4a16_gemv_fused(const void* x, int x_mode, const uint16_t* gamma, float eps,
                             const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
                             const uint16_t* bias, void* y, int y_mode, int K, int N, int G,

@@ -170,3 +170,73 @@ def test_decoder_mlp_qwen05b_shape_and_graph(dev):
         out.append(int(g.token.item()))
     g.check_errors()
     assert out == eager
+
+
+# -- the gate/up GEMV with the SiLU product in its epilogue --------------------
+@pytest.mark.parametrize("x_mode", [0, 1])
+@pytest.mark.parametrize("H,I", [(896, 4864), (4096, 11008), (896, 384)])
+def test_gate_up_silu_epilogue_bit_identical(dev, H, I, x_mode):
+    """ANVILQ_GEMV_Y_SILU_MUL on unit-interleaved gate/up columns against the
+    stored [gate | up] output followed by the SiLU product of the down GEMV's
+    prologue (anvilq_silu_mul_rows restates it): identical bits; and the down
+    GEMV on those activations (HALF in) against its SILU_MUL-in form."""
+    lib = _lib.load()
+    rng = np.random.default_rng(H + I + x_mode)
+    gu = synthetic.awq_layer(H, 2 * I, 128, rng=rng)
+    down = synthetic.awq_layer(I, H, 128, rng=rng)
+    s = torch.cuda.current_stream(dev).cuda_stream
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = torch.zeros(max(lib.anvilq_w4a16_gemm_workspace_size(1, H, 2 * I, 128),
+                         lib.anvilq_w4a16_gemm_workspace_size(1, I, H, 128)), dtype=torch.uint8, device=dev)
+    if x_mode == 1:
+        x = T((rng.standard_normal(H) * 3).astype(np.float32), dev)
+        gamma = T((1 + 0.1 * rng.standard_normal(H)).astype(np.float16), dev)
+    else:
+        x = T(rng.standard_normal(H).astype(np.float16), dev)
+        gamma = None
+    gp = None if gamma is None else gamma.data_ptr()
+
+    def gemv(xin, xm, w, y, ym, K, N):
+        rc = lib.anvilq_w4a16_gemv_fused(xin.data_ptr(), xm, gp if xm == 1 else None, 1e-6, w[0].data_ptr(),
+                                         w[1].data_ptr(), w[2].data_ptr(), None, y.data_ptr(), ym, K, N, 128,
+                                         ws.data_ptr(), ws.numel(), err.data_ptr(), 0, s)
+        assert rc == 0, lib.anvilq_strerror(rc)
+
+    g_cat = [T(a, dev) for a in (gu.qweight, gu.qzeros, gu.scales)]
+    g_il = ops.mlp_interleave(*g_cat)
+    d = [T(a, dev) for a in (down.qweight, down.qzeros, down.scales)]
+    y_cat = torch.empty(2 * I, dtype=torch.float16, device=dev)
+    act_ref = torch.empty(I, dtype=torch.float16, device=dev)
+    act = torch.empty(I, dtype=torch.float16, device=dev)
+    gemv(x, x_mode, g_cat, y_cat, 0, H, 2 * I)
+    assert lib.anvilq_silu_mul_rows(y_cat.data_ptr(), act_ref.data_ptr(), 1, I, 0, s) == 0
+    gemv(x, x_mode, g_il, act, 2, H, 2 * I)
+    r0 = rng.standard_normal(H).astype(np.float32)
+    r_ref, r_new = T(r0, dev), T(r0, dev)
+    gemv(y_cat, 2, d, r_ref, 1, I, H)
+    gemv(act, 0, d, r_new, 1, I, H)
+    torch.cuda.synchronize(dev)
+    assert int(err.item()) == 0
+    assert torch.equal(act, act_ref), (H, I)
+    assert torch.equal(r_new, r_ref), (H, I)
+
+
+def test_decoder_gate_up_epilogue_matches_two_mode_path(dev):
+    """The default decoder (gate/up with the SiLU epilogue) and the SiLU-prologue
+    path give identical logits, step after step."""
+    from anvilq_b200 import decoder
+    w = decoder.synthetic_weights(decoder.QWEN05B_SHAPE, seed=41)
+    a = decoder.Decoder(w, dev, max_seq=32, keep_logits=True)
+    b = decoder.Decoder(w, dev, max_seq=32, keep_logits=True, gu_act=False)
+    assert a.gu_act and not b.gu_act
+    a.reset(11)
+    b.reset(11)
+    for _ in range(3):
+        a.step()
+        b.step()
+        a.stream.synchronize()
+        b.stream.synchronize()
+        a.check_errors()
+        b.check_errors()
+        assert torch.equal(a.logits, b.logits)
+        assert int(a.token.item()) == int(b.token.item())
