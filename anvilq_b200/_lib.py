@@ -47,6 +47,7 @@ SIGNATURES = {
     "anvilq_w4a16_gemv_qkv_rope": (I, [P, I, P, F, P, P, P, P, I, I, P, P, P, P, P, I, I, I, I, F, P, SZ, P,
                                        ctypes.c_uint, P]),
     "anvilq_w4a16_mlp_workspace_size": (SZ, [I, I, I]),
+    "anvilq_gqa_decode_ex": (I, [P, P, P, P, P, I, I, I, I, I, F, P, SZ, P, ctypes.c_uint, P]),
     "anvilq_w4a16_mlp": (I, [P, P, F, P, P, P, P, P, P, I, I, I, P, SZ, P, ctypes.c_uint, P]),
     "anvilq_peer_handle_size": (SZ, []),
     "anvilq_peer_export": (I, [P, P, ctypes.POINTER(ctypes.c_size_t)]),

@@ -251,6 +251,11 @@ __global__ void __launch_bounds__(kThreads, D == 64 ? 2 : 1)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int C = p.cluster, rank = split % C, cl = split / C;
+  // launched with programmatic dependent launch (ANVILQ_GEMM_OVERLAP_PRIOR) the
+  // CTAs may be resident before the previous kernel -- the one that wrote q,
+  // the new cache row and the length -- completes: wait for it before reading
+  // any of them (a no-op otherwise)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int seqlen = p.seqlens[b];
   const bool bad_len = seqlen < 1 || seqlen > p.Tmax;
   const int ntiles = bad_len ? 0 : (seqlen + kTile - 1) / kTile;
@@ -792,19 +797,21 @@ static bool meta_map(CUtensorMap* map, const void* meta, int B, int Hkv, int Tma
 // One launch, clusters of p.cluster CTAs along x.
 template <int D, bool Q8>
 static cudaError_t launch_d(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mkm,
-                            const CUtensorMap& mvm, const Params& p, int B, cudaStream_t st) {
+                            const CUtensorMap& mvm, const Params& p, int B, cudaStream_t st, bool pdl = false) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.cluster * p.clusters, p.Hkv, B);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = Layout<D, Q8>::kTotal;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = p.cluster;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, gqa_decode_kernel<D, Q8>, mk, mv, mkm, mvm, p);
 }
 
@@ -817,12 +824,13 @@ static int finish_launch(cudaError_t e) {
 }
 
 // fp16 caches: tensor maps for both, then one launch.
-static int launch(const Params& p, int B, int D, const void* k_cache, const void* v_cache, cudaStream_t st) {
+static int launch(const Params& p, int B, int D, const void* k_cache, const void* v_cache, cudaStream_t st,
+                  bool pdl = false) {
   CUtensorMap mk, mv;
   if (!cache_map(&mk, k_cache, B, p.Hkv, D, p.Tmax) || !cache_map(&mv, v_cache, B, p.Hkv, D, p.Tmax))
     return ANVILQ_EALIGN;
-  return finish_launch(D == 64 ? launch_d<64, false>(mk, mv, mk, mv, p, B, st)
-                               : launch_d<128, false>(mk, mv, mk, mv, p, B, st));
+  return finish_launch(D == 64 ? launch_d<64, false>(mk, mv, mk, mv, p, B, st, pdl)
+                               : launch_d<128, false>(mk, mv, mk, mv, p, B, st, pdl));
 }
 
 // INT8 caches: code and metadata tensor maps, then one launch.
@@ -909,7 +917,16 @@ size_t anvilq_gqa_decode_workspace_size(int B, int Hq, int Hkv, int D, int Tmax)
 int anvilq_gqa_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* seqlens,
                       uint16_t* out, int B, int Hq, int Hkv, int D, int Tmax, float scale, void* workspace,
                       size_t workspace_bytes, int* dev_err, anvilq_stream_t stream) {
+  return anvilq_gqa_decode_ex(q, k_cache, v_cache, seqlens, out, B, Hq, Hkv, D, Tmax, scale, workspace,
+                              workspace_bytes, dev_err, 0u, stream);
+}
+
+int anvilq_gqa_decode_ex(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                         const int32_t* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D, int Tmax,
+                         float scale, void* workspace, size_t workspace_bytes, int* dev_err, unsigned flags,
+                         anvilq_stream_t stream) {
   if (!q || !k_cache || !v_cache || !seqlens || !out || !dev_err) return ANVILQ_EINVAL;
+  if (flags & ~(unsigned)ANVILQ_GEMM_OVERLAP_PRIOR) return ANVILQ_EINVAL;
   if (!args_ok(B, Hq, Hkv, D, Tmax)) return ANVILQ_ESHAPE;
   if (!a16(q) || !a16(k_cache) || !a16(v_cache) || !a16(out)) return ANVILQ_EALIGN;
   const DeviceInfo* dev = device_info();
@@ -931,7 +948,8 @@ int anvilq_gqa_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t
   const float s = scale > 0.0f ? scale : 1.0f / std::sqrt((float)D);
   p.scale_log2 = s * 1.4426950408889634f;
   p.k_escape = p.v_escape = nullptr;
-  return launch(p, B, D, k_cache, v_cache, reinterpret_cast<cudaStream_t>(stream));
+  return launch(p, B, D, k_cache, v_cache, reinterpret_cast<cudaStream_t>(stream),
+                (flags & ANVILQ_GEMM_OVERLAP_PRIOR) != 0);
 }
 
 int anvilq_gqa_decode_int8(const uint16_t* q, const int8_t* k_codes, const uint32_t* k_meta, const float* k_escape,

@@ -241,6 +241,18 @@ class Decoder:
             QH, KVH, D, self.max_seq, ROPE_THETA, self.workspace.data_ptr(), self.workspace.numel(),
             self.dev_err.data_ptr(), FLAG_OVERLAP, self.stream.cuda_stream), "anvilq_w4a16_gemv_qkv_rope")
 
+    def _mlp_gemvs(self, l, w):
+        """Layer l's MLP as two fused GEMVs: gate/up with the SiLU product in its
+        epilogue and down on those activations (gu_act), or gate/up to fp16
+        [gate | up] and down with the SiLU prologue."""
+        L, H, I, QH, KVH, D, G, V, _ = self.shape
+        if self.gu_act:
+            self._gemv((*self.mlp_gu[l], None), self.x, 1, self.gamma_post[l], self.act, 2, H, 2 * I)
+            self._gemv(w["down"], self.act, 0, None, self.x, 1, I, H)
+        else:
+            self._gemv(w["gu"], self.x, 1, self.gamma_post[l], self.gu, 0, H, 2 * I)
+            self._gemv(w["down"], self.gu, 2, None, self.x, 1, I, H)
+
     def _mlp(self, l, w):
         """Layer l's MLP in one launch: x += down(silu(gate) up) of RMSNorm(x)."""
         L, H, I, QH, KVH, D, G, V, _ = self.shape
@@ -281,19 +293,15 @@ class Decoder:
                                     self.key.data_ptr(), self.dev_err.data_ptr(), FLAG_OVERLAP, s), "anvilq_embed")
         for l, w in enumerate(self.layers):
             self._qkv_rope(l, w)
-            _lib.check(lib.anvilq_gqa_decode(
+            _lib.check(lib.anvilq_gqa_decode_ex(
                 self.q.data_ptr(), self.k_cache[l].data_ptr(), self.v_cache[l].data_ptr(), self.seqlen.data_ptr(),
                 self.attn.data_ptr(), 1, QH, KVH, D, self.max_seq, 0.0, self.workspace.data_ptr(),
-                self.workspace.numel(), self.dev_err.data_ptr(), s), "anvilq_gqa_decode")
+                self.workspace.numel(), self.dev_err.data_ptr(), FLAG_OVERLAP, s), "anvilq_gqa_decode_ex")
             self._gemv(w["o"], self.attn, 0, None, self.x, 1, QH * D, H)
             if self.mlp:
                 self._mlp(l, w)
-            elif self.gu_act:
-                self._gemv((*self.mlp_gu[l], None), self.x, 1, self.gamma_post[l], self.act, 2, H, 2 * I)
-                self._gemv(w["down"], self.act, 0, None, self.x, 1, I, H)
             else:
-                self._gemv(w["gu"], self.x, 1, self.gamma_post[l], self.gu, 0, H, 2 * I)
-                self._gemv(w["down"], self.gu, 2, None, self.x, 1, I, H)
+                self._mlp_gemvs(l, w)
         _lib.check(lib.anvilq_lmhead_argmax(
             self.x.data_ptr(), self.gamma_final.data_ptr(), RMS_EPS, self.embedding.data_ptr(),
             None if self.logits is None else self.logits.data_ptr(), self.key.data_ptr(), H, V, FLAG_OVERLAP, s),
@@ -376,8 +384,10 @@ class Decoder:
             for l, w in enumerate(self.layers):
                 self._qkv_rope(l, w)
                 self._gemv(w["o"], self.attn, 0, None, self.x, 1, QH * D, H)
-                self._gemv(w["gu"], self.x, 1, self.gamma_post[l], self.gu, 0, H, 2 * I)
-                self._gemv(w["down"], self.gu, 2, None, self.x, 1, I, H)
+                if self.mlp:
+                    self._mlp(l, w)
+                else:
+                    self._mlp_gemvs(l, w)
 
         with torch.cuda.stream(self.stream):
             enqueue()

@@ -343,6 +343,15 @@ int anvilq_gqa_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t
                       const int32_t* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D, int Tmax,
                       float scale, void* workspace, size_t workspace_bytes, int* dev_err,
                       anvilq_stream_t stream);
+/* The same with flags: ANVILQ_GEMM_OVERLAP_PRIOR launches the kernel with
+ * programmatic dependent launch -- its CTAs may become resident while the work
+ * enqueued before it (the QKV projection that writes q, the new cache row and
+ * the lengths) still runs, and wait for that work before reading anything.
+ * Results are identical to anvilq_gqa_decode. */
+int anvilq_gqa_decode_ex(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                         const int32_t* seqlens, uint16_t* out, int B, int Hq, int Hkv, int D, int Tmax,
+                         float scale, void* workspace, size_t workspace_bytes, int* dev_err, unsigned flags,
+                         anvilq_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * Decode-step operations around the GEMVs and the attention (batch 1).

@@ -172,3 +172,38 @@ def test_unsupported_shape_rejected_on_host(dev):
     q, k, v = synthetic.kv_case(1, 8, 2, 32, 16, seed=3)   # head_dim 32 is not a supported size
     with pytest.raises(ValueError):
         ops.gqa_decode(T(q, dev), T(k, dev), T(v, dev), T(np.array([16], np.int32), dev))
+
+
+def test_programmatic_launch_matches_plain(dev):
+    """anvilq_gqa_decode_ex with ANVILQ_GEMM_OVERLAP_PRIOR, right after a kernel
+    that writes q and the lengths, gives the bits of the plain launch; unknown
+    flags are rejected."""
+    from anvilq_b200 import _lib
+    lib = _lib.load()
+    B, Hq, Hkv, D, Tmax = 1, 14, 2, 64, 1100
+    g = torch.Generator(device=dev)
+    g.manual_seed(12)
+    k = torch.randn((B, Tmax, Hkv, D), generator=g, device=dev).half()
+    v = torch.randn((B, Tmax, Hkv, D), generator=g, device=dev).half()
+    q_src = torch.randn((B, Hq, D), generator=g, device=dev).half()
+    q = torch.zeros_like(q_src)
+    lens = torch.zeros(B, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = torch.zeros(lib.anvilq_gqa_decode_workspace_size(B, Hq, Hkv, D, Tmax), dtype=torch.uint8, device=dev)
+    s = torch.cuda.current_stream(dev).cuda_stream
+    outs = []
+    for flags in (0, 1, 1):
+        q.zero_()
+        lens.zero_()
+        out = torch.empty((B, Hq, D), dtype=torch.float16, device=dev)
+        q.copy_(q_src)          # the preceding kernels write q and the length
+        lens.fill_(1025)
+        rc = lib.anvilq_gqa_decode_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), lens.data_ptr(), out.data_ptr(),
+                                      B, Hq, Hkv, D, Tmax, 0.0, ws.data_ptr(), ws.numel(), err.data_ptr(), flags, s)
+        assert rc == 0, lib.anvilq_strerror(rc)
+        outs.append(out)
+    torch.cuda.synchronize(dev)
+    assert int(err.item()) == 0
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    assert lib.anvilq_gqa_decode_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), lens.data_ptr(), q.data_ptr(),
+                                    B, Hq, Hkv, D, Tmax, 0.0, ws.data_ptr(), ws.numel(), err.data_ptr(), 4, s) != 0
