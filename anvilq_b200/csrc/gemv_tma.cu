@@ -219,6 +219,12 @@ __device__ __forceinline__ uint32_t dsmem_addr_u32(uint32_t local, uint32_t rank
 __device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
+// v into another CTA's shared memory, its 4 bytes counted on that CTA's mbarrier
+__device__ __forceinline__ void st_async_f32(uint32_t addr, float v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr),
+               "r"(__float_as_uint(v)), "r"(bar)
+               : "memory");
+}
 // system-scope flag accesses between GPUs of the node
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -273,10 +279,14 @@ __global__ void __launch_bounds__(kThreads, 4)
   const unsigned char* xraw = smem + kXrawOff + warp * kStages * kXrawStage;
   const uint32_t xraw0 = smem_u32(smem + kXrawOff) + warp * kStages * kXrawStage;
   const uint32_t bar0 = smem_u32(smem + kBarOff + warp * kStages * 8);
+  // the cluster's partial sums arrive as st.async on this CTA's slot barrier
+  // (kBarOff pad), which expects all kCols values of its slice from every rank
+  const uint32_t slot_bar = smem_u32(smem + kBarOff + kWarps * kStages * 8);
   if (lane == 0) {
     for (int s = 0; s < kStages; ++s)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8 * s) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap) : "memory");
+    if (warp == 0 && c > 1) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(slot_bar) : "memory");
   }
   // kYMlp: this CTA's rows of the down matrix and their groups' zero points and
   // scales do not depend on any earlier kernel: request them now
@@ -289,6 +299,14 @@ __global__ void __launch_bounds__(kThreads, 4)
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(mlp0 + ml.bar) : "memory");
   }
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  if (c > 1) {
+    if (threadIdx.x == 0)
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(slot_bar), "r"(kCols * 4)
+                   : "memory");
+    // every CTA's slot barrier is initialised before any rank pushes to it: this
+    // arrive pairs with the wait just before the pushes
+    cluster_arrive_release();
+  }
   if (YMODE == kYMlp && threadIdx.x == 0) {
     const int H = p.dn_H, g0 = mlp_i0 / p.G;
     const int ng = mlp_nr > 0 ? (mlp_i0 + mlp_nr - 1) / p.G - g0 + 1 : 0;   // <= dn_groups (host)
@@ -595,22 +613,25 @@ __global__ void __launch_bounds__(kThreads, 4)
     const int hd = p.D / 2, head = col / p.D, j = col % p.D;
     return 2 * (head * hd + j % hd) + (j >= hd ? 1 : 0);
   };
+  if (c > 1) cluster_wait_acquire();   // every rank's slot barrier is initialised
   for (int col = threadIdx.x; col < kCols; col += kThreads) {
     float v = 0.0f;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) v += red[w * kCols + col];
     const int L = slot_of(col);
     if (c > 1) {
-      st_dsmem_f32(dsmem_addr_u32(slots_u32 + (rank * per + L % per) * 4, L / per), v);
+      const uint32_t owner = (uint32_t)(L / per);
+      st_async_f32(dsmem_addr_u32(slots_u32 + (rank * per + L % per) * 4, owner), v,
+                   dsmem_addr_u32(slot_bar, owner));
     } else {
       slots[L] = v;
     }
   }
   if (c > 1) {
-    // every CTA of the cluster reaches this, errors included; the release /
-    // acquire pair orders the pushes before the owners' reads
-    cluster_arrive_release();
-    cluster_wait_acquire();
+    // the owner proceeds once all c slices of its columns have landed (every
+    // CTA of the cluster pushes every column, errors included); no cluster-wide
+    // barrier: the mbarrier's completion makes the asynchronous stores visible
+    if (!mbar_wait_bounded(slot_bar, 0) && p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_TIMEOUT);
   } else {
     __syncthreads();
   }
