@@ -31,7 +31,11 @@
 // inside one CTA is written directly, otherwise every CTA that touched it
 // leaves its partial in the workspace and the CTA arriving last at the band's
 // ticket adds the partials in CTA order.  Every sum has a fixed order, so the
-// result is bit-reproducible; no CTA ever waits for another.
+// result is bit-reproducible; no CTA ever waits for another.  A CTA whose range
+// crosses a band boundary takes both bands' steps together (both partials
+// stored, both tickets taken by two threads, both fix-ups in one batch of
+// loads), and the CTA bounds of its bands -- 64-bit divisions -- are computed
+// before griddepcontrol.wait, while the first chunks are in flight.
 //
 // Fused all-gather (PEER, one rank's column slice of a tensor-parallel split):
 // the CTA that finishes a band stores its 256 fp16 columns into every rank's
@@ -157,8 +161,11 @@ __global__ void __launch_bounds__(W * 32, W <= 8 ? 2 : 1)
     gemv_stream_kernel(const __grid_constant__ CUtensorMap tmap, const Params p) {
   using L = Layout<W, S>;
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ int s_last, s_done;
-  __shared__ __align__(16) __half s_y[kBandCols];   // PEER: a finished band, staged for 16-byte stores
+  __shared__ int s_last[2], s_done;
+  // the CTAs sharing the CTA's two bands (first, last) and the slot that
+  // band's first contributor stored it in: {first0, first1, last0, last1, slot0, slot1}
+  __shared__ int s_bounds[6];
+  __shared__ __align__(16) __half s_y[2 * kBandCols];   // PEER: finished bands, staged for 16-byte stores
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int P = gridDim.x, T = p.total;
   const int c0 = (int)((long long)blockIdx.x * T / P), c1 = (int)((long long)(blockIdx.x + 1) * T / P);
@@ -230,6 +237,16 @@ __global__ void __launch_bounds__(W * 32, W <= 8 ? 2 : 1)
     }
   };
   if (nch > 0) load_seg(cb, ck, sc, zq);
+
+  // the reduction's 64-bit divisions, done while the first chunks are in flight
+  // (read only after the barrier that ends the tile loop)
+  if (warp == W - 1 && lane < 6) {
+    const int band = band0 + (lane & 1);
+    const long long c = lane >> 1 == 1 ? (long long)(band + 1) * p.cpb - 1 : (long long)band * p.cpb;
+    int val = cta_of(c, T, P);
+    if (lane >> 1 == 2) val = (int)((long long)val * T / P) / p.cpb < band ? 1 : 0;
+    s_bounds[lane] = val;
+  }
 
   asm volatile("griddepcontrol.wait;" ::: "memory");   // x may come from the previous kernel
   if (lane == 0)
@@ -362,122 +379,137 @@ __global__ void __launch_bounds__(W * 32, W <= 8 ? 2 : 1)
     *reinterpret_cast<float4*>(r1 + 4) = make_float4(v1[4], v1[5], v1[6], v1[7]);
   }
   __syncthreads();
+  // The CTA's bands (slot 0, and slot 1 when its range crosses a band boundary)
+  // go through the cross-CTA steps together: both partials are stored, both
+  // tickets taken by two threads at once, and both fix-ups loaded in one pass.
   const int last_band_cta = n > 0 ? (c1 - 1) / p.cpb : band0 - 1;
-  constexpr int kPer = (kBandCols + W * 32 - 1) / (W * 32);   // columns per thread (512 threads: half idle)
+  const int nslots = last_band_cta - band0 + 1;   // 0, 1 or 2 (uniform over the CTA)
+  const int first_s[2] = {s_bounds[0], s_bounds[1]}, last_s[2] = {s_bounds[2], s_bounds[3]};
+  // (slot, column) entries of this thread: e = threadIdx.x + u W 32, slot e / 256
+  constexpr int kE = (2 * kBandCols + W * 32 - 1) / (W * 32);
+  float v[kE];
+#pragma unroll
+  for (int u = 0; u < kE; ++u) {
+    const int e = threadIdx.x + u * W * 32, s = e / kBandCols, t = e % kBandCols;
+    v[u] = 0.0f;
+    if (e < 2 * kBandCols && s < nslots) {
+#pragma unroll
+      for (int w = 0; w < W; ++w) v[u] += red[(s * W + w) * kBandCols + t];
+      if (s == 0 ? first_s[0] != last_s[0] : first_s[1] != last_s[1])
+        __stcg(p.parts + ((size_t)blockIdx.x * 2 + s) * kBandCols + t, v[u]);
+    }
+  }
+  if (threadIdx.x < 2) s_last[threadIdx.x] = 0;
   if (PEER && threadIdx.x == 0) s_done = 0;
+  __syncthreads();
+  // lane 0 of warp s fences for the CTA (the barrier orders every thread's
+  // stores before it, cumulatively) and takes slot s's ticket; the last
+  // arriver's fence orders its CTA's loads after every contributor's stores
+  if (lane == 0 && warp < nslots && (warp == 0 ? first_s[0] != last_s[0] : first_s[1] != last_s[1])) {
+    const int band = band0 + warp;
+    __threadfence();
+    const int arrived = atomicAdd(p.tickets + band, 1);
+    if (arrived == (warp == 0 ? last_s[0] - first_s[0] : last_s[1] - first_s[1])) {
+      p.tickets[band] = 0;   // re-armed for the next launch
+      __threadfence();
+      s_last[warp] = 1;
+    }
+  }
+  __syncthreads();
+  bool own[2], fix[2];   // this CTA writes the slot's band / adds its contributors first
+#pragma unroll
   for (int s = 0; s < 2; ++s) {
-    const int band = band0 + s;
-    if (band > last_band_cta) break;   // uniform over the CTA
-    const int first = cta_of((long long)band * p.cpb, T, P);
-    const int last = cta_of((long long)(band + 1) * p.cpb - 1, T, P);
-    float v[kPer];
+    fix[s] = s < nslots && first_s[s] != last_s[s] && s_last[s];
+    own[s] = s < nslots && (first_s[s] == last_s[s] || s_last[s]);
+  }
+  if (fix[0] || fix[1]) {
+    // the contributors of both slots as one list of rows (slot 0's, then slot
+    // 1's, each in CTA order), loaded by all threads at once and staged through
+    // the ring (free again) in batches, then summed per slot in CTA order
+    constexpr int kFixRows = L::kRingBytes / (kBandCols * 4) < 64 ? L::kRingBytes / (kBandCols * 4) : 64;
+    float* stage = reinterpret_cast<float*>(smem + L::kRingOff + L::kRedBytes);
+    constexpr int kStageRows = (L::kRingBytes - L::kRedBytes) / (kBandCols * 4) < kFixRows
+                                   ? (L::kRingBytes - L::kRedBytes) / (kBandCols * 4)
+                                   : kFixRows;
+    static_assert(kStageRows >= 4, "room to stage the fix-up");
+    const int rows0 = fix[0] ? last_s[0] - first_s[0] + 1 : 0;
+    const int rows_all = rows0 + (fix[1] ? last_s[1] - first_s[1] + 1 : 0);
+    float acc[kE];
 #pragma unroll
-    for (int u = 0; u < kPer; ++u) {
-      const int t = threadIdx.x + u * W * 32;
-      v[u] = 0.0f;
-      if (t < kBandCols) {
+    for (int u = 0; u < kE; ++u) acc[u] = 0.0f;
+    for (int r0 = 0; r0 < rows_all; r0 += kStageRows) {
+      const int rows = min(kStageRows, rows_all - r0);
+      constexpr int kU = 8;   // loads in flight per thread (a whole batch at 256 or 512 threads)
+      for (int e0 = threadIdx.x; e0 < rows * (kBandCols / 4); e0 += kU * W * 32) {
+        float4 vv[kU];
 #pragma unroll
-        for (int w = 0; w < W; ++w) v[u] += red[(s * W + w) * kBandCols + t];
-      }
-    }
-    if (first != last) {
-      // several CTAs hold partials of this band: the last to arrive adds them in CTA order
-#pragma unroll
-      for (int u = 0; u < kPer; ++u) {
-        const int t = threadIdx.x + u * W * 32;
-        if (t < kBandCols) __stcg(p.parts + ((size_t)blockIdx.x * 2 + s) * kBandCols + t, v[u]);
-      }
-      // one thread fences for the CTA: the barrier orders every thread's stores
-      // before its fence (cumulative), and the last arriver's fence orders its
-      // CTA's loads after every contributor's stores
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        __threadfence();
-        const int arrived = atomicAdd(p.tickets + band, 1);
-        s_last = arrived == last - first;
-        if (s_last) {
-          p.tickets[band] = 0;   // re-armed for the next launch
-          __threadfence();
+        for (int u = 0; u < kU; ++u) {
+          const int e = e0 + u * W * 32, r = r0 + e / (kBandCols / 4), c4 = e % (kBandCols / 4);
+          const int s = r < rows0 ? 0 : 1;
+          const int i = s == 0 ? first_s[0] + r : first_s[1] + (r - rows0);   // contributor CTA
+          // the band's slot in CTA i: every contributor after the first starts inside the band
+          const int slot = i != (s == 0 ? first_s[0] : first_s[1]) ? 0 : s_bounds[4 + s];
+          if (e < rows * (kBandCols / 4))
+            vv[u] = __ldcg(reinterpret_cast<const float4*>(p.parts + ((size_t)i * 2 + slot) * kBandCols) + c4);
         }
-      }
-      __syncthreads();
-      if (!s_last) continue;
-      // the contributors' partials, loaded by all threads at once (not one
-      // dependent L2 round trip per contributor), staged through the ring
-      // (free again) in batches of kFixRows, then summed in CTA order
-      constexpr int kFixRows = L::kRingBytes / (kBandCols * 4) < 64 ? L::kRingBytes / (kBandCols * 4) : 64;
-      float* stage = reinterpret_cast<float*>(smem + L::kRingOff + L::kRedBytes);
-      constexpr int kStageRows = (L::kRingBytes - L::kRedBytes) / (kBandCols * 4) < kFixRows
-                                     ? (L::kRingBytes - L::kRedBytes) / (kBandCols * 4)
-                                     : kFixRows;
-      static_assert(kStageRows >= 4, "room to stage the fix-up");
-      float acc[kPer];
 #pragma unroll
-      for (int u = 0; u < kPer; ++u) acc[u] = 0.0f;
-      for (int i0 = first; i0 <= last; i0 += kStageRows) {
-        const int rows = min(kStageRows, last - i0 + 1);
-        constexpr int kU = 4;   // loads in flight per thread
-        for (int e0 = threadIdx.x; e0 < rows * (kBandCols / 4); e0 += kU * W * 32) {
-          float4 vv[kU];
-#pragma unroll
-          for (int u = 0; u < kU; ++u) {
-            const int e = e0 + u * W * 32, r = e / (kBandCols / 4), c4 = e % (kBandCols / 4), i = i0 + r;
-            const int slot = band - (int)((long long)i * T / P) / p.cpb;
-            if (e < rows * (kBandCols / 4))
-              vv[u] = __ldcg(reinterpret_cast<const float4*>(p.parts + ((size_t)i * 2 + slot) * kBandCols) + c4);
-          }
-#pragma unroll
-          for (int u = 0; u < kU; ++u)
-            if (e0 + u * W * 32 < rows * (kBandCols / 4)) reinterpret_cast<float4*>(stage)[e0 + u * W * 32] = vv[u];
-        }
-        __syncthreads();
-#pragma unroll
-        for (int u = 0; u < kPer; ++u) {
-          const int t = threadIdx.x + u * W * 32;
-          if (t < kBandCols)
-            for (int r = 0; r < rows; ++r) acc[u] += stage[r * kBandCols + t];   // in CTA order
-        }
-        __syncthreads();
-      }
-#pragma unroll
-      for (int u = 0; u < kPer; ++u) v[u] = acc[u];
-    }
-    // the band's final values (uniform: every thread of the CTA is here)
-#pragma unroll
-    for (int u = 0; u < kPer; ++u) {
-      const int t = threadIdx.x + u * W * 32;
-      if (t >= kBandCols) continue;
-      const int col = band * kBandCols + t;
-      float out = v[u];
-      if (col < p.N && p.bias) out += __half2float(p.bias[col]);
-      if (!PEER) {
-        if (col < p.N) p.y[col] = __float2half_rn(out);
-      } else {
-        s_y[t] = __float2half_rn(out);
-      }
-    }
-    if (PEER) {
-      __syncthreads();
-      // 16-byte stores of 8 columns each into every rank's output (its own included)
-      if (threadIdx.x < kBandCols / 8) {
-        const int col = band * kBandCols + 8 * threadIdx.x;
-        if (col < p.N) {
-          const uint4 val = reinterpret_cast<const uint4*>(s_y)[threadIdx.x];
-          for (int r = 0; r < p.world; ++r)
-            *reinterpret_cast<uint4*>(p.peer_y[r] + p.col_base + col) = val;
-        }
+        for (int u = 0; u < kU; ++u)
+          if (e0 + u * W * 32 < rows * (kBandCols / 4)) reinterpret_cast<float4*>(stage)[e0 + u * W * 32] = vv[u];
       }
       __syncthreads();
-      if (threadIdx.x == 0) {
-        __threadfence_system();   // the CTA's peer stores (ordered by the barrier) reach every rank first
-        const int done = atomicAdd(p.tickets + kRankTicket, 1);
-        if (done == p.bands - 1) {
-          p.tickets[kRankTicket] = 0;   // re-armed for the next launch
-          s_done = 1;
+#pragma unroll
+      for (int u = 0; u < kE; ++u) {
+        const int e = threadIdx.x + u * W * 32, s = e / kBandCols, t = e % kBandCols;
+        if (e < 2 * kBandCols && (s == 0 ? fix[0] : fix[1])) {
+          const int rb = s == 0 ? r0 : max(r0, rows0);
+          const int re = s == 0 ? min(r0 + rows, rows0) : r0 + rows;
+          for (int r = rb; r < re; ++r) acc[u] += stage[(r - r0) * kBandCols + t];   // in CTA order
         }
       }
       __syncthreads();
     }
+#pragma unroll
+    for (int u = 0; u < kE; ++u) {
+      const int e = threadIdx.x + u * W * 32, s = e / kBandCols;
+      if (e < 2 * kBandCols && (s == 0 ? fix[0] : fix[1])) v[u] = acc[u];
+    }
+  }
+  // the final values of the bands this CTA owns
+#pragma unroll
+  for (int u = 0; u < kE; ++u) {
+    const int e = threadIdx.x + u * W * 32, s = e / kBandCols, t = e % kBandCols;
+    if (e >= 2 * kBandCols || !(s == 0 ? own[0] : own[1])) continue;
+    const int col = (band0 + s) * kBandCols + t;
+    float out = v[u];
+    if (col < p.N && p.bias) out += __half2float(p.bias[col]);
+    if (!PEER) {
+      if (col < p.N) p.y[col] = __float2half_rn(out);
+    } else {
+      s_y[s * kBandCols + t] = __float2half_rn(out);
+    }
+  }
+  if (PEER) {
+    __syncthreads();
+    // 16-byte stores of 8 columns each into every rank's output (its own included)
+    if (threadIdx.x < 2 * (kBandCols / 8)) {
+      const int s = threadIdx.x / (kBandCols / 8), c8 = threadIdx.x % (kBandCols / 8);
+      const int col = (band0 + s) * kBandCols + 8 * c8;
+      if ((s == 0 ? own[0] : own[1]) && col < p.N) {
+        const uint4 val = reinterpret_cast<const uint4*>(s_y)[threadIdx.x];
+        for (int r = 0; r < p.world; ++r) *reinterpret_cast<uint4*>(p.peer_y[r] + p.col_base + col) = val;
+      }
+    }
+    __syncthreads();
+    const int nfin = (int)own[0] + (int)own[1];
+    if (threadIdx.x == 0 && nfin > 0) {
+      __threadfence_system();   // the CTA's peer stores (ordered by the barrier) reach every rank first
+      const int done = atomicAdd(p.tickets + kRankTicket, nfin);
+      if (done + nfin == p.bands) {
+        p.tickets[kRankTicket] = 0;   // re-armed for the next launch
+        s_done = 1;
+      }
+    }
+    __syncthreads();
   }
   // PEER: the CTA that completed the rank's last band raises this rank's flag in
   // every rank and waits (bounded) until every rank's flag reached this call
