@@ -729,10 +729,18 @@ def tp_measure(args, world, rank, dev, M, e2e=True):
         full_bytes += synthetic.gemv_bytes(M, K, N)
         shard_bytes += synthetic.gemv_bytes(M, K, n)
     stream = torch.cuda.Stream(dev)
+    # at M = 1 the rank's slices run as one chain with one CTA shape (ops.chain_plans)
+    plans = ops.chain_plans([(K, N // world) for K, N in wl["shapes"]]) if M == 1 else None
+
+    def rank_gemm(i, x, qw, qz, sc, y, overlap=True):
+        if plans is None:
+            ops.gemm(x, qw, qz, sc, None, 128, out=y, overlap_prior=overlap)
+        else:
+            ops.gemv_planned(x, qw, qz, sc, None, 128, plan=plans[i], out=y.view(-1), overlap_prior=overlap)
 
     def step(gather=True):
-        for x, qw, qz, sc, y, yg, K, N in layers:
-            ops.gemm(x, qw, qz, sc, None, 128, out=y, overlap_prior=True)
+        for i, (x, qw, qz, sc, y, yg, K, N) in enumerate(layers):
+            rank_gemm(i, x, qw, qz, sc, y)
             if gather and world > 1:
                 dist.all_gather_into_tensor(yg, y)
 
@@ -791,7 +799,7 @@ def tp_measure(args, world, rank, dev, M, e2e=True):
                     if fused:
                         yh.copy_(flins[i](x[0]).view(1, -1), non_blocking=True)
                         continue
-                    ops.gemm(x, qw, qz, sc, None, 128, out=y)
+                    rank_gemm(i, x, qw, qz, sc, y, overlap=False)
                     if world > 1:
                         dist.all_gather_into_tensor(yg, y)
                         yh.copy_(yg.view(world, M, -1).permute(1, 0, 2).reshape(M, -1), non_blocking=True)
@@ -807,12 +815,10 @@ def tp_measure(args, world, rank, dev, M, e2e=True):
     value = full_bytes * args.steps / (ms / 1e3) / 1e9
     per_launch = ms_comp / args.steps / launches
     achieved = shard_bytes / launches / (per_launch / 1e3) / 1e9
-    K0, N0 = wl["shapes"][0]
-    stream_plan = ops.gemv_plan(K0, N0 // world)["kernel"] == 1
-    kernel = ("gemv_stream_kernel" if stream_plan else "gemv_tma_kernel") if M == 1 else "verify_tc_kernel"
-    traffic = weighted_traffic("tp70b", [(synthetic.gemv_bytes(M, K, N // world),
-                                          "gemv_stream_kernel" if ops.gemv_plan(K, N // world)["kernel"] == 1
-                                          else "gemv_tma_kernel") for K, N in wl["shapes"]]) if M == 1 else None
+    kernel_of = lambda pl: "gemv_stream_kernel" if pl["kernel"] == 1 else "gemv_tma_kernel"
+    kernel = kernel_of(plans[0]) if M == 1 else "verify_tc_kernel"
+    traffic = weighted_traffic("tp70b", [(synthetic.gemv_bytes(M, K, N // world), kernel_of(pl))
+                                         for (K, N), pl in zip(wl["shapes"], plans)]) if M == 1 else None
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
@@ -828,6 +834,7 @@ def tp_measure(args, world, rank, dev, M, e2e=True):
                    "fused_allgather_path_ms_per_step": None if ms_fused is None else round(ms_fused / args.steps, 5),
                    "compute_only_ms_per_step": round(ms_comp / args.steps, 5),
                    "exchange_ms_per_step": round(max(0.0, ms - ms_comp) / args.steps, 5),
+                   "rank_plans": plans,
                    "l2": "weights larger than L2 (no flush)"},
         "roofline": {"bound": "hbm", "kernel": kernel, "achieved": round(achieved, 2), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": traffic,

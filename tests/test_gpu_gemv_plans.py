@@ -246,3 +246,34 @@ def test_default_and_planned_agree(dev):
         yp = ops.gemv_planned(T(x, dev), *w, 128, plan=ops.gemv_plan(K, N))
         ops.raise_device_errors(dev)
         assert torch.equal(y.view(-1), yp), (K, N)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_chain_plans_70b_slices(dev, world):
+    """ops.chain_plans for one rank's slices of the 70B-class layer: one stream-K
+    CTA shape for the whole chain (16 warps while a slice holds >= 40 MiB of int4),
+    each slice correct under its plan, twice on one workspace."""
+    from anvilq_b200 import ops
+    shapes = [(K, N // world) for K, N in SHAPES_70B]
+    plans = ops.chain_plans(shapes)
+    assert all(p["kernel"] == _lib.GEMV_KERNEL_STREAM for p in plans), plans
+    assert {p["warps"] for p in plans} == {16 if world <= 2 else 8}, plans
+    for (K, N), plan in zip(SHAPES_70B, plans):
+        x, layer = synthetic.gemv_case(1, K, N, 128, seed=5 * K + N + world)
+        part = slice_layer(layer, 0, world)
+        w = device_layer(part, dev)
+        y1 = ops.gemv_planned(T(x, dev), *w, 128, plan=plan)
+        y2 = ops.gemv_planned(T(x, dev), *w, 128, plan=plan)
+        ops.raise_device_errors(dev)
+        assert torch.equal(y1, y2)
+        check_sampled(y1.float().cpu().numpy(), x, part, (K, N, world, plan))
+
+
+def test_chain_plans_fallback(dev):
+    """Groups of 16 rows fit the cluster kernel but not the stream-K kernel's
+    32-row chunks: the chain keeps each projection's per-shape plan."""
+    from anvilq_b200 import ops
+    shapes = [(4096, 4096), (8192, 8192)]
+    plans = ops.chain_plans(shapes, group=16)
+    assert plans == [ops.gemv_plan(K, N, 16) for K, N in shapes]
+    assert all(p["kernel"] == _lib.GEMV_KERNEL_CLUSTER for p in plans), plans
