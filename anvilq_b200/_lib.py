@@ -54,6 +54,9 @@ SIGNATURES = {
     "anvilq_peer_import": (I, [P, SZ, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)]),
     "anvilq_peer_close": (I, [P]),
     "anvilq_w4a16_gemv_allgather": (I, [P, P, P, P, P, I, I, I, I, I, I, I, P, P, P, P, SZ, P, ctypes.c_uint, P]),
+    "anvilq_w4a16_gemv_allgather_planned": (I, [P, P, P, P, P, I, I, I, I, I, I, I, P, P, P, P, P, SZ, P,
+                                                ctypes.c_uint, P]),
+    "anvilq_peer_wait": (I, [P, I, P, P, P]),
     "anvilq_embed": (I, [P, P, P, I, I, P, P, ctypes.c_uint, P]),
     "anvilq_rope_kv_append": (I, [P, P, P, P, P, P, I, I, I, I, F, P, ctypes.c_uint, P]),
     "anvilq_rope_kv_append_at": (I, [P, P, P, P, P, P, I, I, I, I, F, P, ctypes.c_uint, P]),

@@ -874,6 +874,46 @@ int anvilq_w4a16_gemv_allgather(const uint16_t* x, const int32_t* qweight, const
                          reinterpret_cast<cudaStream_t>(stream), overlap);
 }
 
+int anvilq_w4a16_gemv_allgather_planned(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
+                                        const uint16_t* scales, const uint16_t* bias, int K, int N, int G,
+                                        int rank, int world, int col_base, int n_full, uint16_t* const* peer_y,
+                                        unsigned int* const* peer_flags, unsigned int* epoch,
+                                        const anvilq_gemv_plan* plan, void* workspace, size_t workspace_bytes,
+                                        int* dev_err, unsigned flags, anvilq_stream_t stream) {
+  if (!x || !qweight || !qzeros || !scales || !peer_y || !peer_flags || !epoch || !plan) return ANVILQ_EINVAL;
+  if (flags & ~(unsigned)(ANVILQ_GEMM_OVERLAP_PRIOR | ANVILQ_GATHER_DEFERRED)) return ANVILQ_EINVAL;
+  if (world < 1 || world > 8 || rank < 0 || rank >= world) return ANVILQ_EINVAL;
+  if (!shape_ok(1, K, N, G)) return ANVILQ_EINVAL;
+  if (col_base < 0 || col_base % 8 || n_full < col_base + N) return ANVILQ_EINVAL;
+  for (int r = 0; r < world; ++r)
+    if (!peer_y[r] || !peer_flags[r]) return ANVILQ_EINVAL;
+  const GemvPlan pl = *plan;
+  if (pl.kernel != ANVILQ_GEMV_KERNEL_STREAM) return ANVILQ_EINVAL;
+  if (!aligned16(x) || !gemv_stream_supported(x, qweight, qzeros, scales, K, N, G)) return ANVILQ_ESHAPE;
+  GemvIo io;
+  io.xmode = 0;
+  io.ymode = 3;
+  io.x = x;
+  for (int r = 0; r < world; ++r) {
+    io.peer_y[r] = peer_y[r];
+    io.peer_flags[r] = peer_flags[r];
+  }
+  io.epoch = epoch;
+  io.world = world;
+  io.tp_rank = rank;
+  io.col_base = col_base;
+  io.deferred = (flags & ANVILQ_GATHER_DEFERRED) != 0;
+  return launch_gemv_stream(pl, x, qweight, qzeros, scales, bias, nullptr, K, N, G, workspace, workspace_bytes,
+                            dev_err, reinterpret_cast<cudaStream_t>(stream),
+                            (flags & ANVILQ_GEMM_OVERLAP_PRIOR) != 0, &io);
+}
+
+int anvilq_peer_wait(const unsigned int* flags, int world, const unsigned int* epoch, int* dev_err,
+                     anvilq_stream_t stream) {
+  if (!flags || !epoch || world < 1 || world > 8) return ANVILQ_EINVAL;
+  return launch_peer_wait(flags, world, epoch, dev_err, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int anvilq_w4a16_gemm_exact(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
                             const uint16_t* scales, const uint16_t* bias, float* y32,
                             int M, int K, int N, int G, int* dev_err, anvilq_stream_t stream) {

@@ -102,6 +102,7 @@ struct Params {
   unsigned* peer_flags[kMaxPeers];
   unsigned* epoch;
   int world, tp_rank, col_base;
+  int deferred;      // PEER: raise the flag without waiting; wait for the previous call before reading x
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -249,6 +250,25 @@ __global__ void __launch_bounds__(W * 32, W <= 8 ? 2 : 1)
   }
 
   asm volatile("griddepcontrol.wait;" ::: "memory");   // x may come from the previous kernel
+  if (PEER && p.deferred && lane == 0) {
+    // every rank has finished the previous fused call: its slice of x (when x is
+    // that call's gathered row) is here, and no rank still reads the output slot
+    // this call is about to overwrite.  Bounded like the flag wait at the end.
+    const unsigned e_prev = *reinterpret_cast<volatile unsigned*>(p.epoch);
+    const unsigned* mine = p.peer_flags[p.tp_rank];
+    const unsigned long long t_start = globaltimer();
+    bool all = false;
+    for (uint32_t i = 0; !all; ++i) {
+      all = true;
+      for (int r = 0; r < p.world; ++r) all &= (int)(ld_acquire_sys(mine + r) - e_prev) >= 0;
+      if (!all && (i & 63u) == 63u && globaltimer() - t_start > kWaitLimitNs) {
+        if (p.dev_err) atomicOr(p.dev_err, ANVILQ_DEV_ERR_TIMEOUT);
+        break;
+      }
+    }
+    // the peers' stores (generic proxy) before the bulk copies of x (async proxy)
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+  }
   if (lane == 0)
     for (int j = 0; j < pro; ++j) {
       issue_x(j, xk * kChunkRows);
@@ -517,6 +537,10 @@ __global__ void __launch_bounds__(W * 32, W <= 8 ? 2 : 1)
     __threadfence_system();
     const unsigned e = *p.epoch + 1;
     for (int r = 0; r < p.world; ++r) st_release_sys(p.peer_flags[r] + p.tp_rank, e);
+    if (p.deferred) {   // the next deferred call (or peer_wait_kernel) waits for the others
+      *p.epoch = e;
+      return;
+    }
     const unsigned* mine = p.peer_flags[p.tp_rank];
     const unsigned long long t_start = globaltimer();
     bool all = false;
@@ -529,6 +553,23 @@ __global__ void __launch_bounds__(W * 32, W <= 8 ? 2 : 1)
       }
     }
     *p.epoch = e;
+  }
+}
+
+// One thread: waits, bounded by ~1 s, until every rank's flag in this rank's
+// array has reached *epoch (this rank's count of fused calls), i.e. until the
+// last deferred fused call's row is complete here.
+__global__ void peer_wait_kernel(const unsigned* flags, int world, const unsigned* epoch, int* dev_err) {
+  const unsigned e = *epoch;
+  const unsigned long long t_start = globaltimer();
+  bool all = false;
+  for (uint32_t i = 0; !all; ++i) {
+    all = true;
+    for (int r = 0; r < world; ++r) all &= (int)(ld_acquire_sys(flags + r) - e) >= 0;
+    if (!all && (i & 63u) == 63u && globaltimer() - t_start > kWaitLimitNs) {
+      if (dev_err) atomicOr(dev_err, ANVILQ_DEV_ERR_TIMEOUT);
+      break;
+    }
   }
 }
 
@@ -706,6 +747,7 @@ int launch_gemv_stream(const GemvPlan& pl, const uint16_t* x, const int32_t* qwe
   p.world = peer ? peer->world : 0;
   p.tp_rank = peer ? peer->tp_rank : 0;
   p.col_base = peer ? peer->col_base : 0;
+  p.deferred = peer && peer->deferred ? 1 : 0;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.ctas, 1, 1);
@@ -721,6 +763,12 @@ int launch_gemv_stream(const GemvPlan& pl, const uint16_t* x, const int32_t* qwe
     cudaGetLastError();
     return ANVILQ_ECUDA;
   }
+  return ANVILQ_OK;
+}
+
+int launch_peer_wait(const unsigned* flags, int world, const unsigned* epoch, int* dev_err, cudaStream_t stream) {
+  stream_gemv::peer_wait_kernel<<<1, 1, 0, stream>>>(flags, world, epoch, dev_err);
+  if (cudaGetLastError() != cudaSuccess) return ANVILQ_ECUDA;
   return ANVILQ_OK;
 }
 

@@ -42,6 +42,7 @@ struct GemvIo {
   unsigned* peer_flags[8] = {};
   unsigned* epoch = nullptr;
   int world = 0, tp_rank = 0, col_base = 0;
+  bool deferred = false;   // stream-K only: no flag wait at the end; the next call waits before reading x
   // ymode 4 (the MLP: gate/up in unit-interleaved columns, down in the
   // epilogue, added into yr)
   const int32_t* dn_qweight = nullptr;
@@ -63,6 +64,8 @@ bool gemv_stream_supported(const void* x, const int32_t* qweight, const int32_t*
 bool gemv_stream_default_plan(int K, int N, GemvPlan* plan);
 int gemv_stream_check_plan(int K, int N, const GemvPlan& plan);
 size_t gemv_stream_workspace_bytes(const GemvPlan& plan);
+// one thread waits (bounded) until flags[0 .. world) all reached *epoch
+int launch_peer_wait(const unsigned* flags, int world, const unsigned* epoch, int* dev_err, cudaStream_t stream);
 int launch_gemv_stream(const GemvPlan& plan, const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
                        const uint16_t* scales, const uint16_t* bias, uint16_t* y, int K, int N, int G,
                        void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t stream,

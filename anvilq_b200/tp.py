@@ -127,6 +127,17 @@ class PeerOutputs:
                        for s in range(slots)]
         dist.barrier(group=process_group)   # every rank holds every buffer before anyone writes
 
+    def wait(self, stream=None):
+        """Enqueue on ``stream`` (default: the current stream) a wait until every
+        rank's flag reached this rank's count of fused calls: the last deferred
+        call's row is complete here after it (anvilq_peer_wait)."""
+        from . import _lib, ops
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        err = ops.device_error_word(self.device)
+        _lib.check(self.lib.anvilq_peer_wait(ctypes.c_void_p(self.flag_ptrs[self.rank]), self.world,
+                                             self.epoch.data_ptr(), err.data_ptr(), s.cuda_stream),
+                   "anvilq_peer_wait")
+
     def output(self, slot: int, n: int | None = None):
         """This rank's full-width output of one slot (a view, fp16 [n_full])."""
         off = self._FLAGS + slot * self.slot_bytes
@@ -146,10 +157,19 @@ class FusedTPLinear:
     per call computes this rank's slice and stores it in every rank's output
     slot, then waits for every rank's completion flag.  Returns the full row
     (a view of ``outputs.output(slot)``); slots must alternate between calls
-    (see anvilq_w4a16_gemv_allgather)."""
+    (see anvilq_w4a16_gemv_allgather).
+
+    With ``plan`` (a stream-K plan, e.g. from ``ops.chain_plans``) the slice
+    runs under it (anvilq_w4a16_gemv_allgather_planned); with ``deferred`` too
+    the call does not wait for the other ranks at its end: the next deferred
+    call waits for them before reading x, so x may be the previous call's row
+    and the exchange overlaps the next weight stream.  A deferred call's row is
+    complete only after the next deferred call or ``outputs.wait()``."""
+
+    DEFERRED = 2   # ANVILQ_GATHER_DEFERRED
 
     def __init__(self, qweight, qzeros, scales, bias, group_size: int, outputs: PeerOutputs, slot: int,
-                 sharded: bool = False):
+                 sharded: bool = False, plan: dict | None = None, deferred: bool = False):
         """Full AWQ tensors of the projection, or (``sharded``) this rank's slice already."""
         self.out = outputs
         self.slot = slot
@@ -161,14 +181,32 @@ class FusedTPLinear:
                       else shard_awq(qweight, qzeros, scales, bias, outputs.rank, outputs.world))
         self.group_size = group_size
         self.K = qweight.shape[0]
+        if deferred and plan is None:
+            raise ValueError("a deferred fused call takes an explicit stream-K plan")
+        self.plan = None if plan is None else _plan_struct(plan)
+        self.deferred = deferred
 
     def __call__(self, x, flags: int = 0):
         from . import _lib, ops
         lib = self.out.lib
         qw, qz, sc, b = self.shard
         n = qw.shape[1] * 8
-        ws = ops.workspace(x.device, lib.anvilq_w4a16_gemm_workspace_size(1, self.K, n, self.group_size))
+        need = (lib.anvilq_w4a16_gemm_workspace_size(1, self.K, n, self.group_size) if self.plan is None else
+                lib.anvilq_w4a16_gemv_plan_workspace_size(self.K, n, self.group_size, ctypes.byref(self.plan)))
+        if need == 0:
+            raise ValueError(f"the plan does not fit K={self.K}, N={n}")
+        ws = ops.workspace(x.device, need)
         err = ops.device_error_word(x.device)
+        if self.plan is not None:
+            _lib.check(lib.anvilq_w4a16_gemv_allgather_planned(
+                x.data_ptr(), qw.data_ptr(), qz.data_ptr(), sc.data_ptr(), None if b is None else b.data_ptr(),
+                self.K, n, self.group_size, self.out.rank, self.out.world, self.col_base, self.N,
+                ctypes.cast(self.out.y_ptrs[self.slot], ctypes.c_void_p),
+                ctypes.cast(self.out.flag_ptrs, ctypes.c_void_p), self.out.epoch.data_ptr(),
+                ctypes.byref(self.plan), ws.data_ptr(), ws.numel(), err.data_ptr(),
+                flags | (self.DEFERRED if self.deferred else 0), torch.cuda.current_stream(x.device).cuda_stream),
+                "anvilq_w4a16_gemv_allgather_planned")
+            return self.out.output(self.slot, self.N)
         _lib.check(lib.anvilq_w4a16_gemv_allgather(
             x.data_ptr(), qw.data_ptr(), qz.data_ptr(), sc.data_ptr(), None if b is None else b.data_ptr(),
             self.K, n, self.group_size, self.out.rank, self.out.world, self.col_base, self.N,
@@ -176,3 +214,8 @@ class FusedTPLinear:
             self.out.epoch.data_ptr(), ws.data_ptr(), ws.numel(), err.data_ptr(), flags,
             torch.cuda.current_stream(x.device).cuda_stream), "anvilq_w4a16_gemv_allgather")
         return self.out.output(self.slot, self.N)
+
+
+def _plan_struct(plan: dict):
+    from . import _lib
+    return _lib.GemvPlan(**plan)

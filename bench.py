@@ -769,6 +769,27 @@ def tp_measure(args, world, rank, dev, M, e2e=True):
                 lin(l[0][0], flags=1)
 
         g_fused = capture(step_fused)
+    # the projections chained through their gathered rows (each output row is the
+    # next projection's x) with the deferred exchange: a call raises its flag and
+    # moves on, the next call waits for every rank before reading x, and a flag
+    # wait ends the step, so the exchange overlaps the next weight stream
+    chained = (world > 1 and M == 1 and all(p["kernel"] == 1 for p in plans) and
+               all(layers[i][7] == layers[i + 1][6] for i in range(len(layers) - 1)))
+    g_chain = outs_c = clins = None
+    if chained:
+        from anvilq_b200 import tp
+        outs_c = tp.PeerOutputs(max(l[7] for l in layers), slots=len(layers), device=dev)
+        clins = [tp.FusedTPLinear(qw, qz, sc, None, 128, outs_c, i, sharded=True, plan=plans[i], deferred=True)
+                 for i, (x, qw, qz, sc, y, yg, K, N) in enumerate(layers)]
+
+        def step_chain(x0=None):
+            y = layers[0][0][0] if x0 is None else x0
+            for lin in clins:
+                y = lin(y, flags=1)
+            outs_c.wait()
+            return y
+
+        g_chain = capture(step_chain)
 
     def replay(graph):
         def run():
@@ -779,11 +800,13 @@ def tp_measure(args, world, rank, dev, M, e2e=True):
     with ClockSampler(dev.index) as clocks:
         ms = ms_nccl = timed(replay(g_full), stream, args.steps, args.warmup, world, dev)
         ms_fused = timed(replay(g_fused), stream, args.steps, args.warmup, world, dev) if fused else None
+        ms_chain = timed(replay(g_chain), stream, args.steps, args.warmup, world, dev) if chained else None
     ms_comp = timed(replay(g_comp), stream, args.steps, args.warmup, world, dev)
-    # the step runs whichever exchange was faster here (max over ranks, so every rank agrees)
-    fused = fused and ms_fused < ms_nccl
-    if fused:
-        ms = ms_fused
+    # the step runs whichever exchange was fastest here (max over ranks, so every rank agrees)
+    best = min([("nccl", ms_nccl)] + ([("fused", ms_fused)] if fused else []) +
+               ([("chain", ms_chain)] if chained else []), key=lambda t: t[1])
+    path, ms = best
+    fused, chained = path == "fused", path == "chain"
     ms_e2e = h2d = d2h = None
     if e2e:
         # activations from pinned host memory in, gathered outputs back to the host, every step
@@ -792,8 +815,16 @@ def tp_measure(args, world, rank, dev, M, e2e=True):
         h2d = sum(t.numel() * 2 for t in x_host)
         d2h = sum(t.numel() * 2 for t in y_host)
 
+        if chained:   # the chain's input row in, its last gathered row out
+            h2d, d2h = x_host[0].numel() * 2, y_host[-1].numel() * 2
+
         def e2e_step():
             with torch.cuda.stream(stream):
+                if chained:
+                    x0 = layers[0][0]
+                    x0.copy_(x_host[0], non_blocking=True)
+                    y_host[-1].copy_(step_chain(x0[0]).view(1, -1), non_blocking=True)
+                    return
                 for i, ((x, qw, qz, sc, y, yg, K, N), xh, yh) in enumerate(zip(layers, x_host, y_host)):
                     x.copy_(xh, non_blocking=True)
                     if fused:
@@ -808,9 +839,10 @@ def tp_measure(args, world, rank, dev, M, e2e=True):
 
         ms_e2e = timed(e2e_step, stream, args.steps, args.warmup, world, dev, sync_each=True)
     ops.raise_device_errors(dev)
-    del g_full, g_comp, g_fused
-    if outs is not None:
-        outs.close()
+    del g_full, g_comp, g_fused, g_chain
+    for o in (outs, outs_c):
+        if o is not None:
+            o.close()
     launches = 3
     value = full_bytes * args.steps / (ms / 1e3) / 1e9
     per_launch = ms_comp / args.steps / launches
@@ -826,12 +858,18 @@ def tp_measure(args, world, rank, dev, M, e2e=True):
         "data": "synthetic (seeded on the device; x~N(0,1), u4 uniform, scales |N(0,1)|*0.01+1e-3)",
         "config": {"workload": wl["name"], "M": M, "group": 128, "full_bytes_per_step": full_bytes,
                    "shard_bytes_per_rank": shard_bytes, "parallelism": f"tp{world} (column split)",
-                   "graph": ("one CUDA graph per step: 3 GEMVs, each storing its slice into every rank's "
+                   "graph": ("one CUDA graph per step: 3 GEMVs chained through their gathered rows, each "
+                             "storing its slice into every rank's output over NVLink and raising its flag; "
+                             "each waits for every rank before reading x, a flag wait ends the step"
+                             if chained else
+                             "one CUDA graph per step: 3 GEMVs, each storing its slice into every rank's "
                              "output over NVLink and exchanging completion flags (all-gather fused in)" if fused
                              else "one CUDA graph per step: 3 GEMMs + 3 NCCL all-gathers" if world > 1
                              else "one CUDA graph per step: 3 GEMMs (one GPU holds every column)"),
                    "nccl_allgather_path_ms_per_step": round(ms_nccl / args.steps, 5),
                    "fused_allgather_path_ms_per_step": None if ms_fused is None else round(ms_fused / args.steps, 5),
+                   "deferred_chain_path_ms_per_step": None if ms_chain is None else round(ms_chain / args.steps, 5),
+                   "exchange_path": path,
                    "compute_only_ms_per_step": round(ms_comp / args.steps, 5),
                    "exchange_ms_per_step": round(max(0.0, ms - ms_comp) / args.steps, 5),
                    "rank_plans": plans,

@@ -427,6 +427,42 @@ int anvilq_w4a16_gemv_allgather(const uint16_t* x, const int32_t* qweight, const
                                 unsigned int* const* peer_flags, unsigned int* epoch, void* workspace,
                                 size_t workspace_bytes, int* dev_err, unsigned flags, anvilq_stream_t stream);
 
+/* The same fused call under an explicit stream-K plan (kernel ANVILQ_GEMV_KERNEL_STREAM,
+ * e.g. one CTA shape for every slice of a rank's chain; any other kernel:
+ * ANVILQ_EINVAL), with one more flag:
+ *
+ * ANVILQ_GATHER_DEFERRED: the call raises its flag and advances *epoch without
+ * waiting for the other ranks.  Instead, before reading x, every CTA waits
+ * (bounded by ~1 s, ANVILQ_DEV_ERR_TIMEOUT) until every rank's flag has reached
+ * the count of the previous fused call -- so x may be the previous call's
+ * gathered row (a chain of projections whose exchange overlaps the next
+ * projection's weight stream), and no rank still reads the output buffer this
+ * call overwrites when two or more buffers alternate.  The gathered row of a
+ * deferred call is complete on this rank only once every rank's flag has
+ * reached its count: the next deferred call waits for that before reading x,
+ * and anvilq_peer_wait makes it complete for any other consumer (end a chain
+ * with it).  Buffer reuse: with S output buffers alternating, another rank's
+ * call e + S may overwrite the row of call e as soon as every rank has raised
+ * the flag of call e + S - 1 -- so on every rank, whatever reads the row of
+ * call e other than call e + 1 must be enqueued before that rank's call
+ * e + S - 1.  Same values as the plain fused call, and as a GEMV under `plan`
+ * followed by an all-gather, bit for bit.
+ * flags: ANVILQ_GEMM_OVERLAP_PRIOR, ANVILQ_GATHER_DEFERRED. */
+#define ANVILQ_GATHER_DEFERRED 2u
+int anvilq_w4a16_gemv_allgather_planned(const uint16_t* x, const int32_t* qweight, const int32_t* qzeros,
+                                        const uint16_t* scales, const uint16_t* bias, int K, int N, int G,
+                                        int rank, int world, int col_base, int n_full, uint16_t* const* peer_y,
+                                        unsigned int* const* peer_flags, unsigned int* epoch,
+                                        const anvilq_gemv_plan* plan, void* workspace, size_t workspace_bytes,
+                                        int* dev_err, unsigned flags, anvilq_stream_t stream);
+
+/* Waits on `stream` (one thread, bounded by ~1 s: ANVILQ_DEV_ERR_TIMEOUT) until
+ * flags[0 .. world) -- this rank's flag array, peer_flags[rank] of the fused
+ * calls -- have all reached *epoch, i.e. until the last fused call's gathered
+ * row is complete on this rank. */
+int anvilq_peer_wait(const unsigned int* flags, int world, const unsigned int* epoch, int* dev_err,
+                     anvilq_stream_t stream);
+
 /* ---- every decoder layer of one decode token in one persistent kernel ---------
  *
  * Replaces the per-layer body of FP32Model.token (anvil-q1/tests/official_weights.py:462-503)
