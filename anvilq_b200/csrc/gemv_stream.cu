@@ -148,8 +148,11 @@ __device__ __forceinline__ int cta_of(long long c, int T, int P) {
 }
 
 // system-scope flag accesses between GPUs of the node
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// a strong store at system scope; after a system fence it is a release (fence
+// + relaxed stores: one fence for every rank's flag, where a release store per
+// rank would wait for each remote store before issuing the next)
+__device__ __forceinline__ void st_relaxed_sys(unsigned* p, unsigned v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   unsigned v;
@@ -534,9 +537,9 @@ __global__ void __launch_bounds__(W * 32, W <= 8 ? 2 : 1)
   // PEER: the CTA that completed the rank's last band raises this rank's flag in
   // every rank and waits (bounded) until every rank's flag reached this call
   if (PEER && s_done && threadIdx.x == 0) {
-    __threadfence_system();
+    __threadfence_system();   // with the relaxed stores below: the release of this rank's flag
     const unsigned e = *p.epoch + 1;
-    for (int r = 0; r < p.world; ++r) st_release_sys(p.peer_flags[r] + p.tp_rank, e);
+    for (int r = 0; r < p.world; ++r) st_relaxed_sys(p.peer_flags[r] + p.tp_rank, e);
     if (p.deferred) {   // the next deferred call (or peer_wait_kernel) waits for the others
       *p.epoch = e;
       return;

@@ -226,8 +226,11 @@ __device__ __forceinline__ void st_async_f32(uint32_t addr, float v, uint32_t ba
                : "memory");
 }
 // system-scope flag accesses between GPUs of the node
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// a strong store at system scope; after a system fence it is a release (fence
+// + relaxed stores: one fence for every rank's flag, where a release store per
+// rank would wait for each remote store before issuing the next)
+__device__ __forceinline__ void st_relaxed_sys(unsigned* p, unsigned v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   unsigned v;
@@ -655,9 +658,9 @@ __global__ void __launch_bounds__(kThreads, 4)
     }
     __syncthreads();
     if (!s_last || threadIdx.x != 0) return;
-    __threadfence_system();
+    __threadfence_system();   // with the relaxed stores below: the release of this rank's flag
     const unsigned e = *p.epoch + 1;
-    for (int r = 0; r < p.world; ++r) st_release_sys(p.peer_flags[r] + p.tp_rank, e);
+    for (int r = 0; r < p.world; ++r) st_relaxed_sys(p.peer_flags[r] + p.tp_rank, e);
     const unsigned* mine = p.peer_flags[p.tp_rank];
     const unsigned long long t_start = globaltimer();
     bool done = false;
